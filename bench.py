@@ -1,0 +1,491 @@
+"""Benchmark of the B200 linear-layer path (mruntime's Backend::gemm).
+
+Workload (default): the Qwen2.5-7B projection sweep -- one decoder layer's
+four projections, qkv 3584->4608, o 3584->3584, gate+up 3584->37888 and
+down 18944->3584, BF16 weights uploaded once as FP16, FP16 activations
+x[M,3584] and x_down[M,18944] ~ N(0,1), seed 4 (mruntime_b200/workloads.py).
+A step is one pass of the four GEMMs over one batch of M = 2048 tokens; the
+headline metric is matmul TFLOP/s.  The same run also times every M of the
+sweep (1 .. 2048; M <= 16 is the HBM-bound decode regime, reported in GB/s).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+With N > 1 (launched by torchrun, one rank per GPU) the weights are sharded
+tensor-parallel: qkv and gate/up by rows (column-parallel, no exchange), o and
+down by K (row-parallel, FP32 partials all-reduced over NVLink by NCCL, then
+rounded once to FP16).  Total work is fixed, so scaling is strong.
+
+``--impl reference`` times the reference's own CPU gemm (built from its
+sources into oracle/_ref) on a bounded sample of the same workload on the
+host cores; under torchrun only rank 0 runs it.
+
+Weights total 466 MB per step (larger than the 126 MB L2), so every timed
+step streams them from HBM; no L2 flush is needed.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from mruntime_b200 import workloads as WL  # noqa: E402
+
+METRIC = "matmul TFLOP/s (Qwen2.5-7B projection sweep, M=2048 prefill step)"
+UNIT = "TFLOP/s"
+HEADLINE_M = 2048
+# Per-launch DRAM traffic of the dominant kernel (gate+up GEMM at M=2048) from
+# the ncu capture summarised in profiles/ (dram__bytes_read.sum +
+# dram__bytes_write.sum); None until a capture exists.
+GATEUP_TRAFFIC_BYTES = None
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="mruntime_b200", choices=["mruntime_b200", "reference"])
+    ap.add_argument("--m", type=int, default=HEADLINE_M, help="tokens per step (headline 2048)")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the per-M sweep extras")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def load_peaks() -> dict:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"],
+                "bf16_tflops_sustained": p.get("bf16_tflops_sustained", p["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling while the timed loop runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.dev)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.t = threading.Thread(target=self._read, daemon=True)
+        self.t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.t:
+            self.t.join(timeout=2)
+        sm, smax, power, reasons = [], [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "samples": len(sm), "power_w_max": max(power) if power else None, "reasons": sorted(reasons)}
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+
+class Proj:
+    """One projection of the sweep as held by this rank."""
+
+    def __init__(self, name, kind, weight, x, y, partial, n_full, k_full):
+        self.name, self.kind, self.w, self.x, self.y, self.partial = name, kind, weight, x, y, partial
+        self.n_full, self.k_full = n_full, k_full
+
+
+def setup_gpu(rank: int, world: int, local: int, max_m: int):
+    import torch
+
+    from mruntime_b200 import capi
+
+    torch.cuda.set_device(local)
+    capi.init(local)
+    stream = torch.cuda.current_stream().cuda_stream
+    tp = None
+    if world > 1:
+        import torch.distributed as dist
+
+        uid = [capi.TensorParallel.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        tp = capi.TensorParallel(rank, world, uid[0])
+    d = WL.sweep_7b(max_m=max_m)
+    projs = []
+    for name, parts, k in WL.SWEEP_7B:
+        w = np.ascontiguousarray(d[name])
+        n = sum(parts)
+        kind = WL.SWEEP_7B_PARALLEL[name]
+        xfull = d["x_down"] if name == "down" else d["x"]
+        if world > 1 and kind == "row":
+            k0, k1 = capi.shard_cols(k, world, rank)
+            wt = capi.Weight(w.ctypes.data, capi.BF16, False, n, k, None, (k0, k1), stream)
+            xin = np.ascontiguousarray(xfull[:, k0:k1])
+        else:
+            ranges = capi.shard_rows(list(parts), world, rank) if world > 1 else None
+            wt = capi.Weight(w.ctypes.data, capi.BF16, False, n, k, ranges, None, stream)
+            xin = xfull
+        x = torch.from_numpy(np.ascontiguousarray(xin).view(np.int16)).cuda()
+        y = torch.empty((max_m, wt.n), dtype=torch.int16, device="cuda")
+        partial = torch.empty((max_m, wt.n), dtype=torch.float32, device="cuda") if (world > 1 and kind == "row") else None
+        projs.append(Proj(name, kind, wt, x, y, partial, n, k))
+    del d
+    torch.cuda.synchronize()
+    return projs, tp, stream
+
+
+def run_step(projs, tp, stream, M, ev=None):
+    """One pass of the four projections over M tokens.  ev = (start, end)
+    events recorded around the gate+up GEMM (the dominant kernel)."""
+    from mruntime_b200 import capi
+
+    for p in projs:
+        if p.name == "gateup" and ev is not None:
+            ev[0].record()
+        if p.partial is None:
+            capi.gemm(p.w, p.x.data_ptr(), p.x.shape[1], p.y.data_ptr(), p.w.n, M, False, stream)
+        else:
+            capi.gemm_f32(p.w, p.x.data_ptr(), p.x.shape[1], p.partial.data_ptr(), p.w.n, M, stream)
+            tp.allreduce_f32_to_f16(p.partial.data_ptr(), p.y.data_ptr(), M * p.w.n, stream)
+        if p.name == "gateup" and ev is not None:
+            ev[1].record()
+
+
+def barrier_sync(world):
+    import torch
+
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def time_steps(projs, tp, stream, M, steps, world, dominant=False):
+    import torch
+
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)] \
+        if dominant else [None] * steps
+    barrier_sync(world)
+    start.record()
+    for i in range(steps):
+        run_step(projs, tp, stream, M, evs[i])
+    end.record()
+    torch.cuda.synchronize()
+    total_ms = start.elapsed_time(end)
+    dom_ms = statistics.mean(a.elapsed_time(b) for a, b in evs) if dominant else None
+    return max_over_ranks(total_ms, world), dom_ms
+
+
+def e2e_host_buffers(projs, tp, stream, M, steps, world):
+    """Same step through the host-buffer entry point (N=1: mrt_gemm_host, the
+    reference's calling convention) or, under TP, pinned-host copies around the
+    device calls.  Returns (ms per step, h2d bytes, d2h bytes)."""
+    import torch
+
+    from mruntime_b200 import capi
+
+    hx = [torch.empty((M, p.x.shape[1]), dtype=torch.int16, pin_memory=True) for p in projs]
+    for h, p in zip(hx, projs):
+        h.copy_(p.x[:M].cpu())
+    hy = [torch.empty((M, p.w.n), dtype=torch.int16, pin_memory=True) for p in projs]
+    h2d = sum(h.numel() * 2 for h in hx)
+    d2h = sum(h.numel() * 2 for h in hy)
+
+    def one():
+        if world == 1:
+            for h, g, p in zip(hx, hy, projs):
+                capi.gemm_host(p.w, h.data_ptr(), g.data_ptr(), M, False, stream)
+        else:
+            for h, p in zip(hx, projs):
+                p.x[:M].copy_(h, non_blocking=True)
+            run_step(projs, tp, stream, M)
+            for g, p in zip(hy, projs):
+                g.copy_(p.y[:M], non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+
+    for _ in range(2):
+        one()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    barrier_sync(world)
+    start.record()
+    for _ in range(steps):
+        one()
+    end.record()
+    torch.cuda.synchronize()
+    return max_over_ranks(start.elapsed_time(end), world) / steps, h2d, d2h
+
+
+def step_flops(M: int) -> float:
+    return WL.sweep_flops(M)
+
+
+def gpu_arm(args, rank, world, local):
+    import torch
+
+    from mruntime_b200 import capi
+
+    peaks = load_peaks()
+    M = args.m
+    projs, tp, stream = setup_gpu(rank, world, local, max(M, max(WL.SWEEP_M) if not args.no_sweep else M))
+    clocks = ClockSampler(local)
+    for _ in range(args.warmup):
+        run_step(projs, tp, stream, M)
+    capi.sync(stream)
+    clocks.start()
+    time.sleep(0.3)  # let the sampler attach before the timed region
+    launches0 = capi.launch_count()
+    total_ms, dom_ms = time_steps(projs, tp, stream, M, args.steps, world, dominant=True)
+    launches = capi.launch_count() - launches0
+    clk = clocks.stop()
+    capi.sync(stream)  # raises if any bounded wait inside a kernel gave up
+    ms = total_ms / args.steps
+    value = step_flops(M) / (ms * 1e-3) / 1e12
+
+    gate = next(p for p in projs if p.name == "gateup")
+    dom_flops = 2.0 * M * gate.w.n * gate.w.k
+    dom_tflops = dom_flops / (dom_ms * 1e-3) / 1e12
+    peak = peaks["bf16_tflops_sustained"]
+    roofline = {"bound": "tensor", "achieved": round(dom_tflops, 1), "peak": peak, "unit": "TFLOP/s",
+                "frac": round(dom_tflops / peak, 4), "traffic": GATEUP_TRAFFIC_BYTES,
+                "kernel": f"tc_gemm_kernel gate+up {M}x{gate.w.n}x{gate.w.k} (rank-local shard)",
+                "peak_source": f"{peaks['source']} bf16 cuBLAS, sustained (burst {peaks['bf16_tflops']})",
+                "algorithmic_flops_per_launch": dom_flops, "ms_per_launch": round(dom_ms, 5)}
+
+    e2e_ms, h2d, d2h = e2e_host_buffers(projs, tp, stream, M, max(3, min(args.steps, 10)), world)
+    e2e = {"value": round(step_flops(M) / (e2e_ms * 1e-3) / 1e12, 2), "unit": UNIT, "ms_per_step": round(e2e_ms, 3),
+           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+           "path": "mrt_gemm_host (host buffers, copies inside the timed region)" if world == 1 else
+           "pinned-host copies + mrt_gemm / mrt_gemm_f32 + mrt_tp_allreduce_f32_to_f16"}
+
+    sweep = []
+    if not args.no_sweep:
+        for m in WL.SWEEP_M:
+            for _ in range(3):
+                run_step(projs, tp, stream, m)
+            n_it = 50 if m <= 128 else 20
+            t_ms, _ = time_steps(projs, tp, stream, m, n_it, world)
+            t = t_ms / n_it
+            tf = step_flops(m) / (t * 1e-3) / 1e12
+            gbs = WL.sweep_bytes(m) / (t * 1e-3) / 1e9
+            bound = "hbm" if m <= 64 else "tensor"
+            frac = gbs / peaks["hbm_gbs"] if bound == "hbm" else tf / peaks["bf16_tflops_sustained"]
+            sweep.append({"M": m, "ms": round(t, 4), "TFLOP/s": round(tf, 1), "GB/s": round(gbs, 1), "bound": bound,
+                          "frac": round(frac, 4)})
+        capi.sync(stream)
+    return {"ms": ms, "value": value, "roofline": roofline, "e2e": e2e, "clocks": clk, "launches": launches,
+            "sweep": sweep, "peaks": peaks, "projs": projs, "tp": tp}
+
+
+# ---------------------------------------------------------------------------
+# CPU: the reference's own gemm (oracle/_ref, built from the reference sources)
+# ---------------------------------------------------------------------------
+
+class RefSample:
+    """A bounded sample of the sweep step for the reference's CPU gemm:
+    `rows` rows of x through every projection, restricted to the first
+    `n_frac` of each weight's output rows when even one row is too slow.
+    Rows are independent in the reference (cpu_backend.cpp:143-166), so the
+    sample's throughput is the full step's."""
+
+    def __init__(self, M: int, threads: int = 0):
+        from oracle import oracle as O
+
+        self.O = O
+        self.rb = O.RefBackend(threads)
+        d = WL.sweep_7b(max_m=M)
+        self.items = []
+        for name, parts, k in WL.SWEEP_7B:
+            x = d["x_down"] if name == "down" else d["x"]
+            self.items.append((name, x, d[name]))
+        self.rows, self.n_frac = 1, 1.0
+
+    def flops(self) -> float:
+        return sum(2.0 * self.rows * int(w.shape[0] * self.n_frac) * w.shape[1] for _, _, w in self.items)
+
+    def run(self):
+        for _, x, w in self.items:
+            n = max(1, int(w.shape[0] * self.n_frac))
+            self.rb.gemm(x[: self.rows], self.O.FP16, w[:n], self.O.BF16, trans_b=True)
+
+    def calibrate(self, seconds: float):
+        """Choose rows / n_frac so that one run() takes about `seconds`."""
+        self.rows, self.n_frac = 1, 0.05
+        self.run()  # first call pays for thread start-up and page faults
+        t0 = time.perf_counter()
+        self.run()
+        t = max(time.perf_counter() - t0, 1e-4)
+        per_full_row = t / 0.05
+        if per_full_row <= seconds:
+            self.n_frac = 1.0
+            self.rows = max(1, min(64, int(seconds / per_full_row)))
+        else:
+            self.n_frac = max(0.002, seconds / per_full_row)
+
+    def describe(self, M: int) -> str:
+        return (f"{self.rows} of {M} rows x {self.n_frac:.3f} of each weight's output rows, all four projections "
+                f"(qkv, o, gate+up, down), {self.flops() / 1e9:.2f} GFLOP per sample")
+
+
+def cpu_baseline(M: int, seconds: float) -> dict:
+    s = RefSample(M)
+    s.calibrate(seconds / 3)
+    s.run()  # warm
+    reps, t_total = 0, 0.0
+    while t_total < seconds * 0.66 or reps < 2:
+        t0 = time.perf_counter()
+        s.run()
+        t_total += time.perf_counter() - t0
+        reps += 1
+    value = s.flops() * reps / t_total / 1e12
+    return {"value": value, "unit": UNIT, "cores": os.cpu_count(), "kind": "reference",
+            "sample": s.describe(M) + f"; {reps} samples in {t_total:.1f} s"}
+
+
+def reference_arm(args, rank, world):
+    if rank != 0:
+        return None
+    M = args.m
+    budget = 150.0  # seconds for the whole --warmup + --steps run
+    per_step = min(20.0, max(0.05, budget / max(1, args.steps + args.warmup)))
+    s = RefSample(M)
+    s.calibrate(per_step)
+    for _ in range(args.warmup):
+        s.run()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        s.run()
+    dt = time.perf_counter() - t0
+    value = s.flops() * args.steps / dt / 1e12
+    cpu = {"value": value, "unit": UNIT, "cores": os.cpu_count(), "kind": "reference",
+           "sample": s.describe(M)}
+    return {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32 accumulate (fp16 x, bf16 w)",
+            "data": "synthetic (seeded N(0,1) FP16 activations, N(0,0.02) BF16 weights)",
+            "config": workload_config(M, world), "cpu_baseline": cpu,
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def workload_config(M: int, world: int) -> dict:
+    return {"workload": "qwen2.5-7b projection sweep (qkv 3584->4608, o 3584->3584, gate+up 3584->37888, "
+                        "down 18944->3584), one step = the four GEMMs at M tokens",
+            "M": M, "seed": 4, "weights": "bf16 source, uploaded once as fp16",
+            "parallelism": f"tp{world}" if world > 1 else "single gpu",
+            "l2": "inputs larger than L2 (466 MB of fp16 weights streamed per step)"}
+
+
+def main():
+    args = parse_args()
+    rank, world, local = dist_env()
+    if world != args.gpus and "WORLD_SIZE" in os.environ:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+    if args.impl == "reference":
+        line = reference_arm(args, rank, world)
+        if line is not None:
+            print(json.dumps(line))
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return
+    r = gpu_arm(args, rank, world, local)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            cpu = cpu_baseline(args.m, args.cpu_seconds)
+        except FileNotFoundError as e:
+            cpu = {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "reference",
+                   "sample": f"unavailable: {e}"}
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(r["value"], 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(r["ms"], 5), "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)",
+                "data": "synthetic (seeded N(0,1) FP16 activations, N(0,0.02) BF16 weights)",
+                "config": workload_config(args.m, world), "e2e": r["e2e"], "roofline": r["roofline"],
+                "cpu_baseline": cpu, "clocks": r["clocks"], "gpu_launches": r["launches"], "sweep": r["sweep"]}
+        print(json.dumps(line))
+    if r["tp"] is not None:
+        r["tp"].destroy()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,231 @@
+/*
+ * mrt_b200.h -- C ABI of the B200 linear-layer path for mruntime.
+ *
+ * This is the boundary a host runtime binds (ctypes, cgo, JNI, or the C++
+ * CudaBackend in mruntime_b200/csrc/cuda_backend.h).  It replaces the body of
+ * mruntime::Backend::gemm (reference include/mruntime/backend.h:13-21) and the
+ * pieces around it that the reference runs on the host: the weight load and
+ * repack step, the q/k/v bias add, and the greedy argmax over logits.
+ *
+ * Conventions
+ *   - Every entry point returns an int status (MRT_OK == 0).  On failure
+ *     mrt_last_error_string() describes the error of the calling thread.
+ *   - Pointers named *_dev are device pointers on the current device; *_host
+ *     are host pointers (pinned memory makes the copies asynchronous).
+ *   - 16-bit data travel as raw bit patterns (IEEE binary16 or bfloat16).
+ *   - `stream` is a cudaStream_t (NULL = the legacy default stream).  Calls
+ *     are asynchronous on that stream unless documented otherwise; one
+ *     context's scratch buffers are shared, so calls that use scratch must be
+ *     issued on one stream at a time per device.
+ *   - Weights are W[N, K] row-major (Hugging Face layout) and every GEMM
+ *     computes Y[M, N] = X[M, K] * W^T, i.e. the reference's call pattern
+ *     gemm(A, B, C, 1, 0, trans_a=false, trans_b=true)
+ *     (reference src/models/qwen/qwen_model.cpp:126-128, 256, 278-279, 288, 374).
+ *   - Accumulation is FP32 and outputs are rounded once to FP16 with
+ *     round-to-nearest-even, as float_to_fp16_bits does
+ *     (reference include/mruntime/dtype.h:39-119).
+ */
+#ifndef MRT_B200_H
+#define MRT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define MRT_OK 0
+#define MRT_ERR_INVALID_ARG 1
+#define MRT_ERR_SHAPE 2
+#define MRT_ERR_DTYPE 3
+#define MRT_ERR_CUDA 4
+#define MRT_ERR_NCCL 5
+#define MRT_ERR_TIMEOUT 6
+#define MRT_ERR_UNSUPPORTED 7
+#define MRT_ERR_NOT_INITIALIZED 8
+
+/* Element types, numbered as mruntime::DType (reference include/mruntime/dtype.h:12-16). */
+#define MRT_FP16 0
+#define MRT_BF16 1
+#define MRT_FP32 2
+
+/* mrt_gemm flags. */
+#define MRT_GEMM_BIAS 1u /* add the weight's attached bias after rounding, see mrt_weight_attach_bias */
+
+typedef struct mrt_weight_s* mrt_weight;
+typedef struct mrt_tp_s* mrt_tp;
+
+/* ---------------------------------------------------------------- runtime */
+
+/* Library version (major*10000 + minor*100 + patch). */
+int mrt_version(void);
+
+/* Make `device` current for this thread and create its context (scratch
+ * buffers, device error flag, TMA encoder).  Idempotent.  Replaces the
+ * construction of CpuBackend (reference include/mruntime/cpu_backend.h:10-11). */
+int mrt_init(int device);
+
+/* Text of the last error raised on this thread ("" if none). */
+const char* mrt_last_error_string(void);
+
+/* Wait for all work on `stream`, then read and clear the device-side error
+ * flag that bounded waits inside the kernels set when they give up.
+ * Returns MRT_ERR_TIMEOUT if a kernel reported a timed-out wait. */
+int mrt_sync(void* stream);
+
+/* Grow the context's scratch buffer to at least `bytes` now (call before
+ * capturing a CUDA graph that contains split-K or argmax launches). */
+int mrt_reserve_workspace(size_t bytes);
+
+/* Number of streaming multiprocessors of the current device. */
+int mrt_device_sm_count(int* out);
+
+/* Kernels this library has launched in this process so far (all devices). */
+int mrt_launch_count(int64_t* out);
+
+/* ---------------------------------------------------------------- weights */
+
+/*
+ * Upload a weight (or a tensor-parallel shard of it) once and convert it to
+ * the FP16 K-major layout the kernels stream.  Replaces the reference's
+ * SafeTensorsFile::load_tensor_copy of a projection weight
+ * (src/loader/safetensors.cpp:166-172) together with the packed-RHS cache of
+ * CpuBackend::get_or_create_packed_rhs_fp16 (src/core/cpu_backend.cpp:24-70):
+ * BF16 and FP32 sources are rounded to FP16 with the same converter the
+ * reference's packing step uses (cpu_backend.cpp:48-63), once, on the device.
+ *
+ *   src        full weight W[N, K] of dtype src_dtype (host or device memory)
+ *   row_ranges NULL for all rows, else n_ranges pairs [begin, end) of rows of
+ *              W kept, in order (column-parallel shard of a fused weight takes
+ *              one range per part)
+ *   k_begin/k_end  columns of W kept ([0, K) for the whole row; a row-parallel
+ *              shard keeps a slice)
+ * The handle is the cache key (not the source address), so a freed and
+ * reused host buffer cannot hit a stale entry.
+ */
+int mrt_weight_upload(const void* src, int src_dtype, int src_on_device, int64_t N, int64_t K,
+                      const int64_t* row_ranges, int64_t n_ranges, int64_t k_begin, int64_t k_end,
+                      void* stream, mrt_weight* out);
+
+/* Attach a bias vector b[N] (full length of the original weight; the
+ * handle's row ranges pick the shard).  It is stored in FP16 after the
+ * reference's load-time conversion (src/models/qwen/qwen_model.cpp:93-101). */
+int mrt_weight_attach_bias(mrt_weight w, const void* src, int src_dtype, int src_on_device,
+                           void* stream);
+
+int mrt_weight_free(mrt_weight w);
+
+/* Rows (N) and columns (K) of the uploaded shard, and its FP16 device data. */
+int mrt_weight_shape(mrt_weight w, int64_t* n, int64_t* k);
+int mrt_weight_data(mrt_weight w, void** dev_ptr);
+
+/* ---------------------------------------------------------------- GEMM */
+
+/*
+ * y_dev[M, N] (row stride ldy, FP16) = fp16(x_dev[M, K] (row stride ldx, FP16) * W^T).
+ * With MRT_GEMM_BIAS the attached bias is added as the reference's q/k/v
+ * bias step does it: fp16(fp32(fp16(acc)) + fp32(bias))
+ * (src/models/qwen/qwen_model.cpp:130-155).
+ * M <= 64 runs the HBM-streaming skinny kernel; larger M runs the tcgen05
+ * tensor-core kernel.  Replaces Backend::gemm (include/mruntime/backend.h:13-21)
+ * as implemented by CpuBackend::gemm (src/core/cpu_backend.cpp:72-169).
+ */
+int mrt_gemm(mrt_weight w, const void* x_dev, int64_t ldx, void* y_dev, int64_t ldy, int64_t M,
+             unsigned flags, void* stream);
+
+/* Same product without the final rounding: y_dev is FP32.  Used for the
+ * partial sums of a row-parallel (K-split) shard before the all-reduce. */
+int mrt_gemm_f32(mrt_weight w, const void* x_dev, int64_t ldx, float* y_dev, int64_t ldy,
+                 int64_t M, void* stream);
+
+/* mrt_gemm on host buffers, the reference's own calling convention (its
+ * Tensors live in host memory): copies x_host to the device, runs the
+ * product, copies y back and waits.  x is [M, K] and y [M, N], both dense. */
+int mrt_gemm_host(mrt_weight w, const void* x_host, void* y_host, int64_t M, unsigned flags,
+                  void* stream);
+
+/*
+ * The full Backend::gemm contract (include/mruntime/backend.h:13-21) for call
+ * patterns the model never issues: any of FP16/BF16/FP32 for A, B and C,
+ * trans_a/trans_b, alpha and beta, unaligned shapes.  A is [a_rows, a_cols],
+ * B is [b_rows, b_cols], C is [M, N] dense.  Each output is one FP32 sum in
+ * k order followed by *alpha, +beta*C and the reference's rounding, like the
+ * scalar path of src/core/cpu_backend.cpp:139-168.  Device pointers only.
+ */
+int mrt_gemm_general(const void* a_dev, int a_dtype, int64_t a_rows, int64_t a_cols,
+                     const void* b_dev, int b_dtype, int64_t b_rows, int64_t b_cols, void* c_dev,
+                     int c_dtype, float alpha, float beta, int trans_a, int trans_b, void* stream);
+
+/* ---------------------------------------------------------------- logits */
+
+/*
+ * Greedy argmax of each of M rows of FP16 logits (row stride ld): the first
+ * index holding the largest value, NaN never chosen, an all -inf/NaN row
+ * gives 0 -- the selection of InferenceEngine::sample
+ * (src/engine/inference_engine.cpp:84-95).  Writes the winning index plus
+ * index_base (int64) and its value (FP32) per row; either output may be NULL.
+ */
+int mrt_argmax_f16(const void* logits_dev, int64_t M, int64_t V, int64_t ld, int64_t index_base,
+                   int64_t* idx_dev, float* val_dev, void* stream);
+
+/* lm_head and greedy pick in one call: logits_dev[M, N] = x * W^T (FP16),
+ * then mrt_argmax_f16 on every row (src/models/qwen/qwen_model.cpp:374 followed
+ * by src/engine/inference_engine.cpp:84-95).  index_base offsets the indices
+ * of a vocabulary shard. */
+int mrt_lm_head_argmax(mrt_weight w, const void* x_dev, int64_t ldx, int64_t M, void* logits_dev,
+                       int64_t index_base, int64_t* idx_dev, float* val_dev, void* stream);
+
+/* ---------------------------------------------------------------- conversions */
+
+/* Element-wise conversions on the device with the reference's rounding
+ * (include/mruntime/dtype.h:39-194): src_dtype -> dst_dtype, n elements. */
+int mrt_convert(const void* src_dev, int src_dtype, void* dst_dev, int dst_dtype, int64_t n,
+                void* stream);
+
+/* ---------------------------------------------------------------- tensor parallel */
+
+/*
+ * Shard map.  Column-parallel weights (q/k/v, gate/up, lm_head) keep rows:
+ * for a weight made of n_parts stacked parts (e.g. q,k,v or gate,up) rank r
+ * keeps, from every part p of size part_rows[p], the rows
+ * [off_p + r*part_rows[p]/world, off_p + (r+1)*part_rows[p]/world), so every
+ * rank holds matching columns of each part.  Writes 2*n_parts int64 into
+ * ranges_out.  Row-parallel weights (o_proj, down) keep the column slice
+ * returned by mrt_shard_cols.  The reference has no parallelism beyond its
+ * thread pool (src/core/cpu_backend.cpp:139-168); this is new.
+ */
+int mrt_shard_rows(const int64_t* part_rows, int64_t n_parts, int world, int rank,
+                   int64_t* ranges_out);
+int mrt_shard_cols(int64_t K, int world, int rank, int64_t* k_begin, int64_t* k_end);
+
+/* NCCL unique id for a new tensor-parallel group (written to id_out, len >= 128). */
+int mrt_tp_unique_id(void* id_out, size_t len);
+
+/* Join a group of `world` ranks (one process per GPU) with the id rank 0 made.
+ * Blocks until every rank has joined.  Uses the NCCL already loaded in the
+ * process when there is one. */
+int mrt_tp_init(int rank, int world, const void* id, size_t len, mrt_tp* out);
+int mrt_tp_destroy(mrt_tp tp);
+
+/* Row-parallel output: sum the FP32 partials of all ranks in place, then
+ * round once to FP16 into out_dev (count elements; out may alias nothing). */
+int mrt_tp_allreduce_f32_to_f16(mrt_tp tp, float* partial_dev, void* out_dev, int64_t count,
+                                void* stream);
+
+/* Column-parallel gather: every rank's FP16 [M, n_local] block is assembled
+ * into out_dev[M, world*n_local] in rank order. */
+int mrt_tp_allgather_cols_f16(mrt_tp tp, const void* local_dev, int64_t M, int64_t n_local,
+                              void* out_dev, void* stream);
+
+/* Vocabulary-sharded greedy pick: combine each rank's per-row (value, global
+ * index) into the global first maximum; idx_out_dev[M] is the same on every
+ * rank. */
+int mrt_tp_argmax(mrt_tp tp, const float* val_dev, const int64_t* idx_dev, int64_t M,
+                  int64_t* idx_out_dev, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MRT_B200_H */

@@ -1,0 +1,242 @@
+"""ctypes binding of the C ABI in include/mrt_b200.h.
+
+This is the Python caller of the same entry points a C++ or cgo host binds;
+the tests and bench.py go through it.  Device buffers are passed as raw
+pointers (``tensor.data_ptr()`` of a torch CUDA tensor works), streams as
+``cudaStream_t`` values (``torch.cuda.current_stream().cuda_stream``).
+
+Every failing call raises :class:`MrtError` with the library's message.  The
+library must have been built (``python -m mruntime_b200.build``); there is no
+fallback path.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+
+from . import build as _build
+
+LIB_PATH = _build.LIB
+HEADER = os.path.join(_build.INCLUDE, "mrt_b200.h")
+
+MRT_OK = 0
+MRT_ERR_TIMEOUT = 6
+FP16, BF16, FP32 = 0, 1, 2
+GEMM_BIAS = 1
+
+_lib: C.CDLL | None = None
+
+
+class MrtError(RuntimeError):
+    def __init__(self, code: int, fn: str, msg: str):
+        super().__init__(f"{fn} failed with status {code}: {msg}")
+        self.code = code
+
+
+def header_functions() -> list[str]:
+    """Names of every entry point declared in include/mrt_b200.h."""
+    text = open(HEADER).read()
+    return re.findall(r"^\s*(?:int|const char\*)\s+(mrt_\w+)\s*\(", text, flags=re.M)
+
+
+_vp, _i64, _int, _u32, _sz = C.c_void_p, C.c_int64, C.c_int, C.c_uint, C.c_size_t
+_SIGS = {
+    "mrt_version": (_int, []),
+    "mrt_init": (_int, [_int]),
+    "mrt_last_error_string": (C.c_char_p, []),
+    "mrt_sync": (_int, [_vp]),
+    "mrt_reserve_workspace": (_int, [_sz]),
+    "mrt_device_sm_count": (_int, [C.POINTER(_int)]),
+    "mrt_launch_count": (_int, [C.POINTER(_i64)]),
+    "mrt_weight_upload": (_int, [_vp, _int, _int, _i64, _i64, C.POINTER(_i64), _i64, _i64, _i64, _vp,
+                                 C.POINTER(_vp)]),
+    "mrt_weight_attach_bias": (_int, [_vp, _vp, _int, _int, _vp]),
+    "mrt_weight_free": (_int, [_vp]),
+    "mrt_weight_shape": (_int, [_vp, C.POINTER(_i64), C.POINTER(_i64)]),
+    "mrt_weight_data": (_int, [_vp, C.POINTER(_vp)]),
+    "mrt_gemm": (_int, [_vp, _vp, _i64, _vp, _i64, _i64, _u32, _vp]),
+    "mrt_gemm_f32": (_int, [_vp, _vp, _i64, _vp, _i64, _i64, _vp]),
+    "mrt_gemm_host": (_int, [_vp, _vp, _vp, _i64, _u32, _vp]),
+    "mrt_gemm_general": (_int, [_vp, _int, _i64, _i64, _vp, _int, _i64, _i64, _vp, _int, C.c_float, C.c_float,
+                                _int, _int, _vp]),
+    "mrt_argmax_f16": (_int, [_vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp]),
+    "mrt_lm_head_argmax": (_int, [_vp, _vp, _i64, _i64, _vp, _i64, _vp, _vp, _vp]),
+    "mrt_convert": (_int, [_vp, _int, _vp, _int, _i64, _vp]),
+    "mrt_shard_rows": (_int, [C.POINTER(_i64), _i64, _int, _int, C.POINTER(_i64)]),
+    "mrt_shard_cols": (_int, [_i64, _int, _int, C.POINTER(_i64), C.POINTER(_i64)]),
+    "mrt_tp_unique_id": (_int, [_vp, _sz]),
+    "mrt_tp_init": (_int, [_int, _int, _vp, _sz, C.POINTER(_vp)]),
+    "mrt_tp_destroy": (_int, [_vp]),
+    "mrt_tp_allreduce_f32_to_f16": (_int, [_vp, _vp, _vp, _i64, _vp]),
+    "mrt_tp_allgather_cols_f16": (_int, [_vp, _vp, _i64, _i64, _vp, _vp]),
+    "mrt_tp_argmax": (_int, [_vp, _vp, _vp, _i64, _vp, _vp]),
+}
+
+
+def lib() -> C.CDLL:
+    """Load libmrt_b200.so (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise FileNotFoundError(f"{LIB_PATH} is missing: build it with `python -m mruntime_b200.build`")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(L, name, None)
+            if fn is None:
+                continue
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _check(rc: int, fn: str) -> None:
+    if rc != MRT_OK:
+        msg = lib().mrt_last_error_string()
+        raise MrtError(rc, fn, msg.decode() if msg else "")
+
+
+def call(fn: str, *args) -> None:
+    """Call an entry point and raise MrtError on a non-zero status."""
+    _check(getattr(lib(), fn)(*args), fn)
+
+
+def init(device: int = 0) -> None:
+    call("mrt_init", device)
+
+
+def sync(stream: int | None = None) -> None:
+    call("mrt_sync", stream)
+
+
+def launch_count() -> int:
+    v = C.c_int64(0)
+    call("mrt_launch_count", C.byref(v))
+    return v.value
+
+
+def sm_count() -> int:
+    v = C.c_int(0)
+    call("mrt_device_sm_count", C.byref(v))
+    return v.value
+
+
+class Weight:
+    """An uploaded weight (or shard) -- the handle returned by mrt_weight_upload."""
+
+    def __init__(self, src_ptr: int, src_dtype: int, src_on_device: bool, N: int, K: int,
+                 row_ranges: list[tuple[int, int]] | None = None, k_range: tuple[int, int] | None = None,
+                 stream: int | None = None):
+        h = C.c_void_p()
+        rr = None
+        n_ranges = 0
+        if row_ranges:
+            flat = [v for pair in row_ranges for v in pair]
+            rr = (C.c_int64 * len(flat))(*flat)
+            n_ranges = len(row_ranges)
+        k0, k1 = k_range if k_range is not None else (0, K)
+        call("mrt_weight_upload", src_ptr, src_dtype, int(src_on_device), N, K, rr, n_ranges, k0, k1, stream,
+             C.byref(h))
+        self.h = h
+        n, k = C.c_int64(), C.c_int64()
+        call("mrt_weight_shape", h, C.byref(n), C.byref(k))
+        self.n, self.k = n.value, k.value
+
+    def attach_bias(self, src_ptr: int, src_dtype: int, src_on_device: bool, stream: int | None = None):
+        call("mrt_weight_attach_bias", self.h, src_ptr, src_dtype, int(src_on_device), stream)
+
+    def data_ptr(self) -> int:
+        p = C.c_void_p()
+        call("mrt_weight_data", self.h, C.byref(p))
+        return p.value
+
+    def free(self):
+        if self.h:
+            lib().mrt_weight_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+def gemm(w: Weight, x_ptr: int, ldx: int, y_ptr: int, ldy: int, M: int, bias: bool = False,
+         stream: int | None = None) -> None:
+    call("mrt_gemm", w.h, x_ptr, ldx, y_ptr, ldy, M, GEMM_BIAS if bias else 0, stream)
+
+
+def gemm_f32(w: Weight, x_ptr: int, ldx: int, y_ptr: int, ldy: int, M: int, stream: int | None = None) -> None:
+    call("mrt_gemm_f32", w.h, x_ptr, ldx, y_ptr, ldy, M, stream)
+
+
+def gemm_host(w: Weight, x_host_ptr: int, y_host_ptr: int, M: int, bias: bool = False,
+              stream: int | None = None) -> None:
+    call("mrt_gemm_host", w.h, x_host_ptr, y_host_ptr, M, GEMM_BIAS if bias else 0, stream)
+
+
+def gemm_general(a_ptr, a_dtype, a_shape, b_ptr, b_dtype, b_shape, c_ptr, c_dtype, alpha=1.0, beta=0.0,
+                 trans_a=False, trans_b=False, stream=None) -> None:
+    call("mrt_gemm_general", a_ptr, a_dtype, a_shape[0], a_shape[1], b_ptr, b_dtype, b_shape[0], b_shape[1],
+         c_ptr, c_dtype, alpha, beta, int(trans_a), int(trans_b), stream)
+
+
+def argmax_f16(logits_ptr: int, M: int, V: int, ld: int, index_base: int, idx_ptr: int | None,
+               val_ptr: int | None, stream: int | None = None) -> None:
+    call("mrt_argmax_f16", logits_ptr, M, V, ld, index_base, idx_ptr, val_ptr, stream)
+
+
+def lm_head_argmax(w: Weight, x_ptr: int, ldx: int, M: int, logits_ptr: int, index_base: int, idx_ptr: int,
+                   val_ptr: int | None, stream: int | None = None) -> None:
+    call("mrt_lm_head_argmax", w.h, x_ptr, ldx, M, logits_ptr, index_base, idx_ptr, val_ptr, stream)
+
+
+def convert(src_ptr: int, src_dtype: int, dst_ptr: int, dst_dtype: int, n: int, stream: int | None = None):
+    call("mrt_convert", src_ptr, src_dtype, dst_ptr, dst_dtype, n, stream)
+
+
+def shard_rows(part_rows: list[int], world: int, rank: int) -> list[tuple[int, int]]:
+    parts = (C.c_int64 * len(part_rows))(*part_rows)
+    out = (C.c_int64 * (2 * len(part_rows)))()
+    call("mrt_shard_rows", parts, len(part_rows), world, rank, out)
+    return [(out[2 * i], out[2 * i + 1]) for i in range(len(part_rows))]
+
+
+def shard_cols(K: int, world: int, rank: int) -> tuple[int, int]:
+    k0, k1 = C.c_int64(), C.c_int64()
+    call("mrt_shard_cols", K, world, rank, C.byref(k0), C.byref(k1))
+    return k0.value, k1.value
+
+
+class TensorParallel:
+    """One rank of a tensor-parallel group (NCCL communicator inside the library)."""
+
+    ID_BYTES = 128
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = C.create_string_buffer(TensorParallel.ID_BYTES)
+        call("mrt_tp_unique_id", buf, TensorParallel.ID_BYTES)
+        return buf.raw
+
+    def __init__(self, rank: int, world: int, uid: bytes):
+        h = C.c_void_p()
+        buf = C.create_string_buffer(uid, len(uid))
+        call("mrt_tp_init", rank, world, buf, len(uid), C.byref(h))
+        self.h, self.rank, self.world = h, rank, world
+
+    def allreduce_f32_to_f16(self, partial_ptr: int, out_ptr: int, count: int, stream: int | None = None):
+        call("mrt_tp_allreduce_f32_to_f16", self.h, partial_ptr, out_ptr, count, stream)
+
+    def allgather_cols_f16(self, local_ptr: int, M: int, n_local: int, out_ptr: int, stream: int | None = None):
+        call("mrt_tp_allgather_cols_f16", self.h, local_ptr, M, n_local, out_ptr, stream)
+
+    def argmax(self, val_ptr: int, idx_ptr: int, M: int, out_ptr: int, stream: int | None = None):
+        call("mrt_tp_argmax", self.h, val_ptr, idx_ptr, M, out_ptr, stream)
+
+    def destroy(self):
+        if self.h:
+            lib().mrt_tp_destroy(self.h)
+            self.h = None

@@ -1,0 +1,569 @@
+// capi.cu -- C ABI of the linear-layer path (declared in include/mrt_b200.h):
+// device contexts, weight upload, GEMM planning and dispatch, argmax.
+// Tensor-parallel entry points live in tp.cu.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "ctx.h"
+#include "kernels.h"
+
+namespace mrt {
+
+namespace {
+thread_local std::string g_last_error;
+std::mutex g_ctx_mu;
+DevCtx* g_ctx[64] = {};
+EncodeTiledFn g_encode = nullptr;
+std::once_flag g_encode_once;
+}  // namespace
+
+static std::atomic<int64_t> g_launches{0};
+void note_launches(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+int set_error(int code, const std::string& msg) {
+    g_last_error = msg;
+    return code;
+}
+
+int cuda_error(cudaError_t e, const char* what) {
+    return set_error(MRT_ERR_CUDA, std::string(what) + ": " + cudaGetErrorName(e) + " (" +
+                                       cudaGetErrorString(e) + ")");
+}
+
+void clear_error() { g_last_error.clear(); }
+
+EncodeTiledFn encode_tiled_fn() {
+    std::call_once(g_encode_once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+    });
+    return g_encode;
+}
+
+static DevCtx* create_ctx(int device) {
+    DevCtx* c = new DevCtx();
+    c->device = device;
+    cudaError_t e = cudaDeviceGetAttribute(&c->sms, cudaDevAttrMultiProcessorCount, device);
+    if (e != cudaSuccess) {
+        delete c;
+        cuda_error(e, "cudaDeviceGetAttribute");
+        return nullptr;
+    }
+    int major = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+    if (major != 10) {
+        delete c;
+        set_error(MRT_ERR_UNSUPPORTED, "mruntime_b200 kernels are built for sm_100a (B200); device " +
+                                           std::to_string(device) + " has compute capability major " +
+                                           std::to_string(major));
+        return nullptr;
+    }
+    e = cudaMalloc(&c->d_err, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(c->d_err, 0, sizeof(int));
+    if (e != cudaSuccess) {
+        delete c;
+        cuda_error(e, "allocating the device error flag");
+        return nullptr;
+    }
+    return c;
+}
+
+DevCtx* current_ctx() {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        cuda_error(e, "cudaGetDevice");
+        return nullptr;
+    }
+    if (dev < 0 || dev >= 64) {
+        set_error(MRT_ERR_INVALID_ARG, "device index out of range");
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lk(g_ctx_mu);
+    if (g_ctx[dev] == nullptr) g_ctx[dev] = create_ctx(dev);
+    return g_ctx[dev];
+}
+
+int ensure_buffer(void** buf, size_t* cur, size_t bytes, const char* what) {
+    if (*cur >= bytes) return MRT_OK;
+    size_t want = std::max(bytes, *cur * 2);
+    want = (want + 0xFFFFF) & ~size_t(0xFFFFF);  // 1 MiB granules
+    if (*buf != nullptr) {
+        cudaError_t e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) return cuda_error(e, "synchronising before growing a buffer");
+        cudaFree(*buf);
+        *buf = nullptr;
+        *cur = 0;
+    }
+    cudaError_t e = cudaMalloc(buf, want);
+    if (e != cudaSuccess) {
+        *buf = nullptr;
+        return cuda_error(e, what);
+    }
+    *cur = want;
+    return MRT_OK;
+}
+
+int make_tmap_f16(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld,
+                  int box_rows) {
+    EncodeTiledFn enc = encode_tiled_fn();
+    if (enc == nullptr) return set_error(MRT_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (ld * 2) % 16 != 0)
+        return set_error(MRT_ERR_INVALID_ARG, "TMA operand must be 16-byte aligned with a 16-byte-multiple row pitch");
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
+    const cuuint32_t box[2] = {64u, static_cast<cuuint32_t>(box_rows)};
+    const cuuint32_t estr[2] = {1u, 1u};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return set_error(MRT_ERR_CUDA, "cuTensorMapEncodeTiled failed with CUresult " + std::to_string(static_cast<int>(r)));
+    return MRT_OK;
+}
+
+}  // namespace mrt
+
+using namespace mrt;
+
+// ====================================================================== runtime
+
+extern "C" int mrt_version(void) { return 100; }
+
+extern "C" const char* mrt_last_error_string(void) { return g_last_error.c_str(); }
+
+extern "C" int mrt_init(int device) {
+    clear_error();
+    cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) return cuda_error(e, "cudaSetDevice");
+    return current_ctx() ? MRT_OK : MRT_ERR_CUDA;
+}
+
+extern "C" int mrt_device_sm_count(int* out) {
+    DevCtx* c = current_ctx();
+    if (!c) return MRT_ERR_CUDA;
+    if (out) *out = c->sms;
+    return MRT_OK;
+}
+
+extern "C" int mrt_launch_count(int64_t* out) {
+    if (out == nullptr) return set_error(MRT_ERR_INVALID_ARG, "out is NULL");
+    *out = g_launches.load(std::memory_order_relaxed);
+    return MRT_OK;
+}
+
+extern "C" int mrt_sync(void* stream) {
+    DevCtx* c = current_ctx();
+    if (!c) return MRT_ERR_CUDA;
+    cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_error(e, "cudaStreamSynchronize");
+    int flag = 0;
+    e = cudaMemcpy(&flag, c->d_err, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_error(e, "reading the device error flag");
+    if (flag != 0) {
+        cudaMemset(c->d_err, 0, sizeof(int));
+        static const char* what[] = {"", "TMA producer", "MMA issuer", "epilogue", "clean-up"};
+        return set_error(MRT_ERR_TIMEOUT, std::string("a kernel wait timed out in the ") +
+                                              (flag > 0 && flag < 5 ? what[flag] : "kernel") +
+                                              " (device error code " + std::to_string(flag) + ")");
+    }
+    return MRT_OK;
+}
+
+extern "C" int mrt_reserve_workspace(size_t bytes) {
+    DevCtx* c = current_ctx();
+    if (!c) return MRT_ERR_CUDA;
+    return ensure_buffer(&c->ws, &c->ws_bytes, bytes, "allocating the scratch buffer");
+}
+
+// ====================================================================== weights
+
+static size_t dtype_bytes(int dt) { return dt == MRT_FP32 ? 4 : 2; }
+
+extern "C" int mrt_weight_upload(const void* src, int src_dtype, int src_on_device, int64_t N, int64_t K,
+                                 const int64_t* row_ranges, int64_t n_ranges, int64_t k_begin,
+                                 int64_t k_end, void* stream, mrt_weight* out) {
+    clear_error();
+    if (out == nullptr) return set_error(MRT_ERR_INVALID_ARG, "out is NULL");
+    *out = nullptr;
+    if (src == nullptr || N <= 0 || K <= 0) return set_error(MRT_ERR_INVALID_ARG, "empty or NULL weight");
+    if (src_dtype != MRT_FP16 && src_dtype != MRT_BF16 && src_dtype != MRT_FP32)
+        return set_error(MRT_ERR_DTYPE, "weight dtype must be FP16, BF16 or FP32");
+    if (k_begin < 0 || k_end > K || k_begin >= k_end)
+        return set_error(MRT_ERR_SHAPE, "column range must satisfy 0 <= k_begin < k_end <= K");
+    std::vector<int64_t> ranges;
+    if (row_ranges == nullptr || n_ranges == 0) {
+        ranges = {0, N};
+    } else {
+        if (n_ranges < 0 || n_ranges > 64) return set_error(MRT_ERR_INVALID_ARG, "n_ranges must be in [0, 64]");
+        ranges.assign(row_ranges, row_ranges + 2 * n_ranges);
+    }
+    int64_t n_keep = 0;
+    for (size_t i = 0; i < ranges.size(); i += 2) {
+        if (ranges[i] < 0 || ranges[i + 1] > N || ranges[i] >= ranges[i + 1])
+            return set_error(MRT_ERR_SHAPE, "row range outside [0, N) or empty");
+        n_keep += ranges[i + 1] - ranges[i];
+    }
+    DevCtx* c = current_ctx();
+    if (!c) return MRT_ERR_CUDA;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int64_t k_keep = k_end - k_begin;
+    const size_t es = dtype_bytes(src_dtype);
+
+    mrt_weight_s* w = new mrt_weight_s();
+    w->device = c->device;
+    w->n = n_keep;
+    w->k = k_keep;
+    w->src_n = N;
+    w->n_ranges = static_cast<int64_t>(ranges.size() / 2);
+    w->ranges = new int64_t[ranges.size()];
+    std::copy(ranges.begin(), ranges.end(), w->ranges);
+    cudaError_t e = cudaMalloc(&w->data, static_cast<size_t>(n_keep * k_keep) * 2);
+    if (e != cudaSuccess) {
+        delete[] w->ranges;
+        delete w;
+        return cuda_error(e, "allocating weight storage");
+    }
+    void* stage = nullptr;
+    int64_t row_off = 0;
+    int rc = MRT_OK;
+    for (size_t i = 0; i < ranges.size() && rc == MRT_OK; i += 2) {
+        const int64_t rows = ranges[i + 1] - ranges[i];
+        const char* s0 = static_cast<const char*>(src) + (ranges[i] * K + k_begin) * es;
+        uint16_t* d0 = w->data + row_off * k_keep;
+        if (src_dtype == MRT_FP16) {
+            e = cudaMemcpy2DAsync(d0, k_keep * 2, s0, K * 2, k_keep * 2, rows,
+                                  src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s);
+            if (e != cudaSuccess) rc = cuda_error(e, "copying the weight");
+        } else if (src_on_device) {
+            e = launch_convert_2d_to_f16(s0, src_dtype, K, rows, k_keep, d0, s);
+            if (e != cudaSuccess) rc = cuda_error(e, "converting the weight to FP16");
+        } else {
+            // Stage the native-dtype rows on the device, then round once to FP16.
+            if (stage != nullptr) {
+                cudaStreamSynchronize(s);
+                cudaFree(stage);
+                stage = nullptr;
+            }
+            e = cudaMalloc(&stage, static_cast<size_t>(rows * k_keep) * es);
+            if (e == cudaSuccess)
+                e = cudaMemcpy2DAsync(stage, k_keep * es, s0, K * es, k_keep * es, rows, cudaMemcpyHostToDevice, s);
+            if (e == cudaSuccess) e = launch_convert_2d_to_f16(stage, src_dtype, k_keep, rows, k_keep, d0, s);
+            if (e != cudaSuccess) rc = cuda_error(e, "staging and converting the weight");
+        }
+        row_off += rows;
+    }
+    e = cudaStreamSynchronize(s);
+    if (stage != nullptr) cudaFree(stage);
+    if (rc == MRT_OK && e != cudaSuccess) rc = cuda_error(e, "finishing the weight upload");
+    if (rc != MRT_OK) {
+        cudaFree(w->data);
+        delete[] w->ranges;
+        delete w;
+        return rc;
+    }
+    *out = w;
+    return MRT_OK;
+}
+
+extern "C" int mrt_weight_attach_bias(mrt_weight w, const void* src, int src_dtype, int src_on_device,
+                                      void* stream) {
+    clear_error();
+    if (w == nullptr || src == nullptr) return set_error(MRT_ERR_INVALID_ARG, "NULL weight or bias");
+    if (src_dtype != MRT_FP16 && src_dtype != MRT_BF16 && src_dtype != MRT_FP32)
+        return set_error(MRT_ERR_DTYPE, "bias dtype must be FP16, BF16 or FP32");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t es = dtype_bytes(src_dtype);
+    if (w->bias == nullptr) {
+        cudaError_t e = cudaMalloc(&w->bias, static_cast<size_t>(w->n) * 2);
+        if (e != cudaSuccess) {
+            w->bias = nullptr;
+            return cuda_error(e, "allocating bias storage");
+        }
+    }
+    void* stage = nullptr;
+    cudaError_t e = cudaMalloc(&stage, static_cast<size_t>(w->src_n) * es);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(stage, src, static_cast<size_t>(w->src_n) * es,
+                            src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s);
+    int64_t off = 0;
+    for (int64_t i = 0; i < w->n_ranges && e == cudaSuccess; ++i) {
+        const int64_t b = w->ranges[2 * i], rows = w->ranges[2 * i + 1] - b;
+        e = launch_convert(static_cast<const char*>(stage) + b * es, src_dtype, w->bias + off, MRT_FP16, rows, s);
+        off += rows;
+    }
+    cudaError_t e2 = cudaStreamSynchronize(s);
+    if (stage) cudaFree(stage);
+    if (e != cudaSuccess) return cuda_error(e, "uploading the bias");
+    if (e2 != cudaSuccess) return cuda_error(e2, "finishing the bias upload");
+    return MRT_OK;
+}
+
+extern "C" int mrt_weight_free(mrt_weight w) {
+    if (w == nullptr) return MRT_OK;
+    cudaFree(w->data);
+    if (w->bias) cudaFree(w->bias);
+    delete[] w->ranges;
+    delete w;
+    return MRT_OK;
+}
+
+extern "C" int mrt_weight_shape(mrt_weight w, int64_t* n, int64_t* k) {
+    if (w == nullptr) return set_error(MRT_ERR_INVALID_ARG, "NULL weight");
+    if (n) *n = w->n;
+    if (k) *k = w->k;
+    return MRT_OK;
+}
+
+extern "C" int mrt_weight_data(mrt_weight w, void** dev_ptr) {
+    if (w == nullptr || dev_ptr == nullptr) return set_error(MRT_ERR_INVALID_ARG, "NULL argument");
+    *dev_ptr = w->data;
+    return MRT_OK;
+}
+
+// ====================================================================== GEMM
+
+namespace mrt {
+
+// Tile plan for the tcgen05 kernel.  Cost model in units of one 128x128x64
+// MMA block-step on one SM: a work unit of BN columns and kb_per k-blocks
+// costs (BN/128)*(kb_per + 2) (the +2 is pipeline fill and epilogue), units
+// run in ceil(units / SMs) waves, and a split-K plan pays for writing and
+// re-reading its FP32 partials at HBM speed.
+struct TcPlan {
+    int bn = 256, splits = 1, grid = 1;
+};
+
+static TcPlan plan_tc(int64_t M, int64_t N, int64_t K, int sms) {
+    const int64_t num_m = (M + 127) / 128;
+    const int64_t num_kb = (K + 63) / 64;
+    TcPlan best;
+    double best_cost = 1e300;
+    const int cand_splits[] = {1, 2, 3, 4, 6, 8, 12, 16};
+    for (int bn : {256, 128}) {
+        const int64_t tiles = num_m * ((N + bn - 1) / bn);
+        for (int sp : cand_splits) {
+            if (sp > num_kb) break;
+            const int64_t kb_per = (num_kb + sp - 1) / sp;
+            const int64_t splits = (num_kb + kb_per - 1) / kb_per;  // no empty split
+            if ((num_kb + splits - 1) / splits != kb_per) continue;
+            if (splits > 1 && tiles * splits > 8LL * sms) continue;
+            const int64_t units = tiles * splits;
+            const int64_t waves = (units + sms - 1) / sms;
+            double cost = static_cast<double>(waves) * (bn / 128.0) * (static_cast<double>(kb_per) + 2.0);
+            if (splits > 1) {
+                // ~0.2 us per block-step; partial traffic at ~6 TB/s.
+                const double bytes = static_cast<double>(M) * N * 4.0 * (2.0 * splits + 1.0);
+                cost += bytes / 6.0e6 / 0.2 + 5.0;
+            }
+            if (cost < best_cost - 1e-9) {
+                best_cost = cost;
+                best.bn = bn;
+                best.splits = static_cast<int>(splits);
+                best.grid = static_cast<int>(std::min<int64_t>(units, sms));
+            }
+        }
+    }
+    return best;
+}
+
+// Weight rows per skinny CTA (in 8-row tiles): as many as still leaves about
+// two CTAs per SM, so small N keeps every SM streaming.
+static int plan_skinny_rn(int64_t M, int64_t N, int sms) {
+    const int max_rn = M > 32 ? 2 : 4;
+    for (int rn = max_rn; rn > 1; rn /= 2)
+        if ((N + 8 * rn - 1) / (8 * rn) >= 2LL * sms) return rn;
+    return 1;
+}
+
+static const CUtensorMap* weight_tmap(mrt_weight w, int bn) {
+    if (bn == 256) {
+        if (!w->tmap_ok256) {
+            if (make_tmap_f16(&w->tmap256, w->data, w->n, w->k, w->k, 256) != MRT_OK) return nullptr;
+            w->tmap_ok256 = true;
+        }
+        return &w->tmap256;
+    }
+    if (!w->tmap_ok128) {
+        if (make_tmap_f16(&w->tmap128, w->data, w->n, w->k, w->k, 128) != MRT_OK) return nullptr;
+        w->tmap_ok128 = true;
+    }
+    return &w->tmap128;
+}
+
+// Shared body of mrt_gemm / mrt_gemm_f32.
+static int gemm_dispatch(mrt_weight w, const void* x, int64_t ldx, void* y, int64_t ldy, int64_t M,
+                         bool out_f32, bool use_bias, cudaStream_t s) {
+    if (w == nullptr) return set_error(MRT_ERR_INVALID_ARG, "NULL weight");
+    if (M < 0) return set_error(MRT_ERR_SHAPE, "M must be >= 0");
+    if (M == 0) return MRT_OK;
+    if (x == nullptr || y == nullptr) return set_error(MRT_ERR_INVALID_ARG, "NULL x or y");
+    if (ldx < w->k || ldy < w->n) return set_error(MRT_ERR_SHAPE, "ldx must be >= K and ldy >= N");
+    if (use_bias && w->bias == nullptr) return set_error(MRT_ERR_INVALID_ARG, "MRT_GEMM_BIAS without an attached bias");
+    if (M > (1LL << 31) - 1 || w->n > (1LL << 31) - 1 || w->k > (1LL << 31) - 1)
+        return set_error(MRT_ERR_SHAPE, "dimensions must fit in 31 bits");
+    DevCtx* c = current_ctx();
+    if (!c) return MRT_ERR_CUDA;
+    if (c->device != w->device) return set_error(MRT_ERR_INVALID_ARG, "weight lives on another device");
+    const uint16_t* bias = use_bias ? w->bias : nullptr;
+
+    const bool fast = (w->k % 8 == 0) && (ldx % 8 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+    cudaError_t e;
+    if (!fast) {
+        GeneralGemmArgs g{};
+        g.a = x; g.a_dtype = MRT_FP16; g.a_cols0 = ldx;
+        g.b = w->data; g.b_dtype = MRT_FP16; g.b_cols0 = w->k;
+        g.c = y; g.c_dtype = out_f32 ? MRT_FP32 : MRT_FP16; g.ldc = ldy;
+        g.M = M; g.N = w->n; g.K = w->k; g.alpha = 1.0f; g.beta = 0.0f;
+        g.trans_a = 0; g.trans_b = 1; g.bias = bias;
+        e = launch_general_gemm(g, s);
+        return e == cudaSuccess ? MRT_OK : cuda_error(e, "general gemm launch");
+    }
+    if (M <= 64) {
+        SkinnyArgs a{};
+        a.x = static_cast<const uint16_t*>(x); a.ldx = ldx; a.w = w->data;
+        a.y = y; a.ldy = ldy; a.M = static_cast<int>(M); a.N = static_cast<int>(w->n);
+        a.K = static_cast<int>(w->k); a.bias = bias; a.out_f32 = out_f32 ? 1 : 0;
+        e = launch_skinny(a, plan_skinny_rn(M, w->n, c->sms), s);
+        return e == cudaSuccess ? MRT_OK : cuda_error(e, "skinny gemm launch");
+    }
+    const TcPlan p = plan_tc(M, w->n, w->k, c->sms);
+    CUtensorMap tx;
+    int rc = make_tmap_f16(&tx, x, M, w->k, ldx, 128);
+    if (rc != MRT_OK) return rc;
+    const CUtensorMap* tw = weight_tmap(w, p.bn);
+    if (tw == nullptr) return MRT_ERR_CUDA;
+    TcGemmArgs a{};
+    a.M = static_cast<int>(M); a.N = static_cast<int>(w->n); a.K = static_cast<int>(w->k);
+    a.bn = p.bn; a.splits = p.splits; a.grid = p.grid;
+    a.y = y; a.ldy = ldy; a.out_f32 = out_f32 ? 1 : 0; a.bias = bias; a.err_flag = c->d_err;
+    if (p.splits > 1) {
+        const size_t need = static_cast<size_t>(p.splits) * M * w->n * sizeof(float);
+        rc = ensure_buffer(&c->ws, &c->ws_bytes, need, "allocating split-K scratch");
+        if (rc != MRT_OK) return rc;
+        a.partials = static_cast<float*>(c->ws);
+    }
+    e = launch_tc_gemm(a, tx, *tw, s);
+    if (e != cudaSuccess) return cuda_error(e, "tcgen05 gemm launch");
+    if (p.splits > 1) {
+        e = launch_reduce_splits(a.partials, p.splits, a.M, a.N, y, ldy, a.out_f32, bias, s);
+        if (e != cudaSuccess) return cuda_error(e, "split-K reduction launch");
+    }
+    return MRT_OK;
+}
+
+}  // namespace mrt
+
+extern "C" int mrt_gemm(mrt_weight w, const void* x_dev, int64_t ldx, void* y_dev, int64_t ldy, int64_t M,
+                        unsigned flags, void* stream) {
+    clear_error();
+    return gemm_dispatch(w, x_dev, ldx, y_dev, ldy, M, false, (flags & MRT_GEMM_BIAS) != 0,
+                         static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int mrt_gemm_f32(mrt_weight w, const void* x_dev, int64_t ldx, float* y_dev, int64_t ldy,
+                            int64_t M, void* stream) {
+    clear_error();
+    return gemm_dispatch(w, x_dev, ldx, y_dev, ldy, M, true, false, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int mrt_gemm_host(mrt_weight w, const void* x_host, void* y_host, int64_t M, unsigned flags,
+                             void* stream) {
+    clear_error();
+    if (w == nullptr) return set_error(MRT_ERR_INVALID_ARG, "NULL weight");
+    if (M < 0) return set_error(MRT_ERR_SHAPE, "M must be >= 0");
+    if (M == 0) return MRT_OK;
+    if (x_host == nullptr || y_host == nullptr) return set_error(MRT_ERR_INVALID_ARG, "NULL x or y");
+    DevCtx* c = current_ctx();
+    if (!c) return MRT_ERR_CUDA;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t xb = static_cast<size_t>(M * w->k) * 2, yb = static_cast<size_t>(M * w->n) * 2;
+    int rc = ensure_buffer(&c->io_x, &c->io_x_bytes, xb, "allocating input staging");
+    if (rc == MRT_OK) rc = ensure_buffer(&c->io_y, &c->io_y_bytes, yb, "allocating output staging");
+    if (rc != MRT_OK) return rc;
+    cudaError_t e = cudaMemcpyAsync(c->io_x, x_host, xb, cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) return cuda_error(e, "copying x to the device");
+    rc = gemm_dispatch(w, c->io_x, w->k, c->io_y, w->n, M, false, (flags & MRT_GEMM_BIAS) != 0, s);
+    if (rc != MRT_OK) return rc;
+    e = cudaMemcpyAsync(y_host, c->io_y, yb, cudaMemcpyDeviceToHost, s);
+    if (e != cudaSuccess) return cuda_error(e, "copying y to the host");
+    e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_error(e, "waiting for the host-buffer gemm");
+    return MRT_OK;
+}
+
+extern "C" int mrt_gemm_general(const void* a_dev, int a_dtype, int64_t a_rows, int64_t a_cols,
+                                const void* b_dev, int b_dtype, int64_t b_rows, int64_t b_cols, void* c_dev,
+                                int c_dtype, float alpha, float beta, int trans_a, int trans_b, void* stream) {
+    clear_error();
+    for (int dt : {a_dtype, b_dtype, c_dtype})
+        if (dt != MRT_FP16 && dt != MRT_BF16 && dt != MRT_FP32)
+            return set_error(MRT_ERR_DTYPE, "dtypes must be FP16, BF16 or FP32");
+    if (a_rows < 0 || a_cols < 0 || b_rows < 0 || b_cols < 0) return set_error(MRT_ERR_SHAPE, "negative dimension");
+    const int64_t M = trans_a ? a_cols : a_rows;
+    const int64_t K = trans_a ? a_rows : a_cols;
+    const int64_t N = trans_b ? b_rows : b_cols;
+    if ((trans_b ? b_cols : b_rows) != K)
+        return set_error(MRT_ERR_SHAPE, "inner dimensions of A and B differ");
+    if (M == 0 || N == 0) return MRT_OK;  // cpu_backend.cpp:124-126
+    if (!current_ctx()) return MRT_ERR_CUDA;
+    GeneralGemmArgs g{};
+    g.a = a_dev; g.a_dtype = a_dtype; g.a_cols0 = a_cols;
+    g.b = b_dev; g.b_dtype = b_dtype; g.b_cols0 = b_cols;
+    g.c = c_dev; g.c_dtype = c_dtype; g.ldc = N;
+    g.M = M; g.N = N; g.K = K; g.alpha = alpha; g.beta = beta;
+    g.trans_a = trans_a ? 1 : 0; g.trans_b = trans_b ? 1 : 0; g.bias = nullptr;
+    cudaError_t e = launch_general_gemm(g, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? MRT_OK : cuda_error(e, "general gemm launch");
+}
+
+// ====================================================================== logits
+
+extern "C" int mrt_argmax_f16(const void* logits_dev, int64_t M, int64_t V, int64_t ld, int64_t index_base,
+                              int64_t* idx_dev, float* val_dev, void* stream) {
+    clear_error();
+    if (M < 0 || V < 0 || ld < V) return set_error(MRT_ERR_SHAPE, "need M >= 0, V >= 0, ld >= V");
+    if (M == 0) return MRT_OK;
+    if (V == 0) return set_error(MRT_ERR_SHAPE, "argmax over an empty row");
+    if (M > 65535) return set_error(MRT_ERR_SHAPE, "at most 65535 rows per call");
+    if (logits_dev == nullptr) return set_error(MRT_ERR_INVALID_ARG, "NULL logits");
+    DevCtx* c = current_ctx();
+    if (!c) return MRT_ERR_CUDA;
+    int rc = ensure_buffer(&c->ws, &c->ws_bytes, argmax_scratch_bytes(M, V), "allocating argmax scratch");
+    if (rc != MRT_OK) return rc;
+    cudaError_t e = launch_argmax(static_cast<const uint16_t*>(logits_dev), M, V, ld, index_base, idx_dev,
+                                  val_dev, c->ws, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? MRT_OK : cuda_error(e, "argmax launch");
+}
+
+extern "C" int mrt_lm_head_argmax(mrt_weight w, const void* x_dev, int64_t ldx, int64_t M, void* logits_dev,
+                                  int64_t index_base, int64_t* idx_dev, float* val_dev, void* stream) {
+    int rc = mrt_gemm(w, x_dev, ldx, logits_dev, w ? w->n : 0, M, 0, stream);
+    if (rc != MRT_OK) return rc;
+    return mrt_argmax_f16(logits_dev, M, w->n, w->n, index_base, idx_dev, val_dev, stream);
+}
+
+extern "C" int mrt_convert(const void* src_dev, int src_dtype, void* dst_dev, int dst_dtype, int64_t n,
+                           void* stream) {
+    clear_error();
+    for (int dt : {src_dtype, dst_dtype})
+        if (dt != MRT_FP16 && dt != MRT_BF16 && dt != MRT_FP32)
+            return set_error(MRT_ERR_DTYPE, "dtypes must be FP16, BF16 or FP32");
+    if (n < 0) return set_error(MRT_ERR_SHAPE, "n must be >= 0");
+    if (n == 0) return MRT_OK;
+    if (!current_ctx()) return MRT_ERR_CUDA;
+    cudaError_t e = launch_convert(src_dev, src_dtype, dst_dev, dst_dtype, n, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? MRT_OK : cuda_error(e, "convert launch");
+}

@@ -1,0 +1,251 @@
+// common.cuh -- device helpers shared by the sm_100a kernels.
+//
+// PTX wrappers for mbarriers, TMA tile loads, tcgen05 (TMEM alloc, MMA,
+// commit, loads) and the rounding rule of the reference's FP16 converter.
+// Every wait on an mbarrier is bounded: after a time limit it records an
+// error code in a device flag that the host reads (mrt_sync) and returns
+// false, so a lost arrival ends the kernel instead of hanging the GPU.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mrt {
+
+// Device error codes written to the context's flag.
+enum : int {
+    kErrNone = 0,
+    kErrTmaWait = 1,   // producer gave up waiting for a free pipeline stage
+    kErrMmaWait = 2,   // MMA issuer gave up waiting for data or a free accumulator
+    kErrEpiWait = 3,   // epilogue gave up waiting for a finished accumulator
+    kErrDrainWait = 4, // clean-up wait for in-flight copies/MMAs gave up
+};
+
+// Wall-clock limit of one bounded wait, in nanoseconds of %globaltimer.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ------------------------------------------------------------------ FP16 rounding
+
+// FP32 -> FP16 bits with the reference's rule (include/mruntime/dtype.h:39-119):
+// round-to-nearest-even, overflow to infinity, FP32 denormals to signed zero
+// (they lie far below half the smallest FP16 subnormal, so the hardware
+// conversion already gives that), and NaN keeping the top ten payload bits,
+// forced non-zero -- the one case where the hardware conversion differs.
+__device__ __forceinline__ uint16_t f32_to_f16_bits(float v) {
+    const uint32_t x = __float_as_uint(v);
+    if ((x & 0x7FFFFFFFu) > 0x7F800000u) {
+        uint32_t p = (x >> 13) & 0x3FFu;
+        if (p == 0) p = 1;
+        return static_cast<uint16_t>(((x >> 16) & 0x8000u) | 0x7C00u | p);
+    }
+    return __half_as_ushort(__float2half_rn(v));
+}
+
+__device__ __forceinline__ float f16_bits_to_f32(uint16_t h) {
+    return __half2float(__ushort_as_half(h));
+}
+
+__device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) {
+    return __uint_as_float(static_cast<uint32_t>(b) << 16);
+}
+
+// FP32 -> BF16 bits with the reference's rounding trick (dtype.h:153-160).
+__device__ __forceinline__ uint16_t f32_to_bf16_bits(float v) {
+    uint32_t x = __float_as_uint(v);
+    x += 0x7FFFu + ((x >> 16) & 1u);
+    return static_cast<uint16_t>(x >> 16);
+}
+
+// Output rounding with the optional q/k/v bias of qwen_model.cpp:130-155:
+// round the accumulator to FP16, widen, add the FP16 bias, round again.
+__device__ __forceinline__ uint16_t round_out(float acc, const uint16_t* bias, int64_t n) {
+    uint16_t h = f32_to_f16_bits(acc);
+    if (bias != nullptr) h = f32_to_f16_bits(__fadd_rn(f16_bits_to_f32(h), f16_bits_to_f32(bias[n])));
+    return h;
+}
+
+// ------------------------------------------------------------------ error flag
+
+__device__ __forceinline__ void raise_error(int* flag, int code) {
+    if (flag != nullptr) atomicCAS(flag, 0, code);
+}
+
+__device__ __forceinline__ bool error_raised(const int* flag) {
+    return flag != nullptr && *reinterpret_cast<const volatile int*>(flag) != 0;
+}
+
+// ------------------------------------------------------------------ mbarrier
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+// Make barrier initialisation visible to the async (TMA / tensor core) proxy.
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Wait for the phase with the given parity to complete.  Gives up (returns
+// false, raising `code`) after kWaitLimitNs or as soon as another thread of
+// the grid has raised an error.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* flag, int code) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 255u) == 0) {
+            if (error_raised(flag)) return false;
+            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                raise_error(flag, code);
+                return false;
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------ TMA
+
+// 2-D tiled bulk tensor load global -> shared, completion counted in bytes on
+// `bar`.  c0 is the innermost (contiguous) coordinate in elements.
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, uint64_t* bar,
+                                            int32_t c0, int32_t c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const void* tmap) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
+}
+
+// ------------------------------------------------------------------ tcgen05
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(dst_smem)),
+                 "r"(ncols)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, FP16 inputs, FP32 accumulator.
+__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                           uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrive once on `bar` when every tcgen05 operation this thread issued so far
+// has completed.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+            smem_u32(bar))
+        : "memory");
+}
+
+// Load 32 consecutive FP32 columns of this warp's 32 TMEM lanes (one lane per thread).
+__device__ __forceinline__ void tmem_ld_32cols(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+          "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+          "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor for a K-major tile written by TMA with
+// 128-byte swizzling: rows of 64 FP16 (128 B), 8-row groups 1024 B apart.
+// Fields: start address >> 4 (bits 0-13), leading byte offset >> 4 = 1
+// (bits 16-29, unused for this layout), stride byte offset >> 4 = 64
+// (bits 32-45), descriptor version 1 (bits 46-47), base offset 0, swizzle
+// mode 2 = 128 B (bits 61-63).
+__device__ __forceinline__ uint64_t smem_desc_k128(uint32_t smem_addr) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
+    d |= static_cast<uint64_t>(1) << 16;
+    d |= static_cast<uint64_t>(1024 >> 4) << 32;
+    d |= static_cast<uint64_t>(1) << 46;
+    d |= static_cast<uint64_t>(2) << 61;
+    return d;
+}
+
+// Instruction descriptor of tcgen05.mma kind::f16: FP32 accumulator (bits 4-5
+// = 1), A and B FP16 (bits 7-9 and 10-12 = 0), both K-major (bits 15, 16 = 0),
+// N >> 3 in bits 17-22, M >> 4 in bits 24-28.
+__host__ __device__ constexpr uint32_t idesc_f16_f32(uint32_t m, uint32_t n) {
+    return (1u << 4) | ((n >> 3) << 17) | ((m >> 4) << 24);
+}
+
+// ------------------------------------------------------------------ plain loads
+
+// 16-byte streaming load that skips L1 (weights are read exactly once).
+__device__ __forceinline__ uint4 ld_stream_16B(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+}  // namespace mrt

@@ -1,0 +1,69 @@
+// ctx.h -- per-device context and error helpers shared by the C-ABI sources.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "mrt_b200.h"
+
+namespace mrt {
+
+// One per device, created by mrt_init (or lazily by the first call).
+struct DevCtx {
+    int device = -1;
+    int sms = 0;
+    int* d_err = nullptr;   // device-side error flag written by bounded waits
+    void* ws = nullptr;     // scratch: split-K partials, argmax partials
+    size_t ws_bytes = 0;
+    void* io_x = nullptr;   // staging for host-buffer calls
+    size_t io_x_bytes = 0;
+    void* io_y = nullptr;
+    size_t io_y_bytes = 0;
+};
+
+// Record an error for mrt_last_error_string() and return its code.
+int set_error(int code, const std::string& msg);
+int cuda_error(cudaError_t e, const char* what);
+void clear_error();
+
+// Context of the current device (creating it on first use); nullptr after
+// set_error on failure.
+DevCtx* current_ctx();
+
+// Grow a device buffer to at least `bytes` (synchronises the device before
+// freeing a smaller one, so in-flight kernels never see it vanish).
+int ensure_buffer(void** buf, size_t* cur, size_t bytes, const char* what);
+
+// cuTensorMapEncodeTiled, resolved through the runtime so the library loads
+// on machines without a driver.
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_tiled_fn();
+
+// 2-D FP16 tensor map over a row-major [rows, cols] matrix with row stride
+// `ld` elements, box = 64 columns x box_rows rows, 128-byte swizzle, zero fill.
+int make_tmap_f16(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld,
+                  int box_rows);
+
+}  // namespace mrt
+
+// Opaque handle types of the public header.
+struct mrt_weight_s {
+    int device = -1;
+    int64_t n = 0;  // rows kept
+    int64_t k = 0;  // columns kept
+    uint16_t* data = nullptr;  // dense FP16 [n, k]
+    uint16_t* bias = nullptr;  // FP16 [n] or nullptr
+    int64_t src_n = 0;         // rows of the full source weight
+    int64_t* ranges = nullptr; // row ranges kept (pairs)
+    int64_t n_ranges = 0;
+    CUtensorMap tmap128;
+    CUtensorMap tmap256;
+    bool tmap_ok128 = false;
+    bool tmap_ok256 = false;
+};

@@ -1,0 +1,310 @@
+// gemm_tc.cu -- prefill GEMM on the 5th-generation tensor cores (sm_100a).
+//
+// Y[M,N] = X[M,K] * W[N,K]^T, FP16 operands, FP32 accumulation in tensor
+// memory (TMEM), FP16 (or FP32) output.
+//
+// One persistent CTA per SM walks a static list of work units
+// (m-tile, n-tile, k-split); m varies fastest so the CTAs running at the same
+// time share weight tiles in L2.  Warp roles:
+//   warp 0    TMA producer: one lane streams 128x64 X tiles and BNx64 W tiles
+//             (128-byte swizzle) into a STAGES-deep shared-memory ring,
+//             completion counted on a "full" mbarrier per stage;
+//   warp 1    allocates TMEM (2*BN columns = two accumulators) and one lane
+//             issues tcgen05.mma (M=128, N=BN, K=16; four per stage) and
+//             tcgen05.commit to release ring stages and to publish a finished
+//             accumulator;
+//   warps 2-5 epilogue: tcgen05.ld of their 32 TMEM lanes (= tile rows),
+//             rounding with the reference's FP16 converter (plus the q/k/v
+//             bias double rounding), 16-byte stores; the second accumulator
+//             lets the next tile's MMAs overlap this drain.
+// Every mbarrier wait is bounded (common.cuh); on a timeout the kernel
+// records an error code, waits (bounded) for its own copies and MMAs in flight
+// and frees its TMEM before returning.
+//
+// TMA loads here never use cluster-wide broadcast and every operand is memory
+// of this GPU.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace mrt {
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kThreadsTc = 192;
+constexpr int kEpiThreads = 128;
+
+template <int BN>
+struct TcCfg {
+    static constexpr int kStages = BN >= 256 ? 4 : 6;
+    static constexpr int kABytes = kBM * kBK * 2;
+    static constexpr int kBBytes = BN * kBK * 2;
+    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr uint32_t kTmemCols = BN >= 256 ? 512 : (BN >= 128 ? 256 : 128);
+    static constexpr int kBarBytes = (2 * kStages + 5) * 8 + 16;
+    static constexpr size_t kSmem = static_cast<size_t>(kStages) * kStageBytes + kBarBytes + 1024;
+};
+
+struct Unit {
+    int mt, nt, kb0, kb1;
+};
+
+__device__ __forceinline__ Unit decode_unit(int u, int num_m, int splits, int num_kb, int kb_per) {
+    Unit w;
+    w.mt = u % num_m;
+    const int rest = u / num_m;
+    const int sp = rest % splits;
+    w.nt = rest / splits;
+    w.kb0 = sp * kb_per;
+    w.kb1 = min(w.kb0 + kb_per, num_kb);
+    return w;
+}
+
+__device__ __forceinline__ uint32_t pack_h2(uint16_t lo, uint16_t hi) {
+    return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+}
+
+// Store 32 accumulator columns of one row.
+__device__ __forceinline__ void store_row_chunk(const TcGemmArgs& a, const uint32_t (&r)[32],
+                                                int64_t row, int64_t col0, int sp) {
+    if (a.splits > 1) {
+        float* dst = a.partials + (static_cast<int64_t>(sp) * a.M + row) * a.N + col0;
+        if (col0 + 32 <= a.N && (a.N & 3) == 0) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<uint4*>(dst + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+        } else {
+            for (int j = 0; j < 32 && col0 + j < a.N; ++j) dst[j] = __uint_as_float(r[j]);
+        }
+        return;
+    }
+    if (a.out_f32) {
+        float* dst = static_cast<float*>(a.y) + row * a.ldy + col0;
+        const bool vec = col0 + 32 <= a.N && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0);
+        if (vec) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<uint4*>(dst + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+        } else {
+            for (int j = 0; j < 32 && col0 + j < a.N; ++j) dst[j] = __uint_as_float(r[j]);
+        }
+        return;
+    }
+    uint16_t* dst = static_cast<uint16_t*>(a.y) + row * a.ldy + col0;
+    const bool vec = col0 + 32 <= a.N && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0);
+    if (vec) {
+        uint32_t h[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+            h[j] = pack_h2(round_out(__uint_as_float(r[2 * j]), a.bias, col0 + 2 * j),
+                           round_out(__uint_as_float(r[2 * j + 1]), a.bias, col0 + 2 * j + 1));
+#pragma unroll
+        for (int j = 0; j < 16; j += 4)
+            *reinterpret_cast<uint4*>(dst + 2 * j) = make_uint4(h[j], h[j + 1], h[j + 2], h[j + 3]);
+    } else {
+        for (int j = 0; j < 32 && col0 + j < a.N; ++j)
+            dst[j] = round_out(__uint_as_float(r[j]), a.bias, col0 + j);
+    }
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kThreadsTc, 1)
+    tc_gemm_kernel(const TcGemmArgs a, const __grid_constant__ CUtensorMap tmx,
+                   const __grid_constant__ CUtensorMap tmw) {
+    using Cfg = TcCfg<BN>;
+    constexpr int S = Cfg::kStages;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + S * Cfg::kABytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sB + S * Cfg::kBBytes);
+    uint64_t* full = bars;
+    uint64_t* empty = bars + S;
+    uint64_t* tfull = bars + 2 * S;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* drain = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&tfull[i], 1);
+            mbar_init(&tempty[i], kEpiThreads);
+        }
+        mbar_init(drain, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, Cfg::kTmemCols);
+        tmem_relinquish();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&tmx);
+        prefetch_tmap(&tmw);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int num_m = (a.M + kBM - 1) / kBM;
+    const int num_n = (a.N + BN - 1) / BN;
+    const int num_kb = (a.K + kBK - 1) / kBK;
+    const int kb_per = (num_kb + a.splits - 1) / a.splits;
+    const int total = num_m * num_n * a.splits;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t issued = 0, issued_parity = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+                const Unit w = decode_unit(u, num_m, a.splits, num_kb, kb_per);
+                for (int kb = w.kb0; kb < w.kb1; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, a.err_flag, kErrTmaWait)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+                    tma_load_2d(sA + stage * Cfg::kABytes, &tmx, &full[stage], kb * kBK, w.mt * kBM);
+                    tma_load_2d(sB + stage * Cfg::kBBytes, &tmw, &full[stage], kb * kBK, w.nt * BN);
+                    issued |= 1u << stage;
+                    issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            if (!ok) {
+                // Leave no copy in flight into shared memory we are about to give up.
+                for (int s = 0; s < S; ++s)
+                    if (issued & (1u << s)) mbar_wait(&full[s], (issued_parity >> s) & 1u, nullptr, kErrDrainWait);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t idesc = idesc_f16_f32(kBM, BN);
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool any = false;
+            bool ok = true;
+            for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+                const Unit w = decode_unit(u, num_m, a.splits, num_kb, kb_per);
+                if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, a.err_flag, kErrMmaWait)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+                for (int kb = w.kb0; kb < w.kb1; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, a.err_flag, kErrMmaWait)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(sA + stage * Cfg::kABytes);
+                    const uint32_t b_addr = smem_u32(sB + stage * Cfg::kBBytes);
+#pragma unroll
+                    for (int k = 0; k < kBK / 16; ++k) {
+                        tc_mma_f16(d_tmem, smem_desc_k128(a_addr + k * 32), smem_desc_k128(b_addr + k * 32),
+                                   idesc, (kb > w.kb0 || k > 0) ? 1u : 0u);
+                    }
+                    tc_commit(&empty[stage]);
+                    any = true;
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                tc_commit(&tfull[acc]);
+                acc ^= 1;
+                if (acc == 0) acc_phase ^= 1u;
+            }
+            if (any) {
+                // Every MMA this thread issued must finish before TMEM is freed.
+                tc_commit(drain);
+                mbar_wait(drain, 0, nullptr, kErrDrainWait);
+            }
+        }
+    } else {
+        const int quad = warp & 3;  // TMEM lanes this warp may read: 32*quad .. +31
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int u = blockIdx.x; u < total; u += gridDim.x) {
+            const Unit w = decode_unit(u, num_m, a.splits, num_kb, kb_per);
+            const int sp = w.kb0 / kb_per;
+            // One lane waits; the verdict is shared so the warp stays
+            // converged for the .sync.aligned TMEM loads below.
+            int ok = 1;
+            if (lane == 0) ok = mbar_wait(&tfull[acc], acc_phase, a.err_flag, kErrEpiWait) ? 1 : 0;
+            ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+            if (!ok) break;
+            tc_fence_after();
+            const int64_t row = static_cast<int64_t>(w.mt) * kBM + quad * 32 + lane;
+            const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                                   static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                __syncwarp();
+                tmem_ld_32cols(t_row + c * 32, r);
+                const int64_t col0 = static_cast<int64_t>(w.nt) * BN + c * 32;
+                if (row < a.M && col0 < a.N) store_row_chunk(a, r, row, col0, sp);
+            }
+            tc_fence_before();
+            mbar_arrive(&tempty[acc]);
+            acc ^= 1;
+            if (acc == 0) acc_phase ^= 1u;
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem_base, Cfg::kTmemCols);
+    }
+}
+
+template <int BN>
+cudaError_t launch_bn(const TcGemmArgs& a, const CUtensorMap& tx, const CUtensorMap& tw, cudaStream_t s) {
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(TcCfg<BN>::kSmem));
+        if (e != cudaSuccess) return e;
+        attr_set[dev] = true;
+    }
+    tc_gemm_kernel<BN><<<a.grid, kThreadsTc, TcCfg<BN>::kSmem, s>>>(a, tx, tw);
+    note_launches(1);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+size_t tc_gemm_smem_bytes(int bn) {
+    return bn >= 256 ? TcCfg<256>::kSmem : TcCfg<128>::kSmem;
+}
+
+cudaError_t launch_tc_gemm(const TcGemmArgs& a, const CUtensorMap& tmap_x, const CUtensorMap& tmap_w,
+                           cudaStream_t s) {
+    if (a.M <= 0 || a.N <= 0) return cudaSuccess;
+    if (a.K <= 0 || a.grid <= 0 || a.splits <= 0) return cudaErrorInvalidValue;
+    if (a.bn == 256) return launch_bn<256>(a, tmap_x, tmap_w, s);
+    if (a.bn == 128) return launch_bn<128>(a, tmap_x, tmap_w, s);
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace mrt

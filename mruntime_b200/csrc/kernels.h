@@ -1,0 +1,91 @@
+// kernels.h -- host-side launchers of the sm_100a kernels (internal to the
+// library; the public surface is include/mrt_b200.h).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mrt {
+
+// Count one kernel launch (read through mrt_launch_count).
+void note_launches(int n);
+
+// Y[M,N] = X[M,K] * W[N,K]^T for M <= 64 (decode / skinny shapes).
+// Requirements checked by the caller: K % 8 == 0, ldx % 8 == 0, 16-byte
+// aligned x and w.  out_f32 selects FP32 output (no rounding, no bias).
+struct SkinnyArgs {
+    const uint16_t* x;
+    int64_t ldx;
+    const uint16_t* w;  // dense [N, K]
+    void* y;
+    int64_t ldy;
+    int M, N, K;
+    const uint16_t* bias;  // FP16 [N] or nullptr
+    int out_f32;
+};
+cudaError_t launch_skinny(const SkinnyArgs& a, int rows_per_warp_tiles, cudaStream_t s);
+
+// Y = X * W^T on the tcgen05 tensor cores, for M > 64.
+// tmap_x: [M, K] FP16, box 64 x 128, 128B swizzle.  tmap_w: [N, K] FP16, box
+// 64 x bn, 128B swizzle.  With splits > 1 every split writes FP32 partials
+// into `partials` ([splits, M, N]) and reduce_splits() finishes the job.
+struct TcGemmArgs {
+    int M, N, K;
+    int bn;      // 128 or 256
+    int splits;  // K splits (1 = write the output directly)
+    int grid;    // persistent CTAs
+    void* y;     // FP16 or FP32 output (splits == 1) [M, ldy]
+    int64_t ldy;
+    int out_f32;
+    const uint16_t* bias;  // splits == 1 only
+    float* partials;       // splits > 1
+    int* err_flag;
+};
+cudaError_t launch_tc_gemm(const TcGemmArgs& a, const CUtensorMap& tmap_x, const CUtensorMap& tmap_w,
+                           cudaStream_t s);
+size_t tc_gemm_smem_bytes(int bn);
+
+// out[m, n] = round(sum_s partials[s, m, n]) (+bias), or FP32 sum.
+cudaError_t launch_reduce_splits(const float* partials, int splits, int M, int N, void* y,
+                                 int64_t ldy, int out_f32, const uint16_t* bias, cudaStream_t s);
+
+// Element-wise conversions with the reference's rounding.
+cudaError_t launch_convert(const void* src, int src_dtype, void* dst, int dst_dtype, int64_t n,
+                           cudaStream_t s);
+// Gather rows/columns of a [rows, cols] source of dtype src_dtype into a
+// dense FP16 [rows, k1-k0] destination (weight upload of a shard).
+cudaError_t launch_convert_2d_to_f16(const void* src, int src_dtype, int64_t src_ld, int64_t rows,
+                                     int64_t cols, uint16_t* dst, cudaStream_t s);
+
+// Row argmax in two passes through `scratch` (see argmax_scratch_bytes).
+size_t argmax_scratch_bytes(int64_t M, int64_t V);
+cudaError_t launch_argmax(const uint16_t* logits, int64_t M, int64_t V, int64_t ld,
+                          int64_t index_base, int64_t* idx, float* val, void* scratch,
+                          cudaStream_t s);
+// Combine per-rank (value, index) pairs gathered as [world, M].
+cudaError_t launch_argmax_combine(const float* vals, const int64_t* idxs, int world, int64_t M,
+                                  int64_t* idx_out, cudaStream_t s);
+
+// FP32 -> FP16 rounding of an all-reduced buffer.
+cudaError_t launch_f32_to_f16(const float* src, uint16_t* dst, int64_t n, cudaStream_t s);
+
+// General strided GEMM covering the whole Backend::gemm contract.
+struct GeneralGemmArgs {
+    const void* a;
+    int a_dtype;
+    int64_t a_cols0;
+    const void* b;
+    int b_dtype;
+    int64_t b_cols0;
+    void* c;
+    int c_dtype;
+    int64_t ldc;  // row stride of C (N for a dense C)
+    int64_t M, N, K;
+    float alpha, beta;
+    int trans_a, trans_b;
+    const uint16_t* bias;  // FP16 [N] added after rounding (FP16 C only) or nullptr
+};
+cudaError_t launch_general_gemm(const GeneralGemmArgs& a, cudaStream_t s);
+
+}  // namespace mrt

@@ -1,0 +1,87 @@
+"""Helpers for the GPU parity tests: device copies of uint16 bit arrays,
+calls through the C ABI, and the tolerance checks against the oracle and the
+FP64 ground truth."""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from mruntime_b200 import capi
+from mruntime_b200 import workloads as W
+
+FP16, BF16, FP32 = capi.FP16, capi.BF16, capi.FP32
+
+# Tolerances: relative Frobenius error against FP64 at
+# most 1e-3, and never worse than the reference's own error against the same
+# ground truth.  "Never worse" allows 1% relative slack for the different FP32
+# summation order, which moves an occasional output across an FP16 rounding
+# midpoint in either direction.
+REL_FROB_MAX = 1e-3
+REF_ERR_SLACK = 1.01
+
+
+def stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def dev_u16(a: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.uint16).view(np.int16)).cuda()
+
+
+def host_u16(t: torch.Tensor) -> np.ndarray:
+    return t.cpu().numpy().view(np.uint16)
+
+
+def upload(w: np.ndarray, dtype: int, row_ranges=None, k_range=None, on_device: bool = True) -> capi.Weight:
+    N, K = w.shape
+    if on_device:
+        src = dev_u16(w) if dtype != FP32 else torch.from_numpy(np.ascontiguousarray(w, np.float32)).cuda()
+        wt = capi.Weight(src.data_ptr(), dtype, True, N, K, row_ranges, k_range, stream())
+        torch.cuda.synchronize()
+        del src
+        return wt
+    arr = np.ascontiguousarray(w)
+    return capi.Weight(arr.ctypes.data, dtype, False, N, K, row_ranges, k_range, stream())
+
+
+def gemm(wt: capi.Weight, x: np.ndarray | torch.Tensor, bias: bool = False) -> np.ndarray:
+    xd = x if isinstance(x, torch.Tensor) else dev_u16(x)
+    M = xd.shape[0]
+    y = torch.empty((M, wt.n), dtype=torch.int16, device="cuda")
+    capi.gemm(wt, xd.data_ptr(), xd.shape[1], y.data_ptr(), wt.n, M, bias, stream())
+    capi.sync(stream())
+    return host_u16(y)
+
+
+def f64_truth(x: np.ndarray, w: np.ndarray, w_dtype: int, bias: np.ndarray | None = None) -> np.ndarray:
+    """FP64 ground truth, computed on the GPU in float64."""
+    xf = torch.from_numpy(W.f16_bits_to_f32(x)).cuda().double()
+    wf32 = W.f16_bits_to_f32(w) if w_dtype == FP16 else (W.bf16_bits_to_f32(w) if w_dtype == BF16 else w)
+    wf = torch.from_numpy(np.ascontiguousarray(wf32, np.float32)).cuda().double()
+    y = xf @ wf.T
+    if bias is not None:
+        y = y + torch.from_numpy(W.bf16_bits_to_f32(bias)).cuda().double()[None, :]
+    return y.cpu().numpy()
+
+
+def rel_frob(got_f16: np.ndarray, truth: np.ndarray) -> float:
+    g = W.f16_bits_to_f32(got_f16).astype(np.float64)
+    return float(np.linalg.norm(g - truth) / np.linalg.norm(truth))
+
+
+def check_close(got_f16: np.ndarray, truth: np.ndarray, ref_err: float | None = None, what: str = "") -> float:
+    """Element-wise bound (FP16 rounding of an FP32 sum) plus the Frobenius bars."""
+    g = W.f16_bits_to_f32(got_f16).astype(np.float64)
+    rms = float(np.sqrt(np.mean(truth ** 2))) + 1e-30
+    bound = 2.0 ** -10 * np.abs(truth) + 1e-5 * rms
+    bad = np.abs(g - truth) > bound
+    assert not bad.any(), f"{what}: {int(bad.sum())} elements outside the FP16 rounding bound"
+    err = rel_frob(got_f16, truth)
+    assert err <= REL_FROB_MAX, f"{what}: rel Frobenius {err:.3e} > {REL_FROB_MAX}"
+    if ref_err is not None:
+        assert err <= ref_err * REF_ERR_SLACK, f"{what}: rel Frobenius {err:.4e} worse than reference {ref_err:.4e}"
+    return err
+
+
+def same_fraction(a: np.ndarray, b: np.ndarray) -> float:
+    return float(np.mean(a == b))

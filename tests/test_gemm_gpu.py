@@ -1,0 +1,243 @@
+"""GPU parity of the linear-layer path, through the C ABI, against the oracle
+(the reference's arithmetic, pinned by tests/test_oracle.py) and the FP64
+ground truth, on seeded inputs."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden
+from gpu_util import (BF16, FP16, FP32, check_close, dev_u16, f64_truth, gemm, host_u16, rel_frob,
+                      same_fraction, stream, upload)
+from mruntime_b200 import capi
+from mruntime_b200 import workloads as W
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def rand_f16(rng, shape, std=1.0):
+    return W.to_f16_bits(rng.standard_normal(shape, dtype=np.float32) * np.float32(std))
+
+
+def rand_w(rng, shape, dt):
+    v = rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02)
+    return W.to_f16_bits(v) if dt == FP16 else W.to_bf16_bits(v)
+
+
+# ------------------------------------------------------------------ general contract (bit-exact)
+
+def test_known_answer_backend_test(cuda_dev):
+    g = golden("kat_backend_test.npz")
+    a, b = dev_u16(g["a"]), dev_u16(g["b"])
+    c = torch.zeros((2, 4), dtype=torch.int16, device="cuda")
+    capi.gemm_general(a.data_ptr(), FP16, (2, 3), b.data_ptr(), FP16, (3, 4), c.data_ptr(), FP16, stream=stream())
+    capi.sync(stream())
+    np.testing.assert_array_equal(host_u16(c), g["c"])
+
+
+def _dev_any(a, dt):
+    if dt == FP32:
+        return torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
+    return dev_u16(a)
+
+
+def _host_any(t, dt):
+    return t.cpu().numpy() if dt == FP32 else host_u16(t)
+
+
+def test_general_gemm_bitexact_with_reference(cuda_dev):
+    g = golden("gemm_small.npz")
+    for i in range(int(g["n_cases"])):
+        M, N, K, adt, bdt, cdt, ta, tb = (int(v) for v in g[f"c{i}_spec"])
+        alpha, beta = (float(v) for v in g[f"c{i}_ab"])
+        A, B, C0 = g[f"c{i}_A"], g[f"c{i}_B"], g[f"c{i}_C0"]
+        a, b, c = _dev_any(A, adt), _dev_any(B, bdt), _dev_any(C0, cdt)
+        capi.gemm_general(a.data_ptr(), adt, A.shape, b.data_ptr(), bdt, B.shape, c.data_ptr(), cdt, alpha, beta,
+                          bool(ta), bool(tb), stream())
+        capi.sync(stream())
+        got = _host_any(c, cdt)
+        np.testing.assert_array_equal(got.view(np.uint32) if cdt == FP32 else got,
+                                      g[f"c{i}_C"].view(np.uint32) if cdt == FP32 else g[f"c{i}_C"],
+                                      err_msg=f"case {i}")
+
+
+def test_convert_bitexact_with_reference(cuda_dev):
+    g = golden("convert.npz")
+    src = torch.from_numpy(g["f32_bits"].view(np.float32)).cuda()
+    n = src.numel()
+    out16 = torch.empty(n, dtype=torch.int16, device="cuda")
+    capi.convert(src.data_ptr(), FP32, out16.data_ptr(), FP16, n, stream())
+    outb = torch.empty(n, dtype=torch.int16, device="cuda")
+    capi.convert(src.data_ptr(), FP32, outb.data_ptr(), BF16, n, stream())
+    h = dev_u16(np.arange(65536, dtype=np.uint32).astype(np.uint16))
+    out32 = torch.empty(65536, dtype=torch.float32, device="cuda")
+    capi.convert(h.data_ptr(), FP16, out32.data_ptr(), FP32, 65536, stream())
+    capi.sync(stream())
+    np.testing.assert_array_equal(host_u16(out16), g["f16_of_f32"])
+    np.testing.assert_array_equal(host_u16(outb), g["bf16_of_f32"])
+    got = out32.cpu().numpy()
+    want = g["f32_of_f16"].view(np.float32)
+    nan = np.isnan(want)
+    np.testing.assert_array_equal(np.isnan(got), nan)
+    np.testing.assert_array_equal(got[~nan].view(np.uint32), want[~nan].view(np.uint32))
+
+
+# ------------------------------------------------------------------ weight upload
+
+def weight_fp16(wt) -> np.ndarray:
+    """Read back the library-owned FP16 weight (an FP16 -> FP16 mrt_convert is a copy)."""
+    buf = torch.empty((wt.n, wt.k), dtype=torch.int16, device="cuda")
+    capi.convert(wt.data_ptr(), FP16, buf.data_ptr(), FP16, wt.n * wt.k, stream())
+    capi.sync(stream())
+    return host_u16(buf)
+
+
+@pytest.mark.parametrize("on_device", [True, False])
+@pytest.mark.parametrize("dt", [FP16, BF16, FP32])
+def test_upload_rounds_like_reference_packing(cuda_dev, on_device, dt):
+    rng = np.random.default_rng(5)
+    v = rng.standard_normal((300, 72), dtype=np.float32) * np.float32(0.05)
+    v[0, :4] = [1e-7, -3e-9, 70000.0, 2.0 ** -20]
+    src = {FP16: W.to_f16_bits(v), BF16: W.to_bf16_bits(v), FP32: v}[dt]
+    wt = upload(src, dt, on_device=on_device)
+    got = weight_fp16(wt)
+    want = {FP16: src, BF16: O.bf16_to_f16(src), FP32: O.f32_to_f16(v)}[dt]
+    np.testing.assert_array_equal(got, want)
+
+
+def test_upload_shards_select_rows_and_columns(cuda_dev):
+    rng = np.random.default_rng(6)
+    w = rand_w(rng, (96, 64), BF16)
+    full = O.bf16_to_f16(w)
+    wt = upload(w, BF16, row_ranges=[(8, 24), (48, 56)], k_range=(16, 48))
+    assert (wt.n, wt.k) == (24, 32)
+    want = np.concatenate([full[8:24, 16:48], full[48:56, 16:48]])
+    np.testing.assert_array_equal(weight_fp16(wt), want)
+
+
+# ------------------------------------------------------------------ fast kernels vs oracle
+
+def _check_against_oracle(x, w, wdt, y, rows=None, what=""):
+    idx = np.arange(x.shape[0]) if rows is None else np.asarray(rows)
+    xs = x[idx]
+    y_or = O.gemm(xs, FP16, w, wdt, trans_b=True)
+    truth = f64_truth(xs, w, wdt)
+    ref_err = rel_frob(y_or, truth)
+    err = check_close(y[idx], truth, ref_err, what)
+    return err, ref_err, same_fraction(y[idx], y_or)
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 7, 8, 9, 15, 16, 17, 31, 32, 33, 48, 63, 64])
+@pytest.mark.parametrize("NK", [(200, 64), (257, 136), (1000, 896)])
+def test_skinny_kernel(cuda_dev, M, NK):
+    N, K = NK
+    rng = np.random.default_rng(M * 7 + N)
+    x = rand_f16(rng, (M, K))
+    w = rand_w(rng, (N, K), BF16)
+    wt = upload(w, BF16)
+    y = gemm(wt, x)
+    _, _, same = _check_against_oracle(x, w, BF16, y, what=f"skinny M={M} N={N} K={K}")
+    assert same > 0.9
+
+
+@pytest.mark.parametrize("M", [65, 100, 128, 129, 256, 300, 512])
+@pytest.mark.parametrize("NK", [(64, 64), (200, 72), (256, 896), (1000, 1000 - 1000 % 8), (4864, 896)])
+def test_tensor_core_kernel(cuda_dev, M, NK):
+    N, K = NK
+    rng = np.random.default_rng(M * 13 + N)
+    x = rand_f16(rng, (M, K))
+    w = rand_w(rng, (N, K), FP16)
+    wt = upload(w, FP16)
+    y = gemm(wt, x)
+    rows = None if M * N * K <= 300 * 1000 * 1000 else np.r_[0:8, M // 2, M - 8:M]
+    _, _, same = _check_against_oracle(x, w, FP16, y, rows, what=f"tc M={M} N={N} K={K}")
+    assert same > 0.9
+
+
+@pytest.mark.parametrize("M", [1, 5, 40, 130])
+def test_unaligned_k_uses_general_kernel(cuda_dev, M):
+    rng = np.random.default_rng(M)
+    K, N = 13, 37
+    x = rand_f16(rng, (M, K))
+    w = rand_w(rng, (N, K), FP16)
+    wt = upload(w, FP16)
+    y = gemm(wt, x)
+    np.testing.assert_array_equal(y, O.gemm(x, FP16, w, FP16, trans_b=True))  # same sum order: bit-exact
+
+
+@pytest.mark.parametrize("M", [1, 16, 64, 200])
+def test_bias_double_rounding(cuda_dev, M):
+    rng = np.random.default_rng(40 + M)
+    N, K = 136, 128
+    x = rand_f16(rng, (M, K))
+    w = rand_w(rng, (N, K), BF16)
+    b = rand_w(rng, (N,), BF16)
+    wt = upload(w, BF16)
+    bd = dev_u16(b)
+    wt.attach_bias(bd.data_ptr(), BF16, True, stream())
+    y_plain = gemm(wt, x)
+    y_bias = gemm(wt, x, bias=True)
+    b16 = W.bf16_to_f16_bits(b)
+    np.testing.assert_array_equal(y_bias, O.add_bias(y_plain, b16))  # qwen_model.cpp:130-155 exactly
+    truth = f64_truth(x, w, BF16, bias=b)
+    y_or = O.add_bias(O.gemm(x, FP16, w, BF16, trans_b=True), b16)
+    check_close(y_bias, truth, rel_frob(y_or, truth), f"bias M={M}")
+
+
+@pytest.mark.parametrize("M", [1, 33, 130, 512])
+def test_f32_output(cuda_dev, M):
+    rng = np.random.default_rng(90 + M)
+    N, K = 264, 512
+    x = rand_f16(rng, (M, K))
+    w = rand_w(rng, (N, K), FP16)
+    wt = upload(w, FP16)
+    xd = dev_u16(x)
+    y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    capi.gemm_f32(wt, xd.data_ptr(), K, y.data_ptr(), N, M, stream())
+    capi.sync(stream())
+    truth = f64_truth(x, w, FP16)
+    err = np.linalg.norm(y.cpu().numpy() - truth) / np.linalg.norm(truth)
+    assert err < 1e-5
+
+
+def test_zero_rows_is_a_no_op(cuda_dev):
+    wt = upload(np.zeros((16, 64), np.uint16), FP16)
+    capi.gemm(wt, 0, 64, 0, 16, 0, False, stream())
+    capi.sync(stream())
+
+
+def test_host_buffer_call_matches_device_call(cuda_dev):
+    rng = np.random.default_rng(77)
+    for M in (1, 300):
+        x = rand_f16(rng, (M, 896))
+        w = rand_w(rng, (640, 896), BF16)
+        wt = upload(w, BF16)
+        y_dev = gemm(wt, x)
+        y_host = np.empty((M, 640), np.uint16)
+        xh = np.ascontiguousarray(x)
+        capi.gemm_host(wt, xh.ctypes.data, y_host.ctypes.data, M, False, stream())
+        np.testing.assert_array_equal(y_host, y_dev)
+
+
+# ------------------------------------------------------------------ argmax
+
+def test_argmax_edge_cases_match_reference(cuda_dev):
+    g = golden("bias_argmax.npz")
+    for key, am in (("rows", "am_rows"), ("rand", "am_rand")):
+        rows = g[key]
+        M, V = rows.shape
+        d = dev_u16(rows)
+        idx = torch.empty(M, dtype=torch.int64, device="cuda")
+        capi.argmax_f16(d.data_ptr(), M, V, V, 0, idx.data_ptr(), None, stream())
+        capi.sync(stream())
+        np.testing.assert_array_equal(idx.cpu().numpy(), g[am])
+    # index_base shifts the result (vocabulary shard)
+    d = dev_u16(g["rand"][:1])
+    idx = torch.empty(1, dtype=torch.int64, device="cuda")
+    capi.argmax_f16(d.data_ptr(), 1, g["rand"].shape[1], g["rand"].shape[1], 1000, idx.data_ptr(), None, stream())
+    capi.sync(stream())
+    assert int(idx.item()) == int(g["am_rand"][0]) + 1000
+
+
+def test_no_kernel_timed_out(cuda_dev):
+    capi.sync(stream())  # raises MrtError(MRT_ERR_TIMEOUT) if any bounded wait gave up
