@@ -85,6 +85,26 @@ int mrt_device_sm_count(int* out);
 /* Kernels this library has launched in this process so far (all devices). */
 int mrt_launch_count(int64_t* out);
 
+/* ---------------------------------------------------------------- device storage */
+
+/* Device-resident tensor storage: the device counterpart of Tensor::empty's
+ * host heap allocation (reference src/core/tensor.cpp:8-12).  Blocks are at
+ * least 256-byte aligned. */
+int mrt_device_alloc(size_t bytes, void** out);
+int mrt_device_free(void* p);
+
+/* Copy `bytes` between any two of host / device memory (direction inferred
+ * from the pointers), ordered on `stream`; waits for completion when either
+ * side is pageable host memory. */
+int mrt_memcpy(void* dst, const void* src, size_t bytes, void* stream);
+
+/* Where a pointer lives: 0 = host (pageable or pinned), 1 = device memory,
+ * 2 = managed memory. */
+#define MRT_PTR_HOST 0
+#define MRT_PTR_DEVICE 1
+#define MRT_PTR_MANAGED 2
+int mrt_pointer_kind(const void* p, int* kind);
+
 /* ---------------------------------------------------------------- weights */
 
 /*
@@ -114,6 +134,10 @@ int mrt_weight_upload(const void* src, int src_dtype, int src_on_device, int64_t
  * reference's load-time conversion (src/models/qwen/qwen_model.cpp:93-101). */
 int mrt_weight_attach_bias(mrt_weight w, const void* src, int src_dtype, int src_on_device,
                            void* stream);
+
+/* Borrow an FP16 weight W[N, K] that already lives in device memory, without
+ * copying (the caller keeps it alive until mrt_weight_free of the view). */
+int mrt_weight_view(const void* w_dev_f16, int64_t N, int64_t K, mrt_weight* out);
 
 int mrt_weight_free(mrt_weight w);
 
@@ -183,6 +207,46 @@ int mrt_lm_head_argmax(mrt_weight w, const void* x_dev, int64_t ldx, int64_t M, 
  * (include/mruntime/dtype.h:39-194): src_dtype -> dst_dtype, n elements. */
 int mrt_convert(const void* src_dev, int src_dtype, void* dst_dev, int dst_dtype, int64_t n,
                 void* stream);
+
+/* ---------------------------------------------------------------- support ops */
+
+/*
+ * The other Backend operations (reference include/mruntime/backend.h:23-73),
+ * on device pointers, so a model can run with every tensor on the device.
+ * They restate src/core/cpu_backend.cpp:171-569.  Rounding: element-wise
+ * results are computed in FP32 and stored with the reference's converters;
+ * SiLU on FP16 uses a 65536-entry table built on the host with the
+ * reference's own float expression (x / (1 + exp(-x)), glibc exp), and RoPE's
+ * cos/sin are built on the host with the reference's expressions
+ * (cpu_backend.cpp:363-366), so both match the reference bit for bit.
+ * Reductions (RMSNorm's sum of squares, softmax and attention sums) use
+ * parallel FP32 trees; their results agree with the reference within FP32
+ * rounding.
+ */
+int mrt_rmsnorm(const void* in_dev, int in_dtype, const void* w_dev, int w_dtype, void* out_dev,
+                int out_dtype, int64_t rows, int64_t hidden, float eps, void* stream);
+int mrt_rope(void* x_dev, int dtype, int64_t batch, int64_t seq, int64_t heads, int64_t head_dim,
+             int64_t position_offset, float theta, void* stream);
+int mrt_silu(const void* in_dev, int in_dtype, void* out_dev, int out_dtype, int64_t n, void* stream);
+int mrt_mul(const void* a_dev, int a_dtype, const void* b_dev, int b_dtype, void* out_dev, int out_dtype,
+            int64_t n, void* stream);
+int mrt_add(const void* a_dev, int a_dtype, const void* b_dev, int b_dtype, void* out_dev, int out_dtype,
+            int64_t n, void* stream);
+int mrt_softmax(const void* in_dev, int in_dtype, void* out_dev, int out_dtype, int64_t outer, int64_t dim,
+                int64_t inner, void* stream);
+/* token_ids in host memory; each is checked against vocab (std::out_of_range in
+ * the reference, cpu_backend.cpp:533-537, MRT_ERR_INVALID_ARG here). */
+int mrt_embedding(const void* w_dev, int w_dtype, int64_t vocab, int64_t hidden, const int32_t* token_ids,
+                  int64_t n, void* out_dev, int out_dtype, void* stream);
+/* Q [batch, heads, q_len, qk_dim], K [batch, heads, kv_len, qk_dim],
+ * V [batch, heads, kv_len, v_dim], out [batch, heads, q_len, v_dim], each with
+ * its own element strides (4 per tensor).  Causal masking keeps key positions
+ * <= kv_len - q_len + query index (cpu_backend.cpp:233-247). */
+int mrt_attention(const void* q_dev, int q_dtype, const int64_t* q_strides, const void* k_dev, int k_dtype,
+                  const int64_t* k_strides, const void* v_dev, int v_dtype, const int64_t* v_strides,
+                  void* out_dev, int out_dtype, const int64_t* out_strides, int64_t batch, int64_t heads,
+                  int64_t q_len, int64_t kv_len, int64_t qk_dim, int64_t v_dim, float scale, int causal,
+                  void* stream);
 
 /* ---------------------------------------------------------------- tensor parallel */
 

@@ -53,6 +53,11 @@ _SIGS = {
                                  C.POINTER(_vp)]),
     "mrt_weight_attach_bias": (_int, [_vp, _vp, _int, _int, _vp]),
     "mrt_weight_free": (_int, [_vp]),
+    "mrt_weight_view": (_int, [_vp, _i64, _i64, C.POINTER(_vp)]),
+    "mrt_device_alloc": (_int, [_sz, C.POINTER(_vp)]),
+    "mrt_device_free": (_int, [_vp]),
+    "mrt_memcpy": (_int, [_vp, _vp, _sz, _vp]),
+    "mrt_pointer_kind": (_int, [_vp, C.POINTER(_int)]),
     "mrt_weight_shape": (_int, [_vp, C.POINTER(_i64), C.POINTER(_i64)]),
     "mrt_weight_data": (_int, [_vp, C.POINTER(_vp)]),
     "mrt_gemm": (_int, [_vp, _vp, _i64, _vp, _i64, _i64, _u32, _vp]),

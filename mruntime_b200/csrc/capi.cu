@@ -311,9 +311,81 @@ extern "C" int mrt_weight_attach_bias(mrt_weight w, const void* src, int src_dty
     return MRT_OK;
 }
 
+extern "C" int mrt_weight_view(const void* w_dev_f16, int64_t N, int64_t K, mrt_weight* out) {
+    clear_error();
+    if (out == nullptr || w_dev_f16 == nullptr) return set_error(MRT_ERR_INVALID_ARG, "NULL argument");
+    if (N <= 0 || K <= 0) return set_error(MRT_ERR_SHAPE, "empty weight");
+    DevCtx* c = current_ctx();
+    if (!c) return MRT_ERR_CUDA;
+    mrt_weight_s* w = new mrt_weight_s();
+    w->device = c->device;
+    w->n = N;
+    w->k = K;
+    w->src_n = N;
+    w->data = static_cast<uint16_t*>(const_cast<void*>(w_dev_f16));
+    w->owns_data = false;
+    w->n_ranges = 1;
+    w->ranges = new int64_t[2]{0, N};
+    *out = w;
+    return MRT_OK;
+}
+
+extern "C" int mrt_device_alloc(size_t bytes, void** out) {
+    clear_error();
+    if (out == nullptr) return set_error(MRT_ERR_INVALID_ARG, "out is NULL");
+    *out = nullptr;
+    if (!current_ctx()) return MRT_ERR_CUDA;
+    if (bytes == 0) return MRT_OK;
+    cudaError_t e = cudaMalloc(out, bytes);
+    if (e != cudaSuccess) {
+        *out = nullptr;
+        return cuda_error(e, "cudaMalloc");
+    }
+    return MRT_OK;
+}
+
+extern "C" int mrt_device_free(void* p) {
+    if (p == nullptr) return MRT_OK;
+    cudaError_t e = cudaFree(p);
+    return e == cudaSuccess ? MRT_OK : cuda_error(e, "cudaFree");
+}
+
+extern "C" int mrt_memcpy(void* dst, const void* src, size_t bytes, void* stream) {
+    clear_error();
+    if (bytes == 0) return MRT_OK;
+    if (dst == nullptr || src == nullptr) return set_error(MRT_ERR_INVALID_ARG, "NULL pointer");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, s);
+    if (e != cudaSuccess) return cuda_error(e, "cudaMemcpyAsync");
+    cudaPointerAttributes ad{}, as{};
+    const bool pageable = cudaPointerGetAttributes(&ad, dst) != cudaSuccess || ad.type == cudaMemoryTypeUnregistered ||
+                          cudaPointerGetAttributes(&as, src) != cudaSuccess || as.type == cudaMemoryTypeUnregistered;
+    cudaGetLastError();  // clear a failed attribute query
+    if (pageable) {
+        e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) return cuda_error(e, "waiting for a pageable copy");
+    }
+    return MRT_OK;
+}
+
+extern "C" int mrt_pointer_kind(const void* p, int* kind) {
+    clear_error();
+    if (kind == nullptr) return set_error(MRT_ERR_INVALID_ARG, "kind is NULL");
+    cudaPointerAttributes a{};
+    cudaError_t e = cudaPointerGetAttributes(&a, p);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        *kind = MRT_PTR_HOST;
+        return MRT_OK;
+    }
+    *kind = a.type == cudaMemoryTypeDevice ? MRT_PTR_DEVICE
+                                           : (a.type == cudaMemoryTypeManaged ? MRT_PTR_MANAGED : MRT_PTR_HOST);
+    return MRT_OK;
+}
+
 extern "C" int mrt_weight_free(mrt_weight w) {
     if (w == nullptr) return MRT_OK;
-    cudaFree(w->data);
+    if (w->owns_data) cudaFree(w->data);
     if (w->bias) cudaFree(w->bias);
     delete[] w->ranges;
     delete w;

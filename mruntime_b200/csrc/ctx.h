@@ -58,6 +58,7 @@ struct mrt_weight_s {
     int64_t n = 0;  // rows kept
     int64_t k = 0;  // columns kept
     uint16_t* data = nullptr;  // dense FP16 [n, k]
+    bool owns_data = true;     // false for mrt_weight_view
     uint16_t* bias = nullptr;  // FP16 [n] or nullptr
     int64_t src_n = 0;         // rows of the full source weight
     int64_t* ranges = nullptr; // row ranges kept (pairs)

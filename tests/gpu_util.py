@@ -69,11 +69,29 @@ def rel_frob(got_f16: np.ndarray, truth: np.ndarray) -> float:
     return float(np.linalg.norm(g - truth) / np.linalg.norm(truth))
 
 
-def check_close(got_f16: np.ndarray, truth: np.ndarray, ref_err: float | None = None, what: str = "") -> float:
-    """Element-wise bound (FP16 rounding of an FP32 sum) plus the Frobenius bars."""
+def abs_dot(x: np.ndarray, w: np.ndarray, w_dtype: int) -> np.ndarray:
+    """sum_k |x_mk * w_nk| in float64 (the scale of FP32 summation error)."""
+    xf = torch.from_numpy(W.f16_bits_to_f32(x)).cuda().double().abs()
+    wf32 = W.f16_bits_to_f32(w) if w_dtype == FP16 else W.bf16_bits_to_f32(w)
+    wf = torch.from_numpy(np.ascontiguousarray(wf32, np.float32)).cuda().double().abs()
+    return (xf @ wf.T).cpu().numpy()
+
+
+def check_close(got_f16: np.ndarray, truth: np.ndarray, ref_err: float | None = None, what: str = "",
+                absdot: np.ndarray | None = None, K: int = 0, pre_round: np.ndarray | None = None) -> float:
+    """Element-wise bound plus the Frobenius bars.
+
+    Element bound: half an FP16 ulp of the truth (the output rounding, taken
+    as 2^-10 |t| so it covers subnormal spacing too), plus half an ulp of the
+    pre-bias accumulator when the output was rounded twice (``pre_round``),
+    plus 4 sqrt(K) 2^-24 sum_k|x w| for FP32 summation in any order
+    (``absdot``), plus the smallest FP16 subnormal."""
     g = W.f16_bits_to_f32(got_f16).astype(np.float64)
-    rms = float(np.sqrt(np.mean(truth ** 2))) + 1e-30
-    bound = 2.0 ** -10 * np.abs(truth) + 1e-5 * rms
+    bound = 2.0 ** -10 * np.abs(truth) + 2.0 ** -24
+    if pre_round is not None:
+        bound = bound + 2.0 ** -11 * np.abs(pre_round)
+    if absdot is not None:
+        bound = bound + 4.0 * np.sqrt(max(K, 1)) * 2.0 ** -24 * absdot
     bad = np.abs(g - truth) > bound
     assert not bad.any(), f"{what}: {int(bad.sum())} elements outside the FP16 rounding bound"
     err = rel_frob(got_f16, truth)

@@ -6,7 +6,7 @@ import pytest
 import torch
 
 from conftest import golden
-from gpu_util import (BF16, FP16, FP32, check_close, dev_u16, f64_truth, gemm, host_u16, rel_frob,
+from gpu_util import (BF16, FP16, FP32, abs_dot, check_close, dev_u16, f64_truth, gemm, host_u16, rel_frob,
                       same_fraction, stream, upload)
 from mruntime_b200 import capi
 from mruntime_b200 import workloads as W
@@ -123,7 +123,7 @@ def _check_against_oracle(x, w, wdt, y, rows=None, what=""):
     y_or = O.gemm(xs, FP16, w, wdt, trans_b=True)
     truth = f64_truth(xs, w, wdt)
     ref_err = rel_frob(y_or, truth)
-    err = check_close(y[idx], truth, ref_err, what)
+    err = check_close(y[idx], truth, ref_err, what, absdot=abs_dot(xs, w, wdt), K=x.shape[1])
     return err, ref_err, same_fraction(y[idx], y_or)
 
 
@@ -181,7 +181,8 @@ def test_bias_double_rounding(cuda_dev, M):
     np.testing.assert_array_equal(y_bias, O.add_bias(y_plain, b16))  # qwen_model.cpp:130-155 exactly
     truth = f64_truth(x, w, BF16, bias=b)
     y_or = O.add_bias(O.gemm(x, FP16, w, BF16, trans_b=True), b16)
-    check_close(y_bias, truth, rel_frob(y_or, truth), f"bias M={M}")
+    check_close(y_bias, truth, rel_frob(y_or, truth), f"bias M={M}", absdot=abs_dot(x, w, BF16), K=K,
+                pre_round=f64_truth(x, w, BF16))
 
 
 @pytest.mark.parametrize("M", [1, 33, 130, 512])

@@ -10,7 +10,8 @@ import pytest
 import torch
 
 from conftest import golden
-from gpu_util import BF16, FP16, check_close, dev_u16, f64_truth, gemm, host_u16, rel_frob, stream, upload
+from gpu_util import (BF16, FP16, abs_dot, check_close, dev_u16, f64_truth, gemm, host_u16, rel_frob, stream,
+                      upload)
 from mruntime_b200 import capi
 from mruntime_b200 import workloads as W
 
@@ -29,7 +30,7 @@ def test_decode_gemv_config(cuda_dev):
     d = W.decode_gemv()
     assert sha(d["x"], d["w"]) == str(g["input_sha"]), "input generator changed"
     y = gemm(upload(d["w"], FP16), d["x"])
-    err = check_close(y, g["y_f64"], float(g["ref_err"]), "decode gemv")
+    err = check_close(y, g["y_f64"], float(g["ref_err"]), "decode gemv", absdot=abs_dot(d["x"], d["w"], FP16), K=896)
     print(f"decode gemv rel err {err:.4e} (reference {float(g['ref_err']):.4e}), "
           f"bit-identical to reference: {np.mean(y == g['y_ref']):.4f}")
 
@@ -55,7 +56,8 @@ def test_layer_prefill_05b(cuda_dev, layer, name):
         torch.cuda.synchronize()
     y = gemm(wt, x, bias=bias is not None)
     truth = f64_truth(x, d[name], BF16, bias=bias)
-    err = check_close(y, truth, float(g[f"{name}_ref_err"]), f"layer {name}")
+    err = check_close(y, truth, float(g[f"{name}_ref_err"]), f"layer {name}", absdot=abs_dot(x, d[name], BF16),
+                      K=x.shape[1], pre_round=f64_truth(x, d[name], BF16) if bias is not None else None)
     rows = g["rows"]
     same = np.mean(y[rows] == g[f"{name}_rows"])
     assert same > 0.9
@@ -99,7 +101,8 @@ def test_lm_head_argmax(cuda_dev, lm_head, M):
     assert np.all(am[decisive] == ref_am[decisive])
     assert decisive.mean() > 0.9
     truth0 = f64_truth(d["x"][:1], d["w"], FP16)
-    check_close(lg[:1], truth0, float(g["ref_err_row0"]), "lm_head row 0")
+    check_close(lg[:1], truth0, float(g["ref_err_row0"]), "lm_head row 0", absdot=abs_dot(d["x"][:1], d["w"], FP16),
+                K=896)
     np.testing.assert_allclose(f.astype(np.float64).sum(axis=1), g["row_sum"][:M], rtol=1e-3, atol=1.0)
 
 
@@ -118,14 +121,16 @@ def test_sweep_7b(cuda_dev, sweep, name):
     xfull = d["x_down"] if name == "down" else d["x"]
     xd = dev_u16(xfull)
     rows = g["rows"]
-    truths = {name: f64_truth(xfull[rows], d[name], BF16)}
+    truths = f64_truth(xfull[rows], d[name], BF16)
+    absdots = abs_dot(xfull[rows], d[name], BF16)
     for M in W.SWEEP_M:
         y = gemm(wt, xd[:M])
         sel = rows[rows < M]
-        truth = truths[name][: len(sel)]
+        truth = truths[: len(sel)]
         ref = g[f"{name}_rows"][: len(sel)]
         ref_err = rel_frob(ref, truth)
-        err = check_close(y[sel], truth, ref_err, f"sweep {name} M={M}")
+        err = check_close(y[sel], truth, ref_err, f"sweep {name} M={M}", absdot=absdots[: len(sel)],
+                          K=xfull.shape[1])
         assert np.mean(y[sel] == ref) > 0.9
         print(f"{name} M={M}: rel err {err:.4e} reference {ref_err:.4e}")
     capi.sync(stream())
