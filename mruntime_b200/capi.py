@@ -68,6 +68,15 @@ _SIGS = {
     "mrt_argmax_f16": (_int, [_vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp]),
     "mrt_lm_head_argmax": (_int, [_vp, _vp, _i64, _i64, _vp, _i64, _vp, _vp, _vp]),
     "mrt_convert": (_int, [_vp, _int, _vp, _int, _i64, _vp]),
+    "mrt_rmsnorm": (_int, [_vp, _int, _vp, _int, _vp, _int, _i64, _i64, C.c_float, _vp]),
+    "mrt_rope": (_int, [_vp, _int, _i64, _i64, _i64, _i64, _i64, C.c_float, _vp]),
+    "mrt_silu": (_int, [_vp, _int, _vp, _int, _i64, _vp]),
+    "mrt_mul": (_int, [_vp, _int, _vp, _int, _vp, _int, _i64, _vp]),
+    "mrt_add": (_int, [_vp, _int, _vp, _int, _vp, _int, _i64, _vp]),
+    "mrt_softmax": (_int, [_vp, _int, _vp, _int, _i64, _i64, _i64, _vp]),
+    "mrt_embedding": (_int, [_vp, _int, _i64, _i64, _vp, _i64, _vp, _int, _vp]),
+    "mrt_attention": (_int, [_vp, _int, C.POINTER(_i64), _vp, _int, C.POINTER(_i64), _vp, _int, C.POINTER(_i64),
+                             _vp, _int, C.POINTER(_i64), _i64, _i64, _i64, _i64, _i64, _i64, C.c_float, _int, _vp]),
     "mrt_shard_rows": (_int, [C.POINTER(_i64), _i64, _int, _int, C.POINTER(_i64)]),
     "mrt_shard_cols": (_int, [_i64, _int, _int, C.POINTER(_i64), C.POINTER(_i64)]),
     "mrt_tp_unique_id": (_int, [_vp, _sz]),
