@@ -243,6 +243,22 @@ def time_steps(projs, tp, stream, M, steps, world, dominant=False):
     return max_over_ranks(total_ms, world), dom_ms
 
 
+def time_projections(projs, tp, stream, M, iters):
+    """Mean device time of each projection alone (ms), CUDA events on the stream."""
+    import torch
+
+    evs = {p.name: [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                    for _ in range(iters)] for p in projs}
+    for i in range(iters):
+        for p in projs:
+            a, b = evs[p.name][i]
+            a.record()
+            run_step([p], tp, stream, M)
+            b.record()
+    torch.cuda.synchronize()
+    return {name: statistics.mean(a.elapsed_time(b) for a, b in lst) for name, lst in evs.items()}
+
+
 def e2e_host_buffers(projs, tp, stream, M, steps, world):
     """Same step through the host-buffer entry point (N=1: mrt_gemm_host, the
     reference's calling convention) or, under TP, pinned-host copies around the
@@ -296,11 +312,11 @@ def gpu_arm(args, rank, world, local):
     M = args.m
     projs, tp, stream = setup_gpu(rank, world, local, max(M, max(WL.SWEEP_M) if not args.no_sweep else M))
     clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)  # let the sampler attach; it runs through warm-up and the timed region
     for _ in range(args.warmup):
         run_step(projs, tp, stream, M)
     capi.sync(stream)
-    clocks.start()
-    time.sleep(0.3)  # let the sampler attach before the timed region
     launches0 = capi.launch_count()
     total_ms, dom_ms = time_steps(projs, tp, stream, M, args.steps, world, dominant=True)
     launches = capi.launch_count() - launches0
@@ -335,10 +351,14 @@ def gpu_arm(args, rank, world, local):
             t = t_ms / n_it
             tf = step_flops(m) / (t * 1e-3) / 1e12
             gbs = WL.sweep_bytes(m) / (t * 1e-3) / 1e9
-            bound = "hbm" if m <= 64 else "tensor"
+            bound = "hbm" if m <= 128 else "tensor"
             frac = gbs / peaks["hbm_gbs"] if bound == "hbm" else tf / peaks["bf16_tflops_sustained"]
+            per = time_projections(projs, tp, stream, m, 10)
+            plans = {p.name: capi.gemm_plan(m, p.w.n, p.w.k) for p in projs}
             sweep.append({"M": m, "ms": round(t, 4), "TFLOP/s": round(tf, 1), "GB/s": round(gbs, 1), "bound": bound,
-                          "frac": round(frac, 4)})
+                          "frac": round(frac, 4), "per_projection_ms": {k: round(v, 4) for k, v in per.items()},
+                          "plans": {k: "{kernel} bn={bn} full={full_tiles} splits={tail_splits} kb={kb_per} "
+                                       "grid={grid}".format(**v) for k, v in plans.items()}})
         capi.sync(stream)
     return {"ms": ms, "value": value, "roofline": roofline, "e2e": e2e, "clocks": clk, "launches": launches,
             "sweep": sweep, "peaks": peaks, "projs": projs, "tp": tp}

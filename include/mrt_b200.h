@@ -159,6 +159,14 @@ int mrt_weight_data(mrt_weight w, void** dev_ptr);
 int mrt_gemm(mrt_weight w, const void* x_dev, int64_t ldx, void* y_dev, int64_t ldy, int64_t M,
              unsigned flags, void* stream);
 
+/* The kernel mrt_gemm would run for an M x N x K product on a device with
+ * `sms` multiprocessors (0 = the current device): kernel 0 = skinny
+ * (M <= 16), 1 = tcgen05; for the tcgen05 kernel the tile width, the
+ * number of tiles run over the whole K, the K-slices of each remaining tile,
+ * k-blocks per slice and the persistent grid.  Host-only. */
+int mrt_gemm_plan(int64_t M, int64_t N, int64_t K, int sms, int* kernel, int* bn, int* full_tiles,
+                  int* tail_splits, int* kb_per, int* grid);
+
 /* Same product without the final rounding: y_dev is FP32.  Used for the
  * partial sums of a row-parallel (K-split) shard before the all-reduce. */
 int mrt_gemm_f32(mrt_weight w, const void* x_dev, int64_t ldx, float* y_dev, int64_t ldy,

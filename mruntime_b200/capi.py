@@ -62,6 +62,7 @@ _SIGS = {
     "mrt_weight_data": (_int, [_vp, C.POINTER(_vp)]),
     "mrt_gemm": (_int, [_vp, _vp, _i64, _vp, _i64, _i64, _u32, _vp]),
     "mrt_gemm_f32": (_int, [_vp, _vp, _i64, _vp, _i64, _i64, _vp]),
+    "mrt_gemm_plan": (_int, [_i64, _i64, _i64, _int] + [C.POINTER(_int)] * 6),
     "mrt_gemm_host": (_int, [_vp, _vp, _vp, _i64, _u32, _vp]),
     "mrt_gemm_general": (_int, [_vp, _int, _i64, _i64, _vp, _int, _i64, _i64, _vp, _int, C.c_float, C.c_float,
                                 _int, _int, _vp]),
@@ -180,6 +181,16 @@ class Weight:
 def gemm(w: Weight, x_ptr: int, ldx: int, y_ptr: int, ldy: int, M: int, bias: bool = False,
          stream: int | None = None) -> None:
     call("mrt_gemm", w.h, x_ptr, ldx, y_ptr, ldy, M, GEMM_BIAS if bias else 0, stream)
+
+
+def gemm_plan(M: int, N: int, K: int, sms: int = 0) -> dict:
+    """The kernel and tiling mrt_gemm picks for an M x N x K product."""
+    vals = [C.c_int() for _ in range(6)]
+    call("mrt_gemm_plan", M, N, K, sms, *[C.byref(v) for v in vals])
+    keys = ("kernel", "bn", "full_tiles", "tail_splits", "kb_per", "grid")
+    d = dict(zip(keys, (v.value for v in vals)))
+    d["kernel"] = "skinny" if d["kernel"] == 0 else "tcgen05"
+    return d
 
 
 def gemm_f32(w: Weight, x_ptr: int, ldx: int, y_ptr: int, ldy: int, M: int, stream: int | None = None) -> None:

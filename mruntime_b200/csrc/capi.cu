@@ -409,42 +409,64 @@ extern "C" int mrt_weight_data(mrt_weight w, void** dev_ptr) {
 
 namespace mrt {
 
-// Tile plan for the tcgen05 kernel.  Cost model in units of one 128x128x64
-// MMA block-step on one SM: a work unit of BN columns and kb_per k-blocks
-// costs (BN/128)*(kb_per + 2) (the +2 is pipeline fill and epilogue), units
-// run in ceil(units / SMs) waves, and a split-K plan pays for writing and
-// re-reading its FP32 partials at HBM speed.
+// Tile plan for the tcgen05 kernel.  A work unit of BN columns and kb
+// 64-wide k-blocks on one SM costs the larger of its MMA time (one 128x128x64
+// block-step is ~0.22 us at the sustained clock) and its operand streaming
+// time (the SM's share of HBM bandwidth for W, L2 for X).  Units run round
+// robin over the persistent CTAs.  Three shapes are compared per tile width:
+// every tile over the whole K; whole waves over the whole K plus the last
+// partial wave split along K; every tile split along K (the same formula with
+// no whole wave).  Split slices pay for writing and re-reading FP32 partials.
 struct TcPlan {
-    int bn = 256, splits = 1, grid = 1;
+    int bn = 256, grid = 1, full = 0, splits = 1, kb_per = 0;
 };
+
+static double unit_us(int bn, int64_t kb, int64_t active, int sms, int64_t x_rows) {
+    const double compute = (bn / 128.0) * (static_cast<double>(kb) + 2.0) * 0.22;
+    // One SM streams at most ~50 GB/s (its ring of TMA loads in flight over
+    // the memory latency); together they share ~6.5 TB/s of HBM.
+    const double hbm_share = std::min(50e9, 6.5e12 / static_cast<double>(std::max<int64_t>(1, std::min<int64_t>(active, sms))));
+    const double w_bytes = static_cast<double>(bn) * 128.0 * kb;
+    const double x_bytes = static_cast<double>(x_rows) * 128.0 * kb;
+    const double mem = (w_bytes / hbm_share + x_bytes / (2.0 * hbm_share)) * 1e6;
+    return std::max(compute, mem);
+}
 
 static TcPlan plan_tc(int64_t M, int64_t N, int64_t K, int sms) {
     const int64_t num_m = (M + 127) / 128;
     const int64_t num_kb = (K + 63) / 64;
+    const int64_t x_rows = std::min<int64_t>(M, 128);
     TcPlan best;
     double best_cost = 1e300;
-    const int cand_splits[] = {1, 2, 3, 4, 6, 8, 12, 16};
-    for (int bn : {256, 128}) {
+    for (int bn : {256, 128, 64}) {
         const int64_t tiles = num_m * ((N + bn - 1) / bn);
-        for (int sp : cand_splits) {
-            if (sp > num_kb) break;
-            const int64_t kb_per = (num_kb + sp - 1) / sp;
-            const int64_t splits = (num_kb + kb_per - 1) / kb_per;  // no empty split
-            if ((num_kb + splits - 1) / splits != kb_per) continue;
-            if (splits > 1 && tiles * splits > 8LL * sms) continue;
-            const int64_t units = tiles * splits;
-            const int64_t waves = (units + sms - 1) / sms;
-            double cost = static_cast<double>(waves) * (bn / 128.0) * (static_cast<double>(kb_per) + 2.0);
-            if (splits > 1) {
-                // ~0.2 us per block-step; partial traffic at ~6 TB/s.
-                const double bytes = static_cast<double>(M) * N * 4.0 * (2.0 * splits + 1.0);
-                cost += bytes / 6.0e6 / 0.2 + 5.0;
-            }
+        // every tile over the whole K
+        {
+            const int64_t waves = (tiles + sms - 1) / sms;
+            const double cost = waves * unit_us(bn, num_kb, tiles, sms, x_rows);
             if (cost < best_cost - 1e-9) {
                 best_cost = cost;
-                best.bn = bn;
-                best.splits = static_cast<int>(splits);
-                best.grid = static_cast<int>(std::min<int64_t>(units, sms));
+                best = TcPlan{bn, static_cast<int>(std::min<int64_t>(tiles, sms)), static_cast<int>(tiles), 1, 0};
+            }
+        }
+        // whole waves over K, tail tiles split (no whole wave = every tile split)
+        const int64_t full = (tiles / sms) * sms;
+        const int64_t n_tail = tiles - full;
+        if (n_tail == 0) continue;
+        for (int64_t s = 2; s <= 16 && s <= num_kb; ++s) {
+            const int64_t kb_per = (num_kb + s - 1) / s;
+            const int64_t splits = (num_kb + kb_per - 1) / kb_per;  // no empty slice
+            if (splits < 2) continue;
+            const int64_t tail_units = n_tail * splits;
+            double cost = static_cast<double>(full / sms) * unit_us(bn, num_kb, sms, sms, x_rows);
+            cost += static_cast<double>((tail_units + sms - 1) / sms) * unit_us(bn, kb_per, tail_units, sms, x_rows);
+            const double partial_bytes = static_cast<double>(n_tail) * 128.0 * bn * 4.0 * (splits + 1.0);
+            cost += partial_bytes / 6.0e12 * 1e6 + 3.0;
+            if (cost < best_cost - 1e-9) {
+                best_cost = cost;
+                const int64_t units = full + tail_units;
+                best = TcPlan{bn, static_cast<int>(std::min<int64_t>(units, sms)), static_cast<int>(full),
+                              static_cast<int>(splits), static_cast<int>(kb_per)};
             }
         }
     }
@@ -503,7 +525,7 @@ static int gemm_dispatch(mrt_weight w, const void* x, int64_t ldx, void* y, int6
         e = launch_general_gemm(g, s);
         return e == cudaSuccess ? MRT_OK : cuda_error(e, "general gemm launch");
     }
-    if (M <= 64) {
+    if (M <= 16) {
         SkinnyArgs a{};
         a.x = static_cast<const uint16_t*>(x); a.ldx = ldx; a.w = w->data;
         a.y = y; a.ldy = ldy; a.M = static_cast<int>(M); a.N = static_cast<int>(w->n);
@@ -519,24 +541,46 @@ static int gemm_dispatch(mrt_weight w, const void* x, int64_t ldx, void* y, int6
     if (tw == nullptr) return MRT_ERR_CUDA;
     TcGemmArgs a{};
     a.M = static_cast<int>(M); a.N = static_cast<int>(w->n); a.K = static_cast<int>(w->k);
-    a.bn = p.bn; a.splits = p.splits; a.grid = p.grid;
+    a.bn = p.bn; a.grid = p.grid; a.full_tiles = p.full; a.tail_splits = p.splits; a.kb_per = p.kb_per;
     a.y = y; a.ldy = ldy; a.out_f32 = out_f32 ? 1 : 0; a.bias = bias; a.err_flag = c->d_err;
-    if (p.splits > 1) {
-        const size_t need = static_cast<size_t>(p.splits) * M * w->n * sizeof(float);
+    const int64_t tiles = ((M + 127) / 128) * ((w->n + p.bn - 1) / p.bn);
+    const int64_t n_tail = tiles - p.full;
+    if (n_tail > 0) {
+        const size_t need = static_cast<size_t>(n_tail) * p.splits * 128 * p.bn * sizeof(float);
         rc = ensure_buffer(&c->ws, &c->ws_bytes, need, "allocating split-K scratch");
         if (rc != MRT_OK) return rc;
         a.partials = static_cast<float*>(c->ws);
     }
     e = launch_tc_gemm(a, tx, *tw, s);
     if (e != cudaSuccess) return cuda_error(e, "tcgen05 gemm launch");
-    if (p.splits > 1) {
-        e = launch_reduce_splits(a.partials, p.splits, a.M, a.N, y, ldy, a.out_f32, bias, s);
+    if (n_tail > 0) {
+        e = launch_reduce_tail(a, s);
         if (e != cudaSuccess) return cuda_error(e, "split-K reduction launch");
     }
     return MRT_OK;
 }
 
 }  // namespace mrt
+
+extern "C" int mrt_gemm_plan(int64_t M, int64_t N, int64_t K, int sms, int* kernel, int* bn, int* full_tiles,
+                             int* tail_splits, int* kb_per, int* grid) {
+    clear_error();
+    if (M <= 0 || N <= 0 || K <= 0) return set_error(MRT_ERR_SHAPE, "M, N and K must be positive");
+    if (sms <= 0) {
+        DevCtx* c = current_ctx();
+        if (!c) return MRT_ERR_CUDA;
+        sms = c->sms;
+    }
+    const bool skinny = M <= 16;
+    const TcPlan p = skinny ? TcPlan{} : plan_tc(M, N, K, sms);
+    if (kernel) *kernel = skinny ? 0 : 1;
+    if (bn) *bn = skinny ? 8 * plan_skinny_rn(M, N, sms) : p.bn;
+    if (full_tiles) *full_tiles = skinny ? 0 : p.full;
+    if (tail_splits) *tail_splits = skinny ? 1 : p.splits;
+    if (kb_per) *kb_per = skinny ? 0 : p.kb_per;
+    if (grid) *grid = skinny ? static_cast<int>((N + 8 * plan_skinny_rn(M, N, sms) - 1) / (8 * plan_skinny_rn(M, N, sms))) : p.grid;
+    return MRT_OK;
+}
 
 extern "C" int mrt_gemm(mrt_weight w, const void* x_dev, int64_t ldx, void* y_dev, int64_t ldy, int64_t M,
                         unsigned flags, void* stream) {

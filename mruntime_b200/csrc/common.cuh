@@ -239,10 +239,11 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(uint32_t m, uint32_t n) {
 
 // ------------------------------------------------------------------ plain loads
 
-// 16-byte streaming load that skips L1 (weights are read exactly once).
+// 16-byte streaming load that skips L1 (weights are read exactly once) and
+// asks L2 to fetch the surrounding 256 bytes, which the same warp reads next.
 __device__ __forceinline__ uint4 ld_stream_16B(const void* p) {
     uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0, %1, %2, %3}, [%4];"
                  : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                  : "l"(p));
     return v;

@@ -58,20 +58,37 @@ __global__ void convert_2d_kernel(const void* src, int sdt, int64_t ld, int64_t 
     }
 }
 
-__global__ void reduce_splits_kernel(const float* part, int splits, int M, int N, void* y,
-                                     int64_t ldy, int out_f32, const uint16_t* bias) {
-    const int64_t total = static_cast<int64_t>(M) * N;
-    const int64_t plane = total;
-    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t m = i / N;
-        const int64_t n = i - m * N;
-        float s = part[i];
-        for (int k = 1; k < splits; ++k) s += part[k * plane + i];
-        if (out_f32) {
-            static_cast<float*>(y)[m * ldy + n] = s;
-        } else {
-            static_cast<uint16_t*>(y)[m * ldy + n] = round_out(s, bias, n);
+// Finish the tail tiles of a tensor-core GEMM plan: partials are
+// [tail_splits][n_tail][128][bn] FP32; slices are added in index order.
+__global__ void reduce_tail_kernel(const TcGemmArgs a, int num_m, int n_tail) {
+    const int bn = a.bn;
+    const int64_t per_tile = 128LL * bn;
+    const int64_t total4 = static_cast<int64_t>(n_tail) * per_tile / 4;
+    for (int64_t e4 = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e4 < total4;
+         e4 += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t e = e4 * 4;
+        const int64_t ti = e / per_tile;
+        const int64_t rem = e - ti * per_tile;
+        const int64_t r = rem / bn, c = rem - r * bn;
+        const int64_t t = a.full_tiles + ti;
+        const int64_t row = (t % num_m) * 128 + r;
+        const int64_t col = (t / num_m) * bn + c;
+        if (row >= a.M || col >= a.N) continue;
+        float4 s = *reinterpret_cast<const float4*>(a.partials + e);
+        for (int sp = 1; sp < a.tail_splits; ++sp) {
+            const float4 p = *reinterpret_cast<const float4*>(a.partials + (sp * static_cast<int64_t>(n_tail) + ti) * per_tile + rem);
+            s.x += p.x;
+            s.y += p.y;
+            s.z += p.z;
+            s.w += p.w;
+        }
+        const float v[4] = {s.x, s.y, s.z, s.w};
+        for (int j = 0; j < 4 && col + j < a.N; ++j) {
+            if (a.out_f32) {
+                static_cast<float*>(a.y)[row * a.ldy + col + j] = v[j];
+            } else {
+                static_cast<uint16_t*>(a.y)[row * a.ldy + col + j] = round_out(v[j], a.bias, col + j);
+            }
         }
     }
 }
@@ -210,11 +227,11 @@ cudaError_t launch_convert_2d_to_f16(const void* src, int sdt, int64_t ld, int64
     return cudaGetLastError();
 }
 
-cudaError_t launch_reduce_splits(const float* partials, int splits, int M, int N, void* y,
-                                 int64_t ldy, int out_f32, const uint16_t* bias, cudaStream_t s) {
-    const int64_t n = static_cast<int64_t>(M) * N;
-    if (n <= 0) return cudaSuccess;
-    reduce_splits_kernel<<<grid_for(n), kThreads, 0, s>>>(partials, splits, M, N, y, ldy, out_f32, bias);
+cudaError_t launch_reduce_tail(const TcGemmArgs& a, cudaStream_t s) {
+    const int num_m = (a.M + 127) / 128;
+    const int n_tail = num_m * ((a.N + a.bn - 1) / a.bn) - a.full_tiles;
+    if (n_tail <= 0) return cudaSuccess;
+    reduce_tail_kernel<<<grid_for(static_cast<int64_t>(n_tail) * 128 * a.bn / 4), kThreads, 0, s>>>(a, num_m, n_tail);
     note_launches(1);
     return cudaGetLastError();
 }

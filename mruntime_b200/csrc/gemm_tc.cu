@@ -36,7 +36,7 @@ constexpr int kEpiThreads = 128;
 
 template <int BN>
 struct TcCfg {
-    static constexpr int kStages = BN >= 256 ? 4 : 6;
+    static constexpr int kStages = BN >= 256 ? 4 : (BN >= 128 ? 6 : 8);
     static constexpr int kABytes = kBM * kBK * 2;
     static constexpr int kBBytes = BN * kBK * 2;
     static constexpr int kStageBytes = kABytes + kBBytes;
@@ -45,18 +45,31 @@ struct TcCfg {
     static constexpr size_t kSmem = static_cast<size_t>(kStages) * kStageBytes + kBarBytes + 1024;
 };
 
+// One work unit: an output tile and the k-blocks it covers.  `slot` is -1
+// for a full-K tile (stored directly) or the partials slot of a tail slice.
 struct Unit {
-    int mt, nt, kb0, kb1;
+    int mt, nt, kb0, kb1, slot;
 };
 
-__device__ __forceinline__ Unit decode_unit(int u, int num_m, int splits, int num_kb, int kb_per) {
+__device__ __forceinline__ Unit decode_unit(const TcGemmArgs& a, int u, int num_m, int n_tail, int num_kb) {
     Unit w;
-    w.mt = u % num_m;
-    const int rest = u / num_m;
-    const int sp = rest % splits;
-    w.nt = rest / splits;
-    w.kb0 = sp * kb_per;
-    w.kb1 = min(w.kb0 + kb_per, num_kb);
+    int t;
+    if (u < a.full_tiles) {
+        t = u;
+        w.kb0 = 0;
+        w.kb1 = num_kb;
+        w.slot = -1;
+    } else {
+        const int v = u - a.full_tiles;
+        const int ti = v % n_tail;
+        const int sp = v / n_tail;
+        t = a.full_tiles + ti;
+        w.kb0 = sp * a.kb_per;
+        w.kb1 = min(w.kb0 + a.kb_per, num_kb);
+        w.slot = sp * n_tail + ti;
+    }
+    w.mt = t % num_m;
+    w.nt = t / num_m;
     return w;
 }
 
@@ -64,20 +77,19 @@ __device__ __forceinline__ uint32_t pack_h2(uint16_t lo, uint16_t hi) {
     return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
 }
 
-// Store 32 accumulator columns of one row.
-__device__ __forceinline__ void store_row_chunk(const TcGemmArgs& a, const uint32_t (&r)[32],
-                                                int64_t row, int64_t col0, int sp) {
-    if (a.splits > 1) {
-        float* dst = a.partials + (static_cast<int64_t>(sp) * a.M + row) * a.N + col0;
-        if (col0 + 32 <= a.N && (a.N & 3) == 0) {
+// Store 32 FP32 accumulator columns of one tile row into a tail slot
+// (tile-local layout [128][bn]; always in bounds and 16-byte aligned).
+__device__ __forceinline__ void store_partial_chunk(const TcGemmArgs& a, const uint32_t (&r)[32], int slot,
+                                                   int row_in_tile, int col_in_tile, int bn) {
+    float* dst = a.partials + (static_cast<int64_t>(slot) * kBM + row_in_tile) * bn + col_in_tile;
 #pragma unroll
-            for (int j = 0; j < 32; j += 4)
-                *reinterpret_cast<uint4*>(dst + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
-        } else {
-            for (int j = 0; j < 32 && col0 + j < a.N; ++j) dst[j] = __uint_as_float(r[j]);
-        }
-        return;
-    }
+    for (int j = 0; j < 32; j += 4)
+        *reinterpret_cast<uint4*>(dst + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+}
+
+// Store 32 accumulator columns of one output row.
+__device__ __forceinline__ void store_row_chunk(const TcGemmArgs& a, const uint32_t (&r)[32],
+                                                int64_t row, int64_t col0) {
     if (a.out_f32) {
         float* dst = static_cast<float*>(a.y) + row * a.ldy + col0;
         const bool vec = col0 + 32 <= a.N && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0);
@@ -156,8 +168,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     const int num_m = (a.M + kBM - 1) / kBM;
     const int num_n = (a.N + BN - 1) / BN;
     const int num_kb = (a.K + kBK - 1) / kBK;
-    const int kb_per = (num_kb + a.splits - 1) / a.splits;
-    const int total = num_m * num_n * a.splits;
+    const int n_tail = num_m * num_n - a.full_tiles;
+    const int total = a.full_tiles + n_tail * a.tail_splits;
 
     if (warp == 0) {
         if (lane == 0) {
@@ -166,7 +178,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             uint32_t issued = 0, issued_parity = 0;
             bool ok = true;
             for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
-                const Unit w = decode_unit(u, num_m, a.splits, num_kb, kb_per);
+                const Unit w = decode_unit(a, u, num_m, n_tail, num_kb);
                 for (int kb = w.kb0; kb < w.kb1; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, a.err_flag, kErrTmaWait)) {
                         ok = false;
@@ -199,7 +211,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             bool any = false;
             bool ok = true;
             for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
-                const Unit w = decode_unit(u, num_m, a.splits, num_kb, kb_per);
+                const Unit w = decode_unit(a, u, num_m, n_tail, num_kb);
                 if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, a.err_flag, kErrMmaWait)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
@@ -239,8 +251,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int u = blockIdx.x; u < total; u += gridDim.x) {
-            const Unit w = decode_unit(u, num_m, a.splits, num_kb, kb_per);
-            const int sp = w.kb0 / kb_per;
+            const Unit w = decode_unit(a, u, num_m, n_tail, num_kb);
             // One lane waits; the verdict is shared so the warp stays
             // converged for the .sync.aligned TMEM loads below.
             int ok = 1;
@@ -257,7 +268,11 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
                 __syncwarp();
                 tmem_ld_32cols(t_row + c * 32, r);
                 const int64_t col0 = static_cast<int64_t>(w.nt) * BN + c * 32;
-                if (row < a.M && col0 < a.N) store_row_chunk(a, r, row, col0, sp);
+                if (w.slot >= 0) {
+                    store_partial_chunk(a, r, w.slot, quad * 32 + lane, c * 32, BN);
+                } else if (row < a.M && col0 < a.N) {
+                    store_row_chunk(a, r, row, col0);
+                }
             }
             tc_fence_before();
             mbar_arrive(&tempty[acc]);
@@ -295,15 +310,24 @@ cudaError_t launch_bn(const TcGemmArgs& a, const CUtensorMap& tx, const CUtensor
 }  // namespace
 
 size_t tc_gemm_smem_bytes(int bn) {
-    return bn >= 256 ? TcCfg<256>::kSmem : TcCfg<128>::kSmem;
+    return bn >= 256 ? TcCfg<256>::kSmem : (bn >= 128 ? TcCfg<128>::kSmem : TcCfg<64>::kSmem);
 }
 
 cudaError_t launch_tc_gemm(const TcGemmArgs& a, const CUtensorMap& tmap_x, const CUtensorMap& tmap_w,
                            cudaStream_t s) {
     if (a.M <= 0 || a.N <= 0) return cudaSuccess;
-    if (a.K <= 0 || a.grid <= 0 || a.splits <= 0) return cudaErrorInvalidValue;
+    const int tiles = ((a.M + kBM - 1) / kBM) * ((a.N + a.bn - 1) / a.bn);
+    const int num_kb = (a.K + kBK - 1) / kBK;
+    if (a.K <= 0 || a.grid <= 0 || a.tail_splits <= 0 || a.full_tiles < 0 || a.full_tiles > tiles)
+        return cudaErrorInvalidValue;
+    // Every tail slice must own at least one k-block, or its accumulator
+    // would never be written.
+    if (a.full_tiles < tiles && (a.kb_per <= 0 || (a.tail_splits - 1) * a.kb_per >= num_kb ||
+                                 a.tail_splits * a.kb_per < num_kb || a.partials == nullptr))
+        return cudaErrorInvalidValue;
     if (a.bn == 256) return launch_bn<256>(a, tmap_x, tmap_w, s);
     if (a.bn == 128) return launch_bn<128>(a, tmap_x, tmap_w, s);
+    if (a.bn == 64) return launch_bn<64>(a, tmap_x, tmap_w, s);
     return cudaErrorInvalidValue;
 }
 

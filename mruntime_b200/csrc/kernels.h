@@ -26,29 +26,34 @@ struct SkinnyArgs {
 };
 cudaError_t launch_skinny(const SkinnyArgs& a, int rows_per_warp_tiles, cudaStream_t s);
 
-// Y = X * W^T on the tcgen05 tensor cores, for M > 64.
+// Y = X * W^T on the tcgen05 tensor cores.
 // tmap_x: [M, K] FP16, box 64 x 128, 128B swizzle.  tmap_w: [N, K] FP16, box
-// 64 x bn, 128B swizzle.  With splits > 1 every split writes FP32 partials
-// into `partials` ([splits, M, N]) and reduce_splits() finishes the job.
+// 64 x bn, 128B swizzle.  Output tiles are 128 x bn, numbered m-fastest.
+// Tiles [0, full_tiles) run over the whole K and store the output directly;
+// each remaining ("tail") tile runs as tail_splits K-slices of kb_per
+// 64-wide k-blocks that store FP32 partials, tile-major, into `partials`
+// ([tail_splits][n_tail][128][bn]); reduce_tail() then finishes those tiles.
 struct TcGemmArgs {
     int M, N, K;
-    int bn;      // 128 or 256
-    int splits;  // K splits (1 = write the output directly)
-    int grid;    // persistent CTAs
-    void* y;     // FP16 or FP32 output (splits == 1) [M, ldy]
+    int bn;          // 64, 128 or 256
+    int grid;        // persistent CTAs
+    int full_tiles;  // tiles computed over the whole K
+    int tail_splits; // K-slices per tail tile (>= 1)
+    int kb_per;      // k-blocks per tail slice
+    void* y;         // FP16 or FP32 output [M, ldy]
     int64_t ldy;
     int out_f32;
-    const uint16_t* bias;  // splits == 1 only
-    float* partials;       // splits > 1
+    const uint16_t* bias;
+    float* partials;
     int* err_flag;
 };
 cudaError_t launch_tc_gemm(const TcGemmArgs& a, const CUtensorMap& tmap_x, const CUtensorMap& tmap_w,
                            cudaStream_t s);
 size_t tc_gemm_smem_bytes(int bn);
 
-// out[m, n] = round(sum_s partials[s, m, n]) (+bias), or FP32 sum.
-cudaError_t launch_reduce_splits(const float* partials, int splits, int M, int N, void* y,
-                                 int64_t ldy, int out_f32, const uint16_t* bias, cudaStream_t s);
+// Sum the K-slices of every tail tile of a TcGemmArgs plan (slice order
+// fixed, so results are deterministic), round (+bias) or keep FP32, store.
+cudaError_t launch_reduce_tail(const TcGemmArgs& a, cudaStream_t s);
 
 // Element-wise conversions with the reference's rounding.
 cudaError_t launch_convert(const void* src, int src_dtype, void* dst, int dst_dtype, int64_t n,

@@ -151,21 +151,10 @@ cudaError_t launch_one(const SkinnyArgs& a, cudaStream_t s) {
 // rn: weight rows per CTA in units of 8 (1, 2 or 4).
 cudaError_t launch_skinny(const SkinnyArgs& a, int rn, cudaStream_t s) {
     if (a.M <= 0 || a.N <= 0) return cudaSuccess;
-    if (a.M <= 16) {
-        if (rn >= 4) return launch_one<1, 4, 4>(a, s);
-        if (rn == 2) return launch_one<1, 2, 4>(a, s);
-        return launch_one<1, 1, 4>(a, s);
-    }
-    if (a.M <= 32) {
-        if (rn >= 4) return launch_one<2, 4, 2>(a, s);
-        if (rn == 2) return launch_one<2, 2, 2>(a, s);
-        return launch_one<2, 1, 2>(a, s);
-    }
-    if (a.M <= 64) {
-        if (rn >= 2) return launch_one<4, 2, 2>(a, s);
-        return launch_one<4, 1, 2>(a, s);
-    }
-    return cudaErrorInvalidValue;
+    if (a.M > 16) return cudaErrorInvalidValue;  // larger M runs on the tcgen05 kernel
+    if (rn >= 4) return launch_one<1, 4, 4>(a, s);
+    if (rn == 2) return launch_one<1, 2, 4>(a, s);
+    return launch_one<1, 1, 4>(a, s);
 }
 
 }  // namespace mrt

@@ -154,6 +154,32 @@ def test_tensor_core_kernel(cuda_dev, M, NK):
     assert same > 0.9
 
 
+# One shape per tcgen05 plan kind the planner can pick: tile width 64/128/256
+# x (every tile over the whole K | whole waves + K-split tail | every tile split).
+PLAN_SHAPES = {
+    (64, "full"): (17, 64, 64), (64, "uniform"): (17, 64, 2048),
+    (128, "full"): (200, 4864, 64), (128, "hybrid"): (17, 20000, 2048), (128, "uniform"): (700, 200, 2048),
+    (256, "full"): (40, 20000, 136), (256, "hybrid"): (200, 20000, 896), (256, "uniform"): (40, 4864, 4864),
+}
+
+
+@pytest.mark.parametrize("key", sorted(PLAN_SHAPES))
+def test_tensor_core_plan_kinds(cuda_dev, key):
+    M, N, K = PLAN_SHAPES[key]
+    p = capi.gemm_plan(M, N, K)
+    tiles = -(-M // 128) * -(-N // p["bn"])
+    kind = "full" if p["full_tiles"] == tiles else ("uniform" if p["full_tiles"] == 0 else "hybrid")
+    assert (p["kernel"], p["bn"], kind) == ("tcgen05", key[0], key[1]), p
+    rng = np.random.default_rng(M + N + K)
+    x = rand_f16(rng, (M, K))
+    w = rand_w(rng, (N, K), BF16)
+    wt = upload(w, BF16)
+    y = gemm(wt, x)
+    rows = None if M * N * K <= 100 * 1000 * 1000 else np.r_[0:4, M // 2, M - 4:M]
+    _, _, same = _check_against_oracle(x, w, BF16, y, rows, what=f"plan {key} M={M} N={N} K={K}")
+    assert same > 0.9
+
+
 @pytest.mark.parametrize("M", [1, 5, 40, 130])
 def test_unaligned_k_uses_general_kernel(cuda_dev, M):
     rng = np.random.default_rng(M)
