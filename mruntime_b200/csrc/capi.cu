@@ -482,19 +482,18 @@ static int plan_skinny_rn(int64_t M, int64_t N, int sms) {
     return 1;
 }
 
+// The weight's TMA map whose box is exactly the kernel's W tile (bn rows).
 static const CUtensorMap* weight_tmap(mrt_weight w, int bn) {
-    if (bn == 256) {
-        if (!w->tmap_ok256) {
-            if (make_tmap_f16(&w->tmap256, w->data, w->n, w->k, w->k, 256) != MRT_OK) return nullptr;
-            w->tmap_ok256 = true;
-        }
-        return &w->tmap256;
+    const int slot = bn == 64 ? 0 : (bn == 128 ? 1 : (bn == 256 ? 2 : -1));
+    if (slot < 0) {
+        set_error(MRT_ERR_INVALID_ARG, "no tensor map for tile width " + std::to_string(bn));
+        return nullptr;
     }
-    if (!w->tmap_ok128) {
-        if (make_tmap_f16(&w->tmap128, w->data, w->n, w->k, w->k, 128) != MRT_OK) return nullptr;
-        w->tmap_ok128 = true;
+    if (!w->tmap_ok[slot]) {
+        if (make_tmap_f16(&w->tmap[slot], w->data, w->n, w->k, w->k, bn) != MRT_OK) return nullptr;
+        w->tmap_ok[slot] = true;
     }
-    return &w->tmap128;
+    return &w->tmap[slot];
 }
 
 // Shared body of mrt_gemm / mrt_gemm_f32.

@@ -63,8 +63,8 @@ struct mrt_weight_s {
     int64_t src_n = 0;         // rows of the full source weight
     int64_t* ranges = nullptr; // row ranges kept (pairs)
     int64_t n_ranges = 0;
-    CUtensorMap tmap128;
-    CUtensorMap tmap256;
-    bool tmap_ok128 = false;
-    bool tmap_ok256 = false;
+    // TMA maps of the weight, one per tile width (box rows 64, 128, 256); a
+    // map's box must equal the kernel's W tile or the copy overruns the ring.
+    CUtensorMap tmap[3];
+    bool tmap_ok[3] = {false, false, false};
 };
