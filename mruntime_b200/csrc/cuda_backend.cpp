@@ -76,7 +76,7 @@ CudaBackend::CudaBackend(int device) : device_(device) { throw_on(mrt_init(devic
 CudaBackend::~CudaBackend() {
     mrt_sync(stream_);
     for (auto& kv : uploaded_) mrt_weight_free(kv.second);
-    for (auto& kv : implicit_) mrt_weight_free(kv.second);
+    for (auto& kv : implicit_) mrt_weight_free(kv.second.w);
     for (auto& s : scratch_) mrt_device_free(s.first);
 }
 
@@ -150,12 +150,36 @@ void CudaBackend::attach_bias(const Tensor& uploaded_weight, const Tensor& bias)
           "mrt_weight_attach_bias");
 }
 
+// FNV-1a over 64 elements spread evenly across a host tensor (0 for device
+// tensors, whose contents are not inspected).
+uint64_t CudaBackend::fingerprint(const Tensor& t) {
+    if (on_device(t.data()) || t.numel() == 0) return 0;
+    const size_t es = mruntime::dtype_size(t.dtype());
+    const uint8_t* p = static_cast<const uint8_t*>(t.data());
+    uint64_t h = 1469598103934665603ull;
+    const size_t n = t.numel();
+    for (size_t i = 0; i < 64; ++i) {
+        const size_t idx = (n * i) / 64 + (i * 7919u) % std::max<size_t>(1, n / 64);
+        for (size_t b = 0; b < es; ++b) {
+            h ^= p[std::min(idx, n - 1) * es + b];
+            h *= 1099511628211ull;
+        }
+    }
+    return h;
+}
+
 mrt_weight CudaBackend::weight_for(const Tensor& B, size_t N, size_t K) {
     auto up = uploaded_.find(B.data());
     if (up != uploaded_.end()) return up->second;
     const auto key = std::make_tuple(static_cast<const void*>(B.data()), N, K, to_mrt(B.dtype()));
+    const uint64_t fp = fingerprint(B);
     auto it = implicit_.find(key);
-    if (it != implicit_.end()) return it->second;
+    if (it != implicit_.end()) {
+        if (it->second.fingerprint == fp) return it->second.w;
+        sync();
+        mrt_weight_free(it->second.w);  // the address now holds a different tensor
+        implicit_.erase(it);
+    }
     mrt_weight w = nullptr;
     const bool dev = on_device(B.data());
     if (dev && B.dtype() == DType::FP16) {
@@ -165,7 +189,7 @@ mrt_weight CudaBackend::weight_for(const Tensor& B, size_t N, size_t K) {
                                 static_cast<int64_t>(K), nullptr, 0, 0, static_cast<int64_t>(K), stream_, &w),
               "mrt_weight_upload");
     }
-    implicit_[key] = w;
+    implicit_[key] = Implicit{w, fp};
     return w;
 }
 

@@ -106,8 +106,16 @@ private:
     // Uploaded weights by device data pointer.
     std::map<const void*, mrt_weight> uploaded_;
     // Weights first seen in gemm() (host or unregistered device memory), by
-    // (pointer, rows, cols, dtype) -- the reference's own cache key.
-    std::map<std::tuple<const void*, size_t, size_t, int>, mrt_weight> implicit_;
+    // (pointer, rows, cols, dtype) -- the reference's own cache key -- plus a
+    // fingerprint of sampled host elements, so a freed host weight whose
+    // address is reused by a different tensor is uploaded again instead of
+    // hitting the stale entry (the hazard of cpu_backend.cpp:24-30).
+    struct Implicit {
+        mrt_weight w = nullptr;
+        uint64_t fingerprint = 0;
+    };
+    std::map<std::tuple<const void*, size_t, size_t, int>, Implicit> implicit_;
+    static uint64_t fingerprint(const mruntime::Tensor& t);
     std::vector<std::pair<void*, size_t>> scratch_;
 };
 

@@ -72,6 +72,28 @@ double max_ulp_fp16(const Tensor& a, const Tensor& b) {
     return worst;
 }
 
+// Elements of Y (device) and R (reference) for Y = X * W^T may differ by the
+// FP16 rounding of two different FP32 sums: one FP16 spacing at |R| plus
+// 4 sqrt(K) 2^-24 sum_k |x w| (FP32 summation in any order).  Returns the
+// number of elements outside that bound.
+size_t outside_fp32_sum_bound(const Tensor& X, const Tensor& W, const Tensor& Y, const Tensor& R) {
+    const size_t K = X.dim(X.ndim() - 1), M = X.numel() / K, N = W.dim(0);
+    size_t bad = 0;
+    for (size_t m = 0; m < M; ++m)
+        for (size_t n = 0; n < N; ++n) {
+            double absdot = 0.0;
+            for (size_t k = 0; k < K; ++k)
+                absdot += std::fabs(static_cast<double>(load_scalar_as_fp32(X.data(), X.dtype(), m * K + k)) *
+                                    load_scalar_as_fp32(W.data(), W.dtype(), n * K + k));
+            const double y = load_scalar_as_fp32(Y.data(), Y.dtype(), m * N + n);
+            const double r = load_scalar_as_fp32(R.data(), R.dtype(), m * N + n);
+            const double spacing = std::max(std::ldexp(1.0, std::ilogb(std::max(std::fabs(r), 6.1e-5)) - 10), 5.96e-8);
+            if (std::fabs(y - r) > spacing + 4.0 * std::sqrt(static_cast<double>(K)) * std::ldexp(1.0, -24) * absdot)
+                ++bad;
+        }
+    return bad;
+}
+
 void test_gemm_known_answer(CudaBackend& backend) {
     // reference test/backend_test.cpp:11-29
     Tensor A = Tensor::zeros(Shape({2, 3}), DType::FP16);
@@ -127,9 +149,10 @@ void test_gemm_model_layout(CudaBackend& backend) {
         Tensor R = Tensor::empty(Shape({1, M, 640}), DType::FP16);
         backend.gemm(X, W, Y, 1.0f, 0.0f, false, true);  // host tensors, weight uploaded on first use
         cpu.gemm(X, W, R, 1.0f, 0.0f, false, true);
-        const double ulp = max_ulp_fp16(Y, R);
+        const size_t bad = outside_fp32_sum_bound(X, W, Y, R);
         const double frac = 1.0 - static_cast<double>(count_diff(Y, R)) / Y.numel();
-        CHECK(ulp <= 8.0, "M=" << M << " max ulp " << ulp);
+        CHECK(bad == 0, "M=" << M << ": " << bad << " outputs outside the FP32-sum bound (max ulp "
+                               << max_ulp_fp16(Y, R) << ")");
         CHECK(frac > 0.9, "M=" << M << " identical fraction " << frac);
         // device-resident operands with an explicit weight handle give the same bits
         Tensor Wd = backend.upload_weight(W);
@@ -207,7 +230,8 @@ void test_rope_embedding_attention(CudaBackend& backend) {
     CHECK(count_diff(e, er) == 0, "embedding differs");
     bool threw = false;
     try {
-        backend.embedding_lookup(table, {50}, e);
+        Tensor one = Tensor::empty(Shape({1, 1, 64}), DType::FP16);
+        backend.embedding_lookup(table, {50}, one);
     } catch (const std::out_of_range&) {
         threw = true;
     }
