@@ -43,17 +43,17 @@ from mruntime_b200 import workloads as WL  # noqa: E402
 METRIC = "matmul TFLOP/s (Qwen2.5-7B projection sweep, M=2048 prefill step)"
 UNIT = "TFLOP/s"
 HEADLINE_M = 2048
-# Per-launch DRAM traffic of the dominant kernel (gate+up GEMM at M=2048) from
-# the ncu capture summarised in profiles/ (dram__bytes_read.sum +
-# dram__bytes_write.sum); None until a capture exists.
-GATEUP_TRAFFIC_BYTES = None
+# Per-launch DRAM traffic of the dominant kernel (gate+up GEMM at M=2048):
+# dram__bytes_read.sum + dram__bytes_write.sum = 286.574592 MB + 130.112 MB
+# from the ncu capture summarised in profiles/tc_gemm_gateup_m2048.md.
+GATEUP_TRAFFIC_BYTES = 416686592
 
 
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="mruntime_b200", choices=["mruntime_b200", "reference"])
     ap.add_argument("--m", type=int, default=HEADLINE_M, help="tokens per step (headline 2048)")
     ap.add_argument("--no-sweep", action="store_true", help="skip the per-M sweep extras")
