@@ -189,7 +189,7 @@ def gemm_plan(M: int, N: int, K: int, sms: int = 0) -> dict:
     call("mrt_gemm_plan", M, N, K, sms, *[C.byref(v) for v in vals])
     keys = ("kernel", "bn", "full_tiles", "tail_splits", "kb_per", "grid")
     d = dict(zip(keys, (v.value for v in vals)))
-    d["kernel"] = "skinny" if d["kernel"] == 0 else "tcgen05"
+    d["kernel"] = {0: "skinny", 1: "tcgen05", 2: "tcgen05-swap"}[d["kernel"]]
     return d
 
 

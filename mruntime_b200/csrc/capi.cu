@@ -432,6 +432,50 @@ static double unit_us(int bn, int64_t kb, int64_t active, int sms, int64_t x_row
     return std::max(compute, mem);
 }
 
+// Plan for few tokens (M <= 64), swap mode: the weight is the 128-row MMA
+// operand, so a tile is 128 weight rows x all tokens and the work is streaming
+// W.  Units are costed by their weight bytes at the SM's share of HBM plus a
+// small fixed cost; K is split until about every SM streams.
+static TcPlan plan_swap(int64_t M, int64_t N, int64_t K, int sms) {
+    const int bn = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
+    const int64_t tiles = (N + 127) / 128;
+    const int64_t num_kb = (K + 63) / 64;
+    auto unit = [&](int64_t kb, int64_t active) {
+        const double share = std::min(50e9, 6.5e12 / static_cast<double>(std::max<int64_t>(1, std::min<int64_t>(active, sms))));
+        return (128.0 * 128.0 * kb + bn * 128.0 * kb * 0.5) / share * 1e6 + 0.3;
+    };
+    TcPlan best{bn, static_cast<int>(std::min<int64_t>(tiles, sms)), static_cast<int>(tiles), 1, 0};
+    double best_cost = static_cast<double>((tiles + sms - 1) / sms) * unit(num_kb, tiles);
+    const int64_t full = (tiles / sms) * sms;
+    const int64_t n_tail = tiles - full;
+    if (n_tail == 0) return best;
+    for (int64_t s = 2; s <= 32 && s <= num_kb; ++s) {
+        const int64_t kb_per = (num_kb + s - 1) / s;
+        const int64_t splits = (num_kb + kb_per - 1) / kb_per;
+        if (splits < 2) continue;
+        const int64_t tail_units = n_tail * splits;
+        double cost = static_cast<double>(full / sms) * unit(num_kb, sms);
+        cost += static_cast<double>((tail_units + sms - 1) / sms) * unit(kb_per, tail_units);
+        cost += static_cast<double>(n_tail) * 128.0 * bn * 4.0 * (splits + 1.0) / 6.0e12 * 1e6 + 3.0;
+        if (cost < best_cost - 1e-9) {
+            best_cost = cost;
+            best = TcPlan{bn, static_cast<int>(std::min<int64_t>(full + tail_units, sms)), static_cast<int>(full),
+                          static_cast<int>(splits), static_cast<int>(kb_per)};
+        }
+    }
+    return best;
+}
+
+// Decode shapes (M <= 16) run the swap-mode tensor-core kernel unless the
+// environment sets MRT_DECODE_KERNEL=skinny (the mma.sync streaming kernel).
+static bool use_skinny_for_decode() {
+    static const bool skinny = [] {
+        const char* v = std::getenv("MRT_DECODE_KERNEL");
+        return v != nullptr && std::strcmp(v, "skinny") == 0;
+    }();
+    return skinny;
+}
+
 static TcPlan plan_tc(int64_t M, int64_t N, int64_t K, int sms) {
     const int64_t num_m = (M + 127) / 128;
     const int64_t num_kb = (K + 63) / 64;
@@ -524,7 +568,7 @@ static int gemm_dispatch(mrt_weight w, const void* x, int64_t ldx, void* y, int6
         e = launch_general_gemm(g, s);
         return e == cudaSuccess ? MRT_OK : cuda_error(e, "general gemm launch");
     }
-    if (M <= 16) {
+    if (M <= 16 && use_skinny_for_decode()) {
         SkinnyArgs a{};
         a.x = static_cast<const uint16_t*>(x); a.ldx = ldx; a.w = w->data;
         a.y = y; a.ldy = ldy; a.M = static_cast<int>(M); a.N = static_cast<int>(w->n);
@@ -532,17 +576,20 @@ static int gemm_dispatch(mrt_weight w, const void* x, int64_t ldx, void* y, int6
         e = launch_skinny(a, plan_skinny_rn(M, w->n, c->sms), s);
         return e == cudaSuccess ? MRT_OK : cuda_error(e, "skinny gemm launch");
     }
-    const TcPlan p = plan_tc(M, w->n, w->k, c->sms);
+    const bool swap = M <= 64;
+    const TcPlan p = swap ? plan_swap(M, w->n, w->k, c->sms) : plan_tc(M, w->n, w->k, c->sms);
+    // X's box is 128 rows in normal mode and bn rows in swap mode; W's the other.
     CUtensorMap tx;
-    int rc = make_tmap_f16(&tx, x, M, w->k, ldx, 128);
+    int rc = make_tmap_f16(&tx, x, M, w->k, ldx, swap ? p.bn : 128);
     if (rc != MRT_OK) return rc;
-    const CUtensorMap* tw = weight_tmap(w, p.bn);
+    const CUtensorMap* tw = weight_tmap(w, swap ? 128 : p.bn);
     if (tw == nullptr) return MRT_ERR_CUDA;
     TcGemmArgs a{};
     a.M = static_cast<int>(M); a.N = static_cast<int>(w->n); a.K = static_cast<int>(w->k);
+    a.swap = swap ? 1 : 0;
     a.bn = p.bn; a.grid = p.grid; a.full_tiles = p.full; a.tail_splits = p.splits; a.kb_per = p.kb_per;
     a.y = y; a.ldy = ldy; a.out_f32 = out_f32 ? 1 : 0; a.bias = bias; a.err_flag = c->d_err;
-    const int64_t tiles = ((M + 127) / 128) * ((w->n + p.bn - 1) / p.bn);
+    const int64_t tiles = tc_gemm_tiles(a);
     const int64_t n_tail = tiles - p.full;
     if (n_tail > 0) {
         const size_t need = static_cast<size_t>(n_tail) * p.splits * 128 * p.bn * sizeof(float);
@@ -570,9 +617,10 @@ extern "C" int mrt_gemm_plan(int64_t M, int64_t N, int64_t K, int sms, int* kern
         if (!c) return MRT_ERR_CUDA;
         sms = c->sms;
     }
-    const bool skinny = M <= 16;
-    const TcPlan p = skinny ? TcPlan{} : plan_tc(M, N, K, sms);
-    if (kernel) *kernel = skinny ? 0 : 1;
+    const bool skinny = M <= 16 && use_skinny_for_decode();
+    const bool swap = !skinny && M <= 64;
+    const TcPlan p = skinny ? TcPlan{} : (swap ? plan_swap(M, N, K, sms) : plan_tc(M, N, K, sms));
+    if (kernel) *kernel = skinny ? 0 : (swap ? 2 : 1);
     if (bn) *bn = skinny ? 8 * plan_skinny_rn(M, N, sms) : p.bn;
     if (full_tiles) *full_tiles = skinny ? 0 : p.full;
     if (tail_splits) *tail_splits = skinny ? 1 : p.splits;

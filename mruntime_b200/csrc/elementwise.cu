@@ -69,10 +69,34 @@ __global__ void reduce_tail_kernel(const TcGemmArgs a, int num_m, int n_tail) {
         const int64_t e = e4 * 4;
         const int64_t ti = e / per_tile;
         const int64_t rem = e - ti * per_tile;
-        const int64_t r = rem / bn, c = rem - r * bn;
+        const int64_t r = rem / bn, c = rem - r * bn;  // r: A row in the tile, c: B row
         const int64_t t = a.full_tiles + ti;
-        const int64_t row = (t % num_m) * 128 + r;
-        const int64_t col = (t / num_m) * bn + c;
+        const int64_t a_row = (t % num_m) * 128 + r;
+        const int64_t b_row = (t / num_m) * bn + c;
+        if (a.swap) {
+            // A = weight rows (outputs n), B = tokens (outputs m): the 4 values
+            // are 4 tokens of one output column.
+            if (a_row >= a.N) continue;
+            float v4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            for (int sp = 0; sp < a.tail_splits; ++sp) {
+                const float4 p = *reinterpret_cast<const float4*>(
+                    a.partials + (sp * static_cast<int64_t>(n_tail) + ti) * per_tile + rem);
+                v4[0] += p.x;
+                v4[1] += p.y;
+                v4[2] += p.z;
+                v4[3] += p.w;
+            }
+            for (int j = 0; j < 4 && b_row + j < a.M; ++j) {
+                const int64_t o = (b_row + j) * a.ldy + a_row;
+                if (a.out_f32) {
+                    static_cast<float*>(a.y)[o] = v4[j];
+                } else {
+                    static_cast<uint16_t*>(a.y)[o] = round_out(v4[j], a.bias, a_row);
+                }
+            }
+            continue;
+        }
+        const int64_t row = a_row, col = b_row;
         if (row >= a.M || col >= a.N) continue;
         float4 s = *reinterpret_cast<const float4*>(a.partials + e);
         for (int sp = 1; sp < a.tail_splits; ++sp) {
@@ -228,8 +252,8 @@ cudaError_t launch_convert_2d_to_f16(const void* src, int sdt, int64_t ld, int64
 }
 
 cudaError_t launch_reduce_tail(const TcGemmArgs& a, cudaStream_t s) {
-    const int num_m = (a.M + 127) / 128;
-    const int n_tail = num_m * ((a.N + a.bn - 1) / a.bn) - a.full_tiles;
+    const int num_m = a.swap ? (a.N + 127) / 128 : (a.M + 127) / 128;  // A tiles
+    const int n_tail = tc_gemm_tiles(a) - a.full_tiles;
     if (n_tail <= 0) return cudaSuccess;
     reduce_tail_kernel<<<grid_for(static_cast<int64_t>(n_tail) * 128 * a.bn / 4), kThreads, 0, s>>>(a, num_m, n_tail);
     note_launches(1);

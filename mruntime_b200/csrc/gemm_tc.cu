@@ -36,11 +36,13 @@ constexpr int kEpiThreads = 128;
 
 template <int BN>
 struct TcCfg {
-    static constexpr int kStages = BN >= 256 ? 4 : (BN >= 128 ? 6 : 8);
     static constexpr int kABytes = kBM * kBK * 2;
     static constexpr int kBBytes = BN * kBK * 2;
     static constexpr int kStageBytes = kABytes + kBBytes;
-    static constexpr uint32_t kTmemCols = BN >= 256 ? 512 : (BN >= 128 ? 256 : 128);
+    // As many ring stages as fit in ~200 KB (4 for BN = 256 ... 11 for BN = 16).
+    static constexpr int kStages = (200 * 1024) / kStageBytes > 12 ? 12 : (200 * 1024) / kStageBytes;
+    // Two accumulators of BN FP32 columns, rounded up to a power of two >= 32.
+    static constexpr uint32_t kTmemCols = 2 * BN <= 32 ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
     static constexpr int kBarBytes = (2 * kStages + 5) * 8 + 16;
     static constexpr size_t kSmem = static_cast<size_t>(kStages) * kStageBytes + kBarBytes + 1024;
 };
@@ -119,10 +121,37 @@ __device__ __forceinline__ void store_row_chunk(const TcGemmArgs& a, const uint3
     }
 }
 
-template <int BN>
+// Swap mode: 16 accumulator columns (tokens) of one weight row; each column
+// is one token's output at weight row `n`, so a warp's 32 lanes write 32
+// consecutive outputs of that token.
+__device__ __forceinline__ void store_swap_chunk(const TcGemmArgs& a, const uint32_t (&r)[16], int64_t n,
+                                                 int64_t m0) {
+    if (n >= a.N) return;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        const int64_t m = m0 + j;
+        if (m >= a.M) break;
+        if (a.out_f32) {
+            static_cast<float*>(a.y)[m * a.ldy + n] = __uint_as_float(r[j]);
+        } else {
+            static_cast<uint16_t*>(a.y)[m * a.ldy + n] = round_out(__uint_as_float(r[j]), a.bias, n);
+        }
+    }
+}
+
+// Swap mode: 16 FP32 columns into a tail slot ([128][bn] tile-local).
+__device__ __forceinline__ void store_partial_chunk16(const TcGemmArgs& a, const uint32_t (&r)[16], int slot,
+                                                     int row_in_tile, int col_in_tile, int bn) {
+    float* dst = a.partials + (static_cast<int64_t>(slot) * kBM + row_in_tile) * bn + col_in_tile;
+#pragma unroll
+    for (int j = 0; j < 16; j += 4)
+        *reinterpret_cast<uint4*>(dst + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+}
+
+template <int BN, bool SWAP>
 __global__ void __launch_bounds__(kThreadsTc, 1)
-    tc_gemm_kernel(const TcGemmArgs a, const __grid_constant__ CUtensorMap tmx,
-                   const __grid_constant__ CUtensorMap tmw) {
+    tc_gemm_kernel(const TcGemmArgs a, const __grid_constant__ CUtensorMap tma,
+                   const __grid_constant__ CUtensorMap tmb) {
     using Cfg = TcCfg<BN>;
     constexpr int S = Cfg::kStages;
     extern __shared__ uint8_t smem_raw[];
@@ -157,16 +186,17 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         tmem_relinquish();
     }
     if (warp == 0 && lane == 0) {
-        prefetch_tmap(&tmx);
-        prefetch_tmap(&tmw);
+        prefetch_tmap(&tma);
+        prefetch_tmap(&tmb);
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    const int num_m = (a.M + kBM - 1) / kBM;
-    const int num_n = (a.N + BN - 1) / BN;
+    // A tiles (128 rows) vary fastest; in swap mode A is W and B is X.
+    const int num_m = SWAP ? (a.N + kBM - 1) / kBM : (a.M + kBM - 1) / kBM;
+    const int num_n = SWAP ? (a.M + BN - 1) / BN : (a.N + BN - 1) / BN;
     const int num_kb = (a.K + kBK - 1) / kBK;
     const int n_tail = num_m * num_n - a.full_tiles;
     const int total = a.full_tiles + n_tail * a.tail_splits;
@@ -185,8 +215,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
                         break;
                     }
                     mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
-                    tma_load_2d(sA + stage * Cfg::kABytes, &tmx, &full[stage], kb * kBK, w.mt * kBM);
-                    tma_load_2d(sB + stage * Cfg::kBBytes, &tmw, &full[stage], kb * kBK, w.nt * BN);
+                    tma_load_2d(sA + stage * Cfg::kABytes, &tma, &full[stage], kb * kBK, w.mt * kBM);
+                    tma_load_2d(sB + stage * Cfg::kBBytes, &tmb, &full[stage], kb * kBK, w.nt * BN);
                     issued |= 1u << stage;
                     issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
                     if (++stage == S) {
@@ -259,19 +289,34 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
             if (!ok) break;
             tc_fence_after();
+            // TMEM lane = A row of the tile (x row, or weight row in swap mode).
             const int64_t row = static_cast<int64_t>(w.mt) * kBM + quad * 32 + lane;
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                                    static_cast<uint32_t>(acc * BN);
+            if constexpr (SWAP) {
 #pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
-                uint32_t r[32];
-                __syncwarp();
-                tmem_ld_32cols(t_row + c * 32, r);
-                const int64_t col0 = static_cast<int64_t>(w.nt) * BN + c * 32;
-                if (w.slot >= 0) {
-                    store_partial_chunk(a, r, w.slot, quad * 32 + lane, c * 32, BN);
-                } else if (row < a.M && col0 < a.N) {
-                    store_row_chunk(a, r, row, col0);
+                for (int c = 0; c < BN / 16; ++c) {
+                    uint32_t r[16];
+                    __syncwarp();
+                    tmem_ld_16cols(t_row + c * 16, r);
+                    if (w.slot >= 0) {
+                        store_partial_chunk16(a, r, w.slot, quad * 32 + lane, c * 16, BN);
+                    } else {
+                        store_swap_chunk(a, r, row, static_cast<int64_t>(w.nt) * BN + c * 16);
+                    }
+                }
+            } else {
+#pragma unroll 1
+                for (int c = 0; c < BN / 32; ++c) {
+                    uint32_t r[32];
+                    __syncwarp();
+                    tmem_ld_32cols(t_row + c * 32, r);
+                    const int64_t col0 = static_cast<int64_t>(w.nt) * BN + c * 32;
+                    if (w.slot >= 0) {
+                        store_partial_chunk(a, r, w.slot, quad * 32 + lane, c * 32, BN);
+                    } else if (row < a.M && col0 < a.N) {
+                        store_row_chunk(a, r, row, col0);
+                    }
                 }
             }
             tc_fence_before();
@@ -290,33 +335,36 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     }
 }
 
-template <int BN>
-cudaError_t launch_bn(const TcGemmArgs& a, const CUtensorMap& tx, const CUtensorMap& tw, cudaStream_t s) {
+template <int BN, bool SWAP>
+cudaError_t launch_bn(const TcGemmArgs& a, const CUtensorMap& ta, const CUtensorMap& tb, cudaStream_t s) {
     static bool attr_set[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     if (!attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<BN, SWAP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(TcCfg<BN>::kSmem));
         if (e != cudaSuccess) return e;
         attr_set[dev] = true;
     }
-    tc_gemm_kernel<BN><<<a.grid, kThreadsTc, TcCfg<BN>::kSmem, s>>>(a, tx, tw);
+    tc_gemm_kernel<BN, SWAP><<<a.grid, kThreadsTc, TcCfg<BN>::kSmem, s>>>(a, ta, tb);
     note_launches(1);
     return cudaGetLastError();
 }
 
 }  // namespace
 
-size_t tc_gemm_smem_bytes(int bn) {
-    return bn >= 256 ? TcCfg<256>::kSmem : (bn >= 128 ? TcCfg<128>::kSmem : TcCfg<64>::kSmem);
+int tc_gemm_tiles(const TcGemmArgs& a) {
+    return a.swap ? ((a.N + kBM - 1) / kBM) * ((a.M + a.bn - 1) / a.bn)
+                  : ((a.M + kBM - 1) / kBM) * ((a.N + a.bn - 1) / a.bn);
 }
 
+// tmap_x must have a box of 128 rows (normal mode) or bn rows (swap mode);
+// tmap_w the other one.
 cudaError_t launch_tc_gemm(const TcGemmArgs& a, const CUtensorMap& tmap_x, const CUtensorMap& tmap_w,
                            cudaStream_t s) {
     if (a.M <= 0 || a.N <= 0) return cudaSuccess;
-    const int tiles = ((a.M + kBM - 1) / kBM) * ((a.N + a.bn - 1) / a.bn);
+    const int tiles = tc_gemm_tiles(a);
     const int num_kb = (a.K + kBK - 1) / kBK;
     if (a.K <= 0 || a.grid <= 0 || a.tail_splits <= 0 || a.full_tiles < 0 || a.full_tiles > tiles)
         return cudaErrorInvalidValue;
@@ -325,9 +373,16 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& a, const CUtensorMap& tmap_x, const
     if (a.full_tiles < tiles && (a.kb_per <= 0 || (a.tail_splits - 1) * a.kb_per >= num_kb ||
                                  a.tail_splits * a.kb_per < num_kb || a.partials == nullptr))
         return cudaErrorInvalidValue;
-    if (a.bn == 256) return launch_bn<256>(a, tmap_x, tmap_w, s);
-    if (a.bn == 128) return launch_bn<128>(a, tmap_x, tmap_w, s);
-    if (a.bn == 64) return launch_bn<64>(a, tmap_x, tmap_w, s);
+    if (a.swap) {
+        if (a.M > a.bn) return cudaErrorInvalidValue;  // one token tile
+        if (a.bn == 16) return launch_bn<16, true>(a, tmap_w, tmap_x, s);
+        if (a.bn == 32) return launch_bn<32, true>(a, tmap_w, tmap_x, s);
+        if (a.bn == 64) return launch_bn<64, true>(a, tmap_w, tmap_x, s);
+        return cudaErrorInvalidValue;
+    }
+    if (a.bn == 256) return launch_bn<256, false>(a, tmap_x, tmap_w, s);
+    if (a.bn == 128) return launch_bn<128, false>(a, tmap_x, tmap_w, s);
+    if (a.bn == 64) return launch_bn<64, false>(a, tmap_x, tmap_w, s);
     return cudaErrorInvalidValue;
 }
 

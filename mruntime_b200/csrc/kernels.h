@@ -26,16 +26,19 @@ struct SkinnyArgs {
 };
 cudaError_t launch_skinny(const SkinnyArgs& a, int rows_per_warp_tiles, cudaStream_t s);
 
-// Y = X * W^T on the tcgen05 tensor cores.
-// tmap_x: [M, K] FP16, box 64 x 128, 128B swizzle.  tmap_w: [N, K] FP16, box
-// 64 x bn, 128B swizzle.  Output tiles are 128 x bn, numbered m-fastest.
-// Tiles [0, full_tiles) run over the whole K and store the output directly;
-// each remaining ("tail") tile runs as tail_splits K-slices of kb_per
-// 64-wide k-blocks that store FP32 partials, tile-major, into `partials`
-// ([tail_splits][n_tail][128][bn]); reduce_tail() then finishes those tiles.
+// Y = X * W^T on the tcgen05 tensor cores.  The MMA's 128-row operand ("A")
+// is X (normal mode) or W (swap mode, for few tokens: the weight rows fill the
+// 128 TMEM lanes and the tokens are the MMA's N = bn); the bn-row operand
+// ("B") is the other one.  tmap_a: box 64 x 128, tmap_b: box 64 x bn, both
+// K-major with 128-byte swizzle.  Tiles are 128 A-rows x bn B-rows, numbered
+// A-fastest.  Tiles [0, full_tiles) run over the whole K and store the output
+// directly; each remaining ("tail") tile runs as tail_splits K-slices of
+// kb_per 64-wide k-blocks that store FP32 partials, tile-major, into
+// `partials` ([tail_splits][n_tail][128][bn]); reduce_tail() finishes them.
 struct TcGemmArgs {
-    int M, N, K;
-    int bn;          // 64, 128 or 256
+    int M, N, K;     // tokens, weight rows, reduction length (in both modes)
+    int swap;        // 1: A = W, B = X
+    int bn;          // B rows per tile: 64/128/256 (normal), 16/32/64 (swap)
     int grid;        // persistent CTAs
     int full_tiles;  // tiles computed over the whole K
     int tail_splits; // K-slices per tail tile (>= 1)
@@ -49,7 +52,8 @@ struct TcGemmArgs {
 };
 cudaError_t launch_tc_gemm(const TcGemmArgs& a, const CUtensorMap& tmap_x, const CUtensorMap& tmap_w,
                            cudaStream_t s);
-size_t tc_gemm_smem_bytes(int bn);
+// Output tiles of a plan (128 A rows x bn B rows each).
+int tc_gemm_tiles(const TcGemmArgs& a);
 
 // Sum the K-slices of every tail tile of a TcGemmArgs plan (slice order
 // fixed, so results are deterministic), round (+bias) or keep FP32, store.

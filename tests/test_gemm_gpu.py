@@ -154,12 +154,19 @@ def test_tensor_core_kernel(cuda_dev, M, NK):
     assert same > 0.9
 
 
-# One shape per tcgen05 plan kind the planner can pick: tile width 64/128/256
-# x (every tile over the whole K | whole waves + K-split tail | every tile split).
+# One shape per tcgen05 plan kind the planner can pick: mode (X or W as the
+# 128-row operand) x bn x (every tile over the whole K | whole waves + K-split
+# tail | every tile split).
 PLAN_SHAPES = {
-    (64, "full"): (17, 64, 64), (64, "uniform"): (17, 64, 2048),
-    (128, "full"): (200, 4864, 64), (128, "hybrid"): (17, 20000, 2048), (128, "uniform"): (700, 200, 2048),
-    (256, "full"): (40, 20000, 136), (256, "hybrid"): (200, 20000, 896), (256, "uniform"): (40, 4864, 4864),
+    ("tcgen05", 64, "full"): (65, 64, 64), ("tcgen05", 64, "uniform"): (65, 64, 896),
+    ("tcgen05", 128, "full"): (200, 4864, 64), ("tcgen05", 128, "hybrid"): (65, 20000, 2048),
+    ("tcgen05", 128, "uniform"): (700, 200, 2048), ("tcgen05", 256, "full"): (65, 20000, 136),
+    ("tcgen05", 256, "hybrid"): (65, 40000, 896), ("tcgen05", 256, "uniform"): (65, 4864, 4864),
+    ("tcgen05-swap", 16, "full"): (1, 64, 64), ("tcgen05-swap", 16, "hybrid"): (1, 20000, 896),
+    ("tcgen05-swap", 16, "uniform"): (1, 64, 896), ("tcgen05-swap", 32, "full"): (17, 64, 64),
+    ("tcgen05-swap", 32, "hybrid"): (17, 20000, 896), ("tcgen05-swap", 32, "uniform"): (17, 64, 896),
+    ("tcgen05-swap", 64, "full"): (40, 64, 64), ("tcgen05-swap", 64, "hybrid"): (40, 20000, 896),
+    ("tcgen05-swap", 64, "uniform"): (40, 64, 896),
 }
 
 
@@ -167,9 +174,9 @@ PLAN_SHAPES = {
 def test_tensor_core_plan_kinds(cuda_dev, key):
     M, N, K = PLAN_SHAPES[key]
     p = capi.gemm_plan(M, N, K)
-    tiles = -(-M // 128) * -(-N // p["bn"])
+    tiles = -(-N // 128) if p["kernel"] == "tcgen05-swap" else -(-M // 128) * -(-N // p["bn"])
     kind = "full" if p["full_tiles"] == tiles else ("uniform" if p["full_tiles"] == 0 else "hybrid")
-    assert (p["kernel"], p["bn"], kind) == ("tcgen05", key[0], key[1]), p
+    assert (p["kernel"], p["bn"], kind) == key, p
     rng = np.random.default_rng(M + N + K)
     x = rand_f16(rng, (M, K))
     w = rand_w(rng, (N, K), BF16)
