@@ -85,6 +85,14 @@ int mrt_device_sm_count(int* out);
 /* Kernels this library has launched in this process so far (all devices). */
 int mrt_launch_count(int64_t* out);
 
+/* Self-test of the kernels' bounded waits: launches one block that waits on
+ * an mbarrier no thread ever arrives at, with the same wait routine the GEMM
+ * kernels use but a limit of `limit_ms` milliseconds.  The wait gives up,
+ * records its error code and the kernel returns; the call then reports
+ * MRT_ERR_TIMEOUT through mrt_sync and leaves the context usable.  No
+ * counterpart in the reference (it has no device code). */
+int mrt_selftest_wait_timeout(int limit_ms, void* stream);
+
 /* ---------------------------------------------------------------- device storage */
 
 /* Device-resident tensor storage: the device counterpart of Tensor::empty's

@@ -49,6 +49,7 @@ _SIGS = {
     "mrt_reserve_workspace": (_int, [_sz]),
     "mrt_device_sm_count": (_int, [C.POINTER(_int)]),
     "mrt_launch_count": (_int, [C.POINTER(_i64)]),
+    "mrt_selftest_wait_timeout": (_int, [_int, _vp]),
     "mrt_weight_upload": (_int, [_vp, _int, _int, _i64, _i64, C.POINTER(_i64), _i64, _i64, _i64, _vp,
                                  C.POINTER(_vp)]),
     "mrt_weight_attach_bias": (_int, [_vp, _vp, _int, _int, _vp]),

@@ -174,12 +174,22 @@ extern "C" int mrt_sync(void* stream) {
     if (e != cudaSuccess) return cuda_error(e, "reading the device error flag");
     if (flag != 0) {
         cudaMemset(c->d_err, 0, sizeof(int));
-        static const char* what[] = {"", "TMA producer", "MMA issuer", "epilogue", "clean-up"};
+        static const char* what[] = {"", "TMA producer", "MMA issuer", "epilogue", "clean-up", "wait self-test"};
         return set_error(MRT_ERR_TIMEOUT, std::string("a kernel wait timed out in the ") +
-                                              (flag > 0 && flag < 5 ? what[flag] : "kernel") +
+                                              (flag > 0 && flag < 6 ? what[flag] : "kernel") +
                                               " (device error code " + std::to_string(flag) + ")");
     }
     return MRT_OK;
+}
+
+extern "C" int mrt_selftest_wait_timeout(int limit_ms, void* stream) {
+    clear_error();
+    if (limit_ms < 1 || limit_ms > 10000) return set_error(MRT_ERR_INVALID_ARG, "limit_ms must be in [1, 10000]");
+    DevCtx* c = current_ctx();
+    if (!c) return MRT_ERR_CUDA;
+    cudaError_t e = launch_wait_selftest(c->d_err, static_cast<uint64_t>(limit_ms) * 1000000ull,
+                                         static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? MRT_OK : cuda_error(e, "self-test launch");
 }
 
 extern "C" int mrt_reserve_workspace(size_t bytes) {

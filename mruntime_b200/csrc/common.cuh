@@ -20,6 +20,7 @@ enum : int {
     kErrMmaWait = 2,   // MMA issuer gave up waiting for data or a free accumulator
     kErrEpiWait = 3,   // epilogue gave up waiting for a finished accumulator
     kErrDrainWait = 4, // clean-up wait for in-flight copies/MMAs gave up
+    kErrSelfTest = 5,  // mrt_selftest_wait_timeout's wait gave up (expected)
 };
 
 // Wall-clock limit of one bounded wait, in nanoseconds of %globaltimer.
@@ -121,14 +122,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Wait for the phase with the given parity to complete.  Gives up (returns
 // false, raising `code`) after kWaitLimitNs or as soon as another thread of
 // the grid has raised an error.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* flag, int code) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* flag, int code,
+                                          uint64_t limit_ns = kWaitLimitNs) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t it = 1;; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((it & 255u) == 0) {
             if (error_raised(flag)) return false;
-            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            if (globaltimer_ns() - t0 > limit_ns) {
                 raise_error(flag, code);
                 return false;
             }

@@ -228,6 +228,18 @@ __global__ void argmax_combine_kernel(const float* vals, const int64_t* idxs, in
     out[m] = b.i;
 }
 
+// One thread waits on an mbarrier that never completes a phase (count 1, no
+// arrival) with the GEMM kernels' wait routine and a short limit.
+__global__ void wait_selftest_kernel(int* flag, uint64_t limit_ns) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) mbar_wait(&bar, 0, flag, kErrSelfTest, limit_ns);
+}
+
 unsigned grid_for(int64_t n) {
     int64_t blocks = (n + kThreads - 1) / kThreads;
     if (blocks > 148 * 32) blocks = 148 * 32;
@@ -247,6 +259,12 @@ cudaError_t launch_convert_2d_to_f16(const void* src, int sdt, int64_t ld, int64
                                      int64_t cols, uint16_t* dst, cudaStream_t s) {
     if (rows <= 0 || cols <= 0) return cudaSuccess;
     convert_2d_kernel<<<grid_for(rows * cols), kThreads, 0, s>>>(src, sdt, ld, rows, cols, dst);
+    note_launches(1);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_wait_selftest(int* flag, uint64_t limit_ns, cudaStream_t s) {
+    wait_selftest_kernel<<<1, 32, 0, s>>>(flag, limit_ns);
     note_launches(1);
     return cudaGetLastError();
 }

@@ -76,6 +76,9 @@ cudaError_t launch_argmax(const uint16_t* logits, int64_t M, int64_t V, int64_t 
 cudaError_t launch_argmax_combine(const float* vals, const int64_t* idxs, int world, int64_t M,
                                   int64_t* idx_out, cudaStream_t s);
 
+// A single wait on a barrier that never completes, bounded by limit_ns.
+cudaError_t launch_wait_selftest(int* flag, uint64_t limit_ns, cudaStream_t s);
+
 // FP32 -> FP16 rounding of an all-reduced buffer.
 cudaError_t launch_f32_to_f16(const float* src, uint16_t* dst, int64_t n, cudaStream_t s);
 
