@@ -212,6 +212,27 @@ int mrt_gemm_general(const void* a_dev, int a_dtype, int64_t a_rows, int64_t a_c
 int mrt_argmax_f16(const void* logits_dev, int64_t M, int64_t V, int64_t ld, int64_t index_base,
                    int64_t* idx_dev, float* val_dev, void* stream);
 
+/*
+ * mrt_argmax_f16 for callers that must not allocate device memory: the same
+ * kernels and results, but the per-chunk partials live in a fixed buffer
+ * compiled into the library (96 KiB per device, held by every GPU that loads
+ * the library until the process exits) instead of the context's growable
+ * scratch, and the call never reaches cudaMalloc or cudaFree.  Who needs it:
+ * a host that captures its whole decode step in a CUDA graph (an allocation,
+ * or the device-wide synchronisation a cudaFree implies, cannot happen inside
+ * the capture), and serving runtimes that reserve all device memory for their
+ * own arenas up front.  Limit: M * ceil(V / 8192) <= 8192 (e.g. up to 431
+ * rows of a 152064-entry vocabulary); larger calls fail with MRT_ERR_SHAPE.
+ * The first call on a device resolves the buffer's device address (module
+ * set-up inside the CUDA driver), so make it once before any stream capture.
+ * All calls share the buffer, so calls that overlap on the GPU (different
+ * streams, or the same stream from several threads without ordering) race;
+ * every slot a call reads was written earlier in the same call, so nothing
+ * needs clearing between calls.  No counterpart in the reference.
+ */
+int mrt_argmax_f16_noalloc(const void* logits_dev, int64_t M, int64_t V, int64_t ld, int64_t index_base,
+                           int64_t* idx_dev, float* val_dev, void* stream);
+
 /* lm_head and greedy pick in one call: logits_dev[M, N] = x * W^T (FP16),
  * then mrt_argmax_f16 on every row (src/models/qwen/qwen_model.cpp:374 followed
  * by src/engine/inference_engine.cpp:84-95).  index_base offsets the indices

@@ -68,6 +68,7 @@ _SIGS = {
     "mrt_gemm_general": (_int, [_vp, _int, _i64, _i64, _vp, _int, _i64, _i64, _vp, _int, C.c_float, C.c_float,
                                 _int, _int, _vp]),
     "mrt_argmax_f16": (_int, [_vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp]),
+    "mrt_argmax_f16_noalloc": (_int, [_vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp]),
     "mrt_lm_head_argmax": (_int, [_vp, _vp, _i64, _i64, _vp, _i64, _vp, _vp, _vp]),
     "mrt_convert": (_int, [_vp, _int, _vp, _int, _i64, _vp]),
     "mrt_rmsnorm": (_int, [_vp, _int, _vp, _int, _vp, _int, _i64, _i64, C.c_float, _vp]),
