@@ -174,6 +174,8 @@ extern "C" int mrt_sync(void* stream) {
     if (e != cudaSuccess) return cuda_error(e, "reading the device error flag");
     if (flag != 0) {
         cudaMemset(c->d_err, 0, sizeof(int));
+        // A kernel that gave up may have left K-split tile counters counted.
+        if (c->counters != nullptr) cudaMemset(c->counters, 0, c->counters_bytes);
         static const char* what[] = {"", "TMA producer", "MMA issuer", "epilogue", "clean-up", "wait self-test"};
         return set_error(MRT_ERR_TIMEOUT, std::string("a kernel wait timed out in the ") +
                                               (flag > 0 && flag < 6 ? what[flag] : "kernel") +
@@ -606,13 +608,19 @@ static int gemm_dispatch(mrt_weight w, const void* x, int64_t ldx, void* y, int6
         rc = ensure_buffer(&c->ws, &c->ws_bytes, need, "allocating split-K scratch");
         if (rc != MRT_OK) return rc;
         a.partials = static_cast<float*>(c->ws);
+        const size_t counters = static_cast<size_t>(n_tail) * 4 * sizeof(int);
+        if (c->counters_bytes < counters) {
+            void* p_cnt = c->counters;
+            rc = ensure_buffer(&p_cnt, &c->counters_bytes, counters, "allocating split-K counters");
+            if (rc != MRT_OK) return rc;
+            c->counters = static_cast<int*>(p_cnt);
+            e = cudaMemset(c->counters, 0, c->counters_bytes);  // kernels keep them zero afterwards
+            if (e != cudaSuccess) return cuda_error(e, "clearing split-K counters");
+        }
+        a.tile_counters = c->counters;
     }
     e = launch_tc_gemm(a, tx, *tw, s);
     if (e != cudaSuccess) return cuda_error(e, "tcgen05 gemm launch");
-    if (n_tail > 0) {
-        e = launch_reduce_tail(a, s);
-        if (e != cudaSuccess) return cuda_error(e, "split-K reduction launch");
-    }
     return MRT_OK;
 }
 

@@ -18,6 +18,8 @@ struct DevCtx {
     int* d_err = nullptr;   // device-side error flag written by bounded waits
     void* ws = nullptr;     // scratch: split-K partials, argmax partials
     size_t ws_bytes = 0;
+    int* counters = nullptr;  // K-split tile counters, all zero between calls
+    size_t counters_bytes = 0;
     void* io_x = nullptr;   // staging for host-buffer calls
     size_t io_x_bytes = 0;
     void* io_y = nullptr;

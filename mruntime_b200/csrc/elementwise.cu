@@ -2,8 +2,6 @@
 //   * dtype conversion with the reference's rounding (weight upload: the
 //     BF16 -> FP16 step of src/core/cpu_backend.cpp:48-55, done once on the
 //     device instead of on the host per packed weight);
-//   * the split-K reduction that finishes a tensor-core GEMM whose K was cut
-//     into pieces (deterministic: splits summed in index order);
 //   * FP32 -> FP16 rounding after a row-parallel all-reduce;
 //   * greedy argmax over FP16 logits (src/engine/inference_engine.cpp:84-95),
 //     in two passes: per-chunk (value, index) partials in scratch memory, then
@@ -55,65 +53,6 @@ __global__ void convert_2d_kernel(const void* src, int sdt, int64_t ld, int64_t 
         const int64_t si = r * ld + c;
         dst[i] = (sdt == 0) ? static_cast<const uint16_t*>(src)[si]
                             : f32_to_f16_bits(load_as_f32(src, sdt, si));
-    }
-}
-
-// Finish the tail tiles of a tensor-core GEMM plan: partials are
-// [tail_splits][n_tail][128][bn] FP32; slices are added in index order.
-__global__ void reduce_tail_kernel(const TcGemmArgs a, int num_m, int n_tail) {
-    const int bn = a.bn;
-    const int64_t per_tile = 128LL * bn;
-    const int64_t total4 = static_cast<int64_t>(n_tail) * per_tile / 4;
-    for (int64_t e4 = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e4 < total4;
-         e4 += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t e = e4 * 4;
-        const int64_t ti = e / per_tile;
-        const int64_t rem = e - ti * per_tile;
-        const int64_t r = rem / bn, c = rem - r * bn;  // r: A row in the tile, c: B row
-        const int64_t t = a.full_tiles + ti;
-        const int64_t a_row = (t % num_m) * 128 + r;
-        const int64_t b_row = (t / num_m) * bn + c;
-        if (a.swap) {
-            // A = weight rows (outputs n), B = tokens (outputs m): the 4 values
-            // are 4 tokens of one output column.
-            if (a_row >= a.N) continue;
-            float v4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-            for (int sp = 0; sp < a.tail_splits; ++sp) {
-                const float4 p = *reinterpret_cast<const float4*>(
-                    a.partials + (sp * static_cast<int64_t>(n_tail) + ti) * per_tile + rem);
-                v4[0] += p.x;
-                v4[1] += p.y;
-                v4[2] += p.z;
-                v4[3] += p.w;
-            }
-            for (int j = 0; j < 4 && b_row + j < a.M; ++j) {
-                const int64_t o = (b_row + j) * a.ldy + a_row;
-                if (a.out_f32) {
-                    static_cast<float*>(a.y)[o] = v4[j];
-                } else {
-                    static_cast<uint16_t*>(a.y)[o] = round_out(v4[j], a.bias, a_row);
-                }
-            }
-            continue;
-        }
-        const int64_t row = a_row, col = b_row;
-        if (row >= a.M || col >= a.N) continue;
-        float4 s = *reinterpret_cast<const float4*>(a.partials + e);
-        for (int sp = 1; sp < a.tail_splits; ++sp) {
-            const float4 p = *reinterpret_cast<const float4*>(a.partials + (sp * static_cast<int64_t>(n_tail) + ti) * per_tile + rem);
-            s.x += p.x;
-            s.y += p.y;
-            s.z += p.z;
-            s.w += p.w;
-        }
-        const float v[4] = {s.x, s.y, s.z, s.w};
-        for (int j = 0; j < 4 && col + j < a.N; ++j) {
-            if (a.out_f32) {
-                static_cast<float*>(a.y)[row * a.ldy + col + j] = v[j];
-            } else {
-                static_cast<uint16_t*>(a.y)[row * a.ldy + col + j] = round_out(v[j], a.bias, col + j);
-            }
-        }
     }
 }
 
@@ -269,14 +208,6 @@ cudaError_t launch_wait_selftest(int* flag, uint64_t limit_ns, cudaStream_t s) {
     return cudaGetLastError();
 }
 
-cudaError_t launch_reduce_tail(const TcGemmArgs& a, cudaStream_t s) {
-    const int num_m = a.swap ? (a.N + 127) / 128 : (a.M + 127) / 128;  // A tiles
-    const int n_tail = tc_gemm_tiles(a) - a.full_tiles;
-    if (n_tail <= 0) return cudaSuccess;
-    reduce_tail_kernel<<<grid_for(static_cast<int64_t>(n_tail) * 128 * a.bn / 4), kThreads, 0, s>>>(a, num_m, n_tail);
-    note_launches(1);
-    return cudaGetLastError();
-}
 
 cudaError_t launch_f32_to_f16(const float* src, uint16_t* dst, int64_t n, cudaStream_t s) {
     if (n <= 0) return cudaSuccess;

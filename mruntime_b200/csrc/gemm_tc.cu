@@ -50,7 +50,7 @@ struct TcCfg {
 // One work unit: an output tile and the k-blocks it covers.  `slot` is -1
 // for a full-K tile (stored directly) or the partials slot of a tail slice.
 struct Unit {
-    int mt, nt, kb0, kb1, slot;
+    int mt, nt, kb0, kb1, slot, ti;  // ti: index among the tail tiles (-1 for a full-K tile)
 };
 
 __device__ __forceinline__ Unit decode_unit(const TcGemmArgs& a, int u, int num_m, int n_tail, int num_kb) {
@@ -61,6 +61,7 @@ __device__ __forceinline__ Unit decode_unit(const TcGemmArgs& a, int u, int num_
         w.kb0 = 0;
         w.kb1 = num_kb;
         w.slot = -1;
+        w.ti = -1;
     } else {
         const int v = u - a.full_tiles;
         const int ti = v % n_tail;
@@ -69,6 +70,7 @@ __device__ __forceinline__ Unit decode_unit(const TcGemmArgs& a, int u, int num_
         w.kb0 = sp * a.kb_per;
         w.kb1 = min(w.kb0 + a.kb_per, num_kb);
         w.slot = sp * n_tail + ti;
+        w.ti = ti;
     }
     w.mt = t % num_m;
     w.nt = t / num_m;
@@ -146,6 +148,64 @@ __device__ __forceinline__ void store_partial_chunk16(const TcGemmArgs& a, const
 #pragma unroll
     for (int j = 0; j < 16; j += 4)
         *reinterpret_cast<uint4*>(dst + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+}
+
+// K-split finish for one 32-row quadrant of a tail tile, run by the whole
+// epilogue warp that just stored its partial rows.  The warp counts itself
+// in; only the warp that completes the count (the last of the tail_splits
+// slices to arrive) sums all slices in slice order -- so the result does not
+// depend on arrival order -- stores the output and resets the counter.
+// Nobody waits for anybody, so a slice lost to an error cannot hang the
+// kernel; it only leaves its tile unfinished.
+template <int BN, bool SWAP>
+__device__ __forceinline__ void tail_fixup(const TcGemmArgs& a, const Unit& w, int n_tail, int quad, int lane) {
+    __threadfence();  // this warp's partial rows are visible to the whole GPU
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) {
+        int* cnt = a.tile_counters + w.ti * 4 + quad;
+        last = atomicAdd(cnt, 1) == a.tail_splits - 1;
+        if (last) *cnt = 0;
+    }
+    last = __shfl_sync(0xFFFFFFFFu, last, 0);
+    if (!last) return;
+    __threadfence();  // the other slices' rows are read after the count
+    const int r = quad * 32 + lane;
+    const int64_t row = static_cast<int64_t>(w.mt) * kBM + r;
+    const int64_t slice = static_cast<int64_t>(n_tail) * kBM * BN;
+    const float* base = a.partials + (static_cast<int64_t>(w.ti) * kBM + r) * BN;
+    constexpr int kChunk = SWAP ? 16 : 32;
+#pragma unroll 1
+    for (int c = 0; c < BN / kChunk; ++c) {
+        float s[kChunk];
+#pragma unroll
+        for (int j = 0; j < kChunk; j += 4) {
+            const float4 p = *reinterpret_cast<const float4*>(base + c * kChunk + j);
+            s[j] = p.x;
+            s[j + 1] = p.y;
+            s[j + 2] = p.z;
+            s[j + 3] = p.w;
+        }
+        for (int sp = 1; sp < a.tail_splits; ++sp) {
+#pragma unroll
+            for (int j = 0; j < kChunk; j += 4) {
+                const float4 p = *reinterpret_cast<const float4*>(base + sp * slice + c * kChunk + j);
+                s[j] += p.x;
+                s[j + 1] += p.y;
+                s[j + 2] += p.z;
+                s[j + 3] += p.w;
+            }
+        }
+        uint32_t bits[kChunk];
+#pragma unroll
+        for (int j = 0; j < kChunk; ++j) bits[j] = __float_as_uint(s[j]);
+        if constexpr (SWAP) {
+            store_swap_chunk(a, bits, row, static_cast<int64_t>(w.nt) * BN + c * kChunk);
+        } else {
+            const int64_t col0 = static_cast<int64_t>(w.nt) * BN + c * kChunk;
+            if (row < a.M && col0 < a.N) store_row_chunk(a, bits, row, col0);
+        }
+    }
 }
 
 template <int BN, bool SWAP>
@@ -320,7 +380,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
                 }
             }
             tc_fence_before();
-            mbar_arrive(&tempty[acc]);
+            mbar_arrive(&tempty[acc]);  // the accumulator is free; the fix-up reads global memory only
+            if (w.slot >= 0) tail_fixup<BN, SWAP>(a, w, n_tail, quad, lane);
             acc ^= 1;
             if (acc == 0) acc_phase ^= 1u;
         }
@@ -371,7 +432,8 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& a, const CUtensorMap& tmap_x, const
     // Every tail slice must own at least one k-block, or its accumulator
     // would never be written.
     if (a.full_tiles < tiles && (a.kb_per <= 0 || (a.tail_splits - 1) * a.kb_per >= num_kb ||
-                                 a.tail_splits * a.kb_per < num_kb || a.partials == nullptr))
+                                 a.tail_splits * a.kb_per < num_kb || a.partials == nullptr ||
+                                 a.tile_counters == nullptr))
         return cudaErrorInvalidValue;
     if (a.swap) {
         if (a.M > a.bn) return cudaErrorInvalidValue;  // one token tile

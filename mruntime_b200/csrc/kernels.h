@@ -34,7 +34,8 @@ cudaError_t launch_skinny(const SkinnyArgs& a, int rows_per_warp_tiles, cudaStre
 // A-fastest.  Tiles [0, full_tiles) run over the whole K and store the output
 // directly; each remaining ("tail") tile runs as tail_splits K-slices of
 // kb_per 64-wide k-blocks that store FP32 partials, tile-major, into
-// `partials` ([tail_splits][n_tail][128][bn]); reduce_tail() finishes them.
+// `partials` ([tail_splits][n_tail][128][bn]); the last slice to finish a
+// 32-row quadrant of a tail tile sums the slices and stores it (tile_counters).
 struct TcGemmArgs {
     int M, N, K;     // tokens, weight rows, reduction length (in both modes)
     int swap;        // 1: A = W, B = X
@@ -48,6 +49,11 @@ struct TcGemmArgs {
     int out_f32;
     const uint16_t* bias;
     float* partials;
+    // One counter per (tail tile, 32-row quadrant), zero between calls: every
+    // epilogue warp of a K-slice adds one after storing its partial rows; the
+    // warp that brings it to tail_splits sums the slices in slice order,
+    // stores the output and resets the counter.
+    int* tile_counters;
     int* err_flag;
 };
 cudaError_t launch_tc_gemm(const TcGemmArgs& a, const CUtensorMap& tmap_x, const CUtensorMap& tmap_w,
@@ -55,9 +61,6 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& a, const CUtensorMap& tmap_x, const
 // Output tiles of a plan (128 A rows x bn B rows each).
 int tc_gemm_tiles(const TcGemmArgs& a);
 
-// Sum the K-slices of every tail tile of a TcGemmArgs plan (slice order
-// fixed, so results are deterministic), round (+bias) or keep FP32, store.
-cudaError_t launch_reduce_tail(const TcGemmArgs& a, cudaStream_t s);
 
 // Element-wise conversions with the reference's rounding.
 cudaError_t launch_convert(const void* src, int src_dtype, void* dst, int dst_dtype, int64_t n,
