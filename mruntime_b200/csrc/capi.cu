@@ -609,7 +609,7 @@ static int gemm_dispatch(mrt_weight w, const void* x, int64_t ldx, void* y, int6
         if (rc != MRT_OK) return rc;
         a.partials = static_cast<float*>(c->ws);
         const size_t counters = static_cast<size_t>(n_tail) * 4 * sizeof(int);
-        if (c->counters_bytes < counters) {
+        if (swap && c->counters_bytes < counters) {
             void* p_cnt = c->counters;
             rc = ensure_buffer(&p_cnt, &c->counters_bytes, counters, "allocating split-K counters");
             if (rc != MRT_OK) return rc;
@@ -617,10 +617,14 @@ static int gemm_dispatch(mrt_weight w, const void* x, int64_t ldx, void* y, int6
             e = cudaMemset(c->counters, 0, c->counters_bytes);  // kernels keep them zero afterwards
             if (e != cudaSuccess) return cuda_error(e, "clearing split-K counters");
         }
-        a.tile_counters = c->counters;
+        a.tile_counters = swap ? c->counters : nullptr;
     }
     e = launch_tc_gemm(a, tx, *tw, s);
     if (e != cudaSuccess) return cuda_error(e, "tcgen05 gemm launch");
+    if (n_tail > 0 && !swap) {
+        e = launch_reduce_tail(a, s);
+        if (e != cudaSuccess) return cuda_error(e, "split-K reduction launch");
+    }
     return MRT_OK;
 }
 

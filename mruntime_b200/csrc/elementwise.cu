@@ -56,6 +56,45 @@ __global__ void convert_2d_kernel(const void* src, int sdt, int64_t ld, int64_t 
     }
 }
 
+// Finish the K-split tail tiles of a normal-mode tensor-core GEMM plan (the
+// swap mode finishes its small tiles inside the GEMM kernel): partials are
+// [tail_splits][n_tail][128][bn] FP32; slices are added in index order, so
+// results are deterministic.  The whole GPU shares the work, which matters
+// for wide tiles (a 128 x 256 tile is 128 KB per slice).
+__global__ void reduce_tail_kernel(const TcGemmArgs a, int num_m, int n_tail) {
+    const int bn = a.bn;
+    const int64_t per_tile = 128LL * bn;
+    const int64_t total4 = static_cast<int64_t>(n_tail) * per_tile / 4;
+    for (int64_t e4 = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e4 < total4;
+         e4 += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t e = e4 * 4;
+        const int64_t ti = e / per_tile;
+        const int64_t rem = e - ti * per_tile;
+        const int64_t r = rem / bn, c = rem - r * bn;
+        const int64_t t = a.full_tiles + ti;
+        const int64_t row = (t % num_m) * 128 + r;
+        const int64_t col = (t / num_m) * bn + c;
+        if (row >= a.M || col >= a.N) continue;
+        float4 s = *reinterpret_cast<const float4*>(a.partials + e);
+        for (int sp = 1; sp < a.tail_splits; ++sp) {
+            const float4 p =
+                *reinterpret_cast<const float4*>(a.partials + (sp * static_cast<int64_t>(n_tail) + ti) * per_tile + rem);
+            s.x += p.x;
+            s.y += p.y;
+            s.z += p.z;
+            s.w += p.w;
+        }
+        const float v[4] = {s.x, s.y, s.z, s.w};
+        for (int j = 0; j < 4 && col + j < a.N; ++j) {
+            if (a.out_f32) {
+                static_cast<float*>(a.y)[row * a.ldy + col + j] = v[j];
+            } else {
+                static_cast<uint16_t*>(a.y)[row * a.ldy + col + j] = round_out(v[j], a.bias, col + j);
+            }
+        }
+    }
+}
+
 __global__ void f32_to_f16_kernel(const float* src, uint16_t* dst, int64_t n) {
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x)
@@ -198,6 +237,16 @@ cudaError_t launch_convert_2d_to_f16(const void* src, int sdt, int64_t ld, int64
                                      int64_t cols, uint16_t* dst, cudaStream_t s) {
     if (rows <= 0 || cols <= 0) return cudaSuccess;
     convert_2d_kernel<<<grid_for(rows * cols), kThreads, 0, s>>>(src, sdt, ld, rows, cols, dst);
+    note_launches(1);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_reduce_tail(const TcGemmArgs& a, cudaStream_t s) {
+    if (a.swap) return cudaErrorInvalidValue;  // swap mode finishes its tail tiles in the GEMM kernel
+    const int num_m = (a.M + 127) / 128;
+    const int n_tail = tc_gemm_tiles(a) - a.full_tiles;
+    if (n_tail <= 0) return cudaSuccess;
+    reduce_tail_kernel<<<grid_for(static_cast<int64_t>(n_tail) * 128 * a.bn / 4), kThreads, 0, s>>>(a, num_m, n_tail);
     note_launches(1);
     return cudaGetLastError();
 }

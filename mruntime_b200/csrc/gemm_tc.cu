@@ -381,7 +381,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             }
             tc_fence_before();
             mbar_arrive(&tempty[acc]);  // the accumulator is free; the fix-up reads global memory only
-            if (w.slot >= 0) tail_fixup<BN, SWAP>(a, w, n_tail, quad, lane);
+            if constexpr (SWAP) {
+                if (w.slot >= 0) tail_fixup<BN, SWAP>(a, w, n_tail, quad, lane);
+            }
             acc ^= 1;
             if (acc == 0) acc_phase ^= 1u;
         }
@@ -433,7 +435,7 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& a, const CUtensorMap& tmap_x, const
     // would never be written.
     if (a.full_tiles < tiles && (a.kb_per <= 0 || (a.tail_splits - 1) * a.kb_per >= num_kb ||
                                  a.tail_splits * a.kb_per < num_kb || a.partials == nullptr ||
-                                 a.tile_counters == nullptr))
+                                 (a.swap && a.tile_counters == nullptr)))
         return cudaErrorInvalidValue;
     if (a.swap) {
         if (a.M > a.bn) return cudaErrorInvalidValue;  // one token tile

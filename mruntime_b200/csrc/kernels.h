@@ -34,8 +34,9 @@ cudaError_t launch_skinny(const SkinnyArgs& a, int rows_per_warp_tiles, cudaStre
 // A-fastest.  Tiles [0, full_tiles) run over the whole K and store the output
 // directly; each remaining ("tail") tile runs as tail_splits K-slices of
 // kb_per 64-wide k-blocks that store FP32 partials, tile-major, into
-// `partials` ([tail_splits][n_tail][128][bn]); the last slice to finish a
-// 32-row quadrant of a tail tile sums the slices and stores it (tile_counters).
+// `partials` ([tail_splits][n_tail][128][bn]).  Swap mode: the last slice to
+// finish a 32-row quadrant of a tail tile sums the slices and stores it
+// (tile_counters); normal mode: launch_reduce_tail does it on the whole GPU.
 struct TcGemmArgs {
     int M, N, K;     // tokens, weight rows, reduction length (in both modes)
     int swap;        // 1: A = W, B = X
@@ -60,6 +61,9 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& a, const CUtensorMap& tmap_x, const
                            cudaStream_t s);
 // Output tiles of a plan (128 A rows x bn B rows each).
 int tc_gemm_tiles(const TcGemmArgs& a);
+// Normal mode only: sum the K-slices of every tail tile in slice order on
+// the whole GPU, round (+bias) or keep FP32, and store.
+cudaError_t launch_reduce_tail(const TcGemmArgs& a, cudaStream_t s);
 
 
 // Element-wise conversions with the reference's rounding.

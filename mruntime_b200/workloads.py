@@ -105,6 +105,55 @@ def sweep_7b(seed: int = 4, max_m: int = 2048) -> dict:
     return out
 
 
+DECODER_7B = {
+    "vocab_size": 152064, "hidden_size": 3584, "num_hidden_layers": 28, "num_attention_heads": 28,
+    "num_key_value_heads": 4, "intermediate_size": 18944, "rope_theta": 1000000.0, "rms_norm_eps": 1e-6,
+    "max_position_embeddings": 32768,
+}
+
+
+def decoder_prompt(seed: int = 3, n: int = 512, vocab: int = 152064) -> np.ndarray:
+    """Prompt token ids, uniform in [0, vocab), from the first child stream of `seed`."""
+    prompt_ss, _ = np.random.SeedSequence(seed).spawn(2)
+    return np.random.default_rng(prompt_ss).integers(0, vocab, size=n, dtype=np.int64).astype(np.int32)
+
+
+def decoder_tensor_specs(cfg: dict = DECODER_7B):
+    """(name, shape, kind) of every tensor of a Qwen2 checkpoint in the
+    reference's naming (src/models/qwen/qwen_model.cpp:54-101, 336-353), in
+    generation order; kind is "normal" (N(0, 0.02)) or "ones" (RMSNorm gains)."""
+    h, inter, v = cfg["hidden_size"], cfg["intermediate_size"], cfg["vocab_size"]
+    hd = h // cfg["num_attention_heads"]
+    kv = cfg["num_key_value_heads"] * hd
+    specs = [("model.embed_tokens.weight", (v, h), "normal")]
+    for i in range(cfg["num_hidden_layers"]):
+        p = f"model.layers.{i}"
+        specs += [(f"{p}.input_layernorm.weight", (h,), "ones"),
+                  (f"{p}.self_attn.q_proj.weight", (h, h), "normal"), (f"{p}.self_attn.q_proj.bias", (h,), "normal"),
+                  (f"{p}.self_attn.k_proj.weight", (kv, h), "normal"), (f"{p}.self_attn.k_proj.bias", (kv,), "normal"),
+                  (f"{p}.self_attn.v_proj.weight", (kv, h), "normal"), (f"{p}.self_attn.v_proj.bias", (kv,), "normal"),
+                  (f"{p}.self_attn.o_proj.weight", (h, h), "normal"),
+                  (f"{p}.post_attention_layernorm.weight", (h,), "ones"),
+                  (f"{p}.mlp.gate_proj.weight", (inter, h), "normal"), (f"{p}.mlp.up_proj.weight", (inter, h), "normal"),
+                  (f"{p}.mlp.down_proj.weight", (h, inter), "normal")]
+    specs += [("model.norm.weight", (h,), "ones"), ("lm_head.weight", (v, h), "normal")]
+    return specs
+
+
+def decoder_tensors(seed: int = 3, cfg: dict = DECODER_7B):
+    """Yield (name, FP16 bits) of a random-init Qwen2 decoder: every weight and
+    the q/k/v biases ~ N(0, 0.02), RMSNorm gains = 1, from the second child
+    stream of `seed`, in decoder_tensor_specs order."""
+    _, weight_ss = np.random.SeedSequence(seed).spawn(2)
+    rng = np.random.default_rng(weight_ss)
+    one = np.uint16(0x3C00)
+    for name, shape, kind in decoder_tensor_specs(cfg):
+        if kind == "ones":
+            yield name, np.full(shape, one, dtype=np.uint16)
+        else:
+            yield name, to_f16_bits(_normal(rng, shape, 0.02))
+
+
 def sweep_flops(M: int) -> float:
     return float(sum(2.0 * M * sum(parts) * k for _, parts, k in SWEEP_7B))
 
