@@ -57,6 +57,8 @@ def parse_args():
     ap.add_argument("--impl", default="mruntime_b200", choices=["mruntime_b200", "reference"])
     ap.add_argument("--m", type=int, default=HEADLINE_M, help="tokens per step (headline 2048)")
     ap.add_argument("--no-sweep", action="store_true", help="skip the per-M sweep extras")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="launch every step eagerly instead of replaying one captured CUDA graph")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     return ap.parse_args()
@@ -225,38 +227,73 @@ def max_over_ranks(v: float, world: int) -> float:
     return float(t.item())
 
 
-def time_steps(projs, tp, stream, M, steps, world, dominant=False):
+def capture(fn):
+    """Record fn(stream) into a CUDA graph (scratch buffers were sized by the
+    warm-up calls, so nothing allocates during capture)."""
+    import torch
+
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn(s.cuda_stream)  # one eager pass on the capture stream
+        torch.cuda.synchronize()
+        g.capture_begin()
+        fn(s.cuda_stream)
+        g.capture_end()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    return g
+
+
+def time_steps(projs, tp, stream, M, steps, world, dominant=False, graph=None):
+    """Device time of `steps` steps (max over ranks), replaying `graph` when
+    given; with dominant=True also the mean time of the gate+up GEMM alone
+    (eager launches, CUDA events around each call)."""
     import torch
 
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)] \
-        if dominant else [None] * steps
     barrier_sync(world)
     start.record()
-    for i in range(steps):
-        run_step(projs, tp, stream, M, evs[i])
+    for _ in range(steps):
+        if graph is not None:
+            graph.replay()
+        else:
+            run_step(projs, tp, stream, M)
     end.record()
     torch.cuda.synchronize()
     total_ms = start.elapsed_time(end)
-    dom_ms = statistics.mean(a.elapsed_time(b) for a, b in evs) if dominant else None
+    dom_ms = None
+    if dominant:
+        gate = [p for p in projs if p.name == "gateup"]
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for a, b in evs:
+            a.record()
+            run_step(gate, tp, stream, M)
+            b.record()
+        torch.cuda.synchronize()
+        dom_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
     return max_over_ranks(total_ms, world), dom_ms
 
 
 def time_projections(projs, tp, stream, M, iters):
-    """Mean device time of each projection alone (ms), CUDA events on the stream."""
+    """Mean device time of each projection alone (ms): a CUDA graph of the
+    one projection replayed `iters` times between two events."""
     import torch
 
-    evs = {p.name: [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                    for _ in range(iters)] for p in projs}
-    for i in range(iters):
-        for p in projs:
-            a, b = evs[p.name][i]
-            a.record()
-            run_step([p], tp, stream, M)
-            b.record()
-    torch.cuda.synchronize()
-    return {name: statistics.mean(a.elapsed_time(b) for a, b in lst) for name, lst in evs.items()}
+    out = {}
+    for p in projs:
+        g = capture(lambda s, p=p: run_step([p], tp, s, M))
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(iters):
+            g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        out[p.name] = a.elapsed_time(b) / iters
+        del g
+    return out
 
 
 def e2e_host_buffers(projs, tp, stream, M, steps, world):
@@ -318,9 +355,13 @@ def gpu_arm(args, rank, world, local):
         run_step(projs, tp, stream, M)
     capi.sync(stream)
     launches0 = capi.launch_count()
-    total_ms, dom_ms = time_steps(projs, tp, stream, M, args.steps, world, dominant=True)
-    launches = capi.launch_count() - launches0
+    run_step(projs, tp, stream, M)
+    per_step_launches = capi.launch_count() - launches0
+    graph = None if args.no_graph else capture(lambda s: run_step(projs, tp, s, M))
+    total_ms, dom_ms = time_steps(projs, tp, stream, M, args.steps, world, dominant=True, graph=graph)
+    launches = per_step_launches * args.steps
     clk = clocks.stop()
+    del graph
     capi.sync(stream)  # raises if any bounded wait inside a kernel gave up
     ms = total_ms / args.steps
     value = step_flops(M) / (ms * 1e-3) / 1e12
@@ -347,7 +388,9 @@ def gpu_arm(args, rank, world, local):
             for _ in range(3):
                 run_step(projs, tp, stream, m)
             n_it = 50 if m <= 128 else 20
-            t_ms, _ = time_steps(projs, tp, stream, m, n_it, world)
+            g = None if args.no_graph else capture(lambda s, m=m: run_step(projs, tp, s, m))
+            t_ms, _ = time_steps(projs, tp, stream, m, n_it, world, graph=g)
+            del g
             t = t_ms / n_it
             tf = step_flops(m) / (t * 1e-3) / 1e12
             gbs = WL.sweep_bytes(m) / (t * 1e-3) / 1e9
@@ -454,11 +497,12 @@ def reference_arm(args, rank, world):
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
-def workload_config(M: int, world: int) -> dict:
+def workload_config(M: int, world: int, graph: bool = True) -> dict:
     return {"workload": "qwen2.5-7b projection sweep (qkv 3584->4608, o 3584->3584, gate+up 3584->37888, "
                         "down 18944->3584), one step = the four GEMMs at M tokens",
             "M": M, "seed": 4, "weights": "bf16 source, uploaded once as fp16",
             "parallelism": f"tp{world}" if world > 1 else "single gpu",
+            "launch": "each timed step replays one CUDA graph of the step" if graph else "eager launches",
             "l2": "inputs larger than L2 (466 MB of fp16 weights streamed per step)"}
 
 
@@ -495,10 +539,13 @@ def main():
                 "warmup": args.warmup, "ms_per_step": round(r["ms"], 5), "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)",
                 "data": "synthetic (seeded N(0,1) FP16 activations, N(0,0.02) BF16 weights)",
-                "config": workload_config(args.m, world), "e2e": r["e2e"], "roofline": r["roofline"],
+                "config": workload_config(args.m, world, not args.no_graph), "e2e": r["e2e"], "roofline": r["roofline"],
                 "cpu_baseline": cpu, "clocks": r["clocks"], "gpu_launches": r["launches"], "sweep": r["sweep"]}
         print(json.dumps(line))
     if r["tp"] is not None:
+        import gc
+
+        gc.collect()  # graphs holding NCCL calls are gone before the communicator
         r["tp"].destroy()
     if world > 1:
         import torch.distributed as dist
