@@ -149,9 +149,19 @@ int mrt_weight_view(const void* w_dev_f16, int64_t N, int64_t K, mrt_weight* out
 
 int mrt_weight_free(mrt_weight w);
 
-/* Rows (N) and columns (K) of the uploaded shard, and its FP16 device data. */
+/* Rows (N) and columns (K) of the uploaded shard. */
 int mrt_weight_shape(mrt_weight w, int64_t* n, int64_t* k);
-int mrt_weight_data(mrt_weight w, void** dev_ptr);
+
+/* The weight's FP16 device storage in the library's layout: row-major [N, K]
+ * for views and for K not a multiple of 8; otherwise 128 x 64 tiles
+ * ([N_pad/128][ceil(K/64)][128][64], N_pad a multiple of 256, zero padding)
+ * stored in the order the tensor cores read them with 128-byte swizzling
+ * (16-byte chunk c of row r at chunk position c ^ (r % 8)), so each tile is
+ * one contiguous bulk copy.  *tiled (may be NULL) tells which. */
+int mrt_weight_data(mrt_weight w, void** dev_ptr, int* tiled);
+
+/* Copy the weight as row-major FP16 [N, K] (row stride ld) to dst_dev. */
+int mrt_weight_read(mrt_weight w, void* dst_dev, int64_t ld, void* stream);
 
 /* ---------------------------------------------------------------- GEMM */
 
@@ -160,8 +170,8 @@ int mrt_weight_data(mrt_weight w, void** dev_ptr);
  * With MRT_GEMM_BIAS the attached bias is added as the reference's q/k/v
  * bias step does it: fp16(fp32(fp16(acc)) + fp32(bias))
  * (src/models/qwen/qwen_model.cpp:130-155).
- * M <= 64 runs the HBM-streaming skinny kernel; larger M runs the tcgen05
- * tensor-core kernel.  Replaces Backend::gemm (include/mruntime/backend.h:13-21)
+ * Both regimes run the tcgen05 tensor-core kernel: M <= 64 (decode) with the
+ * weight as the 128-row MMA operand streamed from HBM, larger M with X.  Replaces Backend::gemm (include/mruntime/backend.h:13-21)
  * as implemented by CpuBackend::gemm (src/core/cpu_backend.cpp:72-169).
  */
 int mrt_gemm(mrt_weight w, const void* x_dev, int64_t ldx, void* y_dev, int64_t ldy, int64_t M,
@@ -170,8 +180,7 @@ int mrt_gemm(mrt_weight w, const void* x_dev, int64_t ldx, void* y_dev, int64_t 
 /* The kernel mrt_gemm would run for an M x N x K product on a device with
  * `sms` multiprocessors (0 = the current device): kernel 1 = tcgen05 with X
  * as the 128-row MMA operand (M > 64), 2 = tcgen05 in swap mode with the
- * weight as the 128-row operand and the tokens as N (M <= 64), 0 = the
- * mma.sync streaming kernel (M <= 16 when MRT_DECODE_KERNEL=skinny); then the
+ * weight as the 128-row operand and the tokens as N (M <= 64); then the
  * tile's bn, the number of tiles run over the whole K, the K-slices of each
  * remaining tile, k-blocks per slice and the persistent grid.  Host-only. */
 int mrt_gemm_plan(int64_t M, int64_t N, int64_t K, int sms, int* kernel, int* bn, int* full_tiles,

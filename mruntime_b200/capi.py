@@ -60,7 +60,8 @@ _SIGS = {
     "mrt_memcpy": (_int, [_vp, _vp, _sz, _vp]),
     "mrt_pointer_kind": (_int, [_vp, C.POINTER(_int)]),
     "mrt_weight_shape": (_int, [_vp, C.POINTER(_i64), C.POINTER(_i64)]),
-    "mrt_weight_data": (_int, [_vp, C.POINTER(_vp)]),
+    "mrt_weight_data": (_int, [_vp, C.POINTER(_vp), C.POINTER(_int)]),
+    "mrt_weight_read": (_int, [_vp, _vp, _i64, _vp]),
     "mrt_gemm": (_int, [_vp, _vp, _i64, _vp, _i64, _i64, _u32, _vp]),
     "mrt_gemm_f32": (_int, [_vp, _vp, _i64, _vp, _i64, _i64, _vp]),
     "mrt_gemm_plan": (_int, [_i64, _i64, _i64, _int] + [C.POINTER(_int)] * 6),
@@ -164,9 +165,19 @@ class Weight:
         call("mrt_weight_attach_bias", self.h, src_ptr, src_dtype, int(src_on_device), stream)
 
     def data_ptr(self) -> int:
+        """Device storage in the library's layout (see mrt_weight_data)."""
         p = C.c_void_p()
-        call("mrt_weight_data", self.h, C.byref(p))
+        call("mrt_weight_data", self.h, C.byref(p), None)
         return p.value
+
+    def tiled(self) -> bool:
+        p, t = C.c_void_p(), C.c_int()
+        call("mrt_weight_data", self.h, C.byref(p), C.byref(t))
+        return bool(t.value)
+
+    def read(self, dst_ptr: int, ld: int | None = None, stream: int | None = None) -> None:
+        """Copy the weight as row-major FP16 [n, k] to a device buffer."""
+        call("mrt_weight_read", self.h, dst_ptr, self.k if ld is None else ld, stream)
 
     def free(self):
         if self.h:
@@ -191,7 +202,7 @@ def gemm_plan(M: int, N: int, K: int, sms: int = 0) -> dict:
     call("mrt_gemm_plan", M, N, K, sms, *[C.byref(v) for v in vals])
     keys = ("kernel", "bn", "full_tiles", "tail_splits", "kb_per", "grid")
     d = dict(zip(keys, (v.value for v in vals)))
-    d["kernel"] = {0: "skinny", 1: "tcgen05", 2: "tcgen05-swap"}[d["kernel"]]
+    d["kernel"] = {1: "tcgen05", 2: "tcgen05-swap"}[d["kernel"]]
     return d
 
 

@@ -242,8 +242,16 @@ extern "C" int mrt_weight_upload(const void* src, int src_dtype, int src_on_devi
     w->n_ranges = static_cast<int64_t>(ranges.size() / 2);
     w->ranges = new int64_t[ranges.size()];
     std::copy(ranges.begin(), ranges.end(), w->ranges);
-    cudaError_t e = cudaMalloc(&w->data, static_cast<size_t>(n_keep * k_keep) * 2);
+    // Weights the tensor-core kernels can stream (K a multiple of 8) are stored
+    // pre-swizzled in 128 x 64 tiles; others stay row-major for the general kernel.
+    w->tiled = (k_keep % 8) == 0;
+    w->k_tiles = (k_keep + 63) / 64;
+    w->n_pad = w->tiled ? (n_keep + 255) / 256 * 256 : n_keep;
+    const size_t elems = w->tiled ? static_cast<size_t>(w->n_pad) * w->k_tiles * 64 : static_cast<size_t>(n_keep * k_keep);
+    cudaError_t e = cudaMalloc(&w->data, elems * 2);
+    if (e == cudaSuccess && w->tiled) e = cudaMemsetAsync(w->data, 0, elems * 2, s);
     if (e != cudaSuccess) {
+        if (w->data) cudaFree(w->data);
         delete[] w->ranges;
         delete w;
         return cuda_error(e, "allocating weight storage");
@@ -255,7 +263,26 @@ extern "C" int mrt_weight_upload(const void* src, int src_dtype, int src_on_devi
         const int64_t rows = ranges[i + 1] - ranges[i];
         const char* s0 = static_cast<const char*>(src) + (ranges[i] * K + k_begin) * es;
         uint16_t* d0 = w->data + row_off * k_keep;
-        if (src_dtype == MRT_FP16) {
+        if (w->tiled) {
+            const void* dsrc = s0;
+            int64_t dld = K;
+            if (!src_on_device) {
+                // Stage the native-dtype rows on the device first.
+                if (stage != nullptr) {
+                    cudaStreamSynchronize(s);
+                    cudaFree(stage);
+                    stage = nullptr;
+                }
+                e = cudaMalloc(&stage, static_cast<size_t>(rows * k_keep) * es);
+                if (e == cudaSuccess)
+                    e = cudaMemcpy2DAsync(stage, k_keep * es, s0, K * es, k_keep * es, rows, cudaMemcpyHostToDevice, s);
+                dsrc = stage;
+                dld = k_keep;
+            }
+            if (e == cudaSuccess)
+                e = launch_convert_rows_to_tiled(dsrc, src_dtype, dld, rows, k_keep, w->data, row_off, w->k_tiles, s);
+            if (e != cudaSuccess) rc = cuda_error(e, "uploading the weight into the tiled layout");
+        } else if (src_dtype == MRT_FP16) {
             e = cudaMemcpy2DAsync(d0, k_keep * 2, s0, K * 2, k_keep * 2, rows,
                                   src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s);
             if (e != cudaSuccess) rc = cuda_error(e, "copying the weight");
@@ -411,10 +438,22 @@ extern "C" int mrt_weight_shape(mrt_weight w, int64_t* n, int64_t* k) {
     return MRT_OK;
 }
 
-extern "C" int mrt_weight_data(mrt_weight w, void** dev_ptr) {
+extern "C" int mrt_weight_data(mrt_weight w, void** dev_ptr, int* tiled) {
     if (w == nullptr || dev_ptr == nullptr) return set_error(MRT_ERR_INVALID_ARG, "NULL argument");
     *dev_ptr = w->data;
+    if (tiled) *tiled = w->tiled ? 1 : 0;
     return MRT_OK;
+}
+
+extern "C" int mrt_weight_read(mrt_weight w, void* dst_dev, int64_t ld, void* stream) {
+    clear_error();
+    if (w == nullptr || dst_dev == nullptr) return set_error(MRT_ERR_INVALID_ARG, "NULL argument");
+    if (ld < w->k) return set_error(MRT_ERR_SHAPE, "ld must be >= K");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = w->tiled ? launch_untile(w->data, w->n, w->k, w->k_tiles, static_cast<uint16_t*>(dst_dev), ld, s)
+                             : cudaMemcpy2DAsync(dst_dev, ld * 2, w->data, w->k * 2, w->k * 2, w->n,
+                                                 cudaMemcpyDeviceToDevice, s);
+    return e == cudaSuccess ? MRT_OK : cuda_error(e, "reading the weight");
 }
 
 // ====================================================================== GEMM
@@ -478,16 +517,6 @@ static TcPlan plan_swap(int64_t M, int64_t N, int64_t K, int sms) {
     return best;
 }
 
-// Decode shapes (M <= 16) run the swap-mode tensor-core kernel unless the
-// environment sets MRT_DECODE_KERNEL=skinny (the mma.sync streaming kernel).
-static bool use_skinny_for_decode() {
-    static const bool skinny = [] {
-        const char* v = std::getenv("MRT_DECODE_KERNEL");
-        return v != nullptr && std::strcmp(v, "skinny") == 0;
-    }();
-    return skinny;
-}
-
 static TcPlan plan_tc(int64_t M, int64_t N, int64_t K, int sms) {
     const int64_t num_m = (M + 127) / 128;
     const int64_t num_kb = (K + 63) / 64;
@@ -529,15 +558,6 @@ static TcPlan plan_tc(int64_t M, int64_t N, int64_t K, int sms) {
     return best;
 }
 
-// Weight rows per skinny CTA (in 8-row tiles): as many as still leaves about
-// two CTAs per SM, so small N keeps every SM streaming.
-static int plan_skinny_rn(int64_t M, int64_t N, int sms) {
-    const int max_rn = M > 32 ? 2 : 4;
-    for (int rn = max_rn; rn > 1; rn /= 2)
-        if ((N + 8 * rn - 1) / (8 * rn) >= 2LL * sms) return rn;
-    return 1;
-}
-
 // The weight's TMA map whose box is exactly the kernel's W tile (bn rows).
 static const CUtensorMap* weight_tmap(mrt_weight w, int bn) {
     const int slot = bn == 64 ? 0 : (bn == 128 ? 1 : (bn == 256 ? 2 : -1));
@@ -577,28 +597,27 @@ static int gemm_dispatch(mrt_weight w, const void* x, int64_t ldx, void* y, int6
         g.c = y; g.c_dtype = out_f32 ? MRT_FP32 : MRT_FP16; g.ldc = ldy;
         g.M = M; g.N = w->n; g.K = w->k; g.alpha = 1.0f; g.beta = 0.0f;
         g.trans_a = 0; g.trans_b = 1; g.bias = bias;
+        g.b_k_tiles = w->tiled ? w->k_tiles : 0;
         e = launch_general_gemm(g, s);
         return e == cudaSuccess ? MRT_OK : cuda_error(e, "general gemm launch");
     }
-    if (M <= 16 && use_skinny_for_decode()) {
-        SkinnyArgs a{};
-        a.x = static_cast<const uint16_t*>(x); a.ldx = ldx; a.w = w->data;
-        a.y = y; a.ldy = ldy; a.M = static_cast<int>(M); a.N = static_cast<int>(w->n);
-        a.K = static_cast<int>(w->k); a.bias = bias; a.out_f32 = out_f32 ? 1 : 0;
-        e = launch_skinny(a, plan_skinny_rn(M, w->n, c->sms), s);
-        return e == cudaSuccess ? MRT_OK : cuda_error(e, "skinny gemm launch");
-    }
     const bool swap = M <= 64;
     const TcPlan p = swap ? plan_swap(M, w->n, w->k, c->sms) : plan_tc(M, w->n, w->k, c->sms);
-    // X's box is 128 rows in normal mode and bn rows in swap mode; W's the other.
+    // X's box is 128 rows in normal mode and bn rows in swap mode; a row-major
+    // W needs a tensor map with the other box, a tiled W is copied linearly.
     CUtensorMap tx;
     int rc = make_tmap_f16(&tx, x, M, w->k, ldx, swap ? p.bn : 128);
     if (rc != MRT_OK) return rc;
-    const CUtensorMap* tw = weight_tmap(w, swap ? 128 : p.bn);
-    if (tw == nullptr) return MRT_ERR_CUDA;
+    const CUtensorMap* tw = &tx;
+    if (!w->tiled) {
+        tw = weight_tmap(w, swap ? 128 : p.bn);
+        if (tw == nullptr) return MRT_ERR_CUDA;
+    }
     TcGemmArgs a{};
     a.M = static_cast<int>(M); a.N = static_cast<int>(w->n); a.K = static_cast<int>(w->k);
     a.swap = swap ? 1 : 0;
+    a.w_tiled = w->tiled ? w->data : nullptr;
+    a.w_k_tiles = w->k_tiles;
     a.bn = p.bn; a.grid = p.grid; a.full_tiles = p.full; a.tail_splits = p.splits; a.kb_per = p.kb_per;
     a.y = y; a.ldy = ldy; a.out_f32 = out_f32 ? 1 : 0; a.bias = bias; a.err_flag = c->d_err;
     const int64_t tiles = tc_gemm_tiles(a);
@@ -639,15 +658,14 @@ extern "C" int mrt_gemm_plan(int64_t M, int64_t N, int64_t K, int sms, int* kern
         if (!c) return MRT_ERR_CUDA;
         sms = c->sms;
     }
-    const bool skinny = M <= 16 && use_skinny_for_decode();
-    const bool swap = !skinny && M <= 64;
-    const TcPlan p = skinny ? TcPlan{} : (swap ? plan_swap(M, N, K, sms) : plan_tc(M, N, K, sms));
-    if (kernel) *kernel = skinny ? 0 : (swap ? 2 : 1);
-    if (bn) *bn = skinny ? 8 * plan_skinny_rn(M, N, sms) : p.bn;
-    if (full_tiles) *full_tiles = skinny ? 0 : p.full;
-    if (tail_splits) *tail_splits = skinny ? 1 : p.splits;
-    if (kb_per) *kb_per = skinny ? 0 : p.kb_per;
-    if (grid) *grid = skinny ? static_cast<int>((N + 8 * plan_skinny_rn(M, N, sms) - 1) / (8 * plan_skinny_rn(M, N, sms))) : p.grid;
+    const bool swap = M <= 64;
+    const TcPlan p = swap ? plan_swap(M, N, K, sms) : plan_tc(M, N, K, sms);
+    if (kernel) *kernel = swap ? 2 : 1;
+    if (bn) *bn = p.bn;
+    if (full_tiles) *full_tiles = p.full;
+    if (tail_splits) *tail_splits = p.splits;
+    if (kb_per) *kb_per = p.kb_per;
+    if (grid) *grid = p.grid;
     return MRT_OK;
 }
 

@@ -155,6 +155,26 @@ __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
 
+// Linear bulk copy global -> shared (no tensor map), completion counted in
+// bytes on `bar`.  Both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(gmem_src)), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Element offset of (row r, column k) in the tiled weight layout: 128 x 64
+// tiles, tile (r / 128, k / 64) at ((r / 128) * k_tiles + k / 64) * 8192, and
+// inside a tile row-major 64-element rows whose 16-byte chunks are permuted
+// as the 128-byte shared-memory swizzle does (chunk c of row r at c ^ (r % 8)).
+__host__ __device__ __forceinline__ int64_t tiled_offset(int64_t r, int64_t k, int64_t k_tiles) {
+    const int64_t rr = r & 127, kk = k & 63;
+    const int64_t chunk = (kk >> 3) ^ (rr & 7);
+    return (((r >> 7) * k_tiles + (k >> 6)) << 13) + (rr << 6) + (chunk << 3) + (kk & 7);
+}
+
 // ------------------------------------------------------------------ tcgen05
 
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {

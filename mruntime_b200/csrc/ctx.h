@@ -59,8 +59,17 @@ struct mrt_weight_s {
     int device = -1;
     int64_t n = 0;  // rows kept
     int64_t k = 0;  // columns kept
-    uint16_t* data = nullptr;  // dense FP16 [n, k]
+    // FP16 data.  Row-major [n, k] when !tiled; when tiled, 128 x 64 tiles
+    // [n_pad / 128][k_tiles][128][64], each stored in the byte order the
+    // tensor cores read with 128-byte swizzling (16-byte chunk c of row r at
+    // chunk position c ^ (r % 8)), padded with zeros to n_pad rows (a multiple
+    // of 256) and k_tiles * 64 columns, so one linear bulk copy fills a
+    // shared-memory ring stage.
+    uint16_t* data = nullptr;
     bool owns_data = true;     // false for mrt_weight_view
+    bool tiled = false;
+    int64_t n_pad = 0;
+    int64_t k_tiles = 0;
     uint16_t* bias = nullptr;  // FP16 [n] or nullptr
     int64_t src_n = 0;         // rows of the full source weight
     int64_t* ranges = nullptr; // row ranges kept (pairs)

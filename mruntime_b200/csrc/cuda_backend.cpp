@@ -77,6 +77,7 @@ CudaBackend::~CudaBackend() {
     mrt_sync(stream_);
     for (auto& kv : uploaded_) mrt_weight_free(kv.second);
     for (auto& kv : implicit_) mrt_weight_free(kv.second.w);
+    for (auto& kv : tables_) mrt_device_free(kv.second.data);
     for (auto& s : scratch_) mrt_device_free(s.first);
 }
 
@@ -136,8 +137,10 @@ Tensor CudaBackend::upload_weight(const Tensor& weight) {
                             0, 0, K, stream_, &w),
           "mrt_weight_upload");
     void* data = nullptr;
-    check(mrt_weight_data(w, &data), "mrt_weight_data");
+    check(mrt_weight_data(w, &data, nullptr), "mrt_weight_data");
     uploaded_[data] = w;
+    // A handle: the data is in the library's (tiled) layout, so the view is
+    // meant for gemm/gemm_bias/attach_bias only.
     return Tensor::from_buffer(data, Shape({weight.dim(0), weight.dim(1)}), DType::FP16, false);
 }
 
@@ -166,6 +169,24 @@ uint64_t CudaBackend::fingerprint(const Tensor& t) {
         }
     }
     return h;
+}
+
+const void* CudaBackend::device_table(const Tensor& t) {
+    if (on_device(t.data())) return t.data();
+    const auto key = std::make_tuple(static_cast<const void*>(t.data()), t.dim(0), t.dim(1), to_mrt(t.dtype()));
+    const uint64_t fp = fingerprint(t);
+    auto it = tables_.find(key);
+    if (it != tables_.end()) {
+        if (it->second.fingerprint == fp) return it->second.data;
+        sync();
+        mrt_device_free(it->second.data);
+        tables_.erase(it);
+    }
+    void* d = nullptr;
+    check(mrt_device_alloc(t.nbytes(), &d), "allocating an embedding table");
+    check(mrt_memcpy(d, t.data(), t.nbytes(), stream_), "uploading an embedding table");
+    tables_[key] = Table{d, fp};
+    return d;
 }
 
 mrt_weight CudaBackend::weight_for(const Tensor& B, size_t N, size_t K) {
@@ -372,15 +393,9 @@ void CudaBackend::embedding_lookup(const Tensor& weight, const std::vector<int>&
             throw std::out_of_range("embedding_lookup: token_id out of range");
     if (token_ids.empty()) return;
     // The table can be large: use it in place when it is on the device,
-    // otherwise upload it once per (pointer, shape) like a weight.
-    void* w = nullptr;
-    if (on_device(weight.data())) {
-        w = const_cast<void*>(weight.data());
-    } else {
-        mrt_weight h = weight_for(weight, weight.dim(0), weight.dim(1));
-        check(mrt_weight_data(h, &w), "mrt_weight_data");
-    }
-    const int wdt = on_device(weight.data()) ? to_mrt(weight.dtype()) : MRT_FP16;
+    // otherwise keep one row-major device copy per host table.
+    const void* w = device_table(weight);
+    const int wdt = to_mrt(weight.dtype());
     std::vector<int32_t> ids(token_ids.begin(), token_ids.end());
     Staged o = stage_out(output, 1, false);
     check(mrt_embedding(w, wdt, static_cast<int64_t>(weight.dim(0)), static_cast<int64_t>(weight.dim(1)), ids.data(),

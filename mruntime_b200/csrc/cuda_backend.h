@@ -116,6 +116,13 @@ private:
     };
     std::map<std::tuple<const void*, size_t, size_t, int>, Implicit> implicit_;
     static uint64_t fingerprint(const mruntime::Tensor& t);
+    // Row-major device copies of host embedding tables (same key and check).
+    struct Table {
+        void* data = nullptr;
+        uint64_t fingerprint = 0;
+    };
+    std::map<std::tuple<const void*, size_t, size_t, int>, Table> tables_;
+    const void* device_table(const mruntime::Tensor& t);
     std::vector<std::pair<void*, size_t>> scratch_;
 };
 

@@ -56,6 +56,34 @@ __global__ void convert_2d_kernel(const void* src, int sdt, int64_t ld, int64_t 
     }
 }
 
+// Weight upload into the tiled layout: rows [row0, row0 + rows) of the
+// destination from a [rows, cols] source (row stride ld) of dtype sdt, rounded
+// to FP16 with the reference's converter.  Padding was zeroed beforehand.
+__global__ void convert_rows_to_tiled_kernel(const void* src, int sdt, int64_t ld, int64_t rows, int64_t cols,
+                                             uint16_t* dst, int64_t row0, int64_t k_tiles) {
+    const int64_t total = rows * cols;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t r = i / cols;
+        const int64_t c = i - r * cols;
+        const int64_t si = r * ld + c;
+        const uint16_t v = (sdt == 0) ? static_cast<const uint16_t*>(src)[si]
+                                      : f32_to_f16_bits(load_as_f32(src, sdt, si));
+        dst[tiled_offset(row0 + r, c, k_tiles)] = v;
+    }
+}
+
+// Row-major [n, k] copy (row stride ld) of a tiled weight.
+__global__ void untile_kernel(const uint16_t* src, int64_t n, int64_t k, int64_t k_tiles, uint16_t* dst, int64_t ld) {
+    const int64_t total = n * k;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t r = i / k;
+        const int64_t c = i - r * k;
+        dst[r * ld + c] = src[tiled_offset(r, c, k_tiles)];
+    }
+}
+
 // Finish the K-split tail tiles of a normal-mode tensor-core GEMM plan (the
 // swap mode finishes its small tiles inside the GEMM kernel): partials are
 // [tail_splits][n_tail][128][bn] FP32; slices are added in index order, so
@@ -237,6 +265,22 @@ cudaError_t launch_convert_2d_to_f16(const void* src, int sdt, int64_t ld, int64
                                      int64_t cols, uint16_t* dst, cudaStream_t s) {
     if (rows <= 0 || cols <= 0) return cudaSuccess;
     convert_2d_kernel<<<grid_for(rows * cols), kThreads, 0, s>>>(src, sdt, ld, rows, cols, dst);
+    note_launches(1);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_convert_rows_to_tiled(const void* src, int sdt, int64_t ld, int64_t rows, int64_t cols,
+                                         uint16_t* dst, int64_t row0, int64_t k_tiles, cudaStream_t s) {
+    if (rows <= 0 || cols <= 0) return cudaSuccess;
+    convert_rows_to_tiled_kernel<<<grid_for(rows * cols), kThreads, 0, s>>>(src, sdt, ld, rows, cols, dst, row0, k_tiles);
+    note_launches(1);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_untile(const uint16_t* src, int64_t n, int64_t k, int64_t k_tiles, uint16_t* dst, int64_t ld,
+                          cudaStream_t s) {
+    if (n <= 0 || k <= 0) return cudaSuccess;
+    untile_kernel<<<grid_for(n * k), kThreads, 0, s>>>(src, n, k, k_tiles, dst, ld);
     note_launches(1);
     return cudaGetLastError();
 }

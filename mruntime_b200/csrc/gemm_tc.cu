@@ -275,8 +275,27 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
                         break;
                     }
                     mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
-                    tma_load_2d(sA + stage * Cfg::kABytes, &tma, &full[stage], kb * kBK, w.mt * kBM);
-                    tma_load_2d(sB + stage * Cfg::kBBytes, &tmb, &full[stage], kb * kBK, w.nt * BN);
+                    if (a.w_tiled == nullptr) {
+                        tma_load_2d(sA + stage * Cfg::kABytes, &tma, &full[stage], kb * kBK, w.mt * kBM);
+                        tma_load_2d(sB + stage * Cfg::kBBytes, &tmb, &full[stage], kb * kBK, w.nt * BN);
+                    } else if constexpr (SWAP) {
+                        // W is A: one contiguous, already swizzled 128 x 64 tile.
+                        bulk_load(sA + stage * Cfg::kABytes,
+                                  a.w_tiled + tiled_offset(static_cast<int64_t>(w.mt) * kBM, static_cast<int64_t>(kb) * kBK, a.w_k_tiles),
+                                  Cfg::kABytes, &full[stage]);
+                        tma_load_2d(sB + stage * Cfg::kBBytes, &tmb, &full[stage], kb * kBK, w.nt * BN);
+                    } else {
+                        // W is B: BN rows = BN/128 whole tiles, or half of one for BN = 64.
+                        tma_load_2d(sA + stage * Cfg::kABytes, &tma, &full[stage], kb * kBK, w.mt * kBM);
+                        constexpr int kPieces = BN >= 128 ? BN / 128 : 1;
+                        constexpr uint32_t kPieceBytes = (BN >= 128 ? 128 : BN) * kBK * 2;
+#pragma unroll
+                        for (int h = 0; h < kPieces; ++h)
+                            bulk_load(sB + stage * Cfg::kBBytes + h * kPieceBytes,
+                                      a.w_tiled + tiled_offset(static_cast<int64_t>(w.nt) * BN + h * 128,
+                                                               static_cast<int64_t>(kb) * kBK, a.w_k_tiles),
+                                      kPieceBytes, &full[stage]);
+                    }
                     issued |= 1u << stage;
                     issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
                     if (++stage == S) {

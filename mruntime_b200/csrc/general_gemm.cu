@@ -51,7 +51,8 @@ __global__ void general_gemm_kernel(const GeneralGemmArgs a) {
                 const int64_t nn = static_cast<int64_t>(blockIdx.x) * kT + tx;
                 float v = 0.0f;
                 if (nn < a.N && kk < a.K) {
-                    const int64_t idx = a.trans_b ? nn * a.b_cols0 + kk : kk * a.b_cols0 + nn;
+                    const int64_t idx = a.b_k_tiles > 0 ? tiled_offset(nn, kk, a.b_k_tiles)
+                                                        : (a.trans_b ? nn * a.b_cols0 + kk : kk * a.b_cols0 + nn);
                     v = ld_f32(a.b, a.b_dtype, idx);
                 }
                 sb[ty][tx] = v;

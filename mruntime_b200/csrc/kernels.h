@@ -11,20 +11,6 @@ namespace mrt {
 // Count one kernel launch (read through mrt_launch_count).
 void note_launches(int n);
 
-// Y[M,N] = X[M,K] * W[N,K]^T for M <= 64 (decode / skinny shapes).
-// Requirements checked by the caller: K % 8 == 0, ldx % 8 == 0, 16-byte
-// aligned x and w.  out_f32 selects FP32 output (no rounding, no bias).
-struct SkinnyArgs {
-    const uint16_t* x;
-    int64_t ldx;
-    const uint16_t* w;  // dense [N, K]
-    void* y;
-    int64_t ldy;
-    int M, N, K;
-    const uint16_t* bias;  // FP16 [N] or nullptr
-    int out_f32;
-};
-cudaError_t launch_skinny(const SkinnyArgs& a, int rows_per_warp_tiles, cudaStream_t s);
 
 // Y = X * W^T on the tcgen05 tensor cores.  The MMA's 128-row operand ("A")
 // is X (normal mode) or W (swap mode, for few tokens: the weight rows fill the
@@ -56,6 +42,9 @@ struct TcGemmArgs {
     // stores the output and resets the counter.
     int* tile_counters;
     int* err_flag;
+    // Weight in the tiled layout (nullptr: the weight's tensor map is used).
+    const uint16_t* w_tiled;
+    int64_t w_k_tiles;
 };
 cudaError_t launch_tc_gemm(const TcGemmArgs& a, const CUtensorMap& tmap_x, const CUtensorMap& tmap_w,
                            cudaStream_t s);
@@ -73,6 +62,13 @@ cudaError_t launch_convert(const void* src, int src_dtype, void* dst, int dst_dt
 // dense FP16 [rows, k1-k0] destination (weight upload of a shard).
 cudaError_t launch_convert_2d_to_f16(const void* src, int src_dtype, int64_t src_ld, int64_t rows,
                                      int64_t cols, uint16_t* dst, cudaStream_t s);
+
+// Tiled weight layout (see mrt_weight_s and tiled_offset in common.cuh).
+cudaError_t launch_convert_rows_to_tiled(const void* src, int src_dtype, int64_t src_ld, int64_t rows,
+                                         int64_t cols, uint16_t* dst, int64_t row0, int64_t k_tiles,
+                                         cudaStream_t s);
+cudaError_t launch_untile(const uint16_t* src, int64_t n, int64_t k, int64_t k_tiles, uint16_t* dst,
+                          int64_t ld, cudaStream_t s);
 
 // Row argmax in two passes through `scratch` (see argmax_scratch_bytes).
 size_t argmax_scratch_bytes(int64_t M, int64_t V);
@@ -104,6 +100,7 @@ struct GeneralGemmArgs {
     float alpha, beta;
     int trans_a, trans_b;
     const uint16_t* bias;  // FP16 [N] added after rounding (FP16 C only) or nullptr
+    int64_t b_k_tiles;     // > 0: B is an FP16 weight [N, K] in the tiled layout (trans_b)
 };
 cudaError_t launch_general_gemm(const GeneralGemmArgs& a, cudaStream_t s);
 

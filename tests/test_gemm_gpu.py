@@ -85,11 +85,52 @@ def test_convert_bitexact_with_reference(cuda_dev):
 # ------------------------------------------------------------------ weight upload
 
 def weight_fp16(wt) -> np.ndarray:
-    """Read back the library-owned FP16 weight (an FP16 -> FP16 mrt_convert is a copy)."""
+    """Read back the library-owned FP16 weight as row-major [n, k]."""
     buf = torch.empty((wt.n, wt.k), dtype=torch.int16, device="cuda")
-    capi.convert(wt.data_ptr(), FP16, buf.data_ptr(), FP16, wt.n * wt.k, stream())
+    wt.read(buf.data_ptr(), stream=stream())
     capi.sync(stream())
     return host_u16(buf)
+
+
+def test_tiled_layout_is_the_swizzled_tile_order(cuda_dev):
+    # 128 x 64 tiles, 16-byte chunk c of row r stored at chunk c ^ (r % 8)
+    rng = np.random.default_rng(12)
+    N, K = 300, 200
+    w = W.to_f16_bits(rng.standard_normal((N, K), dtype=np.float32))
+    wt = upload(w, FP16)
+    assert wt.tiled()
+    k_tiles = (K + 63) // 64
+    n_pad = (N + 255) // 256 * 256
+    raw = torch.empty(n_pad * k_tiles * 64, dtype=torch.int16, device="cuda")
+    capi.convert(wt.data_ptr(), FP16, raw.data_ptr(), FP16, raw.numel(), stream())
+    capi.sync(stream())
+    raw = host_u16(raw)
+    r = np.arange(N)[:, None]
+    k = np.arange(K)[None, :]
+    off = (((r >> 7) * k_tiles + (k >> 6)) << 13) + ((r & 127) << 6) + ((((k & 63) >> 3) ^ (r & 7)) << 3) + (k & 7)
+    np.testing.assert_array_equal(raw[off], w)
+    pad = np.ones(raw.size, bool)
+    pad[off.reshape(-1)] = False
+    assert not raw[pad].any()  # padding rows and columns are zero
+    np.testing.assert_array_equal(weight_fp16(wt), w)
+
+
+@pytest.mark.parametrize("M", [3, 70])
+def test_general_kernel_reads_tiled_weight(cuda_dev, M):
+    # an odd row stride of x sends the call to the general kernel, which reads
+    # the weight through the tiled layout; same k-order arithmetic: bit-exact
+    rng = np.random.default_rng(M)
+    N, K = 130, 96
+    x = rand_f16(rng, (M, K))
+    w = rand_w(rng, (N, K), FP16)
+    wt = upload(w, FP16)
+    xs = np.zeros((M, K + 3), np.uint16)
+    xs[:, :K] = x
+    xd = dev_u16(xs)
+    y = torch.empty((M, N), dtype=torch.int16, device="cuda")
+    capi.gemm(wt, xd.data_ptr(), K + 3, y.data_ptr(), N, M, False, stream())
+    capi.sync(stream())
+    np.testing.assert_array_equal(host_u16(y), O.gemm(x, FP16, w, FP16, trans_b=True))
 
 
 @pytest.mark.parametrize("on_device", [True, False])
