@@ -618,6 +618,7 @@ static int gemm_dispatch(mrt_weight w, const void* x, int64_t ldx, void* y, int6
     a.swap = swap ? 1 : 0;
     a.w_tiled = w->tiled ? w->data : nullptr;
     a.w_k_tiles = w->k_tiles;
+    a.w_prefetch = w->tiled ? 1 : 0;  // uploads finish before returning; views are never tiled
     a.bn = p.bn; a.grid = p.grid; a.full_tiles = p.full; a.tail_splits = p.splits; a.kb_per = p.kb_per;
     a.y = y; a.ldy = ldy; a.out_f32 = out_f32 ? 1 : 0; a.bias = bias; a.err_flag = c->d_err;
     const int64_t tiles = tc_gemm_tiles(a);

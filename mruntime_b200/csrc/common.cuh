@@ -175,6 +175,18 @@ __host__ __device__ __forceinline__ int64_t tiled_offset(int64_t r, int64_t k, i
     return (((r >> 7) * k_tiles + (k >> 6)) << 13) + (rr << 6) + (chunk << 3) + (kk & 7);
 }
 
+// ------------------------------------------------------------------ dependent launch
+
+// Let the next kernel in the stream (launched with programmatic stream
+// serialisation) start its prologue while this one still runs.
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Block until the kernels this one depends on have completed and their
+// memory is visible (a no-op when launched without a programmatic edge).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ------------------------------------------------------------------ tcgen05
 
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {

@@ -34,13 +34,17 @@ constexpr int kBK = 64;
 constexpr int kThreadsTc = 192;
 constexpr int kEpiThreads = 128;
 
-template <int BN>
+template <int BN, bool SWAP>
 struct TcCfg {
     static constexpr int kABytes = kBM * kBK * 2;
     static constexpr int kBBytes = BN * kBK * 2;
     static constexpr int kStageBytes = kABytes + kBBytes;
-    // As many ring stages as fit in ~200 KB (4 for BN = 256 ... 11 for BN = 16).
-    static constexpr int kStages = (200 * 1024) / kStageBytes > 12 ? 12 : (200 * 1024) / kStageBytes;
+    // Normal mode: as many ring stages as fit in ~200 KB (4 for BN = 256, 8
+    // for BN = 64).  Swap mode (weight streaming): ~108 KB (6 stages for
+    // BN = 16, 4 for BN = 64), so two CTAs fit on an SM -- the next GEMM's CTA
+    // streams its weights beside this one's epilogue and K-split fix-up.
+    static constexpr int kRingBudget = SWAP ? 108 * 1024 : 200 * 1024;
+    static constexpr int kStages = kRingBudget / kStageBytes > 12 ? 12 : kRingBudget / kStageBytes;
     // Two accumulators of BN FP32 columns, rounded up to a power of two >= 32.
     static constexpr uint32_t kTmemCols = 2 * BN <= 32 ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
     static constexpr int kBarBytes = (2 * kStages + 5) * 8 + 16;
@@ -141,24 +145,38 @@ __device__ __forceinline__ void store_swap_chunk(const TcGemmArgs& a, const uint
     }
 }
 
-// Swap mode: 16 FP32 columns into a tail slot ([128][bn] tile-local).
+// Swap mode: up to 16 FP32 columns (tokens) into a tail slot ([128][bn]
+// tile-local); only the `groups` float4 groups holding real tokens are
+// written (columns past the last token are never read back).
 __device__ __forceinline__ void store_partial_chunk16(const TcGemmArgs& a, const uint32_t (&r)[16], int slot,
-                                                     int row_in_tile, int col_in_tile, int bn) {
+                                                     int row_in_tile, int col_in_tile, int bn, int groups) {
     float* dst = a.partials + (static_cast<int64_t>(slot) * kBM + row_in_tile) * bn + col_in_tile;
 #pragma unroll
-    for (int j = 0; j < 16; j += 4)
-        *reinterpret_cast<uint4*>(dst + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+    for (int g = 0; g < 4; ++g)
+        if (g < groups)
+            *reinterpret_cast<uint4*>(dst + 4 * g) = make_uint4(r[4 * g], r[4 * g + 1], r[4 * g + 2], r[4 * g + 3]);
 }
 
-// K-split finish for one 32-row quadrant of a tail tile, run by the whole
-// epilogue warp that just stored its partial rows.  The warp counts itself
-// in; only the warp that completes the count (the last of the tail_splits
-// slices to arrive) sums all slices in slice order -- so the result does not
-// depend on arrival order -- stores the output and resets the counter.
-// Nobody waits for anybody, so a slice lost to an error cannot hang the
-// kernel; it only leaves its tile unfinished.
-template <int BN, bool SWAP>
-__device__ __forceinline__ void tail_fixup(const TcGemmArgs& a, const Unit& w, int n_tail, int quad, int lane) {
+__device__ __forceinline__ void add4(float4& s, const float4& p) {
+    s.x += p.x;
+    s.y += p.y;
+    s.z += p.z;
+    s.w += p.w;
+}
+
+// Swap-mode K-split finish for one 32-row quadrant of a tail tile, run by the
+// whole epilogue warp that just stored its partial rows.  The warp counts
+// itself in; only the warp that completes the count (the last of the
+// tail_splits slices to arrive) sums all slices in slice order -- so the
+// result does not depend on arrival order -- stores the output and resets the
+// counter.  Nobody waits for anybody, so a slice lost to an error cannot hang
+// the kernel; it only leaves its tile unfinished.
+//
+// The sum is latency-bound (a few KB per warp from L2), so each lane reads
+// only its weight row's real token columns and keeps up to 4 slices x 16
+// tokens of loads in flight before adding them in order.
+template <int BN>
+__device__ __forceinline__ void swap_tail_fixup(const TcGemmArgs& a, const Unit& w, int n_tail, int quad, int lane) {
     __threadfence();  // this warp's partial rows are visible to the whole GPU
     __syncwarp();
     int last = 0;
@@ -171,48 +189,54 @@ __device__ __forceinline__ void tail_fixup(const TcGemmArgs& a, const Unit& w, i
     if (!last) return;
     __threadfence();  // the other slices' rows are read after the count
     const int r = quad * 32 + lane;
-    const int64_t row = static_cast<int64_t>(w.mt) * kBM + r;
+    const int64_t n = static_cast<int64_t>(w.mt) * kBM + r;  // weight row = output column
+    const int cols = min(BN, a.M - w.nt * BN);                 // tokens in this tile
     const int64_t slice = static_cast<int64_t>(n_tail) * kBM * BN;
     const float* base = a.partials + (static_cast<int64_t>(w.ti) * kBM + r) * BN;
-    constexpr int kChunk = SWAP ? 16 : 32;
+    constexpr int kG = 4;  // float4 groups (16 tokens) per pass
+    constexpr int kB = 4;  // slices in flight per batch
 #pragma unroll 1
-    for (int c = 0; c < BN / kChunk; ++c) {
-        float s[kChunk];
+    for (int c0 = 0; c0 < cols; c0 += 16) {
+        const int ng = min(kG, (cols - c0 + 3) / 4);
+        float4 sum[kG];
+#pragma unroll 1
+        for (int sp0 = 0; sp0 < a.tail_splits; sp0 += kB) {
+            float4 p[kB][kG];
 #pragma unroll
-        for (int j = 0; j < kChunk; j += 4) {
-            const float4 p = *reinterpret_cast<const float4*>(base + c * kChunk + j);
-            s[j] = p.x;
-            s[j + 1] = p.y;
-            s[j + 2] = p.z;
-            s[j + 3] = p.w;
+            for (int b = 0; b < kB; ++b)
+#pragma unroll
+                for (int g = 0; g < kG; ++g)
+                    if (sp0 + b < a.tail_splits && g < ng)
+                        p[b][g] = *reinterpret_cast<const float4*>(base + (sp0 + b) * slice + c0 + 4 * g);
+#pragma unroll
+            for (int b = 0; b < kB; ++b)
+#pragma unroll
+                for (int g = 0; g < kG; ++g)
+                    if (sp0 + b < a.tail_splits && g < ng) {
+                        if (sp0 + b == 0)
+                            sum[g] = p[b][g];
+                        else
+                            add4(sum[g], p[b][g]);
+                    }
         }
-        for (int sp = 1; sp < a.tail_splits; ++sp) {
+        uint32_t bits[16] = {};
 #pragma unroll
-            for (int j = 0; j < kChunk; j += 4) {
-                const float4 p = *reinterpret_cast<const float4*>(base + sp * slice + c * kChunk + j);
-                s[j] += p.x;
-                s[j + 1] += p.y;
-                s[j + 2] += p.z;
-                s[j + 3] += p.w;
+        for (int g = 0; g < kG; ++g)
+            if (g < ng) {
+                bits[4 * g] = __float_as_uint(sum[g].x);
+                bits[4 * g + 1] = __float_as_uint(sum[g].y);
+                bits[4 * g + 2] = __float_as_uint(sum[g].z);
+                bits[4 * g + 3] = __float_as_uint(sum[g].w);
             }
-        }
-        uint32_t bits[kChunk];
-#pragma unroll
-        for (int j = 0; j < kChunk; ++j) bits[j] = __float_as_uint(s[j]);
-        if constexpr (SWAP) {
-            store_swap_chunk(a, bits, row, static_cast<int64_t>(w.nt) * BN + c * kChunk);
-        } else {
-            const int64_t col0 = static_cast<int64_t>(w.nt) * BN + c * kChunk;
-            if (row < a.M && col0 < a.N) store_row_chunk(a, bits, row, col0);
-        }
+        store_swap_chunk(a, bits, n, static_cast<int64_t>(w.nt) * BN + c0);
     }
 }
 
 template <int BN, bool SWAP>
-__global__ void __launch_bounds__(kThreadsTc, 1)
+__global__ void __launch_bounds__(kThreadsTc, SWAP ? 2 : 1)
     tc_gemm_kernel(const TcGemmArgs a, const __grid_constant__ CUtensorMap tma,
                    const __grid_constant__ CUtensorMap tmb) {
-    using Cfg = TcCfg<BN>;
+    using Cfg = TcCfg<BN, SWAP>;
     constexpr int S = Cfg::kStages;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -249,6 +273,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         prefetch_tmap(&tma);
         prefetch_tmap(&tmb);
     }
+    // The next launch (if it has a programmatic edge) may start its own
+    // prologue and weight stream while this grid works.
+    griddep_launch_dependents();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -267,41 +294,99 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             uint32_t phase = 0;
             uint32_t issued = 0, issued_parity = 0;
             bool ok = true;
-            for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
-                const Unit w = decode_unit(a, u, num_m, n_tail, num_kb);
-                for (int kb = w.kb0; kb < w.kb1; ++kb) {
-                    if (!mbar_wait(&empty[stage], phase ^ 1u, a.err_flag, kErrTmaWait)) {
-                        ok = false;
-                        break;
-                    }
-                    mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
-                    if (a.w_tiled == nullptr) {
-                        tma_load_2d(sA + stage * Cfg::kABytes, &tma, &full[stage], kb * kBK, w.mt * kBM);
-                        tma_load_2d(sB + stage * Cfg::kBBytes, &tmb, &full[stage], kb * kBK, w.nt * BN);
-                    } else if constexpr (SWAP) {
-                        // W is A: one contiguous, already swizzled 128 x 64 tile.
-                        bulk_load(sA + stage * Cfg::kABytes,
-                                  a.w_tiled + tiled_offset(static_cast<int64_t>(w.mt) * kBM, static_cast<int64_t>(kb) * kBK, a.w_k_tiles),
-                                  Cfg::kABytes, &full[stage]);
-                        tma_load_2d(sB + stage * Cfg::kBBytes, &tmb, &full[stage], kb * kBK, w.nt * BN);
-                    } else {
-                        // W is B: BN rows = BN/128 whole tiles, or half of one for BN = 64.
-                        tma_load_2d(sA + stage * Cfg::kABytes, &tma, &full[stage], kb * kBK, w.mt * kBM);
-                        constexpr int kPieces = BN >= 128 ? BN / 128 : 1;
-                        constexpr uint32_t kPieceBytes = (BN >= 128 ? 128 : BN) * kBK * 2;
+            // The weight half of one ring stage (tiled weights only).
+            auto load_w = [&](const Unit& w, int kb, int st) {
+                if constexpr (SWAP) {
+                    // W is A: one contiguous, already swizzled 128 x 64 tile.
+                    bulk_load(sA + st * Cfg::kABytes,
+                              a.w_tiled + tiled_offset(static_cast<int64_t>(w.mt) * kBM, static_cast<int64_t>(kb) * kBK, a.w_k_tiles),
+                              Cfg::kABytes, &full[st]);
+                } else {
+                    // W is B: BN rows = BN/128 whole tiles, or half of one for BN = 64.
+                    constexpr int kPieces = BN >= 128 ? BN / 128 : 1;
+                    constexpr uint32_t kPieceBytes = (BN >= 128 ? 128 : BN) * kBK * 2;
 #pragma unroll
-                        for (int h = 0; h < kPieces; ++h)
-                            bulk_load(sB + stage * Cfg::kBBytes + h * kPieceBytes,
-                                      a.w_tiled + tiled_offset(static_cast<int64_t>(w.nt) * BN + h * 128,
-                                                               static_cast<int64_t>(kb) * kBK, a.w_k_tiles),
-                                      kPieceBytes, &full[stage]);
+                    for (int h = 0; h < kPieces; ++h)
+                        bulk_load(sB + st * Cfg::kBBytes + h * kPieceBytes,
+                                  a.w_tiled + tiled_offset(static_cast<int64_t>(w.nt) * BN + h * 128,
+                                                           static_cast<int64_t>(kb) * kBK, a.w_k_tiles),
+                                  kPieceBytes, &full[st]);
+                }
+            };
+            // The activation half (always through its tensor map).
+            auto load_x = [&](const Unit& w, int kb, int st) {
+                if constexpr (SWAP) {
+                    tma_load_2d(sB + st * Cfg::kBBytes, &tmb, &full[st], kb * kBK, w.nt * BN);
+                } else {
+                    tma_load_2d(sA + st * Cfg::kABytes, &tma, &full[st], kb * kBK, w.mt * kBM);
+                }
+            };
+            // This CTA's (unit, k-block) sequence.
+            int u = blockIdx.x, kb = 0;
+            Unit w{};
+            if (u < total) {
+                w = decode_unit(a, u, num_m, n_tail, num_kb);
+                kb = w.kb0;
+            }
+            auto advance = [&](int& uu, int& kk, Unit& ww) {
+                if (++kk == ww.kb1) {
+                    uu += gridDim.x;
+                    if (uu < total) {
+                        ww = decode_unit(a, uu, num_m, n_tail, num_kb);
+                        kk = ww.kb0;
                     }
-                    issued |= 1u << stage;
-                    issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+                }
+            };
+            auto claim = [&](int st) {
+                mbar_arrive_expect_tx(&full[st], Cfg::kStageBytes);
+                issued |= 1u << st;
+                issued_parity = (issued_parity & ~(1u << st)) | (phase << st);
+            };
+            // A tiled weight is complete before its upload returns and is never
+            // written again, so the first ring pass of weight tiles is requested
+            // before waiting for the kernel this one overlaps; the activations,
+            // and every global write, come after the wait.
+            int pre = 0;
+            if (a.w_prefetch && a.w_tiled != nullptr) {
+                for (; pre < S && u < total; ++pre) {
+                    claim(stage);  // a fresh ring: no stage to wait for
+                    load_w(w, kb, stage);
+                    advance(u, kb, w);
                     if (++stage == S) {
                         stage = 0;
                         phase ^= 1u;
                     }
+                }
+            }
+            griddep_wait();
+            {
+                int u2 = blockIdx.x, kb2 = 0;
+                Unit w2{};
+                if (pre > 0) {
+                    w2 = decode_unit(a, u2, num_m, n_tail, num_kb);
+                    kb2 = w2.kb0;
+                }
+                for (int i = 0; i < pre; ++i) {
+                    load_x(w2, kb2, i);
+                    advance(u2, kb2, w2);
+                }
+            }
+            for (; u < total; advance(u, kb, w)) {
+                if (!mbar_wait(&empty[stage], phase ^ 1u, a.err_flag, kErrTmaWait)) {
+                    ok = false;
+                    break;
+                }
+                claim(stage);
+                if (a.w_tiled == nullptr) {
+                    tma_load_2d(sA + stage * Cfg::kABytes, &tma, &full[stage], kb * kBK, w.mt * kBM);
+                    tma_load_2d(sB + stage * Cfg::kBBytes, &tmb, &full[stage], kb * kBK, w.nt * BN);
+                } else {
+                    load_w(w, kb, stage);
+                    load_x(w, kb, stage);
+                }
+                if (++stage == S) {
+                    stage = 0;
+                    phase ^= 1u;
                 }
             }
             if (!ok) {
@@ -311,6 +396,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             }
         }
     } else if (warp == 1) {
+        // Bounded waits start only once the kernel this one may overlap is done.
+        griddep_wait();
         if (lane == 0) {
             const uint32_t idesc = idesc_f16_f32(kBM, BN);
             int stage = 0;
@@ -357,6 +444,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         }
     } else {
         const int quad = warp & 3;  // TMEM lanes this warp may read: 32*quad .. +31
+        griddep_wait();  // before any bounded wait and any global write
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int u = blockIdx.x; u < total; u += gridDim.x) {
@@ -373,13 +461,15 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                                    static_cast<uint32_t>(acc * BN);
             if constexpr (SWAP) {
+                // Only the chunks holding real tokens (warp-uniform bound).
+                const int cols = min(BN, a.M - w.nt * BN);
 #pragma unroll 1
-                for (int c = 0; c < BN / 16; ++c) {
+                for (int c = 0; c * 16 < cols; ++c) {
                     uint32_t r[16];
                     __syncwarp();
                     tmem_ld_16cols(t_row + c * 16, r);
                     if (w.slot >= 0) {
-                        store_partial_chunk16(a, r, w.slot, quad * 32 + lane, c * 16, BN);
+                        store_partial_chunk16(a, r, w.slot, quad * 32 + lane, c * 16, BN, min(4, (cols - c * 16 + 3) / 4));
                     } else {
                         store_swap_chunk(a, r, row, static_cast<int64_t>(w.nt) * BN + c * 16);
                     }
@@ -401,7 +491,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             tc_fence_before();
             mbar_arrive(&tempty[acc]);  // the accumulator is free; the fix-up reads global memory only
             if constexpr (SWAP) {
-                if (w.slot >= 0) tail_fixup<BN, SWAP>(a, w, n_tail, quad, lane);
+                if (w.slot >= 0) swap_tail_fixup<BN>(a, w, n_tail, quad, lane);
             }
             acc ^= 1;
             if (acc == 0) acc_phase ^= 1u;
@@ -425,11 +515,28 @@ cudaError_t launch_bn(const TcGemmArgs& a, const CUtensorMap& ta, const CUtensor
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     if (!attr_set[dev]) {
         cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<BN, SWAP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(TcCfg<BN>::kSmem));
+                                             static_cast<int>(TcCfg<BN, SWAP>::kSmem));
+        if (e != cudaSuccess) return e;
+        // All shared memory, no L1 carve-out: every instance then runs under one
+        // SM configuration, so two swap-mode CTAs (of one GEMM and the next)
+        // can share an SM.
+        e = cudaFuncSetAttribute(tc_gemm_kernel<BN, SWAP>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 cudaSharedmemCarveoutMaxShared);
         if (e != cudaSuccess) return e;
         attr_set[dev] = true;
     }
-    tc_gemm_kernel<BN, SWAP><<<a.grid, kThreadsTc, TcCfg<BN>::kSmem, s>>>(a, ta, tb);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(a.grid));
+    cfg.blockDim = dim3(kThreadsTc);
+    cfg.dynamicSmemBytes = TcCfg<BN, SWAP>::kSmem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, SWAP>, a, ta, tb);
+    if (e != cudaSuccess) return e;
     note_launches(1);
     return cudaGetLastError();
 }

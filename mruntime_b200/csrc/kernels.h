@@ -45,6 +45,12 @@ struct TcGemmArgs {
     // Weight in the tiled layout (nullptr: the weight's tensor map is used).
     const uint16_t* w_tiled;
     int64_t w_k_tiles;
+    // Every launch carries a programmatic edge to the previous kernel in the
+    // stream, whose completion the kernel awaits (griddepcontrol.wait) before
+    // it reads activations or writes anything.  1: the first ring pass of
+    // tiled weight tiles may be fetched before that wait (the weights must
+    // not be written by the kernel being overlapped).
+    int w_prefetch;
 };
 cudaError_t launch_tc_gemm(const TcGemmArgs& a, const CUtensorMap& tmap_x, const CUtensorMap& tmap_w,
                            cudaStream_t s);
