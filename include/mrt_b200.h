@@ -337,6 +337,59 @@ int mrt_tp_allgather_cols_f16(mrt_tp tp, const void* local_dev, int64_t M, int64
 int mrt_tp_argmax(mrt_tp tp, const float* val_dev, const int64_t* idx_dev, int64_t M,
                   int64_t* idx_out_dev, void* stream);
 
+/* ------------------------------------------------------------ decoder
+ * Device-resident greedy generation for Qwen2-architecture decoders: the
+ * reference's QwenModel (src/models/qwen/qwen_model.cpp, forward 104-376) run
+ * by InferenceEngine::generate with greedy selection
+ * (src/engine/inference_engine.cpp:26-95).  Weights, KV cache and activations
+ * live in HBM; each decode step after the first is one CUDA-graph replay.
+ * Replaces constructing QwenModel + InferenceEngine over a Backend.
+ */
+typedef struct mrt_decoder_config {
+    int64_t vocab_size;         /* QwenConfig fields (include/mruntime/qwen_model.h) */
+    int64_t hidden_size;
+    int64_t num_layers;
+    int64_t num_attention_heads;
+    int64_t num_kv_heads;
+    int64_t intermediate_size;
+    int64_t max_seq_len;        /* KV-cache capacity: prompt + generated tokens */
+    float rms_norm_eps;
+    float rope_theta;
+} mrt_decoder_config;
+
+typedef struct mrt_decoder_s* mrt_decoder;
+
+typedef struct mrt_decoder_stats {
+    float prefill_ms;       /* batched prompt forward + first greedy pick */
+    float first_step_ms;    /* the first decode step (run eagerly, sizes scratch) */
+    float decode_ms;        /* the remaining decode steps (graph replays) */
+    int64_t decode_steps;   /* number of steps in decode_ms */
+} mrt_decoder_stats;
+
+int mrt_decoder_create(const mrt_decoder_config* cfg, mrt_decoder* out);
+
+/* One checkpoint tensor by its Hugging Face / reference name
+ * (qwen_model.cpp:54-101, 336-353): "model.embed_tokens.weight",
+ * "model.layers.<i>.{input_layernorm,post_attention_layernorm}.weight",
+ * "model.layers.<i>.self_attn.{q,k,v,o}_proj.weight",
+ * "model.layers.<i>.self_attn.{q,k,v}_proj.bias",
+ * "model.layers.<i>.mlp.{gate,up,down}_proj.weight", "model.norm.weight",
+ * "lm_head.weight" (optional: tied to the embedding when absent).  rows x cols
+ * is the tensor's shape (cols = 1 for vectors); dtype FP16/BF16/FP32; src in
+ * host or device memory.  Unknown names are MRT_ERR_INVALID_ARG. */
+int mrt_decoder_load(mrt_decoder d, const char* name, const void* src, int src_dtype, int src_on_device,
+                     int64_t rows, int64_t cols);
+
+/* Greedy generation: prompt[n_prompt] (host) -> out_tokens[max_new] (host),
+ * stopping after eos_token_id (< 0: never); *n_out = tokens written.  Needs
+ * n_prompt + max_new - 1 <= max_seq_len.  Synchronous, like the reference;
+ * stream (may be NULL) is waited on first.  stats may be NULL. */
+int mrt_decoder_generate(mrt_decoder d, const int32_t* prompt, int64_t n_prompt, int64_t max_new,
+                         int32_t eos_token_id, int32_t* out_tokens, int64_t* n_out,
+                         mrt_decoder_stats* stats, void* stream);
+
+void mrt_decoder_free(mrt_decoder d);
+
 #ifdef __cplusplus
 }
 #endif

@@ -37,7 +37,7 @@ class MrtError(RuntimeError):
 def header_functions() -> list[str]:
     """Names of every entry point declared in include/mrt_b200.h."""
     text = open(HEADER).read()
-    return re.findall(r"^\s*(?:int|const char\*)\s+(mrt_\w+)\s*\(", text, flags=re.M)
+    return re.findall(r"^\s*(?:int|void|const char\*)\s+(mrt_\w+)\s*\(", text, flags=re.M)
 
 
 _vp, _i64, _int, _u32, _sz = C.c_void_p, C.c_int64, C.c_int, C.c_uint, C.c_size_t
@@ -89,6 +89,10 @@ _SIGS = {
     "mrt_tp_allreduce_f32_to_f16": (_int, [_vp, _vp, _vp, _i64, _vp]),
     "mrt_tp_allgather_cols_f16": (_int, [_vp, _vp, _i64, _i64, _vp, _vp]),
     "mrt_tp_argmax": (_int, [_vp, _vp, _vp, _i64, _vp, _vp]),
+    "mrt_decoder_create": (_int, [_vp, C.POINTER(_vp)]),
+    "mrt_decoder_load": (_int, [_vp, C.c_char_p, _vp, _int, _int, _i64, _i64]),
+    "mrt_decoder_generate": (_int, [_vp, _vp, _i64, _i64, C.c_int32, _vp, C.POINTER(_i64), _vp, _vp]),
+    "mrt_decoder_free": (None, [_vp]),
 }
 
 
@@ -278,3 +282,59 @@ class TensorParallel:
         if self.h:
             lib().mrt_tp_destroy(self.h)
             self.h = None
+
+
+class DecoderConfig(C.Structure):
+    """mrt_decoder_config (the reference's QwenConfig fields plus the KV capacity)."""
+
+    _fields_ = [("vocab_size", C.c_int64), ("hidden_size", C.c_int64), ("num_layers", C.c_int64),
+                ("num_attention_heads", C.c_int64), ("num_kv_heads", C.c_int64),
+                ("intermediate_size", C.c_int64), ("max_seq_len", C.c_int64), ("rms_norm_eps", C.c_float),
+                ("rope_theta", C.c_float)]
+
+
+class DecoderStats(C.Structure):
+    _fields_ = [("prefill_ms", C.c_float), ("first_step_ms", C.c_float), ("decode_ms", C.c_float),
+                ("decode_steps", C.c_int64)]
+
+
+class Decoder:
+    """Device-resident greedy decoder (mrt_decoder_*): load tensors by their
+    checkpoint names, then generate."""
+
+    def __init__(self, hf_config: dict, max_seq_len: int):
+        cfg = DecoderConfig(hf_config["vocab_size"], hf_config["hidden_size"], hf_config["num_hidden_layers"],
+                            hf_config["num_attention_heads"], hf_config["num_key_value_heads"],
+                            hf_config["intermediate_size"], max_seq_len, hf_config.get("rms_norm_eps", 1e-6),
+                            hf_config.get("rope_theta", 10000.0) or 10000.0)
+        h = C.c_void_p()
+        call("mrt_decoder_create", C.byref(cfg), C.byref(h))
+        self.h = h
+
+    def load(self, name: str, ptr: int, dtype: int, on_device: bool, shape) -> None:
+        rows = int(shape[0])
+        cols = int(shape[1]) if len(shape) > 1 else 1
+        call("mrt_decoder_load", self.h, name.encode(), ptr, dtype, int(on_device), rows, cols)
+
+    def generate(self, prompt, max_new: int, eos: int = -1, stream: int | None = None):
+        """Returns (generated ids, DecoderStats)."""
+        import numpy as np
+
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.zeros(max(max_new, 1), dtype=np.int32)
+        n = C.c_int64()
+        st = DecoderStats()
+        call("mrt_decoder_generate", self.h, p.ctypes.data, len(p), max_new, eos, out.ctypes.data, C.byref(n),
+             C.byref(st), stream)
+        return out[: n.value].tolist(), st
+
+    def free(self):
+        if self.h:
+            lib().mrt_decoder_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass

@@ -176,6 +176,8 @@ extern "C" int mrt_sync(void* stream) {
         cudaMemset(c->d_err, 0, sizeof(int));
         // A kernel that gave up may have left K-split tile counters counted.
         if (c->counters != nullptr) cudaMemset(c->counters, 0, c->counters_bytes);
+        if (flag == 6)  // kErrBadToken: the decoder's embedding met an id outside the vocabulary
+            return set_error(MRT_ERR_INVALID_ARG, "embedding_lookup: token_id out of range (device error code 6)");
         static const char* what[] = {"", "TMA producer", "MMA issuer", "epilogue", "clean-up", "wait self-test"};
         return set_error(MRT_ERR_TIMEOUT, std::string("a kernel wait timed out in the ") +
                                               (flag > 0 && flag < 6 ? what[flag] : "kernel") +

@@ -21,6 +21,7 @@ enum : int {
     kErrEpiWait = 3,   // epilogue gave up waiting for a finished accumulator
     kErrDrainWait = 4, // clean-up wait for in-flight copies/MMAs gave up
     kErrSelfTest = 5,  // mrt_selftest_wait_timeout's wait gave up (expected)
+    kErrBadToken = 6,  // the decoder's embedding met a token id outside the vocabulary
 };
 
 // Wall-clock limit of one bounded wait, in nanoseconds of %globaltimer.

@@ -1,0 +1,873 @@
+// decoder.cu -- device-resident greedy generation for Qwen2-architecture
+// decoders: the reference's QwenModel::forward (src/models/qwen/qwen_model.cpp:
+// 104-376) driven by InferenceEngine::generate's greedy path
+// (src/engine/inference_engine.cpp:26-95), with every tensor resident in HBM.
+//
+// Layout in HBM:
+//   weights    per layer: q|k|v rows fused into one tiled weight with the
+//              three biases attached (FP16, the reference's double rounding),
+//              o, gate|up fused, down; lm_head tiled; the embedding table as a
+//              row-major FP16 copy; RMSNorm gains in their source dtype.
+//   KV cache   K and V [layer][kv_head][max_seq][head_dim] FP16 -- the
+//              reference's KVCache layout (qwen_model.cpp:37-52).
+//   activations [S, width] FP16 rows, reused across layers.
+//   state      {position, step, current token} on the device, so one
+//              captured decode step (a CUDA graph) replays for every token
+//              without a host round trip; generated ids go to a device array.
+//
+// Per layer: add+RMSNorm (the previous layer's residual), q|k|v GEMM with
+// bias, RoPE + KV append, attention, o GEMM, add+RMSNorm, gate|up GEMM,
+// SiLU*up, down GEMM; then the final add+RMSNorm, lm_head on the last row and
+// the greedy pick.  Every small kernel waits (griddepcontrol.wait) for the
+// kernel before it before touching memory and lets the next launch start at
+// once, so each GEMM's weight stream begins while the small kernel runs.
+//
+// Rounding points are the reference's: every op reads FP16 and writes FP16,
+// computing in FP32 with its operand order (no fused multiply-adds).  The
+// reductions (RMSNorm's sum of squares, attention) are summed in a
+// different order than the reference's sequential loops, so results agree
+// within FP32 rounding, not bit for bit.
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "ctx.h"
+#include "kernels.h"
+
+namespace mrt {
+
+const uint16_t* silu_lut_for_device(int device);
+
+namespace {
+
+constexpr int kNT = 256;
+
+struct DecState {
+    int32_t pos;    // position of the first row of the current forward
+    int32_t step;   // generated tokens so far
+    int32_t token;  // last generated token
+    int32_t pad;
+};
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
+    if (e == cudaSuccess) note_launches(1);
+    return e;
+}
+
+__device__ __forceinline__ float ldw(const void* p, int dt, int64_t i) {
+    if (dt == MRT_FP32) return static_cast<const float*>(p)[i];
+    const uint16_t v = static_cast<const uint16_t*>(p)[i];
+    return dt == MRT_BF16 ? bf16_bits_to_f32(v) : f16_bits_to_f32(v);
+}
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float t = 0.0f;
+    for (int w = 0; w < kNT / 32; ++w) t = __fadd_rn(t, red[w]);
+    return t;
+}
+
+// RMSNorm of one FP16 row held in shared memory (cpu_backend.cpp:292-330):
+// rms = sqrt(sum(x^2) / n + eps); out = fp16((x * (1 / rms)) * w).
+__device__ void norm_row(const float* row, int64_t H, const void* w, int wdt, float eps, uint16_t* out, float* red) {
+    float s = 0.0f;
+    for (int64_t i = threadIdx.x; i < H; i += kNT) s = __fadd_rn(s, __fmul_rn(row[i], row[i]));
+    const float total = block_sum(s, red);
+    const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(H)), eps));
+    const float inv = __fdiv_rn(1.0f, rms);
+    for (int64_t i = threadIdx.x; i < H; i += kNT) out[i] = f32_to_f16_bits(__fmul_rn(__fmul_rn(row[i], inv), ldw(w, wdt, i)));
+}
+
+// Row s: hidden = table[id] (qwen_model.cpp:59-64), normed = RMSNorm(hidden).
+// ids == nullptr: the id is the state's current token.
+__global__ void embed_norm_kernel(const uint16_t* table, int64_t vocab, int64_t H, const int32_t* ids,
+                                  const DecState* st, uint16_t* hidden, const void* w, int wdt, float eps,
+                                  uint16_t* normed, int* err) {
+    griddep_wait();
+    griddep_launch_dependents();
+    extern __shared__ float row[];
+    __shared__ float red[kNT / 32];
+    const int64_t s = blockIdx.x;
+    int64_t id = ids != nullptr ? ids[s] : st->token;
+    if (id < 0 || id >= vocab) {
+        if (threadIdx.x == 0) raise_error(err, kErrBadToken);
+        id = 0;
+    }
+    for (int64_t i = threadIdx.x; i < H; i += kNT) {
+        const uint16_t v = table[id * H + i];
+        hidden[s * H + i] = v;
+        row[i] = f16_bits_to_f32(v);
+    }
+    __syncthreads();
+    norm_row(row, H, w, wdt, eps, normed + s * H, red);
+}
+
+// Row s: out = fp16(a + b) (cpu_backend.cpp:403-455), normed = RMSNorm(out).
+__global__ void add_norm_kernel(const uint16_t* a, const uint16_t* b, uint16_t* out, int64_t H, const void* w,
+                                int wdt, float eps, uint16_t* normed) {
+    griddep_wait();
+    griddep_launch_dependents();
+    extern __shared__ float row[];
+    __shared__ float red[kNT / 32];
+    const int64_t s = blockIdx.x;
+    for (int64_t i = threadIdx.x; i < H; i += kNT) {
+        const uint16_t r = f32_to_f16_bits(__fadd_rn(f16_bits_to_f32(a[s * H + i]), f16_bits_to_f32(b[s * H + i])));
+        out[s * H + i] = r;
+        row[i] = f16_bits_to_f32(r);
+    }
+    __syncthreads();
+    norm_row(row, H, w, wdt, eps, normed + s * H, red);
+}
+
+// RoPE on the q and k heads of S rows (cpu_backend.cpp:332-379, cos/sin from
+// a host table built with the reference's expressions) and the KV-cache append
+// (qwen_model.cpp:162-205): q is rotated in place, the rotated k and the v row
+// go to cache position pos + s.  One thread per rotation pair.
+__global__ void rope_append_kernel(uint16_t* qkv, int64_t ldq, int64_t S, int heads, int kv_heads, int D,
+                                   const float* cos_t, const float* sin_t, uint16_t* kc, uint16_t* vc,
+                                   int64_t max_seq, const DecState* st) {
+    griddep_wait();
+    griddep_launch_dependents();
+    const int half = D / 2;
+    const int64_t per_row = static_cast<int64_t>(heads + kv_heads) * half;
+    const int64_t total = S * per_row;
+    const int64_t pos0 = st->pos;
+    for (int64_t e = blockIdx.x * static_cast<int64_t>(kNT) + threadIdx.x; e < total;
+         e += static_cast<int64_t>(gridDim.x) * kNT) {
+        const int64_t s = e / per_row;
+        const int64_t r = e % per_row;
+        const int hh = static_cast<int>(r / half);
+        const int i = static_cast<int>(r % half);
+        const int64_t pos = pos0 + s;
+        if (pos >= max_seq) continue;  // the host checks lengths; never write past the cache
+        const float c = cos_t[pos * half + i], sn = sin_t[pos * half + i];
+        uint16_t* x = qkv + s * ldq + static_cast<int64_t>(hh) * D;
+        const float x0 = f16_bits_to_f32(x[i]);
+        const float x1 = f16_bits_to_f32(x[i + half]);
+        const uint16_t y0 = f32_to_f16_bits(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
+        const uint16_t y1 = f32_to_f16_bits(__fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c)));
+        if (hh < heads) {
+            x[i] = y0;
+            x[i + half] = y1;
+        } else {
+            const int g = hh - heads;
+            const int64_t slot = (static_cast<int64_t>(g) * max_seq + pos) * D;
+            kc[slot + i] = y0;
+            kc[slot + i + half] = y1;
+            const uint16_t* v = qkv + s * ldq + static_cast<int64_t>(heads + kv_heads + g) * D;
+            vc[slot + i] = v[i];
+            vc[slot + i + half] = v[i + half];
+        }
+    }
+}
+
+constexpr int kAttnWarps = 4;
+constexpr int kMaxPerLane = 8;  // head_dim <= 256
+
+// Decode attention for one query row (cpu_backend.cpp:171-290 with
+// q_len = 1): block (h, split) scores keys [k0, k1) of kv head h / group with an
+// online softmax per warp, merges its warps, and writes (max, sum, acc[D]) to
+// `part`; the last split block of a head to finish merges the splits in order
+// and writes out = fp16(acc * (1 / sum)).  kv_len = state position + 1.
+__global__ void __launch_bounds__(kAttnWarps * 32)
+    attn_decode_kernel(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, uint16_t* out, int heads,
+                       int group, int D, int64_t max_seq, float scale, const DecState* st, float* part,
+                       int* counters) {
+    griddep_wait();
+    griddep_launch_dependents();
+    __shared__ float sm_m[kAttnWarps], sm_l[kAttnWarps];
+    __shared__ float sm_acc[kAttnWarps][256];
+    __shared__ int sm_last;
+    const int h = blockIdx.x, sp = blockIdx.y, nsplit = gridDim.y;
+    const int g = h / group;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int per = D / 32;
+    int64_t kv_len = static_cast<int64_t>(st->pos) + 1;
+    if (kv_len > max_seq) kv_len = max_seq;
+    const int64_t chunk = (kv_len + nsplit - 1) / nsplit;
+    const int64_t k0 = sp * chunk;
+    const int64_t k1 = k0 + chunk < kv_len ? k0 + chunk : kv_len;
+    float qv[kMaxPerLane];
+#pragma unroll
+    for (int j = 0; j < kMaxPerLane; ++j) qv[j] = j < per ? f16_bits_to_f32(q[static_cast<int64_t>(h) * D + lane * per + j]) : 0.0f;
+    const uint16_t* kb = kc + static_cast<int64_t>(g) * max_seq * D;
+    const uint16_t* vb = vc + static_cast<int64_t>(g) * max_seq * D;
+    float m = -INFINITY, l = 0.0f, acc[kMaxPerLane];
+#pragma unroll
+    for (int j = 0; j < kMaxPerLane; ++j) acc[j] = 0.0f;
+    for (int64_t k = k0 + warp; k < k1; k += kAttnWarps) {
+        float d = 0.0f;
+#pragma unroll
+        for (int j = 0; j < kMaxPerLane; ++j)
+            if (j < per) d = __fadd_rn(d, __fmul_rn(qv[j], f16_bits_to_f32(kb[k * D + lane * per + j])));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) d = __fadd_rn(d, __shfl_xor_sync(0xFFFFFFFFu, d, o));
+        const float sc = __fmul_rn(d, scale);
+        const float m_new = fmaxf(m, sc);
+        const float corr = expf(__fsub_rn(m, m_new));
+        const float p = expf(__fsub_rn(sc, m_new));
+        l = __fadd_rn(__fmul_rn(l, corr), p);
+#pragma unroll
+        for (int j = 0; j < kMaxPerLane; ++j)
+            if (j < per)
+                acc[j] = __fadd_rn(__fmul_rn(acc[j], corr), __fmul_rn(p, f16_bits_to_f32(vb[k * D + lane * per + j])));
+        m = m_new;
+    }
+    if (lane == 0) {
+        sm_m[warp] = m;
+        sm_l[warp] = l;
+    }
+#pragma unroll
+    for (int j = 0; j < kMaxPerLane; ++j)
+        if (j < per) sm_acc[warp][lane * per + j] = acc[j];
+    __syncthreads();
+    // Merge the warps: thread t owns dimension t (and t + 128).
+    float M = -INFINITY;
+    for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, sm_m[w]);
+    float* dst = part + (static_cast<int64_t>(h) * nsplit + sp) * (D + 2);
+    if (threadIdx.x == 0) {
+        float L = 0.0f;
+        for (int w = 0; w < kAttnWarps; ++w)
+            if (sm_m[w] != -INFINITY) L = __fadd_rn(L, __fmul_rn(sm_l[w], expf(__fsub_rn(sm_m[w], M))));
+        dst[0] = M;
+        dst[1] = L;
+    }
+    for (int d = threadIdx.x; d < D; d += kAttnWarps * 32) {
+        float A = 0.0f;
+        for (int w = 0; w < kAttnWarps; ++w)
+            if (sm_m[w] != -INFINITY) A = __fadd_rn(A, __fmul_rn(sm_acc[w][d], expf(__fsub_rn(sm_m[w], M))));
+        dst[2 + d] = A;
+    }
+    // The last split of this head to arrive merges all splits in split order.
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const int prev = atomicAdd(&counters[h], 1);
+        sm_last = prev == nsplit - 1;
+        if (sm_last) counters[h] = 0;
+    }
+    __syncthreads();
+    if (!sm_last) return;
+    __threadfence();
+    const float* ph = part + static_cast<int64_t>(h) * nsplit * (D + 2);
+    float MM = -INFINITY;
+    for (int s2 = 0; s2 < nsplit; ++s2) MM = fmaxf(MM, ph[s2 * (D + 2)]);
+    float LL = 0.0f;
+    for (int s2 = 0; s2 < nsplit; ++s2) {
+        const float ms = ph[s2 * (D + 2)];
+        if (ms != -INFINITY) LL = __fadd_rn(LL, __fmul_rn(ph[s2 * (D + 2) + 1], expf(__fsub_rn(ms, MM))));
+    }
+    const float inv = __fdiv_rn(1.0f, LL);
+    for (int d = threadIdx.x; d < D; d += kAttnWarps * 32) {
+        float A = 0.0f;
+        for (int s2 = 0; s2 < nsplit; ++s2) {
+            const float ms = ph[s2 * (D + 2)];
+            if (ms != -INFINITY) A = __fadd_rn(A, __fmul_rn(ph[s2 * (D + 2) + 2 + d], expf(__fsub_rn(ms, MM))));
+        }
+        out[static_cast<int64_t>(h) * D + d] = f32_to_f16_bits(__fmul_rn(A, inv));
+    }
+}
+
+// act = fp16(silu(gate) * up) with silu from the FP16 table
+// (qwen_model.cpp:281-285: silu rounded to FP16, then the product rounded).
+__global__ void silu_mul_kernel(const uint16_t* gu, int64_t ld, int64_t I, int64_t S, const uint16_t* lut,
+                                uint16_t* act) {
+    griddep_wait();
+    griddep_launch_dependents();
+    const int64_t total = S * I;
+    for (int64_t e = blockIdx.x * static_cast<int64_t>(kNT) + threadIdx.x; e < total;
+         e += static_cast<int64_t>(gridDim.x) * kNT) {
+        const int64_t s = e / I, i = e % I;
+        const float a = f16_bits_to_f32(lut[gu[s * ld + i]]);
+        const float u = f16_bits_to_f32(gu[s * ld + I + i]);
+        act[e] = f32_to_f16_bits(__fmul_rn(a, u));
+    }
+}
+
+// After the greedy pick of a forward over `rows` tokens: record the token and
+// move the state to the next position.
+__global__ void advance_kernel(const int64_t* idx, DecState* st, int32_t* tokens, int64_t max_tokens, int rows) {
+    griddep_wait();
+    griddep_launch_dependents();
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    const int32_t t = static_cast<int32_t>(idx[0]);
+    if (st->step < max_tokens) tokens[st->step] = t;
+    st->step += 1;
+    st->token = t;
+    st->pos += rows;
+}
+
+}  // namespace
+}  // namespace mrt
+
+using namespace mrt;
+
+namespace {
+
+struct DecLayer {
+    mrt_weight qkv = nullptr, o = nullptr, gateup = nullptr, down = nullptr;
+    void* ln1 = nullptr;
+    int ln1_dt = MRT_FP16;
+    void* ln2 = nullptr;
+    int ln2_dt = MRT_FP16;
+    bool qkv_bias = false;
+    // FP16 staging of the fused weights until every part has arrived.
+    uint16_t* st_qkv = nullptr;
+    uint32_t qkv_have = 0;  // bit 0 q, 1 k, 2 v
+    uint16_t* st_bias = nullptr;
+    uint32_t bias_have = 0;
+    uint16_t* st_gu = nullptr;
+    uint32_t gu_have = 0;  // bit 0 gate, 1 up
+};
+
+}  // namespace
+
+struct mrt_decoder_s {
+    int device = 0;
+    mrt_decoder_config cfg{};
+    int64_t H = 0, D = 0, heads = 0, kvh = 0, I = 0, V = 0, L = 0, max_seq = 0, n_qkv = 0;
+    std::vector<DecLayer> layers;
+    uint16_t* embed = nullptr;  // [V, H] FP16 row-major
+    mrt_weight lm_head = nullptr;
+    void* norm = nullptr;
+    int norm_dt = MRT_FP16;
+    bool ready = false;
+    // activations and state (allocated by finalize)
+    uint16_t *x = nullptr, *r = nullptr, *p = nullptr, *normed = nullptr, *qkv = nullptr, *attn = nullptr,
+             *gu = nullptr, *act = nullptr, *logits = nullptr, *kc = nullptr, *vc = nullptr;
+    float *cos_t = nullptr, *sin_t = nullptr, *part = nullptr, *am_val = nullptr;
+    int* counters = nullptr;
+    int64_t* am_idx = nullptr;
+    void* am_scratch = nullptr;
+    DecState* state = nullptr;
+    int32_t* tokens = nullptr;
+    int64_t tokens_cap = 0;
+    int32_t* ids = nullptr;
+    int64_t ids_cap = 0;
+    int nsplit = 1;
+    cudaStream_t stream = nullptr;
+    std::vector<void*> allocs;
+};
+
+namespace {
+
+int dec_alloc(mrt_decoder d, void** p, size_t bytes, const char* what) {
+    cudaError_t e = cudaMalloc(p, bytes < 16 ? 16 : bytes);
+    if (e != cudaSuccess) return cuda_error(e, what);
+    d->allocs.push_back(*p);
+    return MRT_OK;
+}
+
+void dec_release(mrt_decoder d, void* p) {
+    if (p == nullptr) return;
+    for (auto& a : d->allocs)
+        if (a == p) a = nullptr;
+    cudaFree(p);
+}
+
+size_t es_of(int dt) { return dt == MRT_FP32 ? 4 : 2; }
+
+// n elements of a host or device source of dtype dt into FP16 device memory,
+// rounded once by the reference's converter rule.
+int to_f16(const void* src, int dt, bool on_dev, int64_t n, uint16_t* dst, cudaStream_t s) {
+    if (dt == MRT_FP16) {
+        cudaError_t e = cudaMemcpyAsync(dst, src, static_cast<size_t>(n) * 2,
+                                        on_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        return e == cudaSuccess ? MRT_OK : cuda_error(e, "copying a decoder tensor");
+    }
+    const void* dsrc = src;
+    void* tmp = nullptr;
+    if (!on_dev) {
+        cudaError_t e = cudaMalloc(&tmp, static_cast<size_t>(n) * es_of(dt));
+        if (e == cudaSuccess) e = cudaMemcpy(tmp, src, static_cast<size_t>(n) * es_of(dt), cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) {
+            if (tmp) cudaFree(tmp);
+            return cuda_error(e, "staging a decoder tensor");
+        }
+        dsrc = tmp;
+    }
+    int rc = mrt_convert(dsrc, dt, dst, MRT_FP16, n, s);
+    cudaError_t e = cudaStreamSynchronize(s);
+    if (tmp) cudaFree(tmp);
+    if (rc != MRT_OK) return rc;
+    return e == cudaSuccess ? MRT_OK : cuda_error(e, "converting a decoder tensor");
+}
+
+// A copy of a small tensor in its own dtype (RMSNorm gains).
+int to_native(mrt_decoder d, const void* src, int dt, bool on_dev, int64_t n, void** out) {
+    int rc = dec_alloc(d, out, static_cast<size_t>(n) * es_of(dt), "allocating a norm weight");
+    if (rc != MRT_OK) return rc;
+    cudaError_t e = cudaMemcpy(*out, src, static_cast<size_t>(n) * es_of(dt),
+                               on_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice);
+    return e == cudaSuccess ? MRT_OK : cuda_error(e, "copying a norm weight");
+}
+
+int upload_f16(const uint16_t* dev, int64_t N, int64_t K, cudaStream_t s, mrt_weight* w) {
+    return mrt_weight_upload(dev, MRT_FP16, 1, N, K, nullptr, 0, 0, K, s, w);
+}
+
+bool parse_layer(const std::string& name, int64_t* layer, std::string* suffix) {
+    const std::string pre = "model.layers.";
+    if (name.compare(0, pre.size(), pre) != 0) return false;
+    size_t i = pre.size(), j = i;
+    while (j < name.size() && name[j] >= '0' && name[j] <= '9') ++j;
+    if (j == i || j >= name.size() || name[j] != '.') return false;
+    *layer = std::stoll(name.substr(i, j - i));
+    *suffix = name.substr(j + 1);
+    return true;
+}
+
+}  // namespace
+
+extern "C" int mrt_decoder_create(const mrt_decoder_config* cfg, mrt_decoder* out) {
+    clear_error();
+    if (out == nullptr || cfg == nullptr) return set_error(MRT_ERR_INVALID_ARG, "NULL config or out");
+    *out = nullptr;
+    const mrt_decoder_config& c = *cfg;
+    if (c.vocab_size <= 0 || c.hidden_size <= 0 || c.num_layers <= 0 || c.num_attention_heads <= 0 ||
+        c.num_kv_heads <= 0 || c.intermediate_size <= 0 || c.max_seq_len <= 0)
+        return set_error(MRT_ERR_SHAPE, "decoder sizes must be positive");
+    if (c.hidden_size % c.num_attention_heads != 0 || c.num_attention_heads % c.num_kv_heads != 0)
+        return set_error(MRT_ERR_SHAPE, "hidden_size must split into heads and heads into kv groups");
+    const int64_t D = c.hidden_size / c.num_attention_heads;
+    if (D % 32 != 0 || D > 256) return set_error(MRT_ERR_UNSUPPORTED, "head_dim must be a multiple of 32, at most 256");
+    if (c.hidden_size % 8 != 0 || c.intermediate_size % 8 != 0)
+        return set_error(MRT_ERR_UNSUPPORTED, "hidden and intermediate sizes must be multiples of 8");
+    if (c.hidden_size > 16384) return set_error(MRT_ERR_UNSUPPORTED, "hidden_size above 16384");
+    if (c.max_seq_len > (int64_t{1} << 30)) return set_error(MRT_ERR_SHAPE, "max_seq_len too large");
+    DevCtx* ctx = current_ctx();
+    if (!ctx) return MRT_ERR_CUDA;
+    mrt_decoder d = new mrt_decoder_s();
+    d->device = ctx->device;
+    d->cfg = c;
+    d->H = c.hidden_size;
+    d->D = D;
+    d->heads = c.num_attention_heads;
+    d->kvh = c.num_kv_heads;
+    d->I = c.intermediate_size;
+    d->V = c.vocab_size;
+    d->L = c.num_layers;
+    d->max_seq = c.max_seq_len;
+    d->n_qkv = d->H + 2 * d->kvh * D;
+    d->layers.resize(static_cast<size_t>(d->L));
+    cudaError_t e = cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+        delete d;
+        return cuda_error(e, "creating the decoder stream");
+    }
+    *out = d;
+    return MRT_OK;
+}
+
+extern "C" int mrt_decoder_load(mrt_decoder d, const char* name_c, const void* src, int dt, int on_dev, int64_t rows,
+                                int64_t cols) {
+    clear_error();
+    if (d == nullptr || name_c == nullptr || src == nullptr) return set_error(MRT_ERR_INVALID_ARG, "NULL argument");
+    if (dt != MRT_FP16 && dt != MRT_BF16 && dt != MRT_FP32) return set_error(MRT_ERR_DTYPE, "dtype must be FP16, BF16 or FP32");
+    if (d->ready) return set_error(MRT_ERR_INVALID_ARG, "the decoder has already run; load every tensor first");
+    const std::string name(name_c);
+    cudaStream_t s = d->stream;
+    const int64_t H = d->H, D = d->D, kv = d->kvh * D, I = d->I;
+    auto shape = [&](int64_t r, int64_t k) -> int {
+        if (rows != r || cols != k)
+            return set_error(MRT_ERR_SHAPE, name + ": expected " + std::to_string(r) + " x " + std::to_string(k) + ", got " +
+                                                std::to_string(rows) + " x " + std::to_string(cols));
+        return MRT_OK;
+    };
+    int rc;
+    if (name == "model.embed_tokens.weight") {
+        if ((rc = shape(d->V, H)) != MRT_OK) return rc;
+        if (d->embed == nullptr &&
+            (rc = dec_alloc(d, reinterpret_cast<void**>(&d->embed), static_cast<size_t>(d->V * H) * 2, "allocating the embedding")) != MRT_OK)
+            return rc;
+        return to_f16(src, dt, on_dev != 0, d->V * H, d->embed, s);
+    }
+    if (name == "lm_head.weight") {
+        if ((rc = shape(d->V, H)) != MRT_OK) return rc;
+        if (d->lm_head) mrt_weight_free(d->lm_head);
+        d->lm_head = nullptr;
+        return mrt_weight_upload(src, dt, on_dev, d->V, H, nullptr, 0, 0, H, s, &d->lm_head);
+    }
+    if (name == "model.norm.weight") {
+        if ((rc = shape(H, 1)) != MRT_OK) return rc;
+        dec_release(d, d->norm);
+        d->norm_dt = dt;
+        return to_native(d, src, dt, on_dev != 0, H, &d->norm);
+    }
+    int64_t li = -1;
+    std::string suf;
+    if (!parse_layer(name, &li, &suf) || li < 0 || li >= d->L)
+        return set_error(MRT_ERR_INVALID_ARG, "unknown decoder tensor '" + name + "'");
+    DecLayer& ly = d->layers[static_cast<size_t>(li)];
+    if (suf == "input_layernorm.weight" || suf == "post_attention_layernorm.weight") {
+        if ((rc = shape(H, 1)) != MRT_OK) return rc;
+        const bool first = suf[0] == 'i';
+        void*& p = first ? ly.ln1 : ly.ln2;
+        dec_release(d, p);
+        p = nullptr;
+        (first ? ly.ln1_dt : ly.ln2_dt) = dt;
+        return to_native(d, src, dt, on_dev != 0, H, &p);
+    }
+    if (suf == "self_attn.o_proj.weight" || suf == "mlp.down_proj.weight") {
+        const bool o = suf[0] == 's';
+        if ((rc = o ? shape(H, H) : shape(H, I)) != MRT_OK) return rc;
+        mrt_weight& w = o ? ly.o : ly.down;
+        if (w) mrt_weight_free(w);
+        w = nullptr;
+        return mrt_weight_upload(src, dt, on_dev, H, o ? H : I, nullptr, 0, 0, o ? H : I, s, &w);
+    }
+    // q|k|v rows [0, H), [H, H + kv), [H + kv, H + 2 kv) of one weight.
+    static const char* qkv_w[3] = {"self_attn.q_proj.weight", "self_attn.k_proj.weight", "self_attn.v_proj.weight"};
+    static const char* qkv_b[3] = {"self_attn.q_proj.bias", "self_attn.k_proj.bias", "self_attn.v_proj.bias"};
+    const int64_t off[3] = {0, H, H + kv}, len[3] = {H, kv, kv};
+    for (int part = 0; part < 3; ++part) {
+        if (suf == qkv_w[part]) {
+            if ((rc = shape(len[part], H)) != MRT_OK) return rc;
+            if (ly.qkv != nullptr) return set_error(MRT_ERR_INVALID_ARG, name + ": the fused q|k|v weight is already built");
+            if (ly.st_qkv == nullptr &&
+                (rc = dec_alloc(d, reinterpret_cast<void**>(&ly.st_qkv), static_cast<size_t>(d->n_qkv * H) * 2, "staging q|k|v")) != MRT_OK)
+                return rc;
+            if ((rc = to_f16(src, dt, on_dev != 0, len[part] * H, ly.st_qkv + off[part] * H, s)) != MRT_OK) return rc;
+            ly.qkv_have |= 1u << part;
+            if (ly.qkv_have == 7u) {
+                rc = upload_f16(ly.st_qkv, d->n_qkv, H, s, &ly.qkv);
+                dec_release(d, ly.st_qkv);
+                ly.st_qkv = nullptr;
+                return rc;
+            }
+            return MRT_OK;
+        }
+        if (suf == qkv_b[part]) {
+            if ((rc = shape(len[part], 1)) != MRT_OK) return rc;
+            if (ly.st_bias == nullptr &&
+                (rc = dec_alloc(d, reinterpret_cast<void**>(&ly.st_bias), static_cast<size_t>(d->n_qkv) * 2, "staging q|k|v biases")) != MRT_OK)
+                return rc;
+            // The reference converts biases to FP16 at load (qwen_model.cpp:93-101).
+            if ((rc = to_f16(src, dt, on_dev != 0, len[part], ly.st_bias + off[part], s)) != MRT_OK) return rc;
+            ly.bias_have |= 1u << part;
+            return MRT_OK;
+        }
+    }
+    if (suf == "mlp.gate_proj.weight" || suf == "mlp.up_proj.weight") {
+        const int part = suf[4] == 'g' ? 0 : 1;
+        if ((rc = shape(I, H)) != MRT_OK) return rc;
+        if (ly.gateup != nullptr) return set_error(MRT_ERR_INVALID_ARG, name + ": the fused gate|up weight is already built");
+        if (ly.st_gu == nullptr &&
+            (rc = dec_alloc(d, reinterpret_cast<void**>(&ly.st_gu), static_cast<size_t>(2 * I * H) * 2, "staging gate|up")) != MRT_OK)
+            return rc;
+        if ((rc = to_f16(src, dt, on_dev != 0, I * H, ly.st_gu + part * I * H, s)) != MRT_OK) return rc;
+        ly.gu_have |= 1u << part;
+        if (ly.gu_have == 3u) {
+            rc = upload_f16(ly.st_gu, 2 * I, H, s, &ly.gateup);
+            dec_release(d, ly.st_gu);
+            ly.st_gu = nullptr;
+            return rc;
+        }
+        return MRT_OK;
+    }
+    return set_error(MRT_ERR_INVALID_ARG, "unknown decoder tensor '" + name + "'");
+}
+
+namespace {
+
+// Checks every tensor is present, ties lm_head to the embedding when absent,
+// and allocates the KV cache, activations, RoPE tables and scratch.
+int dec_finalize(mrt_decoder d) {
+    if (d->ready) return MRT_OK;
+    if (d->embed == nullptr) return set_error(MRT_ERR_INVALID_ARG, "model.embed_tokens.weight was not loaded");
+    if (d->norm == nullptr) return set_error(MRT_ERR_INVALID_ARG, "model.norm.weight was not loaded");
+    for (int64_t l = 0; l < d->L; ++l) {
+        DecLayer& ly = d->layers[static_cast<size_t>(l)];
+        const std::string p = "model.layers." + std::to_string(l) + ".";
+        if (!ly.ln1 || !ly.ln2) return set_error(MRT_ERR_INVALID_ARG, p + "*_layernorm.weight missing");
+        if (!ly.qkv) return set_error(MRT_ERR_INVALID_ARG, p + "self_attn.{q,k,v}_proj.weight missing");
+        if (!ly.o || !ly.down) return set_error(MRT_ERR_INVALID_ARG, p + "o_proj / down_proj weight missing");
+        if (!ly.gateup) return set_error(MRT_ERR_INVALID_ARG, p + "mlp.{gate,up}_proj.weight missing");
+        if (ly.bias_have != 0 && ly.bias_have != 7u)
+            return set_error(MRT_ERR_INVALID_ARG, p + "self_attn: only some of the q/k/v biases were loaded");
+        if (ly.bias_have == 7u && !ly.qkv_bias) {
+            int rc = mrt_weight_attach_bias(ly.qkv, ly.st_bias, MRT_FP16, 1, d->stream);
+            if (rc != MRT_OK) return rc;
+            ly.qkv_bias = true;
+            dec_release(d, ly.st_bias);
+            ly.st_bias = nullptr;
+        }
+    }
+    if (d->lm_head == nullptr) {
+        // Tied embeddings (qwen_model.cpp:346-352).
+        int rc = upload_f16(d->embed, d->V, d->H, d->stream, &d->lm_head);
+        if (rc != MRT_OK) return rc;
+    }
+    const int64_t S = d->max_seq, H = d->H, D = d->D;
+    int rc;
+    auto act = [&](uint16_t** p, int64_t elems, const char* w) {
+        return dec_alloc(d, reinterpret_cast<void**>(p), static_cast<size_t>(elems) * 2, w);
+    };
+    if ((rc = act(&d->x, S * H, "activations")) || (rc = act(&d->r, S * H, "activations")) ||
+        (rc = act(&d->p, S * H, "activations")) || (rc = act(&d->normed, S * H, "activations")) ||
+        (rc = act(&d->qkv, S * d->n_qkv, "activations")) || (rc = act(&d->attn, S * H, "activations")) ||
+        (rc = act(&d->gu, S * 2 * d->I, "activations")) || (rc = act(&d->act, S * d->I, "activations")) ||
+        (rc = act(&d->logits, d->V, "logits")) || (rc = act(&d->kc, d->L * d->kvh * S * D, "the KV cache")) ||
+        (rc = act(&d->vc, d->L * d->kvh * S * D, "the KV cache")))
+        return rc;
+    // RoPE tables with the reference's float expressions (cpu_backend.cpp:363-366).
+    const int64_t half = D / 2;
+    std::vector<float> cs(static_cast<size_t>(S * half)), sn(static_cast<size_t>(S * half));
+    const float theta = d->cfg.rope_theta;
+    for (int64_t pos = 0; pos < S; ++pos)
+        for (int64_t i = 0; i < half; ++i) {
+            const float freq = 1.0f / std::pow(theta, static_cast<float>(2 * i) / static_cast<float>(D));
+            const float angle = static_cast<float>(static_cast<size_t>(pos)) * freq;
+            cs[static_cast<size_t>(pos * half + i)] = std::cos(angle);
+            sn[static_cast<size_t>(pos * half + i)] = std::sin(angle);
+        }
+    if ((rc = dec_alloc(d, reinterpret_cast<void**>(&d->cos_t), cs.size() * 4, "RoPE tables")) ||
+        (rc = dec_alloc(d, reinterpret_cast<void**>(&d->sin_t), sn.size() * 4, "RoPE tables")))
+        return rc;
+    cudaError_t e = cudaMemcpy(d->cos_t, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(d->sin_t, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_error(e, "uploading RoPE tables");
+    int64_t ns = (S + 31) / 32;
+    d->nsplit = static_cast<int>(ns < 1 ? 1 : (ns > 32 ? 32 : ns));
+    if ((rc = dec_alloc(d, reinterpret_cast<void**>(&d->part), static_cast<size_t>(d->heads * d->nsplit * (D + 2)) * 4, "attention scratch")) ||
+        (rc = dec_alloc(d, reinterpret_cast<void**>(&d->counters), static_cast<size_t>(d->heads) * 4, "attention counters")) ||
+        (rc = dec_alloc(d, reinterpret_cast<void**>(&d->am_idx), 8, "argmax output")) ||
+        (rc = dec_alloc(d, reinterpret_cast<void**>(&d->am_val), 4, "argmax output")) ||
+        (rc = dec_alloc(d, &d->am_scratch, argmax_scratch_bytes(1, d->V), "argmax scratch")) ||
+        (rc = dec_alloc(d, reinterpret_cast<void**>(&d->state), sizeof(DecState), "decoder state")))
+        return rc;
+    e = cudaMemset(d->counters, 0, static_cast<size_t>(d->heads) * 4);
+    if (e == cudaSuccess) e = cudaMemset(d->kc, 0, static_cast<size_t>(d->L * d->kvh * S * D) * 2);
+    if (e == cudaSuccess) e = cudaMemset(d->vc, 0, static_cast<size_t>(d->L * d->kvh * S * D) * 2);
+    if (e != cudaSuccess) return cuda_error(e, "clearing decoder buffers");
+    if (silu_lut_for_device(d->device) == nullptr) return set_error(MRT_ERR_CUDA, "building the SiLU table failed");
+    // One FP32 row of shared memory per block in the norm kernels.
+    e = cudaFuncSetAttribute(embed_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(H * 4));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(add_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(H * 4));
+    if (e != cudaSuccess) return cuda_error(e, "configuring the norm kernels");
+    d->ready = true;
+    return MRT_OK;
+}
+
+#define DEC_TRY(x)                   \
+    do {                             \
+        int rc_ = (x);               \
+        if (rc_ != MRT_OK) return rc_; \
+    } while (0)
+#define DEC_CU(x, what)                                   \
+    do {                                                  \
+        cudaError_t e_ = (x);                             \
+        if (e_ != cudaSuccess) return cuda_error(e_, what); \
+    } while (0)
+
+// One forward over S rows starting at the state's position: prefill
+// (ids = the prompt on the device, pos0 its host-known start) or one decode
+// step (ids == nullptr: the state's token), ending with the greedy pick of
+// the last row and the state update.
+int dec_forward(mrt_decoder d, int64_t S, const int32_t* ids, int64_t pos0, bool decode) {
+    cudaStream_t s = d->stream;
+    DevCtx* ctx = current_ctx();
+    if (!ctx) return MRT_ERR_CUDA;
+    const int64_t H = d->H, D = d->D, I = d->I, nq = d->n_qkv, group = d->heads / d->kvh;
+    const size_t row_smem = static_cast<size_t>(H) * 4;
+    const float eps = d->cfg.rms_norm_eps;
+    const float scale = 1.0f / std::sqrt(static_cast<float>(D));  // qwen_model.cpp:220
+    const uint16_t* lut = silu_lut_for_device(d->device);
+    const int64_t kv_layer = d->kvh * d->max_seq * D;
+    auto grid_for = [](int64_t n) {
+        int64_t b = (n + kNT - 1) / kNT;
+        return static_cast<unsigned>(b < 1 ? 1 : (b > 148 * 16 ? 148 * 16 : b));
+    };
+    for (int64_t l = 0; l < d->L; ++l) {
+        DecLayer& ly = d->layers[static_cast<size_t>(l)];
+        if (l == 0) {
+            DEC_CU(launch_pdl(embed_norm_kernel, dim3(static_cast<unsigned>(S)), dim3(kNT), row_smem, s, d->embed, d->V, H,
+                              ids, d->state, d->x, ly.ln1, ly.ln1_dt, eps, d->normed, ctx->d_err),
+                   "embedding launch");
+        } else {
+            DEC_CU(launch_pdl(add_norm_kernel, dim3(static_cast<unsigned>(S)), dim3(kNT), row_smem, s, d->r, d->p, d->x, H,
+                              ly.ln1, ly.ln1_dt, eps, d->normed),
+                   "add+rmsnorm launch");
+        }
+        DEC_TRY(mrt_gemm(ly.qkv, d->normed, H, d->qkv, nq, S, ly.qkv_bias ? MRT_GEMM_BIAS : 0, s));
+        uint16_t* kc = d->kc + l * kv_layer;
+        uint16_t* vc = d->vc + l * kv_layer;
+        DEC_CU(launch_pdl(rope_append_kernel, dim3(grid_for(S * (d->heads + d->kvh) * (D / 2))), dim3(kNT), 0, s, d->qkv, nq, S,
+                          static_cast<int>(d->heads), static_cast<int>(d->kvh), static_cast<int>(D), d->cos_t, d->sin_t,
+                          kc, vc, d->max_seq, d->state),
+               "rope launch");
+        if (decode) {
+            DEC_CU(launch_pdl(attn_decode_kernel, dim3(static_cast<unsigned>(d->heads), static_cast<unsigned>(d->nsplit)),
+                              dim3(kAttnWarps * 32), 0, s, d->qkv, kc, vc, d->attn, static_cast<int>(d->heads),
+                              static_cast<int>(group), static_cast<int>(D), d->max_seq, scale, d->state, d->part,
+                              d->counters),
+                   "attention launch");
+        } else {
+            // Per kv head, its query heads over the cached keys (qwen_model.cpp:212-245).
+            for (int64_t g = 0; g < d->kvh; ++g) {
+                const int64_t qs[4] = {0, D, nq, 1}, ks[4] = {0, 0, D, 1}, os[4] = {0, D, H, 1};
+                DEC_TRY(mrt_attention(d->qkv + g * group * D, MRT_FP16, qs, kc + g * d->max_seq * D, MRT_FP16, ks,
+                                      vc + g * d->max_seq * D, MRT_FP16, ks, d->attn + g * group * D, MRT_FP16, os, 1,
+                                      group, S, pos0 + S, D, D, scale, 1, s));
+            }
+        }
+        DEC_TRY(mrt_gemm(ly.o, d->attn, H, d->p, H, S, 0, s));
+        DEC_CU(launch_pdl(add_norm_kernel, dim3(static_cast<unsigned>(S)), dim3(kNT), row_smem, s, d->x, d->p, d->r, H,
+                          ly.ln2, ly.ln2_dt, eps, d->normed),
+               "add+rmsnorm launch");
+        DEC_TRY(mrt_gemm(ly.gateup, d->normed, H, d->gu, 2 * I, S, 0, s));
+        DEC_CU(launch_pdl(silu_mul_kernel, dim3(grid_for(S * I)), dim3(kNT), 0, s, d->gu, 2 * I, I, S, lut, d->act),
+               "silu*mul launch");
+        DEC_TRY(mrt_gemm(ly.down, d->act, I, d->p, H, S, 0, s));
+    }
+    // Final residual and norm of the last row, lm_head, greedy pick.
+    const int64_t last = (S - 1) * H;
+    DEC_CU(launch_pdl(add_norm_kernel, dim3(1), dim3(kNT), row_smem, s, d->r + last, d->p + last, d->x + last, H, d->norm,
+                      d->norm_dt, eps, d->normed + last),
+           "final norm launch");
+    DEC_TRY(mrt_gemm(d->lm_head, d->normed + last, H, d->logits, d->V, 1, 0, s));
+    DEC_CU(launch_argmax(d->logits, 1, d->V, d->V, 0, d->am_idx, d->am_val, d->am_scratch, s), "argmax launch");
+    DEC_CU(launch_pdl(advance_kernel, dim3(1), dim3(32), 0, s, d->am_idx, d->state, d->tokens, d->tokens_cap,
+                      static_cast<int>(S)),
+           "advance launch");
+    return MRT_OK;
+}
+
+}  // namespace
+
+extern "C" int mrt_decoder_generate(mrt_decoder d, const int32_t* prompt, int64_t n_prompt, int64_t max_new,
+                                    int32_t eos, int32_t* out_tokens, int64_t* n_out, mrt_decoder_stats* stats,
+                                    void* user_stream) {
+    clear_error();
+    if (d == nullptr || prompt == nullptr || out_tokens == nullptr || n_out == nullptr)
+        return set_error(MRT_ERR_INVALID_ARG, "NULL argument");
+    *n_out = 0;
+    if (stats) *stats = mrt_decoder_stats{0.0f, 0.0f, 0.0f, 0};
+    if (n_prompt < 1 || max_new < 0) return set_error(MRT_ERR_SHAPE, "need n_prompt >= 1 and max_new >= 0");
+    if (max_new == 0) return MRT_OK;
+    if (n_prompt + max_new - 1 > d->max_seq)
+        return set_error(MRT_ERR_SHAPE, "n_prompt + max_new - 1 exceeds max_seq_len");
+    if (n_prompt > 65535) return set_error(MRT_ERR_SHAPE, "at most 65535 prompt tokens per call");
+    for (int64_t i = 0; i < n_prompt; ++i)
+        if (prompt[i] < 0 || prompt[i] >= d->V)
+            return set_error(MRT_ERR_INVALID_ARG, "embedding_lookup: token_id out of range");
+    DevCtx* ctx = current_ctx();
+    if (!ctx) return MRT_ERR_CUDA;
+    DEC_TRY(dec_finalize(d));
+    cudaStream_t s = d->stream;
+    if (d->ids_cap < n_prompt) {
+        dec_release(d, d->ids);
+        d->ids = nullptr;
+        DEC_TRY(dec_alloc(d, reinterpret_cast<void**>(&d->ids), static_cast<size_t>(n_prompt) * 4, "prompt ids"));
+        d->ids_cap = n_prompt;
+    }
+    if (d->tokens_cap < max_new) {
+        dec_release(d, d->tokens);
+        d->tokens = nullptr;
+        DEC_TRY(dec_alloc(d, reinterpret_cast<void**>(&d->tokens), static_cast<size_t>(max_new) * 4, "generated ids"));
+        d->tokens_cap = max_new;
+    }
+    // Order after the caller's work, then start from position 0.
+    cudaEvent_t ev[5] = {};
+    for (auto& e : ev) DEC_CU(cudaEventCreate(&e), "creating events");
+    struct Cleanup {
+        cudaEvent_t* ev;
+        cudaGraph_t graph = nullptr;
+        cudaGraphExec_t exec = nullptr;
+        ~Cleanup() {
+            if (exec) cudaGraphExecDestroy(exec);
+            if (graph) cudaGraphDestroy(graph);
+            for (int i = 0; i < 5; ++i)
+                if (ev[i]) cudaEventDestroy(ev[i]);
+        }
+    } cleanup{ev};
+    DEC_CU(cudaEventRecord(ev[0], static_cast<cudaStream_t>(user_stream)), "recording an event");
+    DEC_CU(cudaStreamWaitEvent(s, ev[0], 0), "ordering after the caller's stream");
+    const DecState st0{0, 0, 0, 0};
+    DEC_CU(cudaMemcpyAsync(d->state, &st0, sizeof(st0), cudaMemcpyHostToDevice, s), "resetting the decoder state");
+    DEC_CU(cudaMemcpyAsync(d->ids, prompt, static_cast<size_t>(n_prompt) * 4, cudaMemcpyHostToDevice, s), "uploading the prompt");
+    DEC_CU(cudaStreamSynchronize(s), "uploading the prompt");  // prompt and st0 are pageable host memory
+    // The reference prefills one token at a time (inference_engine.cpp:42-48);
+    // every op is row-independent under the causal mask, so one batched
+    // forward gives the same rows.
+    DEC_CU(cudaEventRecord(ev[0], s), "recording an event");
+    DEC_TRY(dec_forward(d, n_prompt, d->ids, 0, false));
+    DEC_CU(cudaEventRecord(ev[1], s), "recording an event");
+    int64_t replays = 0;
+    if (max_new >= 2) {
+        DEC_TRY(dec_forward(d, 1, nullptr, 0, true));  // eager: sizes every scratch buffer
+        DEC_CU(cudaEventRecord(ev[2], s), "recording an event");
+        replays = max_new - 2;
+        if (replays > 0) {
+            DEC_CU(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "beginning the decode-step capture");
+            const int rc = dec_forward(d, 1, nullptr, 0, true);
+            const cudaError_t ec = cudaStreamEndCapture(s, &cleanup.graph);
+            if (rc != MRT_OK) return rc;
+            DEC_CU(ec, "capturing the decode step");
+            DEC_CU(cudaGraphInstantiate(&cleanup.exec, cleanup.graph, 0), "instantiating the decode step");
+            DEC_CU(cudaEventRecord(ev[3], s), "recording an event");
+            for (int64_t i = 0; i < replays; ++i) DEC_CU(cudaGraphLaunch(cleanup.exec, s), "replaying the decode step");
+            DEC_CU(cudaEventRecord(ev[4], s), "recording an event");
+        }
+    }
+    DEC_TRY(mrt_sync(s));
+    std::vector<int32_t> toks(static_cast<size_t>(max_new));
+    DEC_CU(cudaMemcpy(toks.data(), d->tokens, static_cast<size_t>(max_new) * 4, cudaMemcpyDeviceToHost), "reading tokens");
+    int64_t n = 0;
+    for (; n < max_new; ++n) {
+        out_tokens[n] = toks[static_cast<size_t>(n)];
+        if (eos >= 0 && toks[static_cast<size_t>(n)] == eos) {
+            ++n;
+            break;
+        }
+    }
+    *n_out = n;
+    if (stats) {
+        float ms = 0.0f;
+        cudaEventElapsedTime(&ms, ev[0], ev[1]);
+        stats->prefill_ms = ms;
+        if (max_new >= 2) {
+            cudaEventElapsedTime(&ms, ev[1], ev[2]);
+            stats->first_step_ms = ms;
+        }
+        if (replays > 0) {
+            cudaEventElapsedTime(&ms, ev[3], ev[4]);
+            stats->decode_ms = ms;
+            stats->decode_steps = replays;
+        }
+    }
+    return MRT_OK;
+}
+
+extern "C" void mrt_decoder_free(mrt_decoder d) {
+    if (d == nullptr) return;
+    cudaStreamSynchronize(d->stream);
+    for (auto& ly : d->layers)
+        for (mrt_weight w : {ly.qkv, ly.o, ly.gateup, ly.down})
+            if (w) mrt_weight_free(w);
+    if (d->lm_head) mrt_weight_free(d->lm_head);
+    for (void* p : d->allocs)
+        if (p) cudaFree(p);
+    cudaStreamDestroy(d->stream);
+    delete d;
+}

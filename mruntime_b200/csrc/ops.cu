@@ -279,6 +279,10 @@ int launch_status(const char* what) {
 }
 
 }  // namespace
+
+// The FP16 SiLU table of `device` (built on first use), for fused kernels.
+const uint16_t* silu_lut_for_device(int device) { return silu_lut(device); }
+
 }  // namespace mrt
 
 using namespace mrt;

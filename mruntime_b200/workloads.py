@@ -112,6 +112,15 @@ DECODER_7B = {
 }
 
 
+# A 2-layer, 256-wide model of the same structure (head_dim 64, 2 kv heads):
+# the quick pipeline check of the decoder against the reference engine.
+DECODER_TINY = {
+    "vocab_size": 1000, "hidden_size": 256, "num_hidden_layers": 2, "num_attention_heads": 4,
+    "num_key_value_heads": 2, "intermediate_size": 512, "rope_theta": 1000000.0, "rms_norm_eps": 1e-6,
+    "max_position_embeddings": 32768,
+}
+
+
 def decoder_prompt(seed: int = 3, n: int = 512, vocab: int = 152064) -> np.ndarray:
     """Prompt token ids, uniform in [0, vocab), from the first child stream of `seed`."""
     prompt_ss, _ = np.random.SeedSequence(seed).spawn(2)

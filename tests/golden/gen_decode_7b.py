@@ -34,9 +34,7 @@ sys.path.insert(0, ROOT)
 
 from mruntime_b200 import workloads as W  # noqa: E402
 
-TINY = {"vocab_size": 1000, "hidden_size": 256, "num_hidden_layers": 2, "num_attention_heads": 4,
-        "num_key_value_heads": 2, "intermediate_size": 512, "rope_theta": 1000000.0, "rms_norm_eps": 1e-6,
-        "max_position_embeddings": 32768}
+TINY = W.DECODER_TINY
 
 
 def write_safetensors(path: str, cfg: dict, seed: int) -> str:
