@@ -376,7 +376,9 @@ int mrt_decoder_create(const mrt_decoder_config* cfg, mrt_decoder* out);
  * "model.layers.<i>.mlp.{gate,up,down}_proj.weight", "model.norm.weight",
  * "lm_head.weight" (optional: tied to the embedding when absent).  rows x cols
  * is the tensor's shape (cols = 1 for vectors); dtype FP16/BF16/FP32; src in
- * host or device memory.  Unknown names are MRT_ERR_INVALID_ARG. */
+ * host or device memory (a device source is read after the whole device
+ * synchronises, so any stream may have produced it).  Unknown names are
+ * MRT_ERR_INVALID_ARG. */
 int mrt_decoder_load(mrt_decoder d, const char* name, const void* src, int src_dtype, int src_on_device,
                      int64_t rows, int64_t cols);
 

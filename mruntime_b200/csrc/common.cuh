@@ -166,6 +166,24 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, 
         : "memory");
 }
 
+// An L2 policy that evicts first the lines it fills: for data read once per
+// pass (streamed weights), so they do not push out what other kernels reuse.
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+// bulk_load with an L2 cache policy (see l2_policy_evict_first).
+__device__ __forceinline__ void bulk_load_hint(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar,
+                                               uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(gmem_src)), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
 // Element offset of (row r, column k) in the tiled weight layout: 128 x 64
 // tiles, tile (r / 128, k / 64) at ((r / 128) * k_tiles + k / 64) * 8192, and
 // inside a tile row-major 64-element rows whose 16-byte chunks are permuted

@@ -18,9 +18,10 @@
 // Per layer: add+RMSNorm (the previous layer's residual), q|k|v GEMM with
 // bias, RoPE + KV append, attention, o GEMM, add+RMSNorm, gate|up GEMM,
 // SiLU*up, down GEMM; then the final add+RMSNorm, lm_head on the last row and
-// the greedy pick.  Every small kernel waits (griddepcontrol.wait) for the
-// kernel before it before touching memory and lets the next launch start at
-// once, so each GEMM's weight stream begins while the small kernel runs.
+// the greedy pick.  Every small kernel first lets the next launch start
+// (griddepcontrol.launch_dependents) and then waits (griddepcontrol.wait) for
+// the kernel before it before touching memory, so launches are hidden and each
+// GEMM's weight stream begins while the small kernels before it run.
 //
 // Rounding points are the reference's: every op reads FP16 and writes FP16,
 // computing in FP32 with its operand order (no fused multiply-adds).  The
@@ -69,12 +70,6 @@ cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, 
     return e;
 }
 
-__device__ __forceinline__ float ldw(const void* p, int dt, int64_t i) {
-    if (dt == MRT_FP32) return static_cast<const float*>(p)[i];
-    const uint16_t v = static_cast<const uint16_t*>(p)[i];
-    return dt == MRT_BF16 ? bf16_bits_to_f32(v) : f16_bits_to_f32(v);
-}
-
 __device__ __forceinline__ float block_sum(float v, float* red) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
@@ -85,25 +80,78 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
     return t;
 }
 
-// RMSNorm of one FP16 row held in shared memory (cpu_backend.cpp:292-330):
+constexpr int kNormVec = 8;  // 16-byte vectors per thread: hidden <= 256 * 8 * 8 = 16384
+
+__device__ __forceinline__ uint4 ld16(const void* p) { return *reinterpret_cast<const uint4*>(p); }
+
+__device__ __forceinline__ void unpack8(const uint4& v, float (&x)[8]) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        x[2 * e] = f16_bits_to_f32(static_cast<uint16_t>(w[e] & 0xFFFFu));
+        x[2 * e + 1] = f16_bits_to_f32(static_cast<uint16_t>(w[e] >> 16));
+    }
+}
+
+__device__ __forceinline__ uint32_t pack2(uint16_t lo, uint16_t hi) {
+    return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+}
+
+// Eight RMSNorm gains starting at element i, in their dtype.
+__device__ __forceinline__ void gains8(const void* w, int wdt, int64_t i, float (&g)[8]) {
+    if (wdt == MRT_FP32) {
+        const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(w) + i);
+        const float4 b = *reinterpret_cast<const float4*>(static_cast<const float*>(w) + i + 4);
+        g[0] = a.x; g[1] = a.y; g[2] = a.z; g[3] = a.w; g[4] = b.x; g[5] = b.y; g[6] = b.z; g[7] = b.w;
+        return;
+    }
+    const uint4 v = ld16(static_cast<const uint16_t*>(w) + i);
+    const uint32_t q[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const uint16_t lo = static_cast<uint16_t>(q[e] & 0xFFFFu), hi = static_cast<uint16_t>(q[e] >> 16);
+        g[2 * e] = wdt == MRT_BF16 ? bf16_bits_to_f32(lo) : f16_bits_to_f32(lo);
+        g[2 * e + 1] = wdt == MRT_BF16 ? bf16_bits_to_f32(hi) : f16_bits_to_f32(hi);
+    }
+}
+
+// RMSNorm of one row whose FP16-rounded values this thread holds as
+// x[j][e] = element (threadIdx.x + j * kNT) * 8 + e (cpu_backend.cpp:292-330):
 // rms = sqrt(sum(x^2) / n + eps); out = fp16((x * (1 / rms)) * w).
-__device__ void norm_row(const float* row, int64_t H, const void* w, int wdt, float eps, uint16_t* out, float* red) {
-    float s = 0.0f;
-    for (int64_t i = threadIdx.x; i < H; i += kNT) s = __fadd_rn(s, __fmul_rn(row[i], row[i]));
-    const float total = block_sum(s, red);
+__device__ __forceinline__ void norm_vecs(const float (&x)[kNormVec][8], int nv, int64_t H, const void* w, int wdt,
+                                          float eps, uint16_t* __restrict__ out, float* red) {
+    float ss = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kNormVec; ++j)
+        if (static_cast<int>(threadIdx.x) + j * kNT < nv)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) ss = __fadd_rn(ss, __fmul_rn(x[j][e], x[j][e]));
+    const float total = block_sum(ss, red);
     const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(H)), eps));
     const float inv = __fdiv_rn(1.0f, rms);
-    for (int64_t i = threadIdx.x; i < H; i += kNT) out[i] = f32_to_f16_bits(__fmul_rn(__fmul_rn(row[i], inv), ldw(w, wdt, i)));
+#pragma unroll
+    for (int j = 0; j < kNormVec; ++j) {
+        const int v = static_cast<int>(threadIdx.x) + j * kNT;
+        if (v >= nv) continue;
+        float g[8];
+        gains8(w, wdt, static_cast<int64_t>(v) * 8, g);
+        uint16_t h[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) h[e] = f32_to_f16_bits(__fmul_rn(__fmul_rn(x[j][e], inv), g[e]));
+        *reinterpret_cast<uint4*>(out + static_cast<int64_t>(v) * 8) =
+            make_uint4(pack2(h[0], h[1]), pack2(h[2], h[3]), pack2(h[4], h[5]), pack2(h[6], h[7]));
+    }
 }
 
 // Row s: hidden = table[id] (qwen_model.cpp:59-64), normed = RMSNorm(hidden).
-// ids == nullptr: the id is the state's current token.
-__global__ void embed_norm_kernel(const uint16_t* table, int64_t vocab, int64_t H, const int32_t* ids,
-                                  const DecState* st, uint16_t* hidden, const void* w, int wdt, float eps,
-                                  uint16_t* normed, int* err) {
-    griddep_wait();
+// ids == nullptr: the id is the state's current token.  Rows are 16-byte
+// vectors; every load of a thread is issued before any is used.
+__global__ void __launch_bounds__(kNT) embed_norm_kernel(const uint16_t* __restrict__ table, int64_t vocab, int64_t H,
+                                                         const int32_t* ids, const DecState* st,
+                                                         uint16_t* __restrict__ hidden, const void* __restrict__ w,
+                                                         int wdt, float eps, uint16_t* __restrict__ normed, int* err) {
     griddep_launch_dependents();
-    extern __shared__ float row[];
+    griddep_wait();
     __shared__ float red[kNT / 32];
     const int64_t s = blockIdx.x;
     int64_t id = ids != nullptr ? ids[s] : st->token;
@@ -111,30 +159,60 @@ __global__ void embed_norm_kernel(const uint16_t* table, int64_t vocab, int64_t 
         if (threadIdx.x == 0) raise_error(err, kErrBadToken);
         id = 0;
     }
-    for (int64_t i = threadIdx.x; i < H; i += kNT) {
-        const uint16_t v = table[id * H + i];
-        hidden[s * H + i] = v;
-        row[i] = f16_bits_to_f32(v);
+    const int nv = static_cast<int>(H / 8);
+    uint4 v[kNormVec];
+#pragma unroll
+    for (int j = 0; j < kNormVec; ++j) {
+        const int i = static_cast<int>(threadIdx.x) + j * kNT;
+        if (i < nv) v[j] = ld16(table + id * H + static_cast<int64_t>(i) * 8);
     }
-    __syncthreads();
-    norm_row(row, H, w, wdt, eps, normed + s * H, red);
+    float x[kNormVec][8];
+#pragma unroll
+    for (int j = 0; j < kNormVec; ++j) {
+        const int i = static_cast<int>(threadIdx.x) + j * kNT;
+        if (i >= nv) continue;
+        *reinterpret_cast<uint4*>(hidden + s * H + static_cast<int64_t>(i) * 8) = v[j];
+        unpack8(v[j], x[j]);
+    }
+    norm_vecs(x, nv, H, w, wdt, eps, normed + s * H, red);
 }
 
 // Row s: out = fp16(a + b) (cpu_backend.cpp:403-455), normed = RMSNorm(out).
-__global__ void add_norm_kernel(const uint16_t* a, const uint16_t* b, uint16_t* out, int64_t H, const void* w,
-                                int wdt, float eps, uint16_t* normed) {
-    griddep_wait();
+__global__ void __launch_bounds__(kNT) add_norm_kernel(const uint16_t* __restrict__ a, const uint16_t* __restrict__ b,
+                                                       uint16_t* __restrict__ out, int64_t H, const void* __restrict__ w,
+                                                       int wdt, float eps, uint16_t* __restrict__ normed) {
     griddep_launch_dependents();
-    extern __shared__ float row[];
+    griddep_wait();
     __shared__ float red[kNT / 32];
     const int64_t s = blockIdx.x;
-    for (int64_t i = threadIdx.x; i < H; i += kNT) {
-        const uint16_t r = f32_to_f16_bits(__fadd_rn(f16_bits_to_f32(a[s * H + i]), f16_bits_to_f32(b[s * H + i])));
-        out[s * H + i] = r;
-        row[i] = f16_bits_to_f32(r);
+    const int nv = static_cast<int>(H / 8);
+    uint4 va[kNormVec], vb[kNormVec];
+#pragma unroll
+    for (int j = 0; j < kNormVec; ++j) {
+        const int i = static_cast<int>(threadIdx.x) + j * kNT;
+        if (i < nv) {
+            va[j] = ld16(a + s * H + static_cast<int64_t>(i) * 8);
+            vb[j] = ld16(b + s * H + static_cast<int64_t>(i) * 8);
+        }
     }
-    __syncthreads();
-    norm_row(row, H, w, wdt, eps, normed + s * H, red);
+    float x[kNormVec][8];
+#pragma unroll
+    for (int j = 0; j < kNormVec; ++j) {
+        const int i = static_cast<int>(threadIdx.x) + j * kNT;
+        if (i >= nv) continue;
+        float fa[8], fb[8];
+        unpack8(va[j], fa);
+        unpack8(vb[j], fb);
+        uint16_t h[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            h[e] = f32_to_f16_bits(__fadd_rn(fa[e], fb[e]));
+            x[j][e] = f16_bits_to_f32(h[e]);
+        }
+        *reinterpret_cast<uint4*>(out + s * H + static_cast<int64_t>(i) * 8) =
+            make_uint4(pack2(h[0], h[1]), pack2(h[2], h[3]), pack2(h[4], h[5]), pack2(h[6], h[7]));
+    }
+    norm_vecs(x, nv, H, w, wdt, eps, normed + s * H, red);
 }
 
 // RoPE on the q and k heads of S rows (cpu_backend.cpp:332-379, cos/sin from
@@ -144,8 +222,8 @@ __global__ void add_norm_kernel(const uint16_t* a, const uint16_t* b, uint16_t* 
 __global__ void rope_append_kernel(uint16_t* qkv, int64_t ldq, int64_t S, int heads, int kv_heads, int D,
                                    const float* cos_t, const float* sin_t, uint16_t* kc, uint16_t* vc,
                                    int64_t max_seq, const DecState* st) {
-    griddep_wait();
     griddep_launch_dependents();
+    griddep_wait();
     const int half = D / 2;
     const int64_t per_row = static_cast<int64_t>(heads + kv_heads) * half;
     const int64_t total = S * per_row;
@@ -180,71 +258,115 @@ __global__ void rope_append_kernel(uint16_t* qkv, int64_t ldq, int64_t S, int he
 }
 
 constexpr int kAttnWarps = 4;
-constexpr int kMaxPerLane = 8;  // head_dim <= 256
+constexpr int kKeysPerWarp = 8;
+constexpr int kSplitKeys = kAttnWarps * kKeysPerWarp;  // keys per split block
+
+// PER FP16 elements (PER = head_dim / 32) of one row, lane-contiguous.
+template <int PER>
+__device__ __forceinline__ void load_per(const uint16_t* p, float (&x)[PER]) {
+    if constexpr (PER == 2) {
+        const uint32_t v = *reinterpret_cast<const uint32_t*>(p);
+        x[0] = f16_bits_to_f32(static_cast<uint16_t>(v & 0xFFFFu));
+        x[1] = f16_bits_to_f32(static_cast<uint16_t>(v >> 16));
+    } else if constexpr (PER == 4) {
+        const uint2 v = *reinterpret_cast<const uint2*>(p);
+        const uint32_t w[2] = {v.x, v.y};
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            x[2 * e] = f16_bits_to_f32(static_cast<uint16_t>(w[e] & 0xFFFFu));
+            x[2 * e + 1] = f16_bits_to_f32(static_cast<uint16_t>(w[e] >> 16));
+        }
+    } else if constexpr (PER == 8) {
+        const uint4 v = *reinterpret_cast<const uint4*>(p);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            x[2 * e] = f16_bits_to_f32(static_cast<uint16_t>(w[e] & 0xFFFFu));
+            x[2 * e + 1] = f16_bits_to_f32(static_cast<uint16_t>(w[e] >> 16));
+        }
+    } else {
+#pragma unroll
+        for (int e = 0; e < PER; ++e) x[e] = f16_bits_to_f32(p[e]);
+    }
+}
 
 // Decode attention for one query row (cpu_backend.cpp:171-290 with
-// q_len = 1): block (h, split) scores keys [k0, k1) of kv head h / group with an
-// online softmax per warp, merges its warps, and writes (max, sum, acc[D]) to
-// `part`; the last split block of a head to finish merges the splits in order
-// and writes out = fp16(acc * (1 / sum)).  kv_len = state position + 1.
+// q_len = 1).  Block (h, split) covers keys [32 split, 32 split + 32) of kv
+// head h / group; each warp loads its <= 8 keys' K and V rows at once, scores
+// them (q.k as a warp tree sum, times scale), and keeps (max, sum of exp,
+// sum of exp * v).  The block merges its warps and writes the split's partial
+// to `part`; the last split block of the head to finish merges every split
+// in split order and writes out = fp16(acc * (1 / sum)).
+// kv_len = state position + 1 (the current token's key is already cached).
+template <int PER>
 __global__ void __launch_bounds__(kAttnWarps * 32)
-    attn_decode_kernel(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, uint16_t* out, int heads,
-                       int group, int D, int64_t max_seq, float scale, const DecState* st, float* part,
-                       int* counters) {
-    griddep_wait();
+    attn_decode_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ kc,
+                       const uint16_t* __restrict__ vc, uint16_t* __restrict__ out, int heads, int group,
+                       int64_t max_seq, float scale, const DecState* st, float* part, int* counters) {
     griddep_launch_dependents();
+    griddep_wait();
+    constexpr int D = PER * 32;
     __shared__ float sm_m[kAttnWarps], sm_l[kAttnWarps];
-    __shared__ float sm_acc[kAttnWarps][256];
+    __shared__ float sm_acc[kAttnWarps][D];
     __shared__ int sm_last;
     const int h = blockIdx.x, sp = blockIdx.y, nsplit = gridDim.y;
     const int g = h / group;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int per = D / 32;
     int64_t kv_len = static_cast<int64_t>(st->pos) + 1;
     if (kv_len > max_seq) kv_len = max_seq;
-    const int64_t chunk = (kv_len + nsplit - 1) / nsplit;
-    const int64_t k0 = sp * chunk;
-    const int64_t k1 = k0 + chunk < kv_len ? k0 + chunk : kv_len;
-    float qv[kMaxPerLane];
+    const int64_t kw = static_cast<int64_t>(sp) * kSplitKeys + warp * kKeysPerWarp;
+    const int nk = kv_len - kw <= 0 ? 0 : (kv_len - kw >= kKeysPerWarp ? kKeysPerWarp : static_cast<int>(kv_len - kw));
+    float qv[PER];
+    load_per<PER>(q + static_cast<int64_t>(h) * D + lane * PER, qv);
+    const uint16_t* kb = kc + (static_cast<int64_t>(g) * max_seq + kw) * D + lane * PER;
+    const uint16_t* vb = vc + (static_cast<int64_t>(g) * max_seq + kw) * D + lane * PER;
+    float kx[kKeysPerWarp][PER], vx[kKeysPerWarp][PER];
 #pragma unroll
-    for (int j = 0; j < kMaxPerLane; ++j) qv[j] = j < per ? f16_bits_to_f32(q[static_cast<int64_t>(h) * D + lane * per + j]) : 0.0f;
-    const uint16_t* kb = kc + static_cast<int64_t>(g) * max_seq * D;
-    const uint16_t* vb = vc + static_cast<int64_t>(g) * max_seq * D;
-    float m = -INFINITY, l = 0.0f, acc[kMaxPerLane];
+    for (int i = 0; i < kKeysPerWarp; ++i)
+        if (i < nk) {
+            load_per<PER>(kb + i * D, kx[i]);
+            load_per<PER>(vb + i * D, vx[i]);
+        }
+    float sc[kKeysPerWarp];
 #pragma unroll
-    for (int j = 0; j < kMaxPerLane; ++j) acc[j] = 0.0f;
-    for (int64_t k = k0 + warp; k < k1; k += kAttnWarps) {
+    for (int i = 0; i < kKeysPerWarp; ++i) {
         float d = 0.0f;
 #pragma unroll
-        for (int j = 0; j < kMaxPerLane; ++j)
-            if (j < per) d = __fadd_rn(d, __fmul_rn(qv[j], f16_bits_to_f32(kb[k * D + lane * per + j])));
+        for (int e = 0; e < PER; ++e) d = __fadd_rn(d, __fmul_rn(qv[e], i < nk ? kx[i][e] : 0.0f));
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) d = __fadd_rn(d, __shfl_xor_sync(0xFFFFFFFFu, d, o));
-        const float sc = __fmul_rn(d, scale);
-        const float m_new = fmaxf(m, sc);
-        const float corr = expf(__fsub_rn(m, m_new));
-        const float p = expf(__fsub_rn(sc, m_new));
-        l = __fadd_rn(__fmul_rn(l, corr), p);
+        sc[i] = i < nk ? __fmul_rn(d, scale) : -INFINITY;
+    }
+    float m = -INFINITY;
 #pragma unroll
-        for (int j = 0; j < kMaxPerLane; ++j)
-            if (j < per)
-                acc[j] = __fadd_rn(__fmul_rn(acc[j], corr), __fmul_rn(p, f16_bits_to_f32(vb[k * D + lane * per + j])));
-        m = m_new;
+    for (int i = 0; i < kKeysPerWarp; ++i) m = fmaxf(m, sc[i]);
+    float l = 0.0f, acc[PER];
+#pragma unroll
+    for (int e = 0; e < PER; ++e) acc[e] = 0.0f;
+    if (nk > 0) {
+#pragma unroll
+        for (int i = 0; i < kKeysPerWarp; ++i)
+            if (i < nk) {
+                const float p = expf(__fsub_rn(sc[i], m));
+                l = __fadd_rn(l, p);
+#pragma unroll
+                for (int e = 0; e < PER; ++e) acc[e] = __fadd_rn(acc[e], __fmul_rn(p, vx[i][e]));
+            }
     }
     if (lane == 0) {
         sm_m[warp] = m;
         sm_l[warp] = l;
     }
 #pragma unroll
-    for (int j = 0; j < kMaxPerLane; ++j)
-        if (j < per) sm_acc[warp][lane * per + j] = acc[j];
+    for (int e = 0; e < PER; ++e) sm_acc[warp][lane * PER + e] = acc[e];
     __syncthreads();
-    // Merge the warps: thread t owns dimension t (and t + 128).
     float M = -INFINITY;
+#pragma unroll
     for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, sm_m[w]);
     float* dst = part + (static_cast<int64_t>(h) * nsplit + sp) * (D + 2);
     if (threadIdx.x == 0) {
         float L = 0.0f;
+#pragma unroll
         for (int w = 0; w < kAttnWarps; ++w)
             if (sm_m[w] != -INFINITY) L = __fadd_rn(L, __fmul_rn(sm_l[w], expf(__fsub_rn(sm_m[w], M))));
         dst[0] = M;
@@ -252,6 +374,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32)
     }
     for (int d = threadIdx.x; d < D; d += kAttnWarps * 32) {
         float A = 0.0f;
+#pragma unroll
         for (int w = 0; w < kAttnWarps; ++w)
             if (sm_m[w] != -INFINITY) A = __fadd_rn(A, __fmul_rn(sm_acc[w][d], expf(__fsub_rn(sm_m[w], M))));
         dst[2 + d] = A;
@@ -268,21 +391,42 @@ __global__ void __launch_bounds__(kAttnWarps * 32)
     if (!sm_last) return;
     __threadfence();
     const float* ph = part + static_cast<int64_t>(h) * nsplit * (D + 2);
+    const int used = static_cast<int>((kv_len + kSplitKeys - 1) / kSplitKeys);  // splits holding keys
     float MM = -INFINITY;
-    for (int s2 = 0; s2 < nsplit; ++s2) MM = fmaxf(MM, ph[s2 * (D + 2)]);
+    for (int s2 = 0; s2 < used; ++s2) MM = fmaxf(MM, ph[s2 * (D + 2)]);
     float LL = 0.0f;
-    for (int s2 = 0; s2 < nsplit; ++s2) {
-        const float ms = ph[s2 * (D + 2)];
-        if (ms != -INFINITY) LL = __fadd_rn(LL, __fmul_rn(ph[s2 * (D + 2) + 1], expf(__fsub_rn(ms, MM))));
-    }
+    for (int s2 = 0; s2 < used; ++s2) LL = __fadd_rn(LL, __fmul_rn(ph[s2 * (D + 2) + 1], expf(__fsub_rn(ph[s2 * (D + 2)], MM))));
     const float inv = __fdiv_rn(1.0f, LL);
     for (int d = threadIdx.x; d < D; d += kAttnWarps * 32) {
         float A = 0.0f;
-        for (int s2 = 0; s2 < nsplit; ++s2) {
-            const float ms = ph[s2 * (D + 2)];
-            if (ms != -INFINITY) A = __fadd_rn(A, __fmul_rn(ph[s2 * (D + 2) + 2 + d], expf(__fsub_rn(ms, MM))));
-        }
+#pragma unroll 4
+        for (int s2 = 0; s2 < used; ++s2)
+            A = __fadd_rn(A, __fmul_rn(ph[s2 * (D + 2) + 2 + d], expf(__fsub_rn(ph[s2 * (D + 2)], MM))));
         out[static_cast<int64_t>(h) * D + d] = f32_to_f16_bits(__fmul_rn(A, inv));
+    }
+}
+
+template <int PER>
+cudaError_t launch_attn_decode(dim3 grid, cudaStream_t s, const uint16_t* q, const uint16_t* kc, const uint16_t* vc,
+                               uint16_t* out, int heads, int group, int64_t max_seq, float scale, const DecState* st,
+                               float* part, int* counters) {
+    return launch_pdl(attn_decode_kernel<PER>, grid, dim3(kAttnWarps * 32), 0, s, q, kc, vc, out, heads, group,
+                      max_seq, scale, st, part, counters);
+}
+
+cudaError_t attn_decode(int D, dim3 grid, cudaStream_t s, const uint16_t* q, const uint16_t* kc, const uint16_t* vc,
+                        uint16_t* out, int heads, int group, int64_t max_seq, float scale, const DecState* st,
+                        float* part, int* counters) {
+    switch (D / 32) {
+        case 1: return launch_attn_decode<1>(grid, s, q, kc, vc, out, heads, group, max_seq, scale, st, part, counters);
+        case 2: return launch_attn_decode<2>(grid, s, q, kc, vc, out, heads, group, max_seq, scale, st, part, counters);
+        case 3: return launch_attn_decode<3>(grid, s, q, kc, vc, out, heads, group, max_seq, scale, st, part, counters);
+        case 4: return launch_attn_decode<4>(grid, s, q, kc, vc, out, heads, group, max_seq, scale, st, part, counters);
+        case 5: return launch_attn_decode<5>(grid, s, q, kc, vc, out, heads, group, max_seq, scale, st, part, counters);
+        case 6: return launch_attn_decode<6>(grid, s, q, kc, vc, out, heads, group, max_seq, scale, st, part, counters);
+        case 7: return launch_attn_decode<7>(grid, s, q, kc, vc, out, heads, group, max_seq, scale, st, part, counters);
+        case 8: return launch_attn_decode<8>(grid, s, q, kc, vc, out, heads, group, max_seq, scale, st, part, counters);
+        default: return cudaErrorInvalidValue;
     }
 }
 
@@ -290,8 +434,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32)
 // (qwen_model.cpp:281-285: silu rounded to FP16, then the product rounded).
 __global__ void silu_mul_kernel(const uint16_t* gu, int64_t ld, int64_t I, int64_t S, const uint16_t* lut,
                                 uint16_t* act) {
-    griddep_wait();
     griddep_launch_dependents();
+    griddep_wait();
     const int64_t total = S * I;
     for (int64_t e = blockIdx.x * static_cast<int64_t>(kNT) + threadIdx.x; e < total;
          e += static_cast<int64_t>(gridDim.x) * kNT) {
@@ -305,8 +449,8 @@ __global__ void silu_mul_kernel(const uint16_t* gu, int64_t ld, int64_t I, int64
 // After the greedy pick of a forward over `rows` tokens: record the token and
 // move the state to the next position.
 __global__ void advance_kernel(const int64_t* idx, DecState* st, int32_t* tokens, int64_t max_tokens, int rows) {
-    griddep_wait();
     griddep_launch_dependents();
+    griddep_wait();
     if (threadIdx.x != 0 || blockIdx.x != 0) return;
     const int32_t t = static_cast<int32_t>(idx[0]);
     if (st->step < max_tokens) tokens[st->step] = t;
@@ -486,6 +630,12 @@ extern "C" int mrt_decoder_load(mrt_decoder d, const char* name_c, const void* s
     if (d->ready) return set_error(MRT_ERR_INVALID_ARG, "the decoder has already run; load every tensor first");
     const std::string name(name_c);
     cudaStream_t s = d->stream;
+    if (on_dev) {
+        // The decoder's stream does not order after the caller's streams: let
+        // every write of the source finish first (loading is one-time set-up).
+        cudaError_t e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) return cuda_error(e, "waiting for the source tensor");
+    }
     const int64_t H = d->H, D = d->D, kv = d->kvh * D, I = d->I;
     auto shape = [&](int64_t r, int64_t k) -> int {
         if (rows != r || cols != k)
@@ -646,8 +796,10 @@ int dec_finalize(mrt_decoder d) {
     cudaError_t e = cudaMemcpy(d->cos_t, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemcpy(d->sin_t, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice);
     if (e != cudaSuccess) return cuda_error(e, "uploading RoPE tables");
-    int64_t ns = (S + 31) / 32;
-    d->nsplit = static_cast<int>(ns < 1 ? 1 : (ns > 32 ? 32 : ns));
+    // Decode attention: one block per 32 cached positions per query head.
+    const int64_t ns = (S + kSplitKeys - 1) / kSplitKeys;
+    if (ns > 65535) return set_error(MRT_ERR_UNSUPPORTED, "max_seq_len above 2097120");
+    d->nsplit = static_cast<int>(ns);
     if ((rc = dec_alloc(d, reinterpret_cast<void**>(&d->part), static_cast<size_t>(d->heads * d->nsplit * (D + 2)) * 4, "attention scratch")) ||
         (rc = dec_alloc(d, reinterpret_cast<void**>(&d->counters), static_cast<size_t>(d->heads) * 4, "attention counters")) ||
         (rc = dec_alloc(d, reinterpret_cast<void**>(&d->am_idx), 8, "argmax output")) ||
@@ -660,11 +812,6 @@ int dec_finalize(mrt_decoder d) {
     if (e == cudaSuccess) e = cudaMemset(d->vc, 0, static_cast<size_t>(d->L * d->kvh * S * D) * 2);
     if (e != cudaSuccess) return cuda_error(e, "clearing decoder buffers");
     if (silu_lut_for_device(d->device) == nullptr) return set_error(MRT_ERR_CUDA, "building the SiLU table failed");
-    // One FP32 row of shared memory per block in the norm kernels.
-    e = cudaFuncSetAttribute(embed_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(H * 4));
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(add_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(H * 4));
-    if (e != cudaSuccess) return cuda_error(e, "configuring the norm kernels");
     d->ready = true;
     return MRT_OK;
 }
@@ -689,7 +836,7 @@ int dec_forward(mrt_decoder d, int64_t S, const int32_t* ids, int64_t pos0, bool
     DevCtx* ctx = current_ctx();
     if (!ctx) return MRT_ERR_CUDA;
     const int64_t H = d->H, D = d->D, I = d->I, nq = d->n_qkv, group = d->heads / d->kvh;
-    const size_t row_smem = static_cast<size_t>(H) * 4;
+    const size_t row_smem = 0;
     const float eps = d->cfg.rms_norm_eps;
     const float scale = 1.0f / std::sqrt(static_cast<float>(D));  // qwen_model.cpp:220
     const uint16_t* lut = silu_lut_for_device(d->device);
@@ -717,10 +864,9 @@ int dec_forward(mrt_decoder d, int64_t S, const int32_t* ids, int64_t pos0, bool
                           kc, vc, d->max_seq, d->state),
                "rope launch");
         if (decode) {
-            DEC_CU(launch_pdl(attn_decode_kernel, dim3(static_cast<unsigned>(d->heads), static_cast<unsigned>(d->nsplit)),
-                              dim3(kAttnWarps * 32), 0, s, d->qkv, kc, vc, d->attn, static_cast<int>(d->heads),
-                              static_cast<int>(group), static_cast<int>(D), d->max_seq, scale, d->state, d->part,
-                              d->counters),
+            DEC_CU(attn_decode(static_cast<int>(D), dim3(static_cast<unsigned>(d->heads), static_cast<unsigned>(d->nsplit)), s,
+                               d->qkv, kc, vc, d->attn, static_cast<int>(d->heads), static_cast<int>(group), d->max_seq,
+                               scale, d->state, d->part, d->counters),
                    "attention launch");
         } else {
             // Per kv head, its query heads over the cached keys (qwen_model.cpp:212-245).

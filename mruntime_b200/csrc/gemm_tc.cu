@@ -294,13 +294,16 @@ __global__ void __launch_bounds__(kThreadsTc, SWAP ? 2 : 1)
             uint32_t phase = 0;
             uint32_t issued = 0, issued_parity = 0;
             bool ok = true;
-            // The weight half of one ring stage (tiled weights only).
+            // The weight half of one ring stage (tiled weights only).  Decode
+            // (swap mode) reads each weight byte once per step: it streams with
+            // an evict-first L2 policy so the KV cache and activations stay cached.
+            const uint64_t stream_policy = l2_policy_evict_first();
             auto load_w = [&](const Unit& w, int kb, int st) {
                 if constexpr (SWAP) {
                     // W is A: one contiguous, already swizzled 128 x 64 tile.
-                    bulk_load(sA + st * Cfg::kABytes,
-                              a.w_tiled + tiled_offset(static_cast<int64_t>(w.mt) * kBM, static_cast<int64_t>(kb) * kBK, a.w_k_tiles),
-                              Cfg::kABytes, &full[st]);
+                    bulk_load_hint(sA + st * Cfg::kABytes,
+                                   a.w_tiled + tiled_offset(static_cast<int64_t>(w.mt) * kBM, static_cast<int64_t>(kb) * kBK, a.w_k_tiles),
+                                   Cfg::kABytes, &full[st], stream_policy);
                 } else {
                     // W is B: BN rows = BN/128 whole tiles, or half of one for BN = 64.
                     constexpr int kPieces = BN >= 128 ? BN / 128 : 1;
