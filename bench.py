@@ -61,6 +61,8 @@ def parse_args():
                     help="launch every step eagerly instead of replaying one captured CUDA graph")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
+    ap.add_argument("--no-decode", action="store_true", help="skip the 7B greedy-decode measurement")
+    ap.add_argument("--decode-tokens", type=int, default=64, help="tokens generated in the decode measurement")
     return ap.parse_args()
 
 
@@ -408,6 +410,57 @@ def gpu_arm(args, rank, world, local):
 
 
 # ---------------------------------------------------------------------------
+# Greedy decode of the 7B-shaped decoder (mrt_decoder_*), one GPU
+# ---------------------------------------------------------------------------
+
+DECODE_PROMPT = 512
+
+
+def decode_arm(peaks: dict, max_new: int) -> dict:
+    """tok/s of batch-1 greedy decoding on the Qwen2.5-7B-shaped decoder
+    (random N(0, 0.02) FP16 weights made on the GPU, RMSNorm gains 1, seeded
+    512-token prompt): prefill once, then `max_new` tokens; the decode rate
+    counts the graph-replayed steps (every step after the first)."""
+    import torch
+
+    from mruntime_b200 import capi
+
+    cfg = WL.DECODER_7B
+    dec = capi.Decoder(cfg, DECODE_PROMPT + max_new)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(3)
+    wbytes = 0
+    for name, shape, kind in WL.decoder_tensor_specs(cfg):
+        if kind == "ones":
+            t = torch.ones(shape, dtype=torch.float16, device="cuda")
+        else:
+            t = (torch.randn(shape, generator=g, device="cuda", dtype=torch.float32) * 0.02).half()
+            if name != "model.embed_tokens.weight":
+                wbytes += t.numel() * 2
+        dec.load(name, t.data_ptr(), capi.FP16, True, shape)
+        del t
+    prompt = WL.decoder_prompt(3, DECODE_PROMPT, cfg["vocab_size"])
+    launches0 = capi.launch_count()
+    dec.generate(prompt, max_new)  # warm: builds tables, sizes scratch
+    per_run = capi.launch_count() - launches0
+    toks, st = dec.generate(prompt, max_new)
+    dec.free()
+    ms = st.decode_ms / max(1, st.decode_steps)
+    gbs = wbytes / (ms * 1e-3) / 1e9
+    return {"metric": "Qwen2.5-7B-shaped greedy decode tokens/s (batch 1, 512-token prompt, 1 GPU)",
+            "value": round(1000.0 / ms, 1), "unit": "tokens/s", "ms_per_token": round(ms, 4),
+            "decode_steps_timed": st.decode_steps, "first_step_ms": round(st.first_step_ms, 3),
+            "prefill_ms": round(st.prefill_ms, 2), "prefill_tokens_per_s": round(DECODE_PROMPT / (st.prefill_ms * 1e-3), 1),
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(gbs / peaks["hbm_gbs"], 4),
+                         "algorithmic_bytes_per_token": wbytes,
+                         "note": "weights streamed once per token (all projections + lm_head); KV cache and "
+                                 "activations excluded"},
+            "gpu_launches_per_generate": per_run, "tokens_head": toks[:8],
+            "data": "synthetic (torch-seeded N(0,0.02) FP16 weights on the GPU, seeded prompt)"}
+
+
+# ---------------------------------------------------------------------------
 # CPU: the reference's own gemm (oracle/_ref, built from the reference sources)
 # ---------------------------------------------------------------------------
 
@@ -534,13 +587,18 @@ def main():
         except FileNotFoundError as e:
             cpu = {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "reference",
                    "sample": f"unavailable: {e}"}
+    decode = None
+    if rank == 0 and world == 1 and not args.no_decode:
+        r["projs"] = None  # release the sweep's weights first
+        decode = decode_arm(r["peaks"], args.decode_tokens)
     if rank == 0:
         line = {"metric": METRIC, "value": round(r["value"], 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(r["ms"], 5), "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)",
                 "data": "synthetic (seeded N(0,1) FP16 activations, N(0,0.02) BF16 weights)",
                 "config": workload_config(args.m, world, not args.no_graph), "e2e": r["e2e"], "roofline": r["roofline"],
-                "cpu_baseline": cpu, "clocks": r["clocks"], "gpu_launches": r["launches"], "sweep": r["sweep"]}
+                "cpu_baseline": cpu, "clocks": r["clocks"], "gpu_launches": r["launches"], "sweep": r["sweep"],
+                "decode": decode}
         print(json.dumps(line))
     if r["tp"] is not None:
         import gc

@@ -430,6 +430,166 @@ cudaError_t attn_decode(int D, dim3 grid, cudaStream_t s, const uint16_t* q, con
     }
 }
 
+constexpr int kPfTile = 64;    // queries per block and keys per step
+constexpr int kPfThreads = 256; // 16 query groups x 16 key (or dimension) groups
+
+// Causal prefill attention (cpu_backend.cpp:171-290 for q_len = S rows that
+// follow pos0 cached positions): block (h, tile) holds 64 queries of head h in
+// shared memory and walks key tiles of 64 from kv head h / group; thread
+// (tq, tk) scores queries 4 tq..+3 against keys 4 tk..+3, keeps the running
+// max and sum of exp for its rows (the 16 threads of a row share them through
+// shuffles) and accumulates dimensions tk * DPT..+DPT of the output.  Query q
+// sees keys <= pos0 + q.  out row s = fp16(acc * (1 / sum)) at [s, h, :].
+template <int DPT>
+__global__ void __launch_bounds__(kPfThreads)
+    attn_prefill_kernel(const uint16_t* __restrict__ qkv, int64_t ldq, int64_t S, int64_t pos0,
+                        const uint16_t* __restrict__ kc, const uint16_t* __restrict__ vc, int64_t max_seq,
+                        uint16_t* __restrict__ out, int64_t ldo, int group, float scale) {
+    griddep_launch_dependents();
+    griddep_wait();
+    constexpr int D = DPT * 16;
+    constexpr int LD = D + 1;
+    extern __shared__ float pf_smem[];
+    float* Qs = pf_smem;                    // [64][LD]
+    float* Ks = Qs + kPfTile * LD;          // [64][LD]
+    float* Vs = Ks + kPfTile * LD;          // [64][LD]
+    float* Ps = Vs + kPfTile * LD;          // [64][65]
+    const int h = blockIdx.x, g = h / group;
+    const int64_t q0 = static_cast<int64_t>(blockIdx.y) * kPfTile;
+    const int tid = threadIdx.x, tq = tid >> 4, tk = tid & 15;
+    for (int e = tid; e < kPfTile * D; e += kPfThreads) {
+        const int r = e / D, c = e % D;
+        const int64_t s = q0 + r;
+        Qs[r * LD + c] = s < S ? f16_bits_to_f32(qkv[s * ldq + static_cast<int64_t>(h) * D + c]) : 0.0f;
+    }
+    float m[4], l[4], o[4][DPT];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        m[i] = -INFINITY;
+        l[i] = 0.0f;
+#pragma unroll
+        for (int j = 0; j < DPT; ++j) o[i][j] = 0.0f;
+    }
+    const int64_t q_last = (q0 + kPfTile < S ? q0 + kPfTile : S) - 1;
+    const int64_t k_end = pos0 + q_last + 1;  // keys this tile can see
+    const uint16_t* kb = kc + static_cast<int64_t>(g) * max_seq * D;
+    const uint16_t* vb = vc + static_cast<int64_t>(g) * max_seq * D;
+    for (int64_t k0 = 0; k0 < k_end; k0 += kPfTile) {
+        __syncthreads();  // the previous tile's K, V and P are consumed
+        for (int e = tid; e < kPfTile * D; e += kPfThreads) {
+            const int r = e / D, c = e % D;
+            const int64_t kk = k0 + r;
+            const bool in = kk < k_end;
+            Ks[r * LD + c] = in ? f16_bits_to_f32(kb[kk * D + c]) : 0.0f;
+            Vs[r * LD + c] = in ? f16_bits_to_f32(vb[kk * D + c]) : 0.0f;
+        }
+        __syncthreads();
+        float sc[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) sc[i][j] = 0.0f;
+        for (int d = 0; d < D; ++d) {
+            float qv[4], kv[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) qv[i] = Qs[(tq * 4 + i) * LD + d];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) kv[j] = Ks[(tk * 4 + j) * LD + d];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) sc[i][j] = __fadd_rn(sc[i][j], __fmul_rn(qv[i], kv[j]));
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int64_t qpos = pos0 + q0 + tq * 4 + i;
+            float rmax = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int64_t kk = k0 + tk * 4 + j;
+                sc[i][j] = (kk <= qpos && kk < k_end) ? __fmul_rn(sc[i][j], scale) : -INFINITY;
+                rmax = fmaxf(rmax, sc[i][j]);
+            }
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) rmax = fmaxf(rmax, __shfl_xor_sync(0xFFFFFFFFu, rmax, off));
+            const float m_new = fmaxf(m[i], rmax);
+            // Rows past S (or with no visible key in this tile yet) stay at -inf.
+            const float corr = m_new == -INFINITY ? 1.0f : expf(__fsub_rn(m[i], m_new));
+            float psum = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float p = sc[i][j] == -INFINITY ? 0.0f : expf(__fsub_rn(sc[i][j], m_new));
+                Ps[(tq * 4 + i) * (kPfTile + 1) + tk * 4 + j] = p;
+                psum = __fadd_rn(psum, p);
+            }
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) psum = __fadd_rn(psum, __shfl_xor_sync(0xFFFFFFFFu, psum, off));
+            l[i] = __fadd_rn(__fmul_rn(l[i], corr), psum);
+#pragma unroll
+            for (int j = 0; j < DPT; ++j) o[i][j] = __fmul_rn(o[i][j], corr);
+            m[i] = m_new;
+        }
+        __syncthreads();
+        for (int k = 0; k < kPfTile; ++k) {
+            float vv[DPT];
+#pragma unroll
+            for (int j = 0; j < DPT; ++j) vv[j] = Vs[k * LD + tk * DPT + j];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float p = Ps[(tq * 4 + i) * (kPfTile + 1) + k];
+#pragma unroll
+                for (int j = 0; j < DPT; ++j) o[i][j] = __fadd_rn(o[i][j], __fmul_rn(p, vv[j]));
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int64_t s = q0 + tq * 4 + i;
+        if (s >= S) continue;
+        const float inv = __fdiv_rn(1.0f, l[i]);
+#pragma unroll
+        for (int j = 0; j < DPT; ++j)
+            out[s * ldo + static_cast<int64_t>(h) * D + tk * DPT + j] = f32_to_f16_bits(__fmul_rn(o[i][j], inv));
+    }
+}
+
+size_t prefill_smem(int D) { return static_cast<size_t>(3 * kPfTile * (D + 1) + kPfTile * (kPfTile + 1)) * 4; }
+
+template <int DPT>
+cudaError_t launch_attn_prefill_t(int heads, int64_t S, cudaStream_t s, const uint16_t* qkv, int64_t ldq, int64_t pos0,
+                                  const uint16_t* kc, const uint16_t* vc, int64_t max_seq, uint16_t* out, int64_t ldo,
+                                  int group, float scale) {
+    const size_t smem = prefill_smem(DPT * 16);
+    static bool set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(attn_prefill_kernel<DPT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+        set[dev] = true;
+    }
+    const dim3 grid(static_cast<unsigned>(heads), static_cast<unsigned>((S + kPfTile - 1) / kPfTile));
+    return launch_pdl(attn_prefill_kernel<DPT>, grid, dim3(kPfThreads), smem, s, qkv, ldq, S, pos0, kc, vc, max_seq,
+                      out, ldo, group, scale);
+}
+
+cudaError_t attn_prefill(int D, int heads, int64_t S, cudaStream_t s, const uint16_t* qkv, int64_t ldq, int64_t pos0,
+                         const uint16_t* kc, const uint16_t* vc, int64_t max_seq, uint16_t* out, int64_t ldo, int group,
+                         float scale) {
+    switch (D) {
+        case 32: return launch_attn_prefill_t<2>(heads, S, s, qkv, ldq, pos0, kc, vc, max_seq, out, ldo, group, scale);
+        case 64: return launch_attn_prefill_t<4>(heads, S, s, qkv, ldq, pos0, kc, vc, max_seq, out, ldo, group, scale);
+        case 96: return launch_attn_prefill_t<6>(heads, S, s, qkv, ldq, pos0, kc, vc, max_seq, out, ldo, group, scale);
+        case 128: return launch_attn_prefill_t<8>(heads, S, s, qkv, ldq, pos0, kc, vc, max_seq, out, ldo, group, scale);
+        case 160: return launch_attn_prefill_t<10>(heads, S, s, qkv, ldq, pos0, kc, vc, max_seq, out, ldo, group, scale);
+        case 192: return launch_attn_prefill_t<12>(heads, S, s, qkv, ldq, pos0, kc, vc, max_seq, out, ldo, group, scale);
+        case 224: return launch_attn_prefill_t<14>(heads, S, s, qkv, ldq, pos0, kc, vc, max_seq, out, ldo, group, scale);
+        case 256: return launch_attn_prefill_t<16>(heads, S, s, qkv, ldq, pos0, kc, vc, max_seq, out, ldo, group, scale);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
 // act = fp16(silu(gate) * up) with silu from the FP16 table
 // (qwen_model.cpp:281-285: silu rounded to FP16, then the product rounded).
 __global__ void silu_mul_kernel(const uint16_t* gu, int64_t ld, int64_t I, int64_t S, const uint16_t* lut,
@@ -869,13 +1029,10 @@ int dec_forward(mrt_decoder d, int64_t S, const int32_t* ids, int64_t pos0, bool
                                scale, d->state, d->part, d->counters),
                    "attention launch");
         } else {
-            // Per kv head, its query heads over the cached keys (qwen_model.cpp:212-245).
-            for (int64_t g = 0; g < d->kvh; ++g) {
-                const int64_t qs[4] = {0, D, nq, 1}, ks[4] = {0, 0, D, 1}, os[4] = {0, D, H, 1};
-                DEC_TRY(mrt_attention(d->qkv + g * group * D, MRT_FP16, qs, kc + g * d->max_seq * D, MRT_FP16, ks,
-                                      vc + g * d->max_seq * D, MRT_FP16, ks, d->attn + g * group * D, MRT_FP16, os, 1,
-                                      group, S, pos0 + S, D, D, scale, 1, s));
-            }
+            // Query head h over kv head h / group (qwen_model.cpp:212-245).
+            DEC_CU(attn_prefill(static_cast<int>(D), static_cast<int>(d->heads), S, s, d->qkv, nq, pos0, kc, vc,
+                                d->max_seq, d->attn, H, static_cast<int>(group), scale),
+                   "prefill attention launch");
         }
         DEC_TRY(mrt_gemm(ly.o, d->attn, H, d->p, H, S, 0, s));
         DEC_CU(launch_pdl(add_norm_kernel, dim3(static_cast<unsigned>(S)), dim3(kNT), row_smem, s, d->x, d->p, d->r, H,
