@@ -416,17 +416,19 @@ def gpu_arm(args, rank, world, local):
 DECODE_PROMPT = 512
 
 
-def decode_arm(peaks: dict, max_new: int) -> dict:
+def decode_arm(peaks: dict, max_new: int, tp=None, world: int = 1) -> dict:
     """tok/s of batch-1 greedy decoding on the Qwen2.5-7B-shaped decoder
     (random N(0, 0.02) FP16 weights made on the GPU, RMSNorm gains 1, seeded
     512-token prompt): prefill once, then `max_new` tokens; the decode rate
-    counts the graph-replayed steps (every step after the first)."""
+    counts the graph-replayed steps (every step after the first).  With a
+    tensor-parallel handle every rank runs its shard; times are the max over
+    ranks."""
     import torch
 
     from mruntime_b200 import capi
 
     cfg = WL.DECODER_7B
-    dec = capi.Decoder(cfg, DECODE_PROMPT + max_new)
+    dec = capi.Decoder(cfg, DECODE_PROMPT + max_new, tp)
     g = torch.Generator(device="cuda")
     g.manual_seed(3)
     wbytes = 0
@@ -445,17 +447,22 @@ def decode_arm(peaks: dict, max_new: int) -> dict:
     per_run = capi.launch_count() - launches0
     toks, st = dec.generate(prompt, max_new)
     dec.free()
-    ms = st.decode_ms / max(1, st.decode_steps)
+    ms = max_over_ranks(st.decode_ms, world) / max(1, st.decode_steps)
+    prefill_ms = max_over_ranks(st.prefill_ms, world)
+    first_ms = max_over_ranks(st.first_step_ms, world)
+    st.prefill_ms, st.first_step_ms = prefill_ms, first_ms
+    wbytes //= world  # each GPU streams its shard (replicated heads at 8 ranks add a little)
     gbs = wbytes / (ms * 1e-3) / 1e9
-    return {"metric": "Qwen2.5-7B-shaped greedy decode tokens/s (batch 1, 512-token prompt, 1 GPU)",
+    return {"metric": f"Qwen2.5-7B-shaped greedy decode tokens/s (batch 1, 512-token prompt, {world} GPU"
+                      f"{'s, tensor parallel' if world > 1 else ''})",
             "value": round(1000.0 / ms, 1), "unit": "tokens/s", "ms_per_token": round(ms, 4),
             "decode_steps_timed": st.decode_steps, "first_step_ms": round(st.first_step_ms, 3),
             "prefill_ms": round(st.prefill_ms, 2), "prefill_tokens_per_s": round(DECODE_PROMPT / (st.prefill_ms * 1e-3), 1),
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(gbs / peaks["hbm_gbs"], 4),
                          "algorithmic_bytes_per_token": wbytes,
-                         "note": "weights streamed once per token (all projections + lm_head); KV cache and "
-                                 "activations excluded"},
+                         "note": "per GPU: its weight shard streamed once per token (all projections + lm_head); "
+                                 "KV cache, activations and all-reduces excluded"},
             "gpu_launches_per_generate": per_run, "tokens_head": toks[:8],
             "data": "synthetic (torch-seeded N(0,0.02) FP16 weights on the GPU, seeded prompt)"}
 
@@ -588,9 +595,9 @@ def main():
             cpu = {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "reference",
                    "sample": f"unavailable: {e}"}
     decode = None
-    if rank == 0 and world == 1 and not args.no_decode:
+    if not args.no_decode:
         r["projs"] = None  # release the sweep's weights first
-        decode = decode_arm(r["peaks"], args.decode_tokens)
+        decode = decode_arm(r["peaks"], args.decode_tokens, r["tp"], world)
     if rank == 0:
         line = {"metric": METRIC, "value": round(r["value"], 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(r["ms"], 5), "higher_is_better": True, "scaling": "strong",

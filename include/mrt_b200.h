@@ -368,6 +368,16 @@ typedef struct mrt_decoder_stats {
 
 int mrt_decoder_create(const mrt_decoder_config* cfg, mrt_decoder* out);
 
+/* The same decoder, tensor-parallel over the ranks of `tp` (one process per
+ * GPU, every rank loads the full tensors and keeps its shard): q|k|v and
+ * gate|up column-parallel, o and down row-parallel (FP32 partials all-reduced
+ * and rounded once), lm_head sharded by vocabulary with the greedy pick
+ * combined across ranks, embedding and norms replicated.  Ranks own whole kv
+ * groups when world divides num_kv_heads; otherwise each kv head is kept on
+ * world / num_kv_heads ranks that split its query heads.  Every rank must
+ * make the same calls with the same prompt; all return the same tokens. */
+int mrt_decoder_create_tp(const mrt_decoder_config* cfg, mrt_tp tp, mrt_decoder* out);
+
 /* One checkpoint tensor by its Hugging Face / reference name
  * (qwen_model.cpp:54-101, 336-353): "model.embed_tokens.weight",
  * "model.layers.<i>.{input_layernorm,post_attention_layernorm}.weight",

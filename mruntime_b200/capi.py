@@ -90,6 +90,7 @@ _SIGS = {
     "mrt_tp_allgather_cols_f16": (_int, [_vp, _vp, _i64, _i64, _vp, _vp]),
     "mrt_tp_argmax": (_int, [_vp, _vp, _vp, _i64, _vp, _vp]),
     "mrt_decoder_create": (_int, [_vp, C.POINTER(_vp)]),
+    "mrt_decoder_create_tp": (_int, [_vp, _vp, C.POINTER(_vp)]),
     "mrt_decoder_load": (_int, [_vp, C.c_char_p, _vp, _int, _int, _i64, _i64]),
     "mrt_decoder_generate": (_int, [_vp, _vp, _i64, _i64, C.c_int32, _vp, C.POINTER(_i64), _vp, _vp]),
     "mrt_decoder_free": (None, [_vp]),
@@ -302,13 +303,16 @@ class Decoder:
     """Device-resident greedy decoder (mrt_decoder_*): load tensors by their
     checkpoint names, then generate."""
 
-    def __init__(self, hf_config: dict, max_seq_len: int):
+    def __init__(self, hf_config: dict, max_seq_len: int, tp: "TensorParallel | None" = None):
         cfg = DecoderConfig(hf_config["vocab_size"], hf_config["hidden_size"], hf_config["num_hidden_layers"],
                             hf_config["num_attention_heads"], hf_config["num_key_value_heads"],
                             hf_config["intermediate_size"], max_seq_len, hf_config.get("rms_norm_eps", 1e-6),
                             hf_config.get("rope_theta", 10000.0) or 10000.0)
         h = C.c_void_p()
-        call("mrt_decoder_create", C.byref(cfg), C.byref(h))
+        if tp is None:
+            call("mrt_decoder_create", C.byref(cfg), C.byref(h))
+        else:
+            call("mrt_decoder_create_tp", C.byref(cfg), tp.h, C.byref(h))
         self.h = h
 
     def load(self, name: str, ptr: int, dtype: int, on_device: bool, shape) -> None:

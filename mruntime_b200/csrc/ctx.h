@@ -52,6 +52,9 @@ EncodeTiledFn encode_tiled_fn();
 int make_tmap_f16(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld,
                   int box_rows);
 
+// Rank and world size of a tensor-parallel handle (tp.cu).
+int tp_rank_world(mrt_tp tp, int* rank, int* world);
+
 }  // namespace mrt
 
 // Opaque handle types of the public header.

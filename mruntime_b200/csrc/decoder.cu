@@ -301,7 +301,7 @@ __device__ __forceinline__ void load_per(const uint16_t* p, float (&x)[PER]) {
 template <int PER>
 __global__ void __launch_bounds__(kAttnWarps * 32)
     attn_decode_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ kc,
-                       const uint16_t* __restrict__ vc, uint16_t* __restrict__ out, int heads, int group,
+                       const uint16_t* __restrict__ vc, uint16_t* __restrict__ out, int group, int h0, int g0,
                        int64_t max_seq, float scale, const DecState* st, float* part, int* counters) {
     griddep_launch_dependents();
     griddep_wait();
@@ -309,8 +309,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32)
     __shared__ float sm_m[kAttnWarps], sm_l[kAttnWarps];
     __shared__ float sm_acc[kAttnWarps][D];
     __shared__ int sm_last;
+    // Local query head h is global head h0 + h; its kv head, local index g.
     const int h = blockIdx.x, sp = blockIdx.y, nsplit = gridDim.y;
-    const int g = h / group;
+    const int g = (h0 + h) / group - g0;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int64_t kv_len = static_cast<int64_t>(st->pos) + 1;
     if (kv_len > max_seq) kv_len = max_seq;
@@ -408,24 +409,24 @@ __global__ void __launch_bounds__(kAttnWarps * 32)
 
 template <int PER>
 cudaError_t launch_attn_decode(dim3 grid, cudaStream_t s, const uint16_t* q, const uint16_t* kc, const uint16_t* vc,
-                               uint16_t* out, int heads, int group, int64_t max_seq, float scale, const DecState* st,
-                               float* part, int* counters) {
-    return launch_pdl(attn_decode_kernel<PER>, grid, dim3(kAttnWarps * 32), 0, s, q, kc, vc, out, heads, group,
+                               uint16_t* out, int group, int h0, int g0, int64_t max_seq, float scale,
+                               const DecState* st, float* part, int* counters) {
+    return launch_pdl(attn_decode_kernel<PER>, grid, dim3(kAttnWarps * 32), 0, s, q, kc, vc, out, group, h0, g0,
                       max_seq, scale, st, part, counters);
 }
 
 cudaError_t attn_decode(int D, dim3 grid, cudaStream_t s, const uint16_t* q, const uint16_t* kc, const uint16_t* vc,
-                        uint16_t* out, int heads, int group, int64_t max_seq, float scale, const DecState* st,
+                        uint16_t* out, int group, int h0, int g0, int64_t max_seq, float scale, const DecState* st,
                         float* part, int* counters) {
     switch (D / 32) {
-        case 1: return launch_attn_decode<1>(grid, s, q, kc, vc, out, heads, group, max_seq, scale, st, part, counters);
-        case 2: return launch_attn_decode<2>(grid, s, q, kc, vc, out, heads, group, max_seq, scale, st, part, counters);
-        case 3: return launch_attn_decode<3>(grid, s, q, kc, vc, out, heads, group, max_seq, scale, st, part, counters);
-        case 4: return launch_attn_decode<4>(grid, s, q, kc, vc, out, heads, group, max_seq, scale, st, part, counters);
-        case 5: return launch_attn_decode<5>(grid, s, q, kc, vc, out, heads, group, max_seq, scale, st, part, counters);
-        case 6: return launch_attn_decode<6>(grid, s, q, kc, vc, out, heads, group, max_seq, scale, st, part, counters);
-        case 7: return launch_attn_decode<7>(grid, s, q, kc, vc, out, heads, group, max_seq, scale, st, part, counters);
-        case 8: return launch_attn_decode<8>(grid, s, q, kc, vc, out, heads, group, max_seq, scale, st, part, counters);
+        case 1: return launch_attn_decode<1>(grid, s, q, kc, vc, out, group, h0, g0, max_seq, scale, st, part, counters);
+        case 2: return launch_attn_decode<2>(grid, s, q, kc, vc, out, group, h0, g0, max_seq, scale, st, part, counters);
+        case 3: return launch_attn_decode<3>(grid, s, q, kc, vc, out, group, h0, g0, max_seq, scale, st, part, counters);
+        case 4: return launch_attn_decode<4>(grid, s, q, kc, vc, out, group, h0, g0, max_seq, scale, st, part, counters);
+        case 5: return launch_attn_decode<5>(grid, s, q, kc, vc, out, group, h0, g0, max_seq, scale, st, part, counters);
+        case 6: return launch_attn_decode<6>(grid, s, q, kc, vc, out, group, h0, g0, max_seq, scale, st, part, counters);
+        case 7: return launch_attn_decode<7>(grid, s, q, kc, vc, out, group, h0, g0, max_seq, scale, st, part, counters);
+        case 8: return launch_attn_decode<8>(grid, s, q, kc, vc, out, group, h0, g0, max_seq, scale, st, part, counters);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -444,7 +445,7 @@ template <int DPT>
 __global__ void __launch_bounds__(kPfThreads)
     attn_prefill_kernel(const uint16_t* __restrict__ qkv, int64_t ldq, int64_t S, int64_t pos0,
                         const uint16_t* __restrict__ kc, const uint16_t* __restrict__ vc, int64_t max_seq,
-                        uint16_t* __restrict__ out, int64_t ldo, int group, float scale) {
+                        uint16_t* __restrict__ out, int64_t ldo, int group, int h0, int g0, float scale) {
     griddep_launch_dependents();
     griddep_wait();
     constexpr int D = DPT * 16;
@@ -454,7 +455,7 @@ __global__ void __launch_bounds__(kPfThreads)
     float* Ks = Qs + kPfTile * LD;          // [64][LD]
     float* Vs = Ks + kPfTile * LD;          // [64][LD]
     float* Ps = Vs + kPfTile * LD;          // [64][65]
-    const int h = blockIdx.x, g = h / group;
+    const int h = blockIdx.x, g = (h0 + h) / group - g0;  // local query head, local kv head
     const int64_t q0 = static_cast<int64_t>(blockIdx.y) * kPfTile;
     const int tid = threadIdx.x, tq = tid >> 4, tk = tid & 15;
     for (int e = tid; e < kPfTile * D; e += kPfThreads) {
@@ -558,7 +559,7 @@ size_t prefill_smem(int D) { return static_cast<size_t>(3 * kPfTile * (D + 1) + 
 template <int DPT>
 cudaError_t launch_attn_prefill_t(int heads, int64_t S, cudaStream_t s, const uint16_t* qkv, int64_t ldq, int64_t pos0,
                                   const uint16_t* kc, const uint16_t* vc, int64_t max_seq, uint16_t* out, int64_t ldo,
-                                  int group, float scale) {
+                                  int group, int h0, int g0, float scale) {
     const size_t smem = prefill_smem(DPT * 16);
     static bool set[64] = {};
     int dev = 0;
@@ -571,21 +572,21 @@ cudaError_t launch_attn_prefill_t(int heads, int64_t S, cudaStream_t s, const ui
     }
     const dim3 grid(static_cast<unsigned>(heads), static_cast<unsigned>((S + kPfTile - 1) / kPfTile));
     return launch_pdl(attn_prefill_kernel<DPT>, grid, dim3(kPfThreads), smem, s, qkv, ldq, S, pos0, kc, vc, max_seq,
-                      out, ldo, group, scale);
+                      out, ldo, group, h0, g0, scale);
 }
 
 cudaError_t attn_prefill(int D, int heads, int64_t S, cudaStream_t s, const uint16_t* qkv, int64_t ldq, int64_t pos0,
                          const uint16_t* kc, const uint16_t* vc, int64_t max_seq, uint16_t* out, int64_t ldo, int group,
-                         float scale) {
+                         int h0, int g0, float scale) {
     switch (D) {
-        case 32: return launch_attn_prefill_t<2>(heads, S, s, qkv, ldq, pos0, kc, vc, max_seq, out, ldo, group, scale);
-        case 64: return launch_attn_prefill_t<4>(heads, S, s, qkv, ldq, pos0, kc, vc, max_seq, out, ldo, group, scale);
-        case 96: return launch_attn_prefill_t<6>(heads, S, s, qkv, ldq, pos0, kc, vc, max_seq, out, ldo, group, scale);
-        case 128: return launch_attn_prefill_t<8>(heads, S, s, qkv, ldq, pos0, kc, vc, max_seq, out, ldo, group, scale);
-        case 160: return launch_attn_prefill_t<10>(heads, S, s, qkv, ldq, pos0, kc, vc, max_seq, out, ldo, group, scale);
-        case 192: return launch_attn_prefill_t<12>(heads, S, s, qkv, ldq, pos0, kc, vc, max_seq, out, ldo, group, scale);
-        case 224: return launch_attn_prefill_t<14>(heads, S, s, qkv, ldq, pos0, kc, vc, max_seq, out, ldo, group, scale);
-        case 256: return launch_attn_prefill_t<16>(heads, S, s, qkv, ldq, pos0, kc, vc, max_seq, out, ldo, group, scale);
+        case 32: return launch_attn_prefill_t<2>(heads, S, s, qkv, ldq, pos0, kc, vc, max_seq, out, ldo, group, h0, g0, scale);
+        case 64: return launch_attn_prefill_t<4>(heads, S, s, qkv, ldq, pos0, kc, vc, max_seq, out, ldo, group, h0, g0, scale);
+        case 96: return launch_attn_prefill_t<6>(heads, S, s, qkv, ldq, pos0, kc, vc, max_seq, out, ldo, group, h0, g0, scale);
+        case 128: return launch_attn_prefill_t<8>(heads, S, s, qkv, ldq, pos0, kc, vc, max_seq, out, ldo, group, h0, g0, scale);
+        case 160: return launch_attn_prefill_t<10>(heads, S, s, qkv, ldq, pos0, kc, vc, max_seq, out, ldo, group, h0, g0, scale);
+        case 192: return launch_attn_prefill_t<12>(heads, S, s, qkv, ldq, pos0, kc, vc, max_seq, out, ldo, group, h0, g0, scale);
+        case 224: return launch_attn_prefill_t<14>(heads, S, s, qkv, ldq, pos0, kc, vc, max_seq, out, ldo, group, h0, g0, scale);
+        case 256: return launch_attn_prefill_t<16>(heads, S, s, qkv, ldq, pos0, kc, vc, max_seq, out, ldo, group, h0, g0, scale);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -647,7 +648,13 @@ struct DecLayer {
 struct mrt_decoder_s {
     int device = 0;
     mrt_decoder_config cfg{};
-    int64_t H = 0, D = 0, heads = 0, kvh = 0, I = 0, V = 0, L = 0, max_seq = 0, n_qkv = 0;
+    int64_t H = 0, D = 0, heads = 0, kvh = 0, I = 0, V = 0, L = 0, max_seq = 0;
+    // Tensor parallelism (world 1 without a handle): this rank's query heads
+    // [h0, h0 + nh), kv heads [g0, g0 + nkv), intermediate columns [i0, i1) and
+    // vocabulary rows [v0, v1); n_qkv = local q|k|v rows.
+    mrt_tp tp = nullptr;
+    int rank = 0, world = 1;
+    int64_t h0 = 0, nh = 0, g0 = 0, nkv = 0, i0 = 0, i1 = 0, v0 = 0, v1 = 0, n_qkv = 0;
     std::vector<DecLayer> layers;
     uint16_t* embed = nullptr;  // [V, H] FP16 row-major
     mrt_weight lm_head = nullptr;
@@ -666,6 +673,8 @@ struct mrt_decoder_s {
     int64_t tokens_cap = 0;
     int32_t* ids = nullptr;
     int64_t ids_cap = 0;
+    float* partial = nullptr;   // FP32 row-parallel partials [max_seq, H] (world > 1)
+    int64_t* am_gidx = nullptr; // the greedy pick across vocabulary shards
     int nsplit = 1;
     cudaStream_t stream = nullptr;
     std::vector<void*> allocs;
@@ -742,7 +751,34 @@ bool parse_layer(const std::string& name, int64_t* layer, std::string* suffix) {
 
 }  // namespace
 
-extern "C" int mrt_decoder_create(const mrt_decoder_config* cfg, mrt_decoder* out) {
+namespace {
+
+// Query heads [h0, h0 + nh) and kv heads [g0, g0 + nkv) of `rank`: whole kv
+// groups per rank when world divides the kv heads, else every kv head is
+// replicated on world / kv_heads ranks that split its query heads.
+bool head_split(int64_t heads, int64_t kvh, int world, int rank, int64_t* h0, int64_t* nh, int64_t* g0, int64_t* nkv) {
+    const int64_t group = heads / kvh;
+    if (world <= kvh) {
+        if (kvh % world != 0) return false;
+        *nkv = kvh / world;
+        *g0 = rank * *nkv;
+        *h0 = *g0 * group;
+        *nh = *nkv * group;
+        return true;
+    }
+    if (world % kvh != 0) return false;
+    const int64_t R = world / kvh;  // ranks per kv head
+    if (group < R) return false;
+    const int64_t g = rank / R, j = rank % R;
+    const int64_t a = group * j / R, b = group * (j + 1) / R;
+    *g0 = g;
+    *nkv = 1;
+    *h0 = g * group + a;
+    *nh = b - a;
+    return true;
+}
+
+int dec_create(const mrt_decoder_config* cfg, mrt_tp tp, mrt_decoder* out) {
     clear_error();
     if (out == nullptr || cfg == nullptr) return set_error(MRT_ERR_INVALID_ARG, "NULL config or out");
     *out = nullptr;
@@ -771,7 +807,34 @@ extern "C" int mrt_decoder_create(const mrt_decoder_config* cfg, mrt_decoder* ou
     d->V = c.vocab_size;
     d->L = c.num_layers;
     d->max_seq = c.max_seq_len;
-    d->n_qkv = d->H + 2 * d->kvh * D;
+    d->tp = tp;
+    if (tp != nullptr) {
+        int rc = tp_rank_world(tp, &d->rank, &d->world);
+        if (rc != MRT_OK) {
+            delete d;
+            return rc;
+        }
+    }
+    if (!head_split(d->heads, d->kvh, d->world, d->rank, &d->h0, &d->nh, &d->g0, &d->nkv)) {
+        delete d;
+        return set_error(MRT_ERR_UNSUPPORTED, "the attention heads do not split over " + std::to_string(d->world) +
+                                                  " ranks (need world | kv_heads, or kv_heads | world <= heads)");
+    }
+    if (d->world > 1) {
+        int rc = mrt_shard_cols(d->I, d->world, d->rank, &d->i0, &d->i1);
+        if (rc != MRT_OK || (d->i1 - d->i0) % 8 != 0) {
+            delete d;
+            return rc != MRT_OK ? rc : set_error(MRT_ERR_UNSUPPORTED, "intermediate_size must split into multiples of 8");
+        }
+        d->v0 = d->V * d->rank / d->world;
+        d->v1 = d->V * (d->rank + 1) / d->world;
+    } else {
+        d->i0 = 0;
+        d->i1 = d->I;
+        d->v0 = 0;
+        d->v1 = d->V;
+    }
+    d->n_qkv = (d->nh + 2 * d->nkv) * D;
     d->layers.resize(static_cast<size_t>(d->L));
     cudaError_t e = cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking);
     if (e != cudaSuccess) {
@@ -780,6 +843,20 @@ extern "C" int mrt_decoder_create(const mrt_decoder_config* cfg, mrt_decoder* ou
     }
     *out = d;
     return MRT_OK;
+}
+
+}  // namespace
+
+extern "C" int mrt_decoder_create(const mrt_decoder_config* cfg, mrt_decoder* out) {
+    return dec_create(cfg, nullptr, out);
+}
+
+extern "C" int mrt_decoder_create_tp(const mrt_decoder_config* cfg, mrt_tp tp, mrt_decoder* out) {
+    if (tp == nullptr) {
+        clear_error();
+        return set_error(MRT_ERR_INVALID_ARG, "NULL tensor-parallel handle");
+    }
+    return dec_create(cfg, tp, out);
 }
 
 extern "C" int mrt_decoder_load(mrt_decoder d, const char* name_c, const void* src, int dt, int on_dev, int64_t rows,
@@ -815,7 +892,8 @@ extern "C" int mrt_decoder_load(mrt_decoder d, const char* name_c, const void* s
         if ((rc = shape(d->V, H)) != MRT_OK) return rc;
         if (d->lm_head) mrt_weight_free(d->lm_head);
         d->lm_head = nullptr;
-        return mrt_weight_upload(src, dt, on_dev, d->V, H, nullptr, 0, 0, H, s, &d->lm_head);
+        const int64_t vr[2] = {d->v0, d->v1};  // this rank's vocabulary rows
+        return mrt_weight_upload(src, dt, on_dev, d->V, H, vr, 1, 0, H, s, &d->lm_head);
     }
     if (name == "model.norm.weight") {
         if ((rc = shape(H, 1)) != MRT_OK) return rc;
@@ -843,12 +921,21 @@ extern "C" int mrt_decoder_load(mrt_decoder d, const char* name_c, const void* s
         mrt_weight& w = o ? ly.o : ly.down;
         if (w) mrt_weight_free(w);
         w = nullptr;
-        return mrt_weight_upload(src, dt, on_dev, H, o ? H : I, nullptr, 0, 0, o ? H : I, s, &w);
+        // Row-parallel: this rank's input columns (its heads' attention
+        // outputs for o, its intermediate columns for down).
+        const int64_t k0 = o ? d->h0 * D : d->i0, k1 = o ? (d->h0 + d->nh) * D : d->i1;
+        return mrt_weight_upload(src, dt, on_dev, H, o ? H : I, nullptr, 0, k0, k1, s, &w);
     }
     // q|k|v rows [0, H), [H, H + kv), [H + kv, H + 2 kv) of one weight.
     static const char* qkv_w[3] = {"self_attn.q_proj.weight", "self_attn.k_proj.weight", "self_attn.v_proj.weight"};
     static const char* qkv_b[3] = {"self_attn.q_proj.bias", "self_attn.k_proj.bias", "self_attn.v_proj.bias"};
-    const int64_t off[3] = {0, H, H + kv}, len[3] = {H, kv, kv};
+    // Full part rows, this rank's first row within the part, its row count
+    // and where those rows go in the local fused weight.
+    const int64_t len[3] = {H, kv, kv};
+    const int64_t first[3] = {d->h0 * D, d->g0 * D, d->g0 * D};
+    const int64_t take[3] = {d->nh * D, d->nkv * D, d->nkv * D};
+    const int64_t off[3] = {0, d->nh * D, (d->nh + d->nkv) * D};
+    const char* csrc = static_cast<const char*>(src);
     for (int part = 0; part < 3; ++part) {
         if (suf == qkv_w[part]) {
             if ((rc = shape(len[part], H)) != MRT_OK) return rc;
@@ -856,7 +943,9 @@ extern "C" int mrt_decoder_load(mrt_decoder d, const char* name_c, const void* s
             if (ly.st_qkv == nullptr &&
                 (rc = dec_alloc(d, reinterpret_cast<void**>(&ly.st_qkv), static_cast<size_t>(d->n_qkv * H) * 2, "staging q|k|v")) != MRT_OK)
                 return rc;
-            if ((rc = to_f16(src, dt, on_dev != 0, len[part] * H, ly.st_qkv + off[part] * H, s)) != MRT_OK) return rc;
+            if ((rc = to_f16(csrc + first[part] * H * static_cast<int64_t>(es_of(dt)), dt, on_dev != 0, take[part] * H,
+                             ly.st_qkv + off[part] * H, s)) != MRT_OK)
+                return rc;
             ly.qkv_have |= 1u << part;
             if (ly.qkv_have == 7u) {
                 rc = upload_f16(ly.st_qkv, d->n_qkv, H, s, &ly.qkv);
@@ -872,7 +961,9 @@ extern "C" int mrt_decoder_load(mrt_decoder d, const char* name_c, const void* s
                 (rc = dec_alloc(d, reinterpret_cast<void**>(&ly.st_bias), static_cast<size_t>(d->n_qkv) * 2, "staging q|k|v biases")) != MRT_OK)
                 return rc;
             // The reference converts biases to FP16 at load (qwen_model.cpp:93-101).
-            if ((rc = to_f16(src, dt, on_dev != 0, len[part], ly.st_bias + off[part], s)) != MRT_OK) return rc;
+            if ((rc = to_f16(csrc + first[part] * static_cast<int64_t>(es_of(dt)), dt, on_dev != 0, take[part],
+                             ly.st_bias + off[part], s)) != MRT_OK)
+                return rc;
             ly.bias_have |= 1u << part;
             return MRT_OK;
         }
@@ -881,13 +972,16 @@ extern "C" int mrt_decoder_load(mrt_decoder d, const char* name_c, const void* s
         const int part = suf[4] == 'g' ? 0 : 1;
         if ((rc = shape(I, H)) != MRT_OK) return rc;
         if (ly.gateup != nullptr) return set_error(MRT_ERR_INVALID_ARG, name + ": the fused gate|up weight is already built");
+        const int64_t il = d->i1 - d->i0;  // this rank's intermediate rows
         if (ly.st_gu == nullptr &&
-            (rc = dec_alloc(d, reinterpret_cast<void**>(&ly.st_gu), static_cast<size_t>(2 * I * H) * 2, "staging gate|up")) != MRT_OK)
+            (rc = dec_alloc(d, reinterpret_cast<void**>(&ly.st_gu), static_cast<size_t>(2 * il * H) * 2, "staging gate|up")) != MRT_OK)
             return rc;
-        if ((rc = to_f16(src, dt, on_dev != 0, I * H, ly.st_gu + part * I * H, s)) != MRT_OK) return rc;
+        if ((rc = to_f16(static_cast<const char*>(src) + d->i0 * H * static_cast<int64_t>(es_of(dt)), dt, on_dev != 0, il * H,
+                         ly.st_gu + part * il * H, s)) != MRT_OK)
+            return rc;
         ly.gu_have |= 1u << part;
         if (ly.gu_have == 3u) {
-            rc = upload_f16(ly.st_gu, 2 * I, H, s, &ly.gateup);
+            rc = upload_f16(ly.st_gu, 2 * il, H, s, &ly.gateup);
             dec_release(d, ly.st_gu);
             ly.st_gu = nullptr;
             return rc;
@@ -923,8 +1017,9 @@ int dec_finalize(mrt_decoder d) {
         }
     }
     if (d->lm_head == nullptr) {
-        // Tied embeddings (qwen_model.cpp:346-352).
-        int rc = upload_f16(d->embed, d->V, d->H, d->stream, &d->lm_head);
+        // Tied embeddings (qwen_model.cpp:346-352): this rank's vocabulary rows.
+        const int64_t vr[2] = {d->v0, d->v1};
+        int rc = mrt_weight_upload(d->embed, MRT_FP16, 1, d->V, d->H, vr, 1, 0, d->H, d->stream, &d->lm_head);
         if (rc != MRT_OK) return rc;
     }
     const int64_t S = d->max_seq, H = d->H, D = d->D;
@@ -934,10 +1029,13 @@ int dec_finalize(mrt_decoder d) {
     };
     if ((rc = act(&d->x, S * H, "activations")) || (rc = act(&d->r, S * H, "activations")) ||
         (rc = act(&d->p, S * H, "activations")) || (rc = act(&d->normed, S * H, "activations")) ||
-        (rc = act(&d->qkv, S * d->n_qkv, "activations")) || (rc = act(&d->attn, S * H, "activations")) ||
-        (rc = act(&d->gu, S * 2 * d->I, "activations")) || (rc = act(&d->act, S * d->I, "activations")) ||
-        (rc = act(&d->logits, d->V, "logits")) || (rc = act(&d->kc, d->L * d->kvh * S * D, "the KV cache")) ||
-        (rc = act(&d->vc, d->L * d->kvh * S * D, "the KV cache")))
+        (rc = act(&d->qkv, S * d->n_qkv, "activations")) || (rc = act(&d->attn, S * d->nh * D, "activations")) ||
+        (rc = act(&d->gu, S * 2 * (d->i1 - d->i0), "activations")) || (rc = act(&d->act, S * (d->i1 - d->i0), "activations")) ||
+        (rc = act(&d->logits, d->v1 - d->v0, "logits")) || (rc = act(&d->kc, d->L * d->nkv * S * D, "the KV cache")) ||
+        (rc = act(&d->vc, d->L * d->nkv * S * D, "the KV cache")))
+        return rc;
+    if (d->world > 1 &&
+        (rc = dec_alloc(d, reinterpret_cast<void**>(&d->partial), static_cast<size_t>(S * H) * 4, "row-parallel partials")))
         return rc;
     // RoPE tables with the reference's float expressions (cpu_backend.cpp:363-366).
     const int64_t half = D / 2;
@@ -960,16 +1058,17 @@ int dec_finalize(mrt_decoder d) {
     const int64_t ns = (S + kSplitKeys - 1) / kSplitKeys;
     if (ns > 65535) return set_error(MRT_ERR_UNSUPPORTED, "max_seq_len above 2097120");
     d->nsplit = static_cast<int>(ns);
-    if ((rc = dec_alloc(d, reinterpret_cast<void**>(&d->part), static_cast<size_t>(d->heads * d->nsplit * (D + 2)) * 4, "attention scratch")) ||
-        (rc = dec_alloc(d, reinterpret_cast<void**>(&d->counters), static_cast<size_t>(d->heads) * 4, "attention counters")) ||
+    if ((rc = dec_alloc(d, reinterpret_cast<void**>(&d->part), static_cast<size_t>(d->nh * d->nsplit * (D + 2)) * 4, "attention scratch")) ||
+        (rc = dec_alloc(d, reinterpret_cast<void**>(&d->counters), static_cast<size_t>(d->nh) * 4, "attention counters")) ||
         (rc = dec_alloc(d, reinterpret_cast<void**>(&d->am_idx), 8, "argmax output")) ||
+        (rc = dec_alloc(d, reinterpret_cast<void**>(&d->am_gidx), 8, "argmax output")) ||
         (rc = dec_alloc(d, reinterpret_cast<void**>(&d->am_val), 4, "argmax output")) ||
-        (rc = dec_alloc(d, &d->am_scratch, argmax_scratch_bytes(1, d->V), "argmax scratch")) ||
+        (rc = dec_alloc(d, &d->am_scratch, argmax_scratch_bytes(1, d->v1 - d->v0), "argmax scratch")) ||
         (rc = dec_alloc(d, reinterpret_cast<void**>(&d->state), sizeof(DecState), "decoder state")))
         return rc;
-    e = cudaMemset(d->counters, 0, static_cast<size_t>(d->heads) * 4);
-    if (e == cudaSuccess) e = cudaMemset(d->kc, 0, static_cast<size_t>(d->L * d->kvh * S * D) * 2);
-    if (e == cudaSuccess) e = cudaMemset(d->vc, 0, static_cast<size_t>(d->L * d->kvh * S * D) * 2);
+    e = cudaMemset(d->counters, 0, static_cast<size_t>(d->nh) * 4);
+    if (e == cudaSuccess) e = cudaMemset(d->kc, 0, static_cast<size_t>(d->L * d->nkv * S * D) * 2);
+    if (e == cudaSuccess) e = cudaMemset(d->vc, 0, static_cast<size_t>(d->L * d->nkv * S * D) * 2);
     if (e != cudaSuccess) return cuda_error(e, "clearing decoder buffers");
     if (silu_lut_for_device(d->device) == nullptr) return set_error(MRT_ERR_CUDA, "building the SiLU table failed");
     d->ready = true;
@@ -995,12 +1094,20 @@ int dec_forward(mrt_decoder d, int64_t S, const int32_t* ids, int64_t pos0, bool
     cudaStream_t s = d->stream;
     DevCtx* ctx = current_ctx();
     if (!ctx) return MRT_ERR_CUDA;
-    const int64_t H = d->H, D = d->D, I = d->I, nq = d->n_qkv, group = d->heads / d->kvh;
+    const int64_t H = d->H, D = d->D, nq = d->n_qkv, group = d->heads / d->kvh;
+    const int64_t il = d->i1 - d->i0, nh = d->nh, ad = d->nh * D;  // local widths
     const size_t row_smem = 0;
     const float eps = d->cfg.rms_norm_eps;
     const float scale = 1.0f / std::sqrt(static_cast<float>(D));  // qwen_model.cpp:220
     const uint16_t* lut = silu_lut_for_device(d->device);
-    const int64_t kv_layer = d->kvh * d->max_seq * D;
+    const int64_t kv_layer = d->nkv * d->max_seq * D;
+    // Row-parallel output: FP32 partials, summed across ranks, rounded once.
+    auto row_parallel = [&](mrt_weight w, const uint16_t* x, int64_t ldx) -> int {
+        if (d->world == 1) return mrt_gemm(w, x, ldx, d->p, H, S, 0, s);
+        int rc = mrt_gemm_f32(w, x, ldx, d->partial, H, S, s);
+        if (rc != MRT_OK) return rc;
+        return mrt_tp_allreduce_f32_to_f16(d->tp, d->partial, d->p, S * H, s);
+    };
     auto grid_for = [](int64_t n) {
         int64_t b = (n + kNT - 1) / kNT;
         return static_cast<unsigned>(b < 1 ? 1 : (b > 148 * 16 ? 148 * 16 : b));
@@ -1019,38 +1126,46 @@ int dec_forward(mrt_decoder d, int64_t S, const int32_t* ids, int64_t pos0, bool
         DEC_TRY(mrt_gemm(ly.qkv, d->normed, H, d->qkv, nq, S, ly.qkv_bias ? MRT_GEMM_BIAS : 0, s));
         uint16_t* kc = d->kc + l * kv_layer;
         uint16_t* vc = d->vc + l * kv_layer;
-        DEC_CU(launch_pdl(rope_append_kernel, dim3(grid_for(S * (d->heads + d->kvh) * (D / 2))), dim3(kNT), 0, s, d->qkv, nq, S,
-                          static_cast<int>(d->heads), static_cast<int>(d->kvh), static_cast<int>(D), d->cos_t, d->sin_t,
+        DEC_CU(launch_pdl(rope_append_kernel, dim3(grid_for(S * (nh + d->nkv) * (D / 2))), dim3(kNT), 0, s, d->qkv, nq, S,
+                          static_cast<int>(nh), static_cast<int>(d->nkv), static_cast<int>(D), d->cos_t, d->sin_t,
                           kc, vc, d->max_seq, d->state),
                "rope launch");
         if (decode) {
-            DEC_CU(attn_decode(static_cast<int>(D), dim3(static_cast<unsigned>(d->heads), static_cast<unsigned>(d->nsplit)), s,
-                               d->qkv, kc, vc, d->attn, static_cast<int>(d->heads), static_cast<int>(group), d->max_seq,
-                               scale, d->state, d->part, d->counters),
+            DEC_CU(attn_decode(static_cast<int>(D), dim3(static_cast<unsigned>(nh), static_cast<unsigned>(d->nsplit)), s,
+                               d->qkv, kc, vc, d->attn, static_cast<int>(group), static_cast<int>(d->h0),
+                               static_cast<int>(d->g0), d->max_seq, scale, d->state, d->part, d->counters),
                    "attention launch");
         } else {
             // Query head h over kv head h / group (qwen_model.cpp:212-245).
-            DEC_CU(attn_prefill(static_cast<int>(D), static_cast<int>(d->heads), S, s, d->qkv, nq, pos0, kc, vc,
-                                d->max_seq, d->attn, H, static_cast<int>(group), scale),
+            DEC_CU(attn_prefill(static_cast<int>(D), static_cast<int>(nh), S, s, d->qkv, nq, pos0, kc, vc, d->max_seq,
+                                d->attn, ad, static_cast<int>(group), static_cast<int>(d->h0), static_cast<int>(d->g0),
+                                scale),
                    "prefill attention launch");
         }
-        DEC_TRY(mrt_gemm(ly.o, d->attn, H, d->p, H, S, 0, s));
+        DEC_TRY(row_parallel(ly.o, d->attn, ad));
         DEC_CU(launch_pdl(add_norm_kernel, dim3(static_cast<unsigned>(S)), dim3(kNT), row_smem, s, d->x, d->p, d->r, H,
                           ly.ln2, ly.ln2_dt, eps, d->normed),
                "add+rmsnorm launch");
-        DEC_TRY(mrt_gemm(ly.gateup, d->normed, H, d->gu, 2 * I, S, 0, s));
-        DEC_CU(launch_pdl(silu_mul_kernel, dim3(grid_for(S * I)), dim3(kNT), 0, s, d->gu, 2 * I, I, S, lut, d->act),
+        DEC_TRY(mrt_gemm(ly.gateup, d->normed, H, d->gu, 2 * il, S, 0, s));
+        DEC_CU(launch_pdl(silu_mul_kernel, dim3(grid_for(S * il)), dim3(kNT), 0, s, d->gu, 2 * il, il, S, lut, d->act),
                "silu*mul launch");
-        DEC_TRY(mrt_gemm(ly.down, d->act, I, d->p, H, S, 0, s));
+        DEC_TRY(row_parallel(ly.down, d->act, il));
     }
     // Final residual and norm of the last row, lm_head, greedy pick.
     const int64_t last = (S - 1) * H;
     DEC_CU(launch_pdl(add_norm_kernel, dim3(1), dim3(kNT), row_smem, s, d->r + last, d->p + last, d->x + last, H, d->norm,
                       d->norm_dt, eps, d->normed + last),
            "final norm launch");
-    DEC_TRY(mrt_gemm(d->lm_head, d->normed + last, H, d->logits, d->V, 1, 0, s));
-    DEC_CU(launch_argmax(d->logits, 1, d->V, d->V, 0, d->am_idx, d->am_val, d->am_scratch, s), "argmax launch");
-    DEC_CU(launch_pdl(advance_kernel, dim3(1), dim3(32), 0, s, d->am_idx, d->state, d->tokens, d->tokens_cap,
+    const int64_t vl = d->v1 - d->v0;
+    DEC_TRY(mrt_gemm(d->lm_head, d->normed + last, H, d->logits, vl, 1, 0, s));
+    DEC_CU(launch_argmax(d->logits, 1, vl, vl, d->v0, d->am_idx, d->am_val, d->am_scratch, s), "argmax launch");
+    const int64_t* pick = d->am_idx;
+    if (d->world > 1) {
+        // Vocabulary shards: the first maximum over every rank's (value, index).
+        DEC_TRY(mrt_tp_argmax(d->tp, d->am_val, d->am_idx, 1, d->am_gidx, s));
+        pick = d->am_gidx;
+    }
+    DEC_CU(launch_pdl(advance_kernel, dim3(1), dim3(32), 0, s, pick, d->state, d->tokens, d->tokens_cap,
                       static_cast<int>(S)),
            "advance launch");
     return MRT_OK;

@@ -75,6 +75,15 @@ struct mrt_tp_s {
 
 using namespace mrt;
 
+namespace mrt {
+int tp_rank_world(mrt_tp tp, int* rank, int* world) {
+    if (tp == nullptr) return set_error(MRT_ERR_INVALID_ARG, "NULL tensor-parallel handle");
+    *rank = tp->rank;
+    *world = tp->world;
+    return MRT_OK;
+}
+}  // namespace mrt
+
 extern "C" int mrt_shard_rows(const int64_t* part_rows, int64_t n_parts, int world, int rank,
                               int64_t* ranges_out) {
     clear_error();
