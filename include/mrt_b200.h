@@ -400,6 +400,8 @@ int mrt_decoder_generate(mrt_decoder d, const int32_t* prompt, int64_t n_prompt,
                          int32_t eos_token_id, int32_t* out_tokens, int64_t* n_out,
                          mrt_decoder_stats* stats, void* stream);
 
+/* Releases the decoder.  For a tensor-parallel decoder this is collective:
+ * every rank calls it (ranks unmap each other's exchange buffers first). */
 void mrt_decoder_free(mrt_decoder d);
 
 #ifdef __cplusplus

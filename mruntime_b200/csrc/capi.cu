@@ -178,9 +178,10 @@ extern "C" int mrt_sync(void* stream) {
         if (c->counters != nullptr) cudaMemset(c->counters, 0, c->counters_bytes);
         if (flag == 6)  // kErrBadToken: the decoder's embedding met an id outside the vocabulary
             return set_error(MRT_ERR_INVALID_ARG, "embedding_lookup: token_id out of range (device error code 6)");
-        static const char* what[] = {"", "TMA producer", "MMA issuer", "epilogue", "clean-up", "wait self-test"};
+        static const char* what[] = {"", "TMA producer", "MMA issuer", "epilogue", "clean-up", "wait self-test",
+                                     "embedding", "peer all-reduce"};
         return set_error(MRT_ERR_TIMEOUT, std::string("a kernel wait timed out in the ") +
-                                              (flag > 0 && flag < 6 ? what[flag] : "kernel") +
+                                              (flag > 0 && flag < 8 ? what[flag] : "kernel") +
                                               " (device error code " + std::to_string(flag) + ")");
     }
     return MRT_OK;

@@ -22,6 +22,7 @@ enum : int {
     kErrDrainWait = 4, // clean-up wait for in-flight copies/MMAs gave up
     kErrSelfTest = 5,  // mrt_selftest_wait_timeout's wait gave up (expected)
     kErrBadToken = 6,  // the decoder's embedding met a token id outside the vocabulary
+    kErrPeerWait = 7,  // a cross-GPU all-reduce gave up waiting for a peer's partial
 };
 
 // Wall-clock limit of one bounded wait, in nanoseconds of %globaltimer.

@@ -54,6 +54,9 @@ int make_tmap_f16(CUtensorMap* map, const void* base, int64_t rows, int64_t cols
 
 // Rank and world size of a tensor-parallel handle (tp.cu).
 int tp_rank_world(mrt_tp tp, int* rank, int* world);
+// Every rank's `bytes` host bytes, gathered in rank order into out[world * bytes]
+// (synchronous; every rank of tp must call it).
+int tp_allgather_host(mrt_tp tp, const void* in, void* out, size_t bytes);
 
 }  // namespace mrt
 

@@ -591,6 +591,122 @@ cudaError_t attn_prefill(int D, int heads, int64_t S, cudaStream_t s, const uint
     }
 }
 
+constexpr int kMaxRanks = 8;
+
+// Where every rank's exchange region is, as this rank sees it (own region
+// included): the FP32 partial buffer of one call site and the flag array
+// (one 64-bit slot per source rank).
+struct PeerArgs {
+    const float* buf[kMaxRanks];
+    unsigned long long* flags[kMaxRanks];
+    int rank, world;
+};
+
+__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Row-parallel output finished across GPUs, fused with the residual add and
+// RMSNorm that consume it (qwen_model.cpp:321-332).  Every rank's GEMM left
+// its FP32 partial rows in its own exchange buffer.  Block 0 publishes this
+// rank's epoch to every peer (system-scope release store); each block waits
+// (bounded, 2 s) for every peer's epoch, then reads all W partials of its row
+// over NVLink and sums them in rank order -- the same order on every rank, so
+// every rank holds bit-identical rows -- rounds once to FP16 (the projection's
+// output), and continues as add_norm_kernel: out = fp16(a + p), normed =
+// RMSNorm(out).  Rows row0 .. row0 + gridDim.x - 1.  The epoch of call c of a
+// forward is *epoch_base + c + 1; epoch_base advances by the calls per forward.
+// A peer that never arrives leaves its partial out and raises kErrPeerWait.
+__global__ void __launch_bounds__(kNT)
+    ar_add_norm_kernel(const PeerArgs pa, int64_t row0, const uint16_t* __restrict__ a, uint16_t* __restrict__ out,
+                       int64_t H, const void* __restrict__ w, int wdt, float eps, uint16_t* __restrict__ normed,
+                       const unsigned long long* epoch_base, int call, int* err) {
+    griddep_launch_dependents();
+    griddep_wait();
+    __shared__ float red[kNT / 32];
+    __shared__ unsigned arrived;  // bit q: rank q's partial may be read
+    const unsigned long long epoch = *epoch_base + static_cast<unsigned long long>(call) + 1ull;
+    if (threadIdx.x == 0) {
+        if (blockIdx.x == 0) {
+            __threadfence_system();  // this rank's partial (written by the previous kernel) before the flag
+            for (int q = 0; q < pa.world; ++q)
+                if (q != pa.rank) st_release_sys(pa.flags[q] + pa.rank, epoch);
+        }
+        unsigned got = 1u << pa.rank;
+        const unsigned long long t0 = global_ns();
+        bool timed_out = false;
+        for (int q = 0; q < pa.world; ++q) {
+            if (q == pa.rank) continue;
+            while (true) {
+                if (ld_acquire_sys(pa.flags[pa.rank] + q) >= epoch) {
+                    got |= 1u << q;
+                    break;
+                }
+                if (global_ns() - t0 > kWaitLimitNs) {
+                    timed_out = true;
+                    break;
+                }
+            }
+            if (timed_out) break;
+        }
+        if (timed_out) raise_error(err, kErrPeerWait);
+        arrived = got;
+    }
+    __syncthreads();
+    const unsigned got = arrived;
+    const int64_t row = row0 + blockIdx.x;
+    const int nv = static_cast<int>(H / 8);
+    float x[kNormVec][8];
+#pragma unroll
+    for (int j = 0; j < kNormVec; ++j) {
+        const int i = static_cast<int>(threadIdx.x) + j * kNT;
+        if (i >= nv) continue;
+        const int64_t e0 = row * H + static_cast<int64_t>(i) * 8;
+        float4 p0[kMaxRanks], p1[kMaxRanks];
+#pragma unroll
+        for (int q = 0; q < kMaxRanks; ++q)
+            if (q < pa.world && (got >> q & 1u)) {
+                p0[q] = __ldcg(reinterpret_cast<const float4*>(pa.buf[q] + e0));
+                p1[q] = __ldcg(reinterpret_cast<const float4*>(pa.buf[q] + e0 + 4));
+            }
+        float acc[8];
+        bool first = true;
+#pragma unroll
+        for (int q = 0; q < kMaxRanks; ++q) {
+            if (!(q < pa.world && (got >> q & 1u))) continue;
+            const float v[8] = {p0[q].x, p0[q].y, p0[q].z, p0[q].w, p1[q].x, p1[q].y, p1[q].z, p1[q].w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[e] = first ? v[e] : __fadd_rn(acc[e], v[e]);
+            first = false;
+        }
+        const uint4 va = ld16(a + e0);
+        float fa[8];
+        unpack8(va, fa);
+        uint16_t h[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const float pv = f16_bits_to_f32(f32_to_f16_bits(acc[e]));  // the projection's FP16 output
+            h[e] = f32_to_f16_bits(__fadd_rn(fa[e], pv));
+            x[j][e] = f16_bits_to_f32(h[e]);
+        }
+        *reinterpret_cast<uint4*>(out + e0) =
+            make_uint4(pack2(h[0], h[1]), pack2(h[2], h[3]), pack2(h[4], h[5]), pack2(h[6], h[7]));
+    }
+    norm_vecs(x, nv, H, w, wdt, eps, normed + row * H, red);
+}
+
 // act = fp16(silu(gate) * up) with silu from the FP16 table
 // (qwen_model.cpp:281-285: silu rounded to FP16, then the product rounded).
 __global__ void silu_mul_kernel(const uint16_t* gu, int64_t ld, int64_t I, int64_t S, const uint16_t* lut,
@@ -609,7 +725,10 @@ __global__ void silu_mul_kernel(const uint16_t* gu, int64_t ld, int64_t I, int64
 
 // After the greedy pick of a forward over `rows` tokens: record the token and
 // move the state to the next position.
-__global__ void advance_kernel(const int64_t* idx, DecState* st, int32_t* tokens, int64_t max_tokens, int rows) {
+// The cross-GPU all-reduce epoch base (when there is one) advances by the
+// number of all-reduce calls a forward makes.
+__global__ void advance_kernel(const int64_t* idx, DecState* st, int32_t* tokens, int64_t max_tokens, int rows,
+                               unsigned long long* epoch_base, int calls) {
     griddep_launch_dependents();
     griddep_wait();
     if (threadIdx.x != 0 || blockIdx.x != 0) return;
@@ -618,6 +737,7 @@ __global__ void advance_kernel(const int64_t* idx, DecState* st, int32_t* tokens
     st->step += 1;
     st->token = t;
     st->pos += rows;
+    if (epoch_base != nullptr) *epoch_base += static_cast<unsigned long long>(calls);
 }
 
 }  // namespace
@@ -673,8 +793,16 @@ struct mrt_decoder_s {
     int64_t tokens_cap = 0;
     int32_t* ids = nullptr;
     int64_t ids_cap = 0;
-    float* partial = nullptr;   // FP32 row-parallel partials [max_seq, H] (world > 1)
+    float* partial = nullptr;   // FP32 row-parallel partials [max_seq, H] (world > 1, NCCL path)
     int64_t* am_gidx = nullptr; // the greedy pick across vocabulary shards
+    // Peer all-reduce (world > 1): this rank's exchange region (flags, then
+    // one FP32 partial buffer per row-parallel call site), the peers' regions
+    // mapped through CUDA IPC, and the device epoch counter.
+    bool p2p = false;
+    void* xreg = nullptr;
+    void* peer_reg[kMaxRanks] = {};
+    PeerArgs pa[2] = {};
+    unsigned long long* ar_epoch = nullptr;
     int nsplit = 1;
     cudaStream_t stream = nullptr;
     std::vector<void*> allocs;
@@ -993,6 +1121,73 @@ extern "C" int mrt_decoder_load(mrt_decoder d, const char* name_c, const void* s
 
 namespace {
 
+constexpr size_t kFlagBytes = 256;  // kMaxRanks 64-bit flags, padded
+
+// Exchange regions for the peer all-reduce: every rank exports its region by
+// CUDA IPC, the handles travel over the NCCL communicator, and each rank maps
+// its peers' regions.  Any failure leaves p2p off (the NCCL path is used).
+int dec_setup_p2p(mrt_decoder d) {
+    const size_t buf_bytes = static_cast<size_t>(d->max_seq * d->H) * 4;
+    const size_t region = kFlagBytes + 2 * buf_bytes;
+    int rc = dec_alloc(d, &d->xreg, region, "the all-reduce exchange region");
+    if (rc != MRT_OK) return rc;
+    rc = dec_alloc(d, reinterpret_cast<void**>(&d->ar_epoch), 8, "the all-reduce epoch");
+    if (rc != MRT_OK) return rc;
+    cudaError_t e = cudaMemset(d->xreg, 0, kFlagBytes);
+    if (e == cudaSuccess) e = cudaMemset(d->ar_epoch, 0, 8);
+    if (e != cudaSuccess) return cuda_error(e, "clearing the exchange flags");
+    cudaIpcMemHandle_t mine{};
+    e = cudaIpcGetMemHandle(&mine, d->xreg);
+    int ok = e == cudaSuccess ? 1 : 0;
+    struct Rec {
+        cudaIpcMemHandle_t h;
+        int ok;
+        int pad[15];
+    } rec{mine, ok, {}};
+    std::vector<Rec> all(static_cast<size_t>(d->world));
+    rc = tp_allgather_host(d->tp, &rec, all.data(), sizeof(Rec));
+    if (rc != MRT_OK) return rc;
+    bool every = true;
+    for (const Rec& r : all) every = every && r.ok;
+    if (every) {
+        for (int q = 0; q < d->world && every; ++q) {
+            if (q == d->rank) {
+                d->peer_reg[q] = d->xreg;
+                continue;
+            }
+            e = cudaIpcOpenMemHandle(&d->peer_reg[q], all[static_cast<size_t>(q)].h, cudaIpcMemLazyEnablePeerAccess);
+            if (e != cudaSuccess) {
+                d->peer_reg[q] = nullptr;
+                every = false;
+                cudaGetLastError();
+            }
+        }
+    }
+    // Every rank must agree before using the peer path.
+    int mine_ok = every ? 1 : 0;
+    std::vector<int> oks(static_cast<size_t>(d->world));
+    rc = tp_allgather_host(d->tp, &mine_ok, oks.data(), sizeof(int));
+    if (rc != MRT_OK) return rc;
+    for (int v : oks) every = every && v;
+    if (!every) {
+        for (int q = 0; q < d->world; ++q)
+            if (q != d->rank && d->peer_reg[q]) cudaIpcCloseMemHandle(d->peer_reg[q]);
+        for (auto& r : d->peer_reg) r = nullptr;
+        return MRT_OK;
+    }
+    for (int par = 0; par < 2; ++par) {
+        d->pa[par].rank = d->rank;
+        d->pa[par].world = d->world;
+        for (int q = 0; q < d->world; ++q) {
+            char* base = static_cast<char*>(d->peer_reg[q]);
+            d->pa[par].buf[q] = reinterpret_cast<const float*>(base + kFlagBytes + par * buf_bytes);
+            d->pa[par].flags[q] = reinterpret_cast<unsigned long long*>(base);
+        }
+    }
+    d->p2p = true;
+    return MRT_OK;
+}
+
 // Checks every tensor is present, ties lm_head to the embedding when absent,
 // and allocates the KV cache, activations, RoPE tables and scratch.
 int dec_finalize(mrt_decoder d) {
@@ -1037,6 +1232,7 @@ int dec_finalize(mrt_decoder d) {
     if (d->world > 1 &&
         (rc = dec_alloc(d, reinterpret_cast<void**>(&d->partial), static_cast<size_t>(S * H) * 4, "row-parallel partials")))
         return rc;
+    if (d->world > 1 && d->world <= kMaxRanks && (rc = dec_setup_p2p(d)) != MRT_OK) return rc;
     // RoPE tables with the reference's float expressions (cpu_backend.cpp:363-366).
     const int64_t half = D / 2;
     std::vector<float> cs(static_cast<size_t>(S * half)), sn(static_cast<size_t>(S * half));
@@ -1102,12 +1298,25 @@ int dec_forward(mrt_decoder d, int64_t S, const int32_t* ids, int64_t pos0, bool
     const uint16_t* lut = silu_lut_for_device(d->device);
     const int64_t kv_layer = d->nkv * d->max_seq * D;
     // Row-parallel output: FP32 partials, summed across ranks, rounded once.
-    auto row_parallel = [&](mrt_weight w, const uint16_t* x, int64_t ldx) -> int {
+    // With the peer path the partial stays in this rank's exchange buffer of
+    // the call site (0 = o, 1 = down) and the next add+norm kernel finishes it.
+    auto row_parallel = [&](mrt_weight w, const uint16_t* x, int64_t ldx, int site) -> int {
         if (d->world == 1) return mrt_gemm(w, x, ldx, d->p, H, S, 0, s);
+        if (d->p2p) return mrt_gemm_f32(w, x, ldx, const_cast<float*>(d->pa[site].buf[d->rank]), H, S, s);
         int rc = mrt_gemm_f32(w, x, ldx, d->partial, H, S, s);
         if (rc != MRT_OK) return rc;
         return mrt_tp_allreduce_f32_to_f16(d->tp, d->partial, d->p, S * H, s);
     };
+    // out = fp16(a + the row-parallel output of `site`), normed = RMSNorm(out).
+    auto add_norm = [&](const uint16_t* a, uint16_t* out, const void* gw, int gdt, int site, int call, int64_t row0,
+                        int64_t rows) -> cudaError_t {
+        if (d->p2p)
+            return launch_pdl(ar_add_norm_kernel, dim3(static_cast<unsigned>(rows)), dim3(kNT), 0, s, d->pa[site], row0, a,
+                              out, H, gw, gdt, eps, d->normed, d->ar_epoch, call, ctx->d_err);
+        return launch_pdl(add_norm_kernel, dim3(static_cast<unsigned>(rows)), dim3(kNT), row_smem, s, a + row0 * H,
+                          d->p + row0 * H, out + row0 * H, H, gw, gdt, eps, d->normed + row0 * H);
+    };
+    const int calls = static_cast<int>(2 * d->L);
     auto grid_for = [](int64_t n) {
         int64_t b = (n + kNT - 1) / kNT;
         return static_cast<unsigned>(b < 1 ? 1 : (b > 148 * 16 ? 148 * 16 : b));
@@ -1119,9 +1328,7 @@ int dec_forward(mrt_decoder d, int64_t S, const int32_t* ids, int64_t pos0, bool
                               ids, d->state, d->x, ly.ln1, ly.ln1_dt, eps, d->normed, ctx->d_err),
                    "embedding launch");
         } else {
-            DEC_CU(launch_pdl(add_norm_kernel, dim3(static_cast<unsigned>(S)), dim3(kNT), row_smem, s, d->r, d->p, d->x, H,
-                              ly.ln1, ly.ln1_dt, eps, d->normed),
-                   "add+rmsnorm launch");
+            DEC_CU(add_norm(d->r, d->x, ly.ln1, ly.ln1_dt, 1, static_cast<int>(2 * (l - 1) + 1), 0, S), "add+rmsnorm launch");
         }
         DEC_TRY(mrt_gemm(ly.qkv, d->normed, H, d->qkv, nq, S, ly.qkv_bias ? MRT_GEMM_BIAS : 0, s));
         uint16_t* kc = d->kc + l * kv_layer;
@@ -1142,20 +1349,16 @@ int dec_forward(mrt_decoder d, int64_t S, const int32_t* ids, int64_t pos0, bool
                                 scale),
                    "prefill attention launch");
         }
-        DEC_TRY(row_parallel(ly.o, d->attn, ad));
-        DEC_CU(launch_pdl(add_norm_kernel, dim3(static_cast<unsigned>(S)), dim3(kNT), row_smem, s, d->x, d->p, d->r, H,
-                          ly.ln2, ly.ln2_dt, eps, d->normed),
-               "add+rmsnorm launch");
+        DEC_TRY(row_parallel(ly.o, d->attn, ad, 0));
+        DEC_CU(add_norm(d->x, d->r, ly.ln2, ly.ln2_dt, 0, static_cast<int>(2 * l), 0, S), "add+rmsnorm launch");
         DEC_TRY(mrt_gemm(ly.gateup, d->normed, H, d->gu, 2 * il, S, 0, s));
         DEC_CU(launch_pdl(silu_mul_kernel, dim3(grid_for(S * il)), dim3(kNT), 0, s, d->gu, 2 * il, il, S, lut, d->act),
                "silu*mul launch");
-        DEC_TRY(row_parallel(ly.down, d->act, il));
+        DEC_TRY(row_parallel(ly.down, d->act, il, 1));
     }
     // Final residual and norm of the last row, lm_head, greedy pick.
     const int64_t last = (S - 1) * H;
-    DEC_CU(launch_pdl(add_norm_kernel, dim3(1), dim3(kNT), row_smem, s, d->r + last, d->p + last, d->x + last, H, d->norm,
-                      d->norm_dt, eps, d->normed + last),
-           "final norm launch");
+    DEC_CU(add_norm(d->r, d->x, d->norm, d->norm_dt, 1, calls - 1, S - 1, 1), "final norm launch");
     const int64_t vl = d->v1 - d->v0;
     DEC_TRY(mrt_gemm(d->lm_head, d->normed + last, H, d->logits, vl, 1, 0, s));
     DEC_CU(launch_argmax(d->logits, 1, vl, vl, d->v0, d->am_idx, d->am_val, d->am_scratch, s), "argmax launch");
@@ -1166,7 +1369,7 @@ int dec_forward(mrt_decoder d, int64_t S, const int32_t* ids, int64_t pos0, bool
         pick = d->am_gidx;
     }
     DEC_CU(launch_pdl(advance_kernel, dim3(1), dim3(32), 0, s, pick, d->state, d->tokens, d->tokens_cap,
-                      static_cast<int>(S)),
+                      static_cast<int>(S), d->p2p ? d->ar_epoch : nullptr, calls),
            "advance launch");
     return MRT_OK;
 }
@@ -1280,6 +1483,14 @@ extern "C" int mrt_decoder_generate(mrt_decoder d, const int32_t* prompt, int64_
 extern "C" void mrt_decoder_free(mrt_decoder d) {
     if (d == nullptr) return;
     cudaStreamSynchronize(d->stream);
+    if (d->p2p) {
+        for (int q = 0; q < d->world; ++q)
+            if (q != d->rank && d->peer_reg[q]) cudaIpcCloseMemHandle(d->peer_reg[q]);
+        // No rank frees its exchange region while a peer still maps it.
+        int one = 1;
+        std::vector<int> all(static_cast<size_t>(d->world));
+        tp_allgather_host(d->tp, &one, all.data(), sizeof(int));
+    }
     for (auto& ly : d->layers)
         for (mrt_weight w : {ly.qkv, ly.o, ly.gateup, ly.down})
             if (w) mrt_weight_free(w);

@@ -82,6 +82,29 @@ int tp_rank_world(mrt_tp tp, int* rank, int* world) {
     *world = tp->world;
     return MRT_OK;
 }
+
+int tp_allgather_host(mrt_tp tp, const void* in, void* out, size_t bytes) {
+    if (tp == nullptr || in == nullptr || out == nullptr) return set_error(MRT_ERR_INVALID_ARG, "NULL argument");
+    void* dev = nullptr;
+    cudaError_t e = cudaMalloc(&dev, bytes * (tp->world + 1));
+    if (e != cudaSuccess) return cuda_error(e, "allocating the exchange buffer");
+    char* mine = static_cast<char*>(dev) + bytes * tp->world;
+    e = cudaMemcpy(mine, in, bytes, cudaMemcpyHostToDevice);
+    int rc = MRT_OK;
+    if (e != cudaSuccess) {
+        rc = cuda_error(e, "staging the exchange buffer");
+    } else {
+        ncclResult_t r = g_nccl.AllGather(mine, dev, bytes, ncclUint8, tp->comm, nullptr);
+        if (r != ncclSuccess) {
+            rc = nccl_error(r, "ncclAllGather of exchange records");
+        } else {
+            e = cudaMemcpy(out, dev, bytes * tp->world, cudaMemcpyDeviceToHost);  // waits for the gather
+            if (e != cudaSuccess) rc = cuda_error(e, "reading the exchange records");
+        }
+    }
+    cudaFree(dev);
+    return rc;
+}
 }  // namespace mrt
 
 extern "C" int mrt_shard_rows(const int64_t* part_rows, int64_t n_parts, int world, int rank,

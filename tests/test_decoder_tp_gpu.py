@@ -87,9 +87,9 @@ def _worker(rank: int, world: int, port: int, out_dir: str, case: str):
             toks, st = dec.generate(prompt, 32)
             out["tokens"] = toks
             out["ms_per_token"] = st.decode_ms / max(1, st.decode_steps)
+            dec.free()  # collective: every rank frees its shard together
+            dec = None
             if rank == 0:
-                dec.free()
-                dec = None
                 one = capi.Decoder(cfg, 232)
                 _load_random(one, cfg, 5)
                 out["single"], _ = one.generate(prompt, 32)
