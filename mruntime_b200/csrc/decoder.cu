@@ -29,6 +29,7 @@
 // different order than the reference's sequential loops, so results agree
 // within FP32 rounding, not bit for bit.
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <string>
@@ -36,6 +37,7 @@
 
 #include "common.cuh"
 #include "ctx.h"
+#include "decode_step.h"
 #include "kernels.h"
 
 namespace mrt {
@@ -803,6 +805,11 @@ struct mrt_decoder_s {
     void* peer_reg[kMaxRanks] = {};
     PeerArgs pa[2] = {};
     unsigned long long* ar_epoch = nullptr;
+    // Persistent decode step (one launch per token) when the shapes allow it.
+    bool fused_step = false;
+    int step_grid = 0;
+    StepArgs step{};
+    StepLayer* step_layers = nullptr;
     int nsplit = 1;
     cudaStream_t stream = nullptr;
     std::vector<void*> allocs;
@@ -1121,6 +1128,17 @@ extern "C" int mrt_decoder_load(mrt_decoder d, const char* name_c, const void* s
 
 namespace {
 
+#define DEC_TRY(x)                   \
+    do {                             \
+        int rc_ = (x);               \
+        if (rc_ != MRT_OK) return rc_; \
+    } while (0)
+#define DEC_CU(x, what)                                   \
+    do {                                                  \
+        cudaError_t e_ = (x);                             \
+        if (e_ != cudaSuccess) return cuda_error(e_, what); \
+    } while (0)
+
 constexpr size_t kFlagBytes = 256;  // kMaxRanks 64-bit flags, padded
 
 // Exchange regions for the peer all-reduce: every rank exports its region by
@@ -1185,6 +1203,120 @@ int dec_setup_p2p(mrt_decoder d) {
         }
     }
     d->p2p = true;
+    return MRT_OK;
+}
+
+// The persistent decode-step kernel's tables and scratch.  It covers tiled
+// weights, head_dim 64 / 128 / 256, at most 256 intermediate rows per CTA,
+// and tensor parallelism over mapped peers; other decoders keep the per-op
+// step.
+int dec_setup_step(mrt_decoder d) {
+    // Opt-in while the per-op step is faster on the 7B shape:
+    // MRT_DECODE_STEP=persistent selects the persistent kernel.
+    const char* sel = std::getenv("MRT_DECODE_STEP");
+    if (sel == nullptr || std::string(sel) != "persistent") return MRT_OK;
+    if (d->world > 1 && !d->p2p) return MRT_OK;
+    const int grid = decode_step_grid();
+    if (grid <= 0) return MRT_OK;
+    const int64_t D = d->D, il = d->i1 - d->i0;
+    if (!(D == 64 || D == 128 || D == 256) || d->H % 8 != 0 || d->H > 16384) return MRT_OK;
+    if ((il + grid - 1) / grid > 256 || (d->nh * D) % 8 != 0 || il % 8 != 0) return MRT_OK;
+    for (auto& ly : d->layers)
+        for (mrt_weight w : {ly.qkv, ly.o, ly.gateup, ly.down})
+            if (!w->tiled) return MRT_OK;
+    if (!d->lm_head->tiled) return MRT_OK;
+    const int64_t att_split = std::max<int64_t>(1, grid / d->nh);
+    std::vector<StepLayer> hl(static_cast<size_t>(d->L));
+    const int64_t kv_layer = d->nkv * d->max_seq * D;
+    for (int64_t l = 0; l < d->L; ++l) {
+        const DecLayer& ly = d->layers[static_cast<size_t>(l)];
+        StepLayer& t = hl[static_cast<size_t>(l)];
+        t.qkv = ly.qkv->data;
+        t.bias = ly.qkv_bias ? ly.qkv->bias : nullptr;
+        t.o = ly.o->data;
+        t.gu = ly.gateup->data;
+        t.down = ly.down->data;
+        t.ln1 = ly.ln1;
+        t.ln2 = ly.ln2;
+        t.ln1_dt = ly.ln1_dt;
+        t.ln2_dt = ly.ln2_dt;
+        t.kc = d->kc + l * kv_layer;
+        t.vc = d->vc + l * kv_layer;
+    }
+    int rc;
+    StepArgs& a = d->step;
+    auto buf = [&](void** p, size_t bytes, const char* w) { return dec_alloc(d, p, bytes, w); };
+    if ((rc = buf(reinterpret_cast<void**>(&d->step_layers), hl.size() * sizeof(StepLayer), "decode-step tables")) ||
+        (rc = buf(reinterpret_cast<void**>(&a.x), static_cast<size_t>(d->H) * 2, "decode-step scratch")) ||
+        (rc = buf(reinterpret_cast<void**>(&a.r1), static_cast<size_t>(d->H) * 2, "decode-step scratch")) ||
+        (rc = buf(reinterpret_cast<void**>(&a.qkv_out), static_cast<size_t>(d->n_qkv) * 2, "decode-step scratch")) ||
+        (rc = buf(reinterpret_cast<void**>(&a.attn), static_cast<size_t>(d->nh * D) * 2, "decode-step scratch")) ||
+        (rc = buf(reinterpret_cast<void**>(&a.yo), static_cast<size_t>(d->H) * 2, "decode-step scratch")) ||
+        (rc = buf(reinterpret_cast<void**>(&a.act), static_cast<size_t>(il) * 2, "decode-step scratch")) ||
+        (rc = buf(reinterpret_cast<void**>(&a.yd), static_cast<size_t>(d->H) * 2, "decode-step scratch")) ||
+        (rc = buf(reinterpret_cast<void**>(&a.att_part), static_cast<size_t>(d->nh * att_split * (D + 2)) * 4, "decode-step scratch")) ||
+        (rc = buf(reinterpret_cast<void**>(&a.att_cnt), static_cast<size_t>(d->nh) * 4, "decode-step scratch")) ||
+        (rc = buf(reinterpret_cast<void**>(&a.cand_val), static_cast<size_t>(grid) * 4, "decode-step scratch")) ||
+        (rc = buf(reinterpret_cast<void**>(&a.cand_idx), static_cast<size_t>(grid) * 8, "decode-step scratch")) ||
+        (rc = buf(reinterpret_cast<void**>(&a.bar), 256, "decode-step barrier")))
+        return rc;
+    cudaError_t e = cudaMemcpy(d->step_layers, hl.data(), hl.size() * sizeof(StepLayer), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemset(a.att_cnt, 0, static_cast<size_t>(d->nh) * 4);
+    if (e != cudaSuccess) return cuda_error(e, "initialising the decode step");
+    a.layers = d->step_layers;
+    a.L = static_cast<int>(d->L);
+    a.H = d->H;
+    a.D = D;
+    a.nh = d->nh;
+    a.nkv = d->nkv;
+    a.group = d->heads / d->kvh;
+    a.h0 = d->h0;
+    a.g0 = d->g0;
+    a.I = il;
+    a.V = d->v1 - d->v0;
+    a.max_seq = d->max_seq;
+    a.n_qkv = d->n_qkv;
+    a.embed = d->embed;
+    a.vocab = d->V;
+    a.norm = d->norm;
+    a.norm_dt = d->norm_dt;
+    a.lm = d->lm_head->data;
+    a.eps = d->cfg.rms_norm_eps;
+    a.scale = 1.0f / std::sqrt(static_cast<float>(D));  // qwen_model.cpp:220
+    a.cos_t = d->cos_t;
+    a.sin_t = d->sin_t;
+    a.silu_lut = silu_lut_for_device(d->device);
+    a.att_split = static_cast<int>(att_split);
+    a.st = reinterpret_cast<StepState*>(d->state);
+    a.err = current_ctx()->d_err;
+    a.rank = d->rank;
+    a.world = d->world;
+    a.v0 = d->v0;
+    if (d->world > 1) {
+        for (int q = 0; q < d->world; ++q) {
+            a.peer_buf[0][q] = d->pa[0].buf[q];
+            a.peer_buf[1][q] = d->pa[1].buf[q];
+            a.peer_flags[q] = d->pa[0].flags[q];
+            a.peer_cand[q] = reinterpret_cast<float*>(static_cast<char*>(d->peer_reg[q]) + 128);
+        }
+        a.epoch = d->ar_epoch;
+    }
+    d->step_grid = grid;
+    d->fused_step = true;
+    return MRT_OK;
+}
+
+// One decode step as a single persistent launch (the barrier counter is
+// cleared first; both are stream-ordered, so the pair can be captured).
+int dec_step_fused(mrt_decoder d) {
+    d->step.tokens = d->tokens;
+    d->step.tokens_cap = d->tokens_cap;
+    DEC_CU(cudaMemsetAsync(d->step.bar, 0, 256, d->stream), "clearing the step barrier");
+    const cudaError_t e = launch_decode_step(d->step, d->step_grid, d->stream);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(MRT_ERR_CUDA, std::string("decode-step launch: ") + cudaGetErrorString(e) + "; " + decode_step_diag());
+    }
     return MRT_OK;
 }
 
@@ -1267,20 +1399,11 @@ int dec_finalize(mrt_decoder d) {
     if (e == cudaSuccess) e = cudaMemset(d->vc, 0, static_cast<size_t>(d->L * d->nkv * S * D) * 2);
     if (e != cudaSuccess) return cuda_error(e, "clearing decoder buffers");
     if (silu_lut_for_device(d->device) == nullptr) return set_error(MRT_ERR_CUDA, "building the SiLU table failed");
+    if ((rc = dec_setup_step(d)) != MRT_OK) return rc;
     d->ready = true;
     return MRT_OK;
 }
 
-#define DEC_TRY(x)                   \
-    do {                             \
-        int rc_ = (x);               \
-        if (rc_ != MRT_OK) return rc_; \
-    } while (0)
-#define DEC_CU(x, what)                                   \
-    do {                                                  \
-        cudaError_t e_ = (x);                             \
-        if (e_ != cudaSuccess) return cuda_error(e_, what); \
-    } while (0)
 
 // One forward over S rows starting at the state's position: prefill
 // (ids = the prompt on the device, pos0 its host-known start) or one decode
@@ -1435,13 +1558,14 @@ extern "C" int mrt_decoder_generate(mrt_decoder d, const int32_t* prompt, int64_
     DEC_TRY(dec_forward(d, n_prompt, d->ids, 0, false));
     DEC_CU(cudaEventRecord(ev[1], s), "recording an event");
     int64_t replays = 0;
+    auto step = [&]() { return d->fused_step ? dec_step_fused(d) : dec_forward(d, 1, nullptr, 0, true); };
     if (max_new >= 2) {
-        DEC_TRY(dec_forward(d, 1, nullptr, 0, true));  // eager: sizes every scratch buffer
+        DEC_TRY(step());  // eager: sizes every scratch buffer
         DEC_CU(cudaEventRecord(ev[2], s), "recording an event");
         replays = max_new - 2;
         if (replays > 0) {
             DEC_CU(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "beginning the decode-step capture");
-            const int rc = dec_forward(d, 1, nullptr, 0, true);
+            const int rc = step();
             const cudaError_t ec = cudaStreamEndCapture(s, &cleanup.graph);
             if (rc != MRT_OK) return rc;
             DEC_CU(ec, "capturing the decode step");
