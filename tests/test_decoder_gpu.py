@@ -149,3 +149,61 @@ def test_7b_matches_reference_engine(cuda_dev):
           f"({1000.0 * st.decode_steps / max(st.decode_ms, 1e-9):.1f} tok/s); tokens {toks}")
     assert toks == g["tokens"], f"decoder {toks} != reference {g['tokens']}"
     dec.free()
+
+
+class _PersistentStep:
+    """Select the persistent decode-step kernel for decoders built inside."""
+
+    def __enter__(self):
+        self.old = os.environ.get("MRT_DECODE_STEP")
+        os.environ["MRT_DECODE_STEP"] = "persistent"
+
+    def __exit__(self, *exc):
+        if self.old is None:
+            os.environ.pop("MRT_DECODE_STEP", None)
+        else:
+            os.environ["MRT_DECODE_STEP"] = self.old
+
+
+def test_tiny_persistent_step_matches_reference_engine(cuda_dev):
+    g = _golden("tiny")
+    cfg = W.DECODER_TINY
+    prompt = W.decoder_prompt(g["seed"], g["prompt_len"], cfg["vocab_size"])
+    with _PersistentStep():  # read when the decoder finalises, at its first generate
+        dec = _build(cfg, g["prompt_len"] + g["max_new"], g["seed"])
+        toks, st = dec.generate(prompt, g["max_new"])
+    assert toks == g["tokens"], f"persistent step {toks} != reference {g['tokens']}"
+    assert st.decode_steps == g["max_new"] - 2
+    dec.free()
+
+
+def _random_7b_shape(layers: int, max_seq: int, seed: int) -> capi.Decoder:
+    cfg = dict(W.DECODER_7B)
+    cfg["num_hidden_layers"] = layers
+    dec = capi.Decoder(cfg, max_seq)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(seed)
+    for name, shape, kind in W.decoder_tensor_specs(cfg):
+        if kind == "ones":
+            t = torch.ones(shape, dtype=torch.float16, device="cuda")
+        else:
+            t = (torch.randn(shape, generator=gen, device="cuda", dtype=torch.float32) * 0.02).half()
+        dec.load(name, t.data_ptr(), capi.FP16, True, shape)
+        del t
+    return dec
+
+
+def test_persistent_step_matches_per_op_step_7b_shape(cuda_dev):
+    """The persistent kernel (FP32 sums on the tensor cores in its own order)
+    and the per-op kernels pick the same tokens on a 4-layer 7B-shaped model."""
+    prompt = W.decoder_prompt(13, 300, W.DECODER_7B["vocab_size"])
+    ops = _random_7b_shape(4, 340, 9)
+    t_ops, _ = ops.generate(prompt, 32)
+    ops.free()
+    with _PersistentStep():
+        per = _random_7b_shape(4, 340, 9)
+        t_per, st = per.generate(prompt, 32)
+    per.free()
+    same = sum(a == b for a, b in zip(t_ops, t_per))
+    print(f"persistent step {st.decode_ms / max(1, st.decode_steps):.3f} ms/token; {same}/32 tokens equal")
+    assert t_per[:16] == t_ops[:16], f"persistent {t_per} vs per-op {t_ops}"
