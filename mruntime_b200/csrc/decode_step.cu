@@ -94,10 +94,11 @@ __device__ bool grid_sync(const StepArgs& a, unsigned& nbar, int ct, volatile in
     ++nbar;
     if (ct == 0) {
         int ok = 1;
-        __threadfence();
-        const unsigned old = atomicAdd(a.bar, 1u);
+        unsigned old;
+        // Release this CTA's writes with the arrival; the last arrival also
+        // acquires everyone's and releases them with the flag.
+        asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(a.bar) : "memory");
         if (old == nbar * gridDim.x - 1) {
-            __threadfence();
             st_release_gpu_u32(a.bar + 32, nbar);
         } else {
             const unsigned long long t0 = now_ns();
@@ -126,7 +127,14 @@ struct Gemv {
     const uint16_t* w;
     int64_t kt;          // k-tiles (64 columns each)
     int64_t a0, a1, b0, b1;
+    // Split mode: units u = tile * kt + k-tile (128-row tile, 64-column
+    // k-tile) in [u0, u1), i.e. whole 16 KB tiles read front to back; the CTA
+    // leaves FP32 partial sums per tile it touches (at most two).
+    int split;
+    int64_t u0, u1, units;
 };
+
+
 
 __device__ __forceinline__ int64_t gemv_rows(const Gemv& g) { return (g.a1 - g.a0) + (g.b1 - g.b0); }
 
@@ -176,6 +184,18 @@ __device__ __forceinline__ void my_rows(int64_t n, int64_t* r0, int64_t* r1) {
     *r1 = n * (blockIdx.x + 1) / gridDim.x;
 }
 
+// Units of a split GEMV for this CTA: [U * c / G, U * (c + 1) / G).
+__device__ __forceinline__ Gemv split_gemv(const uint16_t* w, int64_t n, int64_t k) {
+    Gemv g{};
+    g.w = w;
+    g.kt = (k + 63) / 64;
+    g.split = 1;
+    g.units = ((n + 127) / 128) * g.kt;
+    g.u0 = g.units * blockIdx.x / gridDim.x;
+    g.u1 = g.units * (blockIdx.x + 1) / gridDim.x;
+    return g;
+}
+
 __device__ __forceinline__ Gemv gemv_of(const StepArgs& a, int l, int which) {
     Gemv g{};
     int64_t r0, r1;
@@ -198,9 +218,8 @@ __device__ __forceinline__ Gemv gemv_of(const StepArgs& a, int l, int which) {
             my_rows(a.I, &r0, &r1);
             g = Gemv{ly.gu, (a.H + 63) / 64, r0, r1, a.I + r0, a.I + r1};
             break;
-        default:  // down
-            my_rows(a.H, &r0, &r1);
-            g = Gemv{ly.down, (a.I + 63) / 64, r0, r1, 0, 0};
+        default:  // down, split along K: whole tiles, contiguous per CTA
+            g = split_gemv(ly.down, a.H, a.I);
             break;
     }
     return g;
@@ -227,6 +246,24 @@ __device__ void produce(const StepArgs& a, uint8_t* ring, uint64_t* full, uint64
         const int nw = l == a.L ? 1 : 4;
         for (int which = 0; which < nw && ok; ++which) {
             const Gemv g = gemv_of(a, l, which);
+            if (g.split) {
+                // Whole tiles, one per stage: unit u is the 16 KB at element u * 8192.
+                for (int64_t u = g.u0; u < g.u1; ++u) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, a.err, kErrTmaWait)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full[stage], kStage);
+                    bulk_load_hint(ring + static_cast<int64_t>(stage) * kStage, g.w + (u << 13), kStage, &full[stage], pol);
+                    issued |= 1u << stage;
+                    issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
+                    if (++stage == kRingStages) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                continue;
+            }
             const StageGeo geo = stage_geo(g);
             for (int64_t ch = 0; ch < geo.chunks && ok; ++ch) {
                 const int64_t cr0 = ch * kRowsPerChunk;
@@ -307,6 +344,139 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a
         "{%0, %1, %2, %3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Consumer side of a split GEMV: every stage is a whole 128 x 64 tile; warp w
+// takes row block w % 8 and k-steps {0, 1} (w < 8) or {2, 3} (w >= 8) of it.
+// When the unit range moves to the next tile (and at its end) the two k
+// halves are added through `red` and the tile's 128 FP32 row sums go to
+// part[blockIdx.x][segment][row] (segment 0 = first tile of the range).
+__device__ __forceinline__ bool gemv_split(const Gemv& g, const uint16_t* xs, const uint8_t* ring, uint64_t* full,
+                                           uint64_t* empty, int& stage, uint32_t& phase, int ct, int* err, float* red,
+                                           float* part) {
+    const int w = ct >> 5, lane = ct & 31;
+    const int rb = w & 7, kh2 = w >> 3;
+    const uint32_t ring_s = smem_u32(ring);
+    const uint32_t xs_s = smem_u32(xs);
+    const int rr = rb * 16 + (lane & 15);
+    const int kh = lane >> 4;
+    const int swz = rr & 7;
+    float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    int seg = 0;
+    int64_t tile = g.u0 / g.kt;
+    auto flush = [&]() {
+        if ((lane & 3) == 0) {
+            const int q = lane >> 2;
+            red[kh2 * 128 + rb * 16 + q] = d[0];
+            red[kh2 * 128 + rb * 16 + q + 8] = d[2];
+        }
+        cons_sync();
+        // A range of at most kt units touches at most two tiles (the host keeps
+        // the tiles no more than the CTAs); never write past the two slots.
+        if (ct < 128 && seg < 2) part[(static_cast<int64_t>(blockIdx.x) * 2 + seg) * 128 + ct] = red[ct] + red[128 + ct];
+        cons_sync();
+        d[0] = d[1] = d[2] = d[3] = 0.0f;
+    };
+    for (int64_t u = g.u0; u < g.u1; ++u) {
+        const int64_t t = u / g.kt, kt = u % g.kt;
+        if (t != tile) {
+            flush();
+            ++seg;
+            tile = t;
+        }
+        if (!mbar_wait(&full[stage], phase, err, kErrMmaWait)) return false;
+        const uint32_t rowb = ring_s + static_cast<uint32_t>(stage) * kStage + static_cast<uint32_t>(rr) * 128;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int st4 = 2 * kh2 + j;
+            uint32_t a0, a1, a2, a3;
+            ldsm_x4(rowb + (((2 * st4 + kh) ^ swz) << 4), a0, a1, a2, a3);
+            uint32_t b0 = 0, b1 = 0;
+            if (lane < 4) {
+                const uint32_t xa = xs_s + static_cast<uint32_t>((kt * 64 + st4 * 16 + 2 * lane) * 2);
+                asm volatile("ld.shared.b32 %0, [%1];" : "=r"(b0) : "r"(xa));
+                asm volatile("ld.shared.b32 %0, [%1];" : "=r"(b1) : "r"(xa + 16));
+            }
+            mma_16816(d, a0, a1, a2, a3, b0, b1);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[stage]);
+        if (++stage == kRingStages) {
+            stage = 0;
+            phase ^= 1u;
+        }
+    }
+    if (g.u1 > g.u0) flush();
+    return true;
+}
+
+// The CTAs that covered one 128-row tile of a split GEMV: c0 .. c1 in order;
+// c0's partial of the tile is in its segment seg0 (1 when its range began in
+// the tile before), every later CTA's in segment 0.  Units are < 2^31 / G, so
+// 32-bit arithmetic is exact.
+struct TileSrc {
+    int c0, c1, seg0;
+};
+
+__device__ __forceinline__ int unit_owner(int u, int units) {
+    const int G = static_cast<int>(gridDim.x);
+    int c = u * G / units;
+    while (c + 1 < G && units * (c + 1) / G <= u) ++c;
+    while (c > 0 && units * c / G > u) --c;
+    return c;
+}
+
+__device__ __forceinline__ TileSrc tile_src(int64_t t, int64_t kt, int64_t units) {
+    const int u = static_cast<int>(t * kt), U = static_cast<int>(units), G = static_cast<int>(gridDim.x);
+    TileSrc s;
+    s.c0 = unit_owner(u, U);
+    s.c1 = unit_owner(u + static_cast<int>(kt) - 1, U);
+    s.seg0 = (U * s.c0 / G) / static_cast<int>(kt) == static_cast<int>(t) ? 0 : 1;
+    return s;
+}
+
+__device__ __forceinline__ const float* tile_part(const float* part, const TileSrc& s, int c) {
+    return part + (c == s.c0 ? (static_cast<int64_t>(c) * 2 + s.seg0) * 128 : static_cast<int64_t>(c) * 256);
+}
+
+// Row r (0..127) of a tile: the CTAs' partials added in CTA order (loads of
+// up to 8 CTAs issued together).
+__device__ __forceinline__ float tile_sum(const float* part, const TileSrc& s, int r) {
+    float v = 0.0f;
+    for (int cb = s.c0; cb <= s.c1; cb += 8) {
+        float p[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) p[j] = cb + j <= s.c1 ? __ldcg(tile_part(part, s, cb + j) + r) : 0.0f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (cb + j <= s.c1) v = cb + j == s.c0 ? p[j] : __fadd_rn(v, p[j]);
+    }
+    return v;
+}
+
+// Rows r0 .. r0 + 7 of a tile (r0 a multiple of 8), as tile_sum.
+__device__ __forceinline__ void tile_sum8(const float* part, const TileSrc& s, int r0, float (&v)[8]) {
+    for (int cb = s.c0; cb <= s.c1; cb += 8) {
+        float4 p0[8], p1[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (cb + j <= s.c1) {
+                const float4* q = reinterpret_cast<const float4*>(tile_part(part, s, cb + j) + r0);
+                p0[j] = __ldcg(q);
+                p1[j] = __ldcg(q + 1);
+            }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if (cb + j > s.c1) continue;
+            const float w[8] = {p0[j].x, p0[j].y, p0[j].z, p0[j].w, p1[j].x, p1[j].y, p1[j].z, p1[j].w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[e] = cb + j == s.c0 ? w[e] : __fadd_rn(v[e], w[e]);
+        }
+    }
+}
+
+__device__ __forceinline__ float split_row(const float* part, int64_t n, int64_t kt, int64_t units) {
+    return tile_sum(part, tile_src(n >> 7, kt, units), static_cast<int>(n & 127));
 }
 
 template <typename Out>
@@ -549,13 +719,24 @@ __device__ __noinline__ void attention_unit(const StepArgs& a, const StepLayer& 
 // passes through xs (FP16 values are exact as floats), so no thread holds it
 // in registers.
 __device__ __noinline__ void add_norm_cons(const uint16_t* a, const uint16_t* b, int64_t H, const void* w, int wdt,
-                                           float eps, uint16_t* xs, uint16_t* res, int ct, float* red) {
+                                           float eps, uint16_t* xs, uint16_t* res, int ct, float* red,
+                                           const float* bpart = nullptr, int64_t bkt = 0, int64_t bunits = 0) {
     const int nv = static_cast<int>(H / 8);
     float ss = 0.0f;
     for (int v = ct; v < nv; v += kStepCons) {
         const uint4 va = *reinterpret_cast<const uint4*>(a + static_cast<int64_t>(v) * 8);
         uint4 vr = va;
-        if (b != nullptr) {
+        if (bpart != nullptr) {  // b = a split GEMV's rows, summed over its CTAs and rounded to FP16
+            float fa[8];
+            unpack8h(va, fa);
+            const int64_t n0 = static_cast<int64_t>(v) * 8;  // 8 rows of one tile
+            float bs[8];
+            tile_sum8(bpart, tile_src(n0 >> 7, bkt, bunits), static_cast<int>(n0 & 127), bs);
+            uint16_t h[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) h[e] = f32_to_f16_bits(__fadd_rn(fa[e], f16_bits_to_f32(f32_to_f16_bits(bs[e]))));
+            vr = make_uint4(pk2(h[0], h[1]), pk2(h[2], h[3]), pk2(h[4], h[5]), pk2(h[6], h[7]));
+        } else if (b != nullptr) {
             const uint4 vb = *reinterpret_cast<const uint4*>(b + static_cast<int64_t>(v) * 8);
             float fa[8], fb[8];
             unpack8h(va, fa);
@@ -642,7 +823,7 @@ __device__ __forceinline__ bool tp_wait(const StepArgs& a, unsigned long long ep
 // every rank), rounds once to FP16 into y, and a grid barrier hands y to
 // every CTA.
 __device__ __noinline__ bool tp_reduce(const StepArgs& a, int site, unsigned long long epoch, uint16_t* y, int ct,
-                                       unsigned& nbar, volatile int* ok_sh) {
+                                       unsigned& nbar, volatile int* ok_sh, int64_t kt = 0, int64_t units = 0) {
     if (ct == 0) {
         if (blockIdx.x == 0) tp_signal(a, epoch);
         *ok_sh = tp_wait(a, epoch) ? 1 : 0;
@@ -651,9 +832,14 @@ __device__ __noinline__ bool tp_reduce(const StepArgs& a, int site, unsigned lon
     if (!*ok_sh) return false;
     int64_t s0, s1;
     my_rows(a.H, &s0, &s1);
+    // Each rank's row: a plain FP32 row (units == 0) or a split GEMV's
+    // partials summed over its CTAs; ranks added in rank order.
+    auto rank_row = [&](int q, int64_t n) {
+        return units > 0 ? split_row(a.peer_buf[site][q], n, kt, units) : __ldcg(a.peer_buf[site][q] + n);
+    };
     for (int64_t n = s0 + ct; n < s1; n += kStepCons) {
-        float acc = __ldcg(a.peer_buf[site][0] + n);
-        for (int q = 1; q < a.world; ++q) acc = __fadd_rn(acc, __ldcg(a.peer_buf[site][q] + n));
+        float acc = rank_row(0, n);
+        for (int q = 1; q < a.world; ++q) acc = __fadd_rn(acc, rank_row(q, n));
         y[n] = f32_to_f16_bits(acc);
     }
     return grid_sync(a, nbar, ct, ok_sh);
@@ -757,21 +943,21 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         if (!grid_sync(a, nbar, ct, &ok_sh)) return;
         load_operand(xs, a.act, a.I, ((a.I + 63) / 64) * 64, ct);
         g = gemv_of(a, l, 3);
-        if (!gemv_consume(g, xs, ring, full, empty, stage, phase, ct, a.err, red_rows, [&](int64_t row, float v) {
-                const int64_t n = gemv_grow(g, row);
-                if (tp)
-                    const_cast<float*>(a.peer_buf[1][a.rank])[n] = v;
-                else
-                    a.yd[n] = f32_to_f16_bits(v);
-            }))
-            return;
+        const int64_t kt_d = g.kt, units_d = g.units;
+        if (!gemv_split(g, xs, ring, full, empty, stage, phase, ct, a.err, red_rows, a.part_down)) return;
         if (!grid_sync(a, nbar, ct, &ok_sh)) return;
-        if (tp && !tp_reduce(a, 1, ep0 + 2 * l + 2, a.yd, ct, nbar, &ok_sh)) return;
         // x = fp16(r1 + down); normed = RMSNorm(x) with the next layer's input
         // gains, or the final norm (qwen_model.cpp:331-332, 368-370).
         const bool last_layer = l + 1 == a.L;
-        add_norm_cons(a.r1, a.yd, H, last_layer ? a.norm : a.layers[l + 1].ln1,
-                      last_layer ? a.norm_dt : a.layers[l + 1].ln1_dt, a.eps, xs, writer ? a.x : nullptr, ct, red);
+        const void* nw = last_layer ? a.norm : a.layers[l + 1].ln1;
+        const int ndt = last_layer ? a.norm_dt : a.layers[l + 1].ln1_dt;
+        if (tp) {
+            if (!tp_reduce(a, 1, ep0 + 2 * l + 2, a.yd, ct, nbar, &ok_sh, kt_d, units_d)) return;
+            add_norm_cons(a.r1, a.yd, H, nw, ndt, a.eps, xs, writer ? a.x : nullptr, ct, red);
+        } else {
+            add_norm_cons(a.r1, nullptr, H, nw, ndt, a.eps, xs, writer ? a.x : nullptr, ct, red, a.part_down, kt_d,
+                          units_d);
+        }
         for (int64_t i = H + ct; i < ktH * 64; i += kStepCons) xs[i] = 0;
         cons_sync();
     }

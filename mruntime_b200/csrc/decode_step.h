@@ -49,6 +49,7 @@ struct StepArgs {
     uint16_t* yo;               // o projection output [hidden]
     uint16_t* act;              // SiLU(gate) * up [local I]
     uint16_t* yd;               // down projection output [hidden]
+    float* part_down;           // down's split partials [grid][2][128] (own exchange buffer under TP)
     float* att_part;            // [local heads][att_split][head_dim + 2]
     int* att_cnt;               // [local heads], zero between steps
     int att_split;

@@ -28,6 +28,7 @@
 // reductions (RMSNorm's sum of squares, attention) are summed in a
 // different order than the reference's sequential loops, so results agree
 // within FP32 rounding, not bit for bit.
+#include <algorithm>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -1145,7 +1146,10 @@ constexpr size_t kFlagBytes = 256;  // kMaxRanks 64-bit flags, padded
 // CUDA IPC, the handles travel over the NCCL communicator, and each rank maps
 // its peers' regions.  Any failure leaves p2p off (the NCCL path is used).
 int dec_setup_p2p(mrt_decoder d) {
-    const size_t buf_bytes = static_cast<size_t>(d->max_seq * d->H) * 4;
+    // Each buffer holds a prefill's FP32 partial rows and, for the persistent
+    // decode step, one [SMs][2][128] block of split-GEMV partials.
+    const size_t buf_bytes = std::max(static_cast<size_t>(d->max_seq * d->H) * 4,
+                                      static_cast<size_t>(current_ctx()->sms) * 256 * 4);
     const size_t region = kFlagBytes + 2 * buf_bytes;
     int rc = dec_alloc(d, &d->xreg, region, "the all-reduce exchange region");
     if (rc != MRT_OK) return rc;
@@ -1221,6 +1225,9 @@ int dec_setup_step(mrt_decoder d) {
     const int64_t D = d->D, il = d->i1 - d->i0;
     if (!(D == 64 || D == 128 || D == 256) || d->H % 8 != 0 || d->H > 16384) return MRT_OK;
     if ((il + grid - 1) / grid > 256 || (d->nh * D) % 8 != 0 || il % 8 != 0) return MRT_OK;
+    // The split down GEMV: at most one 128-row tile per CTA, so a CTA's unit
+    // range spans at most two tiles.
+    if ((d->H + 127) / 128 > grid) return MRT_OK;
     for (auto& ly : d->layers)
         for (mrt_weight w : {ly.qkv, ly.o, ly.gateup, ly.down})
             if (!w->tiled) return MRT_OK;
@@ -1300,6 +1307,9 @@ int dec_setup_step(mrt_decoder d) {
             a.peer_cand[q] = reinterpret_cast<float*>(static_cast<char*>(d->peer_reg[q]) + 128);
         }
         a.epoch = d->ar_epoch;
+        a.part_down = const_cast<float*>(d->pa[1].buf[d->rank]);
+    } else if ((rc = buf(reinterpret_cast<void**>(&a.part_down), static_cast<size_t>(grid) * 256 * 4, "decode-step partials"))) {
+        return rc;
     }
     d->step_grid = grid;
     d->fused_step = true;
