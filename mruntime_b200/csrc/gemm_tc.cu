@@ -177,17 +177,20 @@ __device__ __forceinline__ void add4(float4& s, const float4& p) {
 // tokens of loads in flight before adding them in order.
 template <int BN>
 __device__ __forceinline__ void swap_tail_fixup(const TcGemmArgs& a, const Unit& w, int n_tail, int quad, int lane) {
-    __threadfence();  // this warp's partial rows are visible to the whole GPU
+    // The warp's partial rows are ordered before lane 0's arrival (__syncwarp),
+    // which releases them with one acquire-release atomic; the last arrival's
+    // acquire makes every slice's rows visible to the warp after the shuffle.
     __syncwarp();
     int last = 0;
     if (lane == 0) {
         int* cnt = a.tile_counters + w.ti * 4 + quad;
-        last = atomicAdd(cnt, 1) == a.tail_splits - 1;
+        int old;
+        asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;" : "=r"(old) : "l"(cnt) : "memory");
+        last = old == a.tail_splits - 1;
         if (last) *cnt = 0;
     }
     last = __shfl_sync(0xFFFFFFFFu, last, 0);
     if (!last) return;
-    __threadfence();  // the other slices' rows are read after the count
     const int r = quad * 32 + lane;
     const int64_t n = static_cast<int64_t>(w.mt) * kBM + r;  // weight row = output column
     const int cols = min(BN, a.M - w.nt * BN);                 // tokens in this tile
@@ -207,7 +210,7 @@ __device__ __forceinline__ void swap_tail_fixup(const TcGemmArgs& a, const Unit&
 #pragma unroll
                 for (int g = 0; g < kG; ++g)
                     if (sp0 + b < a.tail_splits && g < ng)
-                        p[b][g] = *reinterpret_cast<const float4*>(base + (sp0 + b) * slice + c0 + 4 * g);
+                        p[b][g] = __ldcg(reinterpret_cast<const float4*>(base + (sp0 + b) * slice + c0 + 4 * g));
 #pragma unroll
             for (int b = 0; b < kB; ++b)
 #pragma unroll
