@@ -403,7 +403,8 @@ def gpu_arm(args, rank, world, local):
             sweep.append({"M": m, "ms": round(t, 4), "TFLOP/s": round(tf, 1), "GB/s": round(gbs, 1), "bound": bound,
                           "frac": round(frac, 4), "per_projection_ms": {k: round(v, 4) for k, v in per.items()},
                           "plans": {k: "{kernel} bn={bn} full={full_tiles} splits={tail_splits} kb={kb_per} "
-                                       "grid={grid}".format(**v) for k, v in plans.items()}})
+                                       "grid={grid}{c}".format(c=" cluster" if v["cluster"] else "", **v)
+                                    for k, v in plans.items()}})
         capi.sync(stream)
     return {"ms": ms, "value": value, "roofline": roofline, "e2e": e2e, "clocks": clk, "launches": launches,
             "sweep": sweep, "peaks": peaks, "projs": projs, "tp": tp}

@@ -180,9 +180,11 @@ int mrt_gemm(mrt_weight w, const void* x_dev, int64_t ldx, void* y_dev, int64_t 
 /* The kernel mrt_gemm would run for an M x N x K product on a device with
  * `sms` multiprocessors (0 = the current device): kernel 1 = tcgen05 with X
  * as the 128-row MMA operand (M > 64), 2 = tcgen05 in swap mode with the
- * weight as the 128-row operand and the tokens as N (M <= 64); then the
- * tile's bn, the number of tiles run over the whole K, the K-slices of each
- * remaining tile, k-blocks per slice and the persistent grid.  Host-only. */
+ * weight as the 128-row operand and the tokens as N (M <= 64), 3 = swap mode
+ * whose K-slices (every tile split, 2..8 slices, one per CTA) are summed
+ * inside thread-block clusters on the current device; then the tile's bn,
+ * the number of tiles run over the whole K, the K-slices of each remaining
+ * tile, k-blocks per slice and the persistent grid.  Host-only. */
 int mrt_gemm_plan(int64_t M, int64_t N, int64_t K, int sms, int* kernel, int* bn, int* full_tiles,
                   int* tail_splits, int* kb_per, int* grid);
 

@@ -207,7 +207,8 @@ def gemm_plan(M: int, N: int, K: int, sms: int = 0) -> dict:
     call("mrt_gemm_plan", M, N, K, sms, *[C.byref(v) for v in vals])
     keys = ("kernel", "bn", "full_tiles", "tail_splits", "kb_per", "grid")
     d = dict(zip(keys, (v.value for v in vals)))
-    d["kernel"] = {1: "tcgen05", 2: "tcgen05-swap"}[d["kernel"]]
+    d["cluster"] = d["kernel"] == 3  # swap mode, K-slices summed inside clusters
+    d["kernel"] = {1: "tcgen05", 2: "tcgen05-swap", 3: "tcgen05-swap"}[d["kernel"]]
     return d
 
 

@@ -8,6 +8,7 @@
 #include <atomic>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -561,6 +562,23 @@ static TcPlan plan_tc(int64_t M, int64_t N, int64_t K, int sms) {
     return best;
 }
 
+// Swap-mode plans of 32 or 64 tokens per tile whose every tile is split into
+// 2..8 K-slices, one slice per CTA, sum the slices inside thread-block
+// clusters (distributed shared memory) instead of through global memory:
+// there the global finish re-reads 32..64 FP32 columns per slice in several
+// dependent passes.  With 16 tokens per tile the global finish is one pass
+// and cheaper than the cost of cluster placement (clusters of 4..5 CTAs do
+// not tile the GPCs' SM counts, so some SMs take two CTAs of the launch).
+// MRT_GEMM_CLUSTER=0 (read once) keeps the global-memory finish everywhere.
+static bool use_cluster(bool swap, const TcPlan& p, int64_t tiles) {
+    static const bool enabled = [] {
+        const char* v = std::getenv("MRT_GEMM_CLUSTER");
+        return v == nullptr || std::strcmp(v, "0") != 0;
+    }();
+    return enabled && swap && p.bn >= 32 && p.full == 0 && p.splits >= 2 && p.splits <= 8 &&
+           static_cast<int64_t>(p.grid) == tiles * p.splits && tc_cluster_ok(p.bn, p.splits);
+}
+
 // The weight's TMA map whose box is exactly the kernel's W tile (bn rows).
 static const CUtensorMap* weight_tmap(mrt_weight w, int bn) {
     const int slot = bn == 64 ? 0 : (bn == 128 ? 1 : (bn == 256 ? 2 : -1));
@@ -626,7 +644,8 @@ static int gemm_dispatch(mrt_weight w, const void* x, int64_t ldx, void* y, int6
     a.y = y; a.ldy = ldy; a.out_f32 = out_f32 ? 1 : 0; a.bias = bias; a.err_flag = c->d_err;
     const int64_t tiles = tc_gemm_tiles(a);
     const int64_t n_tail = tiles - p.full;
-    if (n_tail > 0) {
+    if (use_cluster(swap, p, tiles)) a.cluster_k = p.splits;
+    if (n_tail > 0 && a.cluster_k == 0) {
         const size_t need = static_cast<size_t>(n_tail) * p.splits * 128 * p.bn * sizeof(float);
         rc = ensure_buffer(&c->ws, &c->ws_bytes, need, "allocating split-K scratch");
         if (rc != MRT_OK) return rc;
@@ -664,7 +683,8 @@ extern "C" int mrt_gemm_plan(int64_t M, int64_t N, int64_t K, int sms, int* kern
     }
     const bool swap = M <= 64;
     const TcPlan p = swap ? plan_swap(M, N, K, sms) : plan_tc(M, N, K, sms);
-    if (kernel) *kernel = swap ? 2 : 1;
+    const int64_t tiles = swap ? ((N + 127) / 128) : 0;
+    if (kernel) *kernel = swap ? (use_cluster(true, p, tiles) ? 3 : 2) : 1;
     if (bn) *bn = p.bn;
     if (full_tiles) *full_tiles = p.full;
     if (tail_splits) *tail_splits = p.splits;

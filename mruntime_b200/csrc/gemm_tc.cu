@@ -47,7 +47,8 @@ struct TcCfg {
     static constexpr int kStages = kRingBudget / kStageBytes > 12 ? 12 : kRingBudget / kStageBytes;
     // Two accumulators of BN FP32 columns, rounded up to a power of two >= 32.
     static constexpr uint32_t kTmemCols = 2 * BN <= 32 ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
-    static constexpr int kBarBytes = (2 * kStages + 5) * 8 + 16;
+    // full[S], empty[S], tfull[2], tempty[2], drain, cl_ready, cl_done; TMEM slot.
+    static constexpr int kBarBytes = (2 * kStages + 7) * 8 + 16;
     static constexpr size_t kSmem = static_cast<size_t>(kStages) * kStageBytes + kBarBytes + 1024;
 };
 
@@ -66,6 +67,16 @@ __device__ __forceinline__ Unit decode_unit(const TcGemmArgs& a, int u, int num_
         w.kb1 = num_kb;
         w.slot = -1;
         w.ti = -1;
+    } else if (a.cluster_k > 1) {
+        // One slice per CTA; the slices of tail tile ti are CTAs
+        // ti * cluster_k .. + cluster_k - 1, one cluster.
+        const int ti = u / a.cluster_k;
+        const int sp = u % a.cluster_k;
+        t = ti;
+        w.kb0 = sp * a.kb_per;
+        w.kb1 = min(w.kb0 + a.kb_per, num_kb);
+        w.slot = sp;
+        w.ti = ti;
     } else {
         const int v = u - a.full_tiles;
         const int ti = v % n_tail;
@@ -235,6 +246,208 @@ __device__ __forceinline__ void swap_tail_fixup(const TcGemmArgs& a, const Unit&
     }
 }
 
+// ------------------------------------------------ cluster K-split (swap mode)
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_size() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+    return r;
+}
+
+// Hardware cluster barrier, split: every thread arrives once right after the
+// barriers are initialised (nothing before that can fail or return), and
+// waits once later; the wait therefore always completes.
+__device__ __forceinline__ void cluster_arrive() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void cluster_wait() {
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_map(uint32_t smem_addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+    return r;
+}
+
+// Arrive on mbarrier `bar` of CTA `rank`, releasing this thread's (and,
+// through the preceding CTA barrier, its CTA's) shared-memory writes to the
+// cluster.
+__device__ __forceinline__ void mbar_arrive_cluster(uint64_t* bar, uint32_t rank) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_map(smem_u32(bar), rank))
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait with cluster-scope acquire.  With give_up_on_error it also
+// stops as soon as any thread of the grid has raised an error; without it
+// only the time limit ends the wait (used where the caller's shared memory
+// may still be read by another CTA of the cluster).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* flag, int code,
+                                                  bool give_up_on_error) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try_wait_cluster(bar, parity)) return true;
+        if ((it & 255u) == 0) {
+            if (give_up_on_error && error_raised(flag)) return false;
+            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                raise_error(flag, code);
+                return false;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr)
+                 : "memory");
+    return v;
+}
+
+// Named barrier of the 128 epilogue threads (id 1); returns whether `pred`
+// held on all of them.
+__device__ __forceinline__ bool epi_bar_and(bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.and.pred q, 1, 128, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"(pred ? 1u : 0u)
+        : "memory");
+    return r != 0;
+}
+
+__device__ __forceinline__ void epi_bar_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// Four consecutive outputs n..n+3 of one token (swap mode: consecutive weight
+// rows), rounded like every other store of this kernel.
+__device__ __forceinline__ void store_swap_rows4(const TcGemmArgs& a, const float4& s, int64_t n, int64_t token) {
+    if (n >= a.N) return;
+    const float v[4] = {s.x, s.y, s.z, s.w};
+    const bool whole = n + 4 <= a.N;
+    if (a.out_f32) {
+        float* dst = static_cast<float*>(a.y) + token * a.ldy + n;
+        if (whole && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+            *reinterpret_cast<float4*>(dst) = s;
+        } else {
+            for (int i = 0; i < 4 && n + i < a.N; ++i) dst[i] = v[i];
+        }
+        return;
+    }
+    uint16_t* dst = static_cast<uint16_t*>(a.y) + token * a.ldy + n;
+    if (whole && (reinterpret_cast<uintptr_t>(dst) & 7) == 0) {
+        *reinterpret_cast<uint2*>(dst) = make_uint2(pack_h2(round_out(v[0], a.bias, n), round_out(v[1], a.bias, n + 1)),
+                                                    pack_h2(round_out(v[2], a.bias, n + 2), round_out(v[3], a.bias, n + 3)));
+    } else {
+        for (int i = 0; i < 4 && n + i < a.N; ++i) dst[i] = round_out(v[i], a.bias, n + i);
+    }
+}
+
+// Cluster K-split finish, run by the 128 epilogue threads of every CTA of the
+// cluster (one K-slice each).  Each CTA copies its FP32 accumulator (real
+// token columns only) into its own shared memory -- the operand ring, idle
+// once the last MMA has completed -- as [token][128 rows], and arrives on
+// every CTA's `ready` barrier.  CTA r then sums rows [128 r / S, 128 (r+1) / S)
+// (in 4-row groups) over the S slices, in slice order like the global-memory
+// finish, reading the other CTAs' copies through distributed shared memory,
+// and stores them.  A CTA leaves only after all S CTAs arrived on its `done`
+// barrier (they have finished reading its copy).  Every wait is bounded; a
+// slice that never arrives leaves its tile unwritten with an error raised.
+template <int BN>
+__device__ __forceinline__ void swap_cluster_finish(const TcGemmArgs& a, uint8_t* smem, uint32_t tmem_base,
+                                                    uint64_t* tfull, uint64_t* ready, uint64_t* done, int num_m,
+                                                    int n_tail, int num_kb, int quad, int lane, int et) {
+    const uint32_t S = static_cast<uint32_t>(a.cluster_k);
+    const uint32_t rank = cluster_rank();
+    const Unit w = decode_unit(a, blockIdx.x, num_m, n_tail, num_kb);
+    const int cols = min(BN, a.M - w.nt * BN);
+    float* stg = reinterpret_cast<float*>(smem);
+    // The launch's cluster shape must match the slice numbering (the host
+    // guarantees it); otherwise no CTA of the cluster is addressed at all.
+    if (cluster_size() != S || rank != static_cast<uint32_t>(w.slot)) {
+        if (et == 0) raise_error(a.err_flag, kErrEpiWait);
+        cluster_wait();
+        return;
+    }
+    int ok = 1;
+    if (lane == 0) ok = mbar_wait(&tfull[0], 0, a.err_flag, kErrEpiWait) ? 1 : 0;
+    ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+    if (ok) {
+        tc_fence_after();
+        const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+        const int r = quad * 32 + lane;
+#pragma unroll 1
+        for (int c = 0; c * 16 < cols; ++c) {
+            uint32_t v[16];
+            __syncwarp();
+            tmem_ld_16cols(t_row + c * 16, v);
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                if (c * 16 + j < cols) stg[(c * 16 + j) * kBM + r] = __uint_as_float(v[j]);
+        }
+    }
+    const bool staged = epi_bar_and(ok != 0);
+    cluster_wait();  // every CTA of the cluster has initialised its barriers
+    if (staged && et == 0)
+        for (uint32_t p = 0; p < S; ++p) mbar_arrive_cluster(ready, p);
+    const bool go = staged && mbar_wait_cluster(ready, 0, a.err_flag, kErrEpiWait, true);
+    if (go) {
+        const int g0 = static_cast<int>(32u * rank / S);
+        const int G = static_cast<int>(32u * (rank + 1) / S) - g0;
+        const uint32_t base = smem_u32(stg);
+        uint32_t peer[8];
+#pragma unroll
+        for (int p = 0; p < 8; ++p) peer[p] = p < static_cast<int>(S) ? cluster_map(base, p) : 0u;
+#pragma unroll 1
+        for (int e = et; e < G * cols; e += kEpiThreads) {
+            const int m = e / G;
+            const int nl = (g0 + e - m * G) * 4;  // row within the tile
+            const uint32_t off = static_cast<uint32_t>(m * kBM + nl) * 4u;
+            float4 v[8];
+#pragma unroll
+            for (int p = 0; p < 8; ++p)
+                if (p < static_cast<int>(S)) v[p] = ld_cluster_f4(peer[p] + off);
+            float4 sum = v[0];
+#pragma unroll
+            for (int p = 1; p < 8; ++p)
+                if (p < static_cast<int>(S)) add4(sum, v[p]);
+            store_swap_rows4(a, sum, static_cast<int64_t>(w.mt) * kBM + nl, static_cast<int64_t>(w.nt) * BN + m);
+        }
+    }
+    epi_bar_sync();  // this CTA's reads of the cluster's copies are complete
+    if (et == 0) {
+        for (uint32_t p = 0; p < S; ++p) mbar_arrive_cluster(done, p);
+        // Stay resident (shared memory valid) until every CTA has read this
+        // one's copy; only the time limit ends this wait.
+        mbar_wait_cluster(done, 0, a.err_flag, kErrEpiWait, false);
+    }
+}
+
 template <int BN, bool SWAP>
 __global__ void __launch_bounds__(kThreadsTc, SWAP ? 2 : 1)
     tc_gemm_kernel(const TcGemmArgs a, const __grid_constant__ CUtensorMap tma,
@@ -251,7 +464,10 @@ __global__ void __launch_bounds__(kThreadsTc, SWAP ? 2 : 1)
     uint64_t* tfull = bars + 2 * S;
     uint64_t* tempty = tfull + 2;
     uint64_t* drain = tempty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* cl_ready = drain + 1;  // cluster K-split finish (swap mode)
+    uint64_t* cl_done = drain + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 3);
+    const bool clustered = SWAP && a.cluster_k > 1;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -266,6 +482,10 @@ __global__ void __launch_bounds__(kThreadsTc, SWAP ? 2 : 1)
             mbar_init(&tempty[i], kEpiThreads);
         }
         mbar_init(drain, 1);
+        if (clustered) {
+            mbar_init(cl_ready, static_cast<uint32_t>(a.cluster_k));
+            mbar_init(cl_done, static_cast<uint32_t>(a.cluster_k));
+        }
         fence_barrier_init();
     }
     if (warp == 1) {
@@ -282,6 +502,7 @@ __global__ void __launch_bounds__(kThreadsTc, SWAP ? 2 : 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    if (clustered) cluster_arrive();  // barriers initialised; every thread, once
     const uint32_t tmem_base = *tmem_slot;
 
     // A tiles (128 rows) vary fastest; in swap mode A is W and B is X.
@@ -448,6 +669,11 @@ __global__ void __launch_bounds__(kThreadsTc, SWAP ? 2 : 1)
                 mbar_wait(drain, 0, nullptr, kErrDrainWait);
             }
         }
+    } else if (clustered) {
+        griddep_wait();  // before any bounded wait and any global write
+        if constexpr (SWAP)
+            swap_cluster_finish<BN>(a, smem, tmem_base, tfull, cl_ready, cl_done, num_m, n_tail, num_kb, warp & 3,
+                                    lane, threadIdx.x - 64);
     } else {
         const int quad = warp & 3;  // TMEM lanes this warp may read: 32*quad .. +31
         griddep_wait();  // before any bounded wait and any global write
@@ -504,6 +730,10 @@ __global__ void __launch_bounds__(kThreadsTc, SWAP ? 2 : 1)
         }
     }
 
+    if (clustered && warp < 2) {
+        __syncwarp();
+        cluster_wait();  // pairs with the arrive above (the epilogue warps wait in the finish)
+    }
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
@@ -513,8 +743,9 @@ __global__ void __launch_bounds__(kThreadsTc, SWAP ? 2 : 1)
     }
 }
 
+// Kernel attributes, once per device.
 template <int BN, bool SWAP>
-cudaError_t launch_bn(const TcGemmArgs& a, const CUtensorMap& ta, const CUtensorMap& tb, cudaStream_t s) {
+cudaError_t prepare_bn() {
     static bool attr_set[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -531,23 +762,78 @@ cudaError_t launch_bn(const TcGemmArgs& a, const CUtensorMap& ta, const CUtensor
         if (e != cudaSuccess) return e;
         attr_set[dev] = true;
     }
+    return cudaSuccess;
+}
+
+template <int BN, bool SWAP>
+cudaError_t launch_bn(const TcGemmArgs& a, const CUtensorMap& ta, const CUtensorMap& tb, cudaStream_t s) {
+    cudaError_t e = prepare_bn<BN, SWAP>();
+    if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(static_cast<unsigned>(a.grid));
     cfg.blockDim = dim3(kThreadsTc);
     cfg.dynamicSmemBytes = TcCfg<BN, SWAP>::kSmem;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
+    int n_attr = 1;
+    if (SWAP && a.cluster_k > 1) {
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = static_cast<unsigned>(a.cluster_k);
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = 1;
+        n_attr = 2;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, SWAP>, a, ta, tb);
+    cfg.numAttrs = n_attr;
+    e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, SWAP>, a, ta, tb);
     if (e != cudaSuccess) return e;
     note_launches(1);
     return cudaGetLastError();
 }
 
+// Whether clusters of k swap-mode CTAs of width BN can be resident at all.
+template <int BN>
+bool cluster_fits(int k) {
+    if (prepare_bn<BN, true>() != cudaSuccess) return false;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(k));
+    cfg.blockDim = dim3(kThreadsTc);
+    cfg.dynamicSmemBytes = TcCfg<BN, true>::kSmem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(k);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    const cudaError_t e = cudaOccupancyMaxActiveClusters(&n, tc_gemm_kernel<BN, true>, &cfg);
+    if (e != cudaSuccess) {
+        (void)cudaGetLastError();
+        return false;
+    }
+    return n > 0;
+}
+
 }  // namespace
+
+bool tc_cluster_ok(int bn, int k) {
+    if (k < 2 || k > 8) return false;
+    const int slot = bn == 16 ? 0 : (bn == 32 ? 1 : (bn == 64 ? 2 : -1));
+    if (slot < 0) return false;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+    // 0 unknown, 1 no, 2 yes
+    static signed char known[64][3][9] = {};
+    signed char& v = known[dev][slot][k];
+    if (v == 0) {
+        const bool ok = slot == 0 ? cluster_fits<16>(k) : (slot == 1 ? cluster_fits<32>(k) : cluster_fits<64>(k));
+        v = ok ? 2 : 1;
+    }
+    return v == 2;
+}
 
 int tc_gemm_tiles(const TcGemmArgs& a) {
     return a.swap ? ((a.N + kBM - 1) / kBM) * ((a.M + a.bn - 1) / a.bn)
@@ -565,9 +851,14 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& a, const CUtensorMap& tmap_x, const
         return cudaErrorInvalidValue;
     // Every tail slice must own at least one k-block, or its accumulator
     // would never be written.
+    const bool clustered = a.cluster_k > 1;
     if (a.full_tiles < tiles && (a.kb_per <= 0 || (a.tail_splits - 1) * a.kb_per >= num_kb ||
-                                 a.tail_splits * a.kb_per < num_kb || a.partials == nullptr ||
-                                 (a.swap && a.tile_counters == nullptr)))
+                                 a.tail_splits * a.kb_per < num_kb ||
+                                 (!clustered && (a.partials == nullptr || (a.swap && a.tile_counters == nullptr)))))
+        return cudaErrorInvalidValue;
+    // Clusters: swap mode, every tile split, one slice per CTA.
+    if (clustered && (!a.swap || a.cluster_k > 8 || a.full_tiles != 0 || a.tail_splits != a.cluster_k ||
+                      static_cast<int64_t>(a.grid) != static_cast<int64_t>(tiles) * a.cluster_k))
         return cudaErrorInvalidValue;
     if (a.swap) {
         if (a.M > a.bn) return cudaErrorInvalidValue;  // one token tile

@@ -51,7 +51,15 @@ struct TcGemmArgs {
     // tiled weight tiles may be fetched before that wait (the weights must
     // not be written by the kernel being overlapped).
     int w_prefetch;
+    // Swap mode, every tile split into cluster_k (2..8) K-slices and one slice
+    // per CTA: the slices of a tile run as one thread-block cluster and are
+    // summed through distributed shared memory (partials and tile_counters
+    // unused).  0: slices are summed through global memory.
+    int cluster_k;
 };
+// Whether a swap-mode launch of tile width bn may use clusters of k CTAs on
+// the current device (checked once per device, width and k).
+bool tc_cluster_ok(int bn, int k);
 cudaError_t launch_tc_gemm(const TcGemmArgs& a, const CUtensorMap& tmap_x, const CUtensorMap& tmap_w,
                            cudaStream_t s);
 // Output tiles of a plan (128 A rows x bn B rows each).
