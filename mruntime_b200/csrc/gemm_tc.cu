@@ -156,16 +156,19 @@ __device__ __forceinline__ void store_swap_chunk(const TcGemmArgs& a, const uint
     }
 }
 
-// Swap mode: up to 16 FP32 columns (tokens) into a tail slot ([128][bn]
-// tile-local); only the `groups` float4 groups holding real tokens are
-// written (columns past the last token are never read back).
+// Swap mode: up to 16 FP32 columns (tokens) into a tail slot, laid out as
+// [bn / 4 token groups][128 rows][4 tokens] so that one float4 per lane of a
+// warp (32 consecutive rows) is one contiguous 512-byte run.  Only the
+// `groups` float4 groups holding real tokens are written (columns past the
+// last token are never read back).
 __device__ __forceinline__ void store_partial_chunk16(const TcGemmArgs& a, const uint32_t (&r)[16], int slot,
                                                      int row_in_tile, int col_in_tile, int bn, int groups) {
-    float* dst = a.partials + (static_cast<int64_t>(slot) * kBM + row_in_tile) * bn + col_in_tile;
+    float* dst = a.partials + static_cast<int64_t>(slot) * kBM * bn + (col_in_tile / 4) * (kBM * 4) + row_in_tile * 4;
 #pragma unroll
     for (int g = 0; g < 4; ++g)
         if (g < groups)
-            *reinterpret_cast<uint4*>(dst + 4 * g) = make_uint4(r[4 * g], r[4 * g + 1], r[4 * g + 2], r[4 * g + 3]);
+            *reinterpret_cast<uint4*>(dst + g * (kBM * 4)) =
+                make_uint4(r[4 * g], r[4 * g + 1], r[4 * g + 2], r[4 * g + 3]);
 }
 
 __device__ __forceinline__ void add4(float4& s, const float4& p) {
@@ -173,6 +176,34 @@ __device__ __forceinline__ void add4(float4& s, const float4& p) {
     s.y += p.y;
     s.z += p.z;
     s.w += p.w;
+}
+
+// Sum of `splits` partial slices (slice order) of `ng` float4 groups starting
+// at token column c0 of one weight row (layout of store_partial_chunk16);
+// KB slices x KG groups of loads are issued before any of them is added.
+template <int KB, int KG>
+__device__ __forceinline__ void sum_slices(const float* base, int64_t slice, int splits, int c0, int ng,
+                                           float4 (&sum)[4]) {
+#pragma unroll 1
+    for (int sp0 = 0; sp0 < splits; sp0 += KB) {
+        float4 p[KB][KG];
+#pragma unroll
+        for (int b = 0; b < KB; ++b)
+#pragma unroll
+            for (int g = 0; g < KG; ++g)
+                if (sp0 + b < splits && g < ng)
+                    p[b][g] = __ldcg(reinterpret_cast<const float4*>(base + (sp0 + b) * slice + (c0 / 4 + g) * (kBM * 4)));
+#pragma unroll
+        for (int b = 0; b < KB; ++b)
+#pragma unroll
+            for (int g = 0; g < KG; ++g)
+                if (sp0 + b < splits && g < ng) {
+                    if (sp0 + b == 0)
+                        sum[g] = p[b][g];
+                    else
+                        add4(sum[g], p[b][g]);
+                }
+    }
 }
 
 // Swap-mode K-split finish for one 32-row quadrant of a tail tile, run by the
@@ -185,7 +216,8 @@ __device__ __forceinline__ void add4(float4& s, const float4& p) {
 //
 // The sum is latency-bound (a few KB per warp from L2), so each lane reads
 // only its weight row's real token columns and keeps up to 4 slices x 16
-// tokens of loads in flight before adding them in order.
+// tokens (or 8 slices x 4 tokens) of loads in flight before adding them in
+// order.
 template <int BN>
 __device__ __forceinline__ void swap_tail_fixup(const TcGemmArgs& a, const Unit& w, int n_tail, int quad, int lane) {
     // The warp's partial rows are ordered before lane 0's arrival (__syncwarp),
@@ -206,33 +238,19 @@ __device__ __forceinline__ void swap_tail_fixup(const TcGemmArgs& a, const Unit&
     const int64_t n = static_cast<int64_t>(w.mt) * kBM + r;  // weight row = output column
     const int cols = min(BN, a.M - w.nt * BN);                 // tokens in this tile
     const int64_t slice = static_cast<int64_t>(n_tail) * kBM * BN;
-    const float* base = a.partials + (static_cast<int64_t>(w.ti) * kBM + r) * BN;
+    const float* base = a.partials + static_cast<int64_t>(w.ti) * kBM * BN + r * 4;  // slice 0, token group 0
     constexpr int kG = 4;  // float4 groups (16 tokens) per pass
-    constexpr int kB = 4;  // slices in flight per batch
 #pragma unroll 1
     for (int c0 = 0; c0 < cols; c0 += 16) {
         const int ng = min(kG, (cols - c0 + 3) / 4);
         float4 sum[kG];
-#pragma unroll 1
-        for (int sp0 = 0; sp0 < a.tail_splits; sp0 += kB) {
-            float4 p[kB][kG];
-#pragma unroll
-            for (int b = 0; b < kB; ++b)
-#pragma unroll
-                for (int g = 0; g < kG; ++g)
-                    if (sp0 + b < a.tail_splits && g < ng)
-                        p[b][g] = __ldcg(reinterpret_cast<const float4*>(base + (sp0 + b) * slice + c0 + 4 * g));
-#pragma unroll
-            for (int b = 0; b < kB; ++b)
-#pragma unroll
-                for (int g = 0; g < kG; ++g)
-                    if (sp0 + b < a.tail_splits && g < ng) {
-                        if (sp0 + b == 0)
-                            sum[g] = p[b][g];
-                        else
-                            add4(sum[g], p[b][g]);
-                    }
-        }
+        // One batch of loads covers up to 8 slices of one group (<= 4
+        // tokens, 16-token tiles) or 4 slices of 2..4 groups (more would
+        // spill registers).
+        if (BN == 16 && ng == 1)
+            sum_slices<8, 1>(base, slice, a.tail_splits, c0, ng, sum);
+        else
+            sum_slices<4, kG>(base, slice, a.tail_splits, c0, ng, sum);
         uint32_t bits[16] = {};
 #pragma unroll
         for (int g = 0; g < kG; ++g)
