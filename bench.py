@@ -394,14 +394,28 @@ def gpu_arm(args, rank, world, local):
             t_ms, _ = time_steps(projs, tp, stream, m, n_it, world, graph=g)
             del g
             t = t_ms / n_it
+            # Decode shapes also back to back: one graph of 8 consecutive
+            # steps (as the layers of a decoder follow each other), so each
+            # step's first GEMM overlaps the previous step's last one.
+            chained = None
+            if m <= 128 and not args.no_graph:
+                gc = capture(lambda s, m=m: [run_step(projs, tp, s, m) for _ in range(8)])
+                c_ms, _ = time_steps(projs, tp, stream, m, 7, world, graph=gc)
+                del gc
+                chained = c_ms / 56
             tf = step_flops(m) / (t * 1e-3) / 1e12
             gbs = WL.sweep_bytes(m) / (t * 1e-3) / 1e9
             bound = "hbm" if m <= 128 else "tensor"
             frac = gbs / peaks["hbm_gbs"] if bound == "hbm" else tf / peaks["bf16_tflops_sustained"]
             per = time_projections(projs, tp, stream, m, 10)
             plans = {p.name: capi.gemm_plan(m, p.w.n, p.w.k) for p in projs}
-            sweep.append({"M": m, "ms": round(t, 4), "TFLOP/s": round(tf, 1), "GB/s": round(gbs, 1), "bound": bound,
-                          "frac": round(frac, 4), "per_projection_ms": {k: round(v, 4) for k, v in per.items()},
+            row = {"M": m, "ms": round(t, 4), "TFLOP/s": round(tf, 1), "GB/s": round(gbs, 1), "bound": bound,
+                   "frac": round(frac, 4)}
+            if chained is not None:
+                c_gbs = WL.sweep_bytes(m) / (chained * 1e-3) / 1e9
+                row.update({"ms_back_to_back": round(chained, 4), "GB/s_back_to_back": round(c_gbs, 1),
+                            "frac_back_to_back": round(c_gbs / peaks["hbm_gbs"], 4)})
+            sweep.append({**row, "per_projection_ms": {k: round(v, 4) for k, v in per.items()},
                           "plans": {k: "{kernel} bn={bn} full={full_tiles} splits={tail_splits} kb={kb_per} "
                                        "grid={grid}{c}".format(c=" cluster" if v["cluster"] else "", **v)
                                     for k, v in plans.items()}})
