@@ -44,9 +44,9 @@ METRIC = "matmul TFLOP/s (Qwen2.5-7B projection sweep, M=2048 prefill step)"
 UNIT = "TFLOP/s"
 HEADLINE_M = 2048
 # Per-launch DRAM traffic of the dominant kernel (gate+up GEMM at M=2048):
-# dram__bytes_read.sum + dram__bytes_write.sum = 286.574592 MB + 130.112 MB
+# dram__bytes_read.sum + dram__bytes_write.sum = 286.717440 MB + 131.527168 MB
 # from the ncu capture summarised in profiles/tc_gemm_gateup_m2048.md.
-GATEUP_TRAFFIC_BYTES = 416686592
+GATEUP_TRAFFIC_BYTES = 418244608
 
 
 def parse_args():
