@@ -293,44 +293,107 @@ __device__ __forceinline__ void load_per(const uint16_t* p, float (&x)[PER]) {
     }
 }
 
-// Decode attention for one query row (cpu_backend.cpp:171-290 with
-// q_len = 1).  Block (h, split) covers keys [32 split, 32 split + 32) of kv
-// head h / group; each warp loads its <= 8 keys' K and V rows at once, scores
-// them (q.k as a warp tree sum, times scale), and keeps (max, sum of exp,
-// sum of exp * v).  The block merges its warps and writes the split's partial
-// to `part`; the last split block of the head to finish merges every split
-// in split order and writes out = fp16(acc * (1 / sum)).
-// kv_len = state position + 1 (the current token's key is already cached).
+// RoPE of one head held lane-contiguously (lane l: elements l*PER .. +PER-1):
+// element i < D/2 pairs with i + D/2, which lane l ^ 16 holds.  Same
+// arithmetic and rounding as rope_append_kernel; `bits` gets the FP16 result,
+// `x` its value.
+template <int PER>
+__device__ __forceinline__ void rope_lane_f16(float (&x)[PER], uint16_t (&bits)[PER], int lane, const float* cos_row,
+                                              const float* sin_row) {
+    const int i0 = (lane & 15) * PER;
+#pragma unroll
+    for (int e = 0; e < PER; ++e) {
+        const float other = __shfl_xor_sync(0xFFFFFFFFu, x[e], 16);
+        const float c = cos_row[i0 + e], sn = sin_row[i0 + e];
+        if (lane < 16)
+            bits[e] = f32_to_f16_bits(__fsub_rn(__fmul_rn(x[e], c), __fmul_rn(other, sn)));
+        else
+            bits[e] = f32_to_f16_bits(__fadd_rn(__fmul_rn(other, sn), __fmul_rn(x[e], c)));
+    }
+#pragma unroll
+    for (int e = 0; e < PER; ++e) x[e] = f16_bits_to_f32(bits[e]);
+}
+
+constexpr int kMergeChunk = 128;  // splits merged per pass (one per thread)
+
+// Decode attention for one query row (cpu_backend.cpp:171-290 with q_len = 1)
+// with the step's RoPE and KV-cache append folded in (qwen_model.cpp:162-205).
+// Block (h, split) covers keys [32 split, 32 split + 32) of local kv head g:
+// it rotates its raw query head from the q|k|v projection in registers; the
+// current position's key and value come straight from the projection (the key
+// rotated the same way), and the first local query head of each kv head
+// writes them to the cache at that position -- no block of this launch reads
+// that slot from the cache.  Each warp loads its <= 8 keys' K and V rows at
+// once, scores them (q.k as a warp tree sum, times scale) and keeps (max, sum
+// of exp, sum of exp * v).  The block merges its warps and writes the split's
+// partial to `part`; the last split block of the head to arrive merges every
+// split in split order (per-split weights exp(m_s - M) computed once) and
+// writes out = fp16(acc * (1 / sum)).  kv_len = state position + 1.
 template <int PER>
 __global__ void __launch_bounds__(kAttnWarps * 32)
-    attn_decode_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ kc,
-                       const uint16_t* __restrict__ vc, uint16_t* __restrict__ out, int group, int h0, int g0,
-                       int64_t max_seq, float scale, const DecState* st, float* part, int* counters) {
+    attn_decode_kernel(const uint16_t* __restrict__ qkv, int nh, int nkv, uint16_t* __restrict__ kc,
+                       uint16_t* __restrict__ vc, uint16_t* __restrict__ out, int group, int h0, int g0,
+                       int64_t max_seq, float scale, const DecState* st, float* part, int* counters,
+                       const float* __restrict__ cos_t, const float* __restrict__ sin_t) {
     griddep_launch_dependents();
     griddep_wait();
     constexpr int D = PER * 32;
     __shared__ float sm_m[kAttnWarps], sm_l[kAttnWarps];
     __shared__ float sm_acc[kAttnWarps][D];
+    __shared__ float sm_w[kMergeChunk], sm_ls[kMergeChunk], sm_red[kAttnWarps];
     __shared__ int sm_last;
     // Local query head h is global head h0 + h; its kv head, local index g.
     const int h = blockIdx.x, sp = blockIdx.y, nsplit = gridDim.y;
     const int g = (h0 + h) / group - g0;
+    const bool writer = h == 0 || (h0 + h - 1) / group - g0 != g;  // first local head of kv head g
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    int64_t kv_len = static_cast<int64_t>(st->pos) + 1;
+    const int64_t pos = st->pos;
+    int64_t kv_len = pos + 1;
     if (kv_len > max_seq) kv_len = max_seq;
+    const float* cos_row = cos_t + pos * (D / 2);
+    const float* sin_row = sin_t + pos * (D / 2);
     const int64_t kw = static_cast<int64_t>(sp) * kSplitKeys + warp * kKeysPerWarp;
     const int nk = kv_len - kw <= 0 ? 0 : (kv_len - kw >= kKeysPerWarp ? kKeysPerWarp : static_cast<int>(kv_len - kw));
+    const int icur = pos < max_seq && pos >= kw && pos < kw + nk ? static_cast<int>(pos - kw) : -1;  // warp-uniform
     float qv[PER];
-    load_per<PER>(q + static_cast<int64_t>(h) * D + lane * PER, qv);
+    uint16_t qb[PER];
+    load_per<PER>(qkv + static_cast<int64_t>(h) * D + lane * PER, qv);
+    rope_lane_f16<PER>(qv, qb, lane, cos_row, sin_row);
     const uint16_t* kb = kc + (static_cast<int64_t>(g) * max_seq + kw) * D + lane * PER;
     const uint16_t* vb = vc + (static_cast<int64_t>(g) * max_seq + kw) * D + lane * PER;
     float kx[kKeysPerWarp][PER], vx[kKeysPerWarp][PER];
 #pragma unroll
     for (int i = 0; i < kKeysPerWarp; ++i)
-        if (i < nk) {
+        if (i < nk && i != icur) {
             load_per<PER>(kb + i * D, kx[i]);
             load_per<PER>(vb + i * D, vx[i]);
         }
+    if (icur >= 0) {
+        const uint16_t* kr = qkv + static_cast<int64_t>(nh + g) * D + lane * PER;
+        const uint16_t* vr = qkv + static_cast<int64_t>(nh + nkv + g) * D + lane * PER;
+        float kcur[PER], vcur[PER];
+        uint16_t kbits[PER];
+        load_per<PER>(kr, kcur);
+        load_per<PER>(vr, vcur);
+        rope_lane_f16<PER>(kcur, kbits, lane, cos_row, sin_row);
+#pragma unroll
+        for (int i = 0; i < kKeysPerWarp; ++i)
+            if (i == icur) {
+#pragma unroll
+                for (int e = 0; e < PER; ++e) {
+                    kx[i][e] = kcur[e];
+                    vx[i][e] = vcur[e];
+                }
+            }
+        if (writer) {
+            const int64_t slot = (static_cast<int64_t>(g) * max_seq + pos) * D + lane * PER;
+#pragma unroll
+            for (int e = 0; e < PER; ++e) {
+                kc[slot + e] = kbits[e];
+                vc[slot + e] = vr[e];
+            }
+        }
+    }
     float sc[kKeysPerWarp];
 #pragma unroll
     for (int i = 0; i < kKeysPerWarp; ++i) {
@@ -383,55 +446,102 @@ __global__ void __launch_bounds__(kAttnWarps * 32)
             if (sm_m[w] != -INFINITY) A = __fadd_rn(A, __fmul_rn(sm_acc[w][d], expf(__fsub_rn(sm_m[w], M))));
         dst[2 + d] = A;
     }
-    // The last split of this head to arrive merges all splits in split order.
-    __threadfence();
+    // Count this split in: the block's partial writes are ordered before
+    // thread 0's acquire-release atomic by the barrier; the last split's
+    // acquire (shared by the barrier after it) makes every split visible.
     __syncthreads();
     if (threadIdx.x == 0) {
-        const int prev = atomicAdd(&counters[h], 1);
+        int prev;
+        asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;" : "=r"(prev) : "l"(counters + h) : "memory");
         sm_last = prev == nsplit - 1;
         if (sm_last) counters[h] = 0;
     }
     __syncthreads();
     if (!sm_last) return;
-    __threadfence();
     const float* ph = part + static_cast<int64_t>(h) * nsplit * (D + 2);
     const int used = static_cast<int>((kv_len + kSplitKeys - 1) / kSplitKeys);  // splits holding keys
+    // M = max over the splits' maxima (order-free).
+    float mx = -INFINITY;
+    for (int s2 = threadIdx.x; s2 < used; s2 += kAttnWarps * 32) mx = fmaxf(mx, __ldcg(ph + s2 * (D + 2)));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+    if (lane == 0) sm_red[warp] = mx;
+    __syncthreads();
     float MM = -INFINITY;
-    for (int s2 = 0; s2 < used; ++s2) MM = fmaxf(MM, ph[s2 * (D + 2)]);
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) MM = fmaxf(MM, sm_red[w]);
+    // LL and every output element summed in split order, chunk by chunk, with
+    // each split's weight exp(m_s - MM) computed once.
     float LL = 0.0f;
-    for (int s2 = 0; s2 < used; ++s2) LL = __fadd_rn(LL, __fmul_rn(ph[s2 * (D + 2) + 1], expf(__fsub_rn(ph[s2 * (D + 2)], MM))));
-    const float inv = __fdiv_rn(1.0f, LL);
-    for (int d = threadIdx.x; d < D; d += kAttnWarps * 32) {
-        float A = 0.0f;
-#pragma unroll 4
-        for (int s2 = 0; s2 < used; ++s2)
-            A = __fadd_rn(A, __fmul_rn(ph[s2 * (D + 2) + 2 + d], expf(__fsub_rn(ph[s2 * (D + 2)], MM))));
-        out[static_cast<int64_t>(h) * D + d] = f32_to_f16_bits(__fmul_rn(A, inv));
+    float A[(D + kAttnWarps * 32 - 1) / (kAttnWarps * 32)];
+#pragma unroll
+    for (int j = 0; j < (D + kAttnWarps * 32 - 1) / (kAttnWarps * 32); ++j) A[j] = 0.0f;
+    for (int c0 = 0; c0 < used; c0 += kMergeChunk) {
+        const int cn = used - c0 < kMergeChunk ? used - c0 : kMergeChunk;
+        __syncthreads();  // the previous chunk's weights are no longer read
+        if (threadIdx.x < cn) {
+            const float* q2 = ph + static_cast<int64_t>(c0 + threadIdx.x) * (D + 2);
+            sm_w[threadIdx.x] = expf(__fsub_rn(__ldcg(q2), MM));
+            sm_ls[threadIdx.x] = __ldcg(q2 + 1);
+        }
+        __syncthreads();
+        if (threadIdx.x == 0)
+            for (int s2 = 0; s2 < cn; ++s2) LL = __fadd_rn(LL, __fmul_rn(sm_ls[s2], sm_w[s2]));
+#pragma unroll
+        for (int j = 0; j < (D + kAttnWarps * 32 - 1) / (kAttnWarps * 32); ++j) {
+            const int d = threadIdx.x + j * kAttnWarps * 32;
+            if (d >= D) break;
+            const float* col = ph + static_cast<int64_t>(c0) * (D + 2) + 2 + d;
+            int s2 = 0;
+            for (; s2 + 8 <= cn; s2 += 8) {
+                float v8[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) v8[u] = __ldcg(col + (s2 + u) * (D + 2));
+#pragma unroll
+                for (int u = 0; u < 8; ++u) A[j] = __fadd_rn(A[j], __fmul_rn(v8[u], sm_w[s2 + u]));
+            }
+            for (; s2 < cn; ++s2) A[j] = __fadd_rn(A[j], __fmul_rn(__ldcg(col + s2 * (D + 2)), sm_w[s2]));
+        }
+    }
+    if (threadIdx.x == 0) sm_red[0] = __fdiv_rn(1.0f, LL);
+    __syncthreads();
+    const float inv = sm_red[0];
+#pragma unroll
+    for (int j = 0; j < (D + kAttnWarps * 32 - 1) / (kAttnWarps * 32); ++j) {
+        const int d = threadIdx.x + j * kAttnWarps * 32;
+        if (d < D) out[static_cast<int64_t>(h) * D + d] = f32_to_f16_bits(__fmul_rn(A[j], inv));
     }
 }
 
 template <int PER>
-cudaError_t launch_attn_decode(dim3 grid, cudaStream_t s, const uint16_t* q, const uint16_t* kc, const uint16_t* vc,
-                               uint16_t* out, int group, int h0, int g0, int64_t max_seq, float scale,
-                               const DecState* st, float* part, int* counters) {
-    return launch_pdl(attn_decode_kernel<PER>, grid, dim3(kAttnWarps * 32), 0, s, q, kc, vc, out, group, h0, g0,
-                      max_seq, scale, st, part, counters);
+cudaError_t launch_attn_decode(dim3 grid, cudaStream_t s, const uint16_t* qkv, int nh, int nkv, uint16_t* kc,
+                               uint16_t* vc, uint16_t* out, int group, int h0, int g0, int64_t max_seq, float scale,
+                               const DecState* st, float* part, int* counters, const float* cos_t,
+                               const float* sin_t) {
+    return launch_pdl(attn_decode_kernel<PER>, grid, dim3(kAttnWarps * 32), 0, s, qkv, nh, nkv, kc, vc, out, group, h0,
+                      g0, max_seq, scale, st, part, counters, cos_t, sin_t);
 }
 
-cudaError_t attn_decode(int D, dim3 grid, cudaStream_t s, const uint16_t* q, const uint16_t* kc, const uint16_t* vc,
-                        uint16_t* out, int group, int h0, int g0, int64_t max_seq, float scale, const DecState* st,
-                        float* part, int* counters) {
+// Decode attention with the step's RoPE and KV append (see attn_decode_kernel).
+cudaError_t attn_decode(int D, dim3 grid, cudaStream_t s, const uint16_t* qkv, int nh, int nkv, uint16_t* kc,
+                        uint16_t* vc, uint16_t* out, int group, int h0, int g0, int64_t max_seq, float scale,
+                        const DecState* st, float* part, int* counters, const float* cos_t, const float* sin_t) {
+#define MRT_ATTN_CASE(P)                                                                                      \
+    case P:                                                                                                   \
+        return launch_attn_decode<P>(grid, s, qkv, nh, nkv, kc, vc, out, group, h0, g0, max_seq, scale, st, \
+                                     part, counters, cos_t, sin_t);
     switch (D / 32) {
-        case 1: return launch_attn_decode<1>(grid, s, q, kc, vc, out, group, h0, g0, max_seq, scale, st, part, counters);
-        case 2: return launch_attn_decode<2>(grid, s, q, kc, vc, out, group, h0, g0, max_seq, scale, st, part, counters);
-        case 3: return launch_attn_decode<3>(grid, s, q, kc, vc, out, group, h0, g0, max_seq, scale, st, part, counters);
-        case 4: return launch_attn_decode<4>(grid, s, q, kc, vc, out, group, h0, g0, max_seq, scale, st, part, counters);
-        case 5: return launch_attn_decode<5>(grid, s, q, kc, vc, out, group, h0, g0, max_seq, scale, st, part, counters);
-        case 6: return launch_attn_decode<6>(grid, s, q, kc, vc, out, group, h0, g0, max_seq, scale, st, part, counters);
-        case 7: return launch_attn_decode<7>(grid, s, q, kc, vc, out, group, h0, g0, max_seq, scale, st, part, counters);
-        case 8: return launch_attn_decode<8>(grid, s, q, kc, vc, out, group, h0, g0, max_seq, scale, st, part, counters);
+        MRT_ATTN_CASE(1)
+        MRT_ATTN_CASE(2)
+        MRT_ATTN_CASE(3)
+        MRT_ATTN_CASE(4)
+        MRT_ATTN_CASE(5)
+        MRT_ATTN_CASE(6)
+        MRT_ATTN_CASE(7)
+        MRT_ATTN_CASE(8)
         default: return cudaErrorInvalidValue;
     }
+#undef MRT_ATTN_CASE
 }
 
 constexpr int kPfTile = 64;    // queries per block and keys per step
@@ -1466,16 +1576,18 @@ int dec_forward(mrt_decoder d, int64_t S, const int32_t* ids, int64_t pos0, bool
         DEC_TRY(mrt_gemm(ly.qkv, d->normed, H, d->qkv, nq, S, ly.qkv_bias ? MRT_GEMM_BIAS : 0, s));
         uint16_t* kc = d->kc + l * kv_layer;
         uint16_t* vc = d->vc + l * kv_layer;
-        DEC_CU(launch_pdl(rope_append_kernel, dim3(grid_for(S * (nh + d->nkv) * (D / 2))), dim3(kNT), 0, s, d->qkv, nq, S,
-                          static_cast<int>(nh), static_cast<int>(d->nkv), static_cast<int>(D), d->cos_t, d->sin_t,
-                          kc, vc, d->max_seq, d->state),
-               "rope launch");
         if (decode) {
+            // RoPE and the KV append run inside the attention launch.
             DEC_CU(attn_decode(static_cast<int>(D), dim3(static_cast<unsigned>(nh), static_cast<unsigned>(d->nsplit)), s,
-                               d->qkv, kc, vc, d->attn, static_cast<int>(group), static_cast<int>(d->h0),
-                               static_cast<int>(d->g0), d->max_seq, scale, d->state, d->part, d->counters),
+                               d->qkv, static_cast<int>(nh), static_cast<int>(d->nkv), kc, vc, d->attn,
+                               static_cast<int>(group), static_cast<int>(d->h0), static_cast<int>(d->g0), d->max_seq,
+                               scale, d->state, d->part, d->counters, d->cos_t, d->sin_t),
                    "attention launch");
         } else {
+            DEC_CU(launch_pdl(rope_append_kernel, dim3(grid_for(S * (nh + d->nkv) * (D / 2))), dim3(kNT), 0, s, d->qkv,
+                              nq, S, static_cast<int>(nh), static_cast<int>(d->nkv), static_cast<int>(D), d->cos_t,
+                              d->sin_t, kc, vc, d->max_seq, d->state),
+                   "rope launch");
             // Query head h over kv head h / group (qwen_model.cpp:212-245).
             DEC_CU(attn_prefill(static_cast<int>(D), static_cast<int>(nh), S, s, d->qkv, nq, pos0, kc, vc, d->max_seq,
                                 d->attn, ad, static_cast<int>(group), static_cast<int>(d->h0), static_cast<int>(d->g0),
