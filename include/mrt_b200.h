@@ -188,6 +188,16 @@ int mrt_gemm(mrt_weight w, const void* x_dev, int64_t ldx, void* y_dev, int64_t 
 int mrt_gemm_plan(int64_t M, int64_t N, int64_t K, int sms, int* kernel, int* bn, int* full_tiles,
                   int* tail_splits, int* kb_per, int* grid);
 
+/* Gate|up projection with SwiGLU: w's rows interleave the gate and up
+ * projections (row 2j = gate row j, row 2j + 1 = up row j, N = 2 I rows) and
+ * act_dev[m][j] = fp16(silu(fp16(x.gate_j)) * fp16(x.up_j)), act of I columns
+ * with row stride ld_act >= I -- the reference's gate GEMM, up GEMM, FP16
+ * SiLU and multiply (qwen_model.cpp:278-285) in one call.  Plans that keep
+ * whole tiles do it in the GEMM's epilogue; K-split plans store the product
+ * in per-device scratch and run one more kernel. */
+int mrt_gemm_swiglu(mrt_weight w, const void* x_dev, int64_t ldx, void* act_dev, int64_t ld_act, int64_t M,
+                    void* stream);
+
 /* Same product without the final rounding: y_dev is FP32.  Used for the
  * partial sums of a row-parallel (K-split) shard before the all-reduce. */
 int mrt_gemm_f32(mrt_weight w, const void* x_dev, int64_t ldx, float* y_dev, int64_t ldy,

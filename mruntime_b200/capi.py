@@ -64,6 +64,7 @@ _SIGS = {
     "mrt_weight_read": (_int, [_vp, _vp, _i64, _vp]),
     "mrt_gemm": (_int, [_vp, _vp, _i64, _vp, _i64, _i64, _u32, _vp]),
     "mrt_gemm_f32": (_int, [_vp, _vp, _i64, _vp, _i64, _i64, _vp]),
+    "mrt_gemm_swiglu": (_int, [_vp, _vp, _i64, _vp, _i64, _i64, _vp]),
     "mrt_gemm_plan": (_int, [_i64, _i64, _i64, _int] + [C.POINTER(_int)] * 6),
     "mrt_gemm_host": (_int, [_vp, _vp, _vp, _i64, _u32, _vp]),
     "mrt_gemm_general": (_int, [_vp, _int, _i64, _i64, _vp, _int, _i64, _i64, _vp, _int, C.c_float, C.c_float,
@@ -214,6 +215,12 @@ def gemm_plan(M: int, N: int, K: int, sms: int = 0) -> dict:
 
 def gemm_f32(w: Weight, x_ptr: int, ldx: int, y_ptr: int, ldy: int, M: int, stream: int | None = None) -> None:
     call("mrt_gemm_f32", w.h, x_ptr, ldx, y_ptr, ldy, M, stream)
+
+
+def gemm_swiglu(w: Weight, x_ptr: int, ldx: int, act_ptr: int, ld_act: int, M: int,
+                stream: int | None = None) -> None:
+    """act = fp16(silu(gate) * up) for a weight whose rows interleave gate and up."""
+    call("mrt_gemm_swiglu", w.h, x_ptr, ldx, act_ptr, ld_act, M, stream)
 
 
 def gemm_host(w: Weight, x_host_ptr: int, y_host_ptr: int, M: int, bias: bool = False,

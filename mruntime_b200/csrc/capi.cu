@@ -595,12 +595,15 @@ static const CUtensorMap* weight_tmap(mrt_weight w, int bn) {
 
 // Shared body of mrt_gemm / mrt_gemm_f32.
 static int gemm_dispatch(mrt_weight w, const void* x, int64_t ldx, void* y, int64_t ldy, int64_t M,
-                         bool out_f32, bool use_bias, cudaStream_t s) {
+                         bool out_f32, bool use_bias, cudaStream_t s, const uint16_t* swiglu_lut = nullptr,
+                         bool* fused = nullptr) {
+    if (fused) *fused = false;
     if (w == nullptr) return set_error(MRT_ERR_INVALID_ARG, "NULL weight");
     if (M < 0) return set_error(MRT_ERR_SHAPE, "M must be >= 0");
     if (M == 0) return MRT_OK;
     if (x == nullptr || y == nullptr) return set_error(MRT_ERR_INVALID_ARG, "NULL x or y");
-    if (ldx < w->k || ldy < w->n) return set_error(MRT_ERR_SHAPE, "ldx must be >= K and ldy >= N");
+    if (ldx < w->k || ldy < (swiglu_lut ? w->n / 2 : w->n))
+        return set_error(MRT_ERR_SHAPE, "ldx must be >= K and ldy >= N");
     if (use_bias && w->bias == nullptr) return set_error(MRT_ERR_INVALID_ARG, "MRT_GEMM_BIAS without an attached bias");
     if (M > (1LL << 31) - 1 || w->n > (1LL << 31) - 1 || w->k > (1LL << 31) - 1)
         return set_error(MRT_ERR_SHAPE, "dimensions must fit in 31 bits");
@@ -611,6 +614,7 @@ static int gemm_dispatch(mrt_weight w, const void* x, int64_t ldx, void* y, int6
 
     const bool fast = (w->k % 8 == 0) && (ldx % 8 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
     cudaError_t e;
+    if (swiglu_lut != nullptr && (!fast || (w->n & 1) != 0)) return MRT_OK;  // not fused: the caller falls back
     if (!fast) {
         GeneralGemmArgs g{};
         g.a = x; g.a_dtype = MRT_FP16; g.a_cols0 = ldx;
@@ -624,6 +628,10 @@ static int gemm_dispatch(mrt_weight w, const void* x, int64_t ldx, void* y, int6
     }
     const bool swap = M <= 64;
     const TcPlan p = swap ? plan_swap(M, w->n, w->k, c->sms) : plan_tc(M, w->n, w->k, c->sms);
+    if (swiglu_lut != nullptr) {
+        const int64_t tiles = swap ? (w->n + 127) / 128 : ((M + 127) / 128) * ((w->n + p.bn - 1) / p.bn);
+        if (p.full != tiles) return MRT_OK;  // K-split plan: not fused
+    }
     // X's box is 128 rows in normal mode and bn rows in swap mode; a row-major
     // W needs a tensor map with the other box, a tiled W is copied linearly.
     CUtensorMap tx;
@@ -642,6 +650,7 @@ static int gemm_dispatch(mrt_weight w, const void* x, int64_t ldx, void* y, int6
     a.w_prefetch = w->tiled ? 1 : 0;  // uploads finish before returning; views are never tiled
     a.bn = p.bn; a.grid = p.grid; a.full_tiles = p.full; a.tail_splits = p.splits; a.kb_per = p.kb_per;
     a.y = y; a.ldy = ldy; a.out_f32 = out_f32 ? 1 : 0; a.bias = bias; a.err_flag = c->d_err;
+    a.swiglu_lut = swiglu_lut;
     const int64_t tiles = tc_gemm_tiles(a);
     const int64_t n_tail = tiles - p.full;
     if (use_cluster(swap, p, tiles)) a.cluster_k = p.splits;
@@ -663,11 +672,18 @@ static int gemm_dispatch(mrt_weight w, const void* x, int64_t ldx, void* y, int6
     }
     e = launch_tc_gemm(a, tx, *tw, s);
     if (e != cudaSuccess) return cuda_error(e, "tcgen05 gemm launch");
+    if (fused) *fused = swiglu_lut != nullptr;
     if (n_tail > 0 && !swap) {
         e = launch_reduce_tail(a, s);
         if (e != cudaSuccess) return cuda_error(e, "split-K reduction launch");
     }
     return MRT_OK;
+}
+
+int gemm_swiglu(mrt_weight w, const void* x, int64_t ldx, void* act, int64_t ld_act, int64_t M,
+                const uint16_t* lut, cudaStream_t s, bool* fused) {
+    if (lut == nullptr || fused == nullptr) return set_error(MRT_ERR_INVALID_ARG, "NULL SiLU table or flag");
+    return gemm_dispatch(w, x, ldx, act, ld_act, M, false, false, s, lut, fused);
 }
 
 }  // namespace mrt
@@ -698,6 +714,30 @@ extern "C" int mrt_gemm(mrt_weight w, const void* x_dev, int64_t ldx, void* y_de
     clear_error();
     return gemm_dispatch(w, x_dev, ldx, y_dev, ldy, M, false, (flags & MRT_GEMM_BIAS) != 0,
                          static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int mrt_gemm_swiglu(mrt_weight w, const void* x_dev, int64_t ldx, void* act_dev, int64_t ld_act,
+                               int64_t M, void* stream) {
+    clear_error();
+    if (w == nullptr) return set_error(MRT_ERR_INVALID_ARG, "NULL weight");
+    if (w->n % 2 != 0) return set_error(MRT_ERR_SHAPE, "an interleaved gate|up weight has an even row count");
+    if (M < 0) return set_error(MRT_ERR_SHAPE, "M must be >= 0");
+    if (M == 0) return MRT_OK;
+    DevCtx* c = current_ctx();
+    if (!c) return MRT_ERR_CUDA;
+    const uint16_t* lut = silu_lut_for_device(c->device);
+    if (lut == nullptr) return set_error(MRT_ERR_CUDA, "building the SiLU table failed");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    bool fused = false;
+    int rc = gemm_swiglu(w, x_dev, ldx, act_dev, ld_act, M, lut, s, &fused);
+    if (rc != MRT_OK || fused) return rc;
+    // The plan splits K: the interleaved product into scratch, then the pairs.
+    const size_t bytes = static_cast<size_t>(M) * static_cast<size_t>(w->n) * 2;
+    if ((rc = ensure_buffer(&c->gu, &c->gu_bytes, bytes, "allocating gate|up scratch")) != MRT_OK) return rc;
+    if ((rc = gemm_dispatch(w, x_dev, ldx, c->gu, w->n, M, false, false, s)) != MRT_OK) return rc;
+    const cudaError_t e = launch_swiglu_pairs(static_cast<const uint16_t*>(c->gu), w->n, w->n / 2, M, lut,
+                                              static_cast<uint16_t*>(act_dev), ld_act, s);
+    return e == cudaSuccess ? MRT_OK : cuda_error(e, "swiglu launch");
 }
 
 extern "C" int mrt_gemm_f32(mrt_weight w, const void* x_dev, int64_t ldx, float* y_dev, int64_t ldy,

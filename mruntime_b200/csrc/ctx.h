@@ -24,6 +24,8 @@ struct DevCtx {
     size_t io_x_bytes = 0;
     void* io_y = nullptr;
     size_t io_y_bytes = 0;
+    void* gu = nullptr;     // interleaved gate|up product of an unfused mrt_gemm_swiglu
+    size_t gu_bytes = 0;
 };
 
 // Record an error for mrt_last_error_string() and return its code.
@@ -57,6 +59,19 @@ int tp_rank_world(mrt_tp tp, int* rank, int* world);
 // Every rank's `bytes` host bytes, gathered in rank order into out[world * bytes]
 // (synchronous; every rank of tp must call it).
 int tp_allgather_host(mrt_tp tp, const void* in, void* out, size_t bytes);
+
+// mrt_gemm with the SwiGLU epilogue for a weight whose rows interleave gate
+// and up (row 2j = gate j, row 2j + 1 = up j): act[m][j] = fp16(lut[fp16(g)] *
+// fp16(u)), act of w->n / 2 columns with row stride ld_act.  Runs only when
+// the plan computes every tile over the whole K (*fused = true); otherwise
+// launches nothing and sets *fused = false.
+int gemm_swiglu(mrt_weight w, const void* x, int64_t ldx, void* act, int64_t ld_act, int64_t M,
+                const uint16_t* lut, cudaStream_t s, bool* fused);
+// The FP16 SiLU table of a device (ops.cu; nullptr if it cannot be built).
+const uint16_t* silu_lut_for_device(int device);
+// act[m][i] = fp16(lut[gu[m][2i]] * gu[m][2i+1]) for i < I (ops.cu).
+cudaError_t launch_swiglu_pairs(const uint16_t* gu, int64_t ld_gu, int64_t I, int64_t M, const uint16_t* lut,
+                                uint16_t* act, int64_t ld_act, cudaStream_t s);
 
 }  // namespace mrt
 

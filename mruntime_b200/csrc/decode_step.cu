@@ -214,9 +214,9 @@ __device__ __forceinline__ Gemv gemv_of(const StepArgs& a, int l, int which) {
             my_rows(a.H, &r0, &r1);
             g = Gemv{ly.o, (a.nh * a.D + 63) / 64, r0, r1, 0, 0};
             break;
-        case 2:  // gate | up: the same intermediate rows of both halves
+        case 2:  // gate | up, rows interleaved (2j gate j, 2j + 1 up j): one range
             my_rows(a.I, &r0, &r1);
-            g = Gemv{ly.gu, (a.H + 63) / 64, r0, r1, a.I + r0, a.I + r1};
+            g = Gemv{ly.gu, (a.H + 63) / 64, 2 * r0, 2 * r1, 0, 0};
             break;
         default:  // down, split along K: whole tiles, contiguous per CTA
             g = split_gemv(ly.down, a.H, a.I);
@@ -935,10 +935,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
                           [&](int64_t row, float v) { gu_rows[row] = f32_to_f16_bits(v); }))
             return;
         cons_sync();
-        for (int64_t j = ct; j < la; j += kStepCons) {
-            const float sg = f16_bits_to_f32(a.silu_lut[gu_rows[j]]);
-            const float up = f16_bits_to_f32(gu_rows[la + j]);
-            a.act[g.a0 + j] = f32_to_f16_bits(__fmul_rn(sg, up));
+        for (int64_t j = ct; 2 * j < la; j += kStepCons) {
+            const float sg = f16_bits_to_f32(a.silu_lut[gu_rows[2 * j]]);
+            const float up = f16_bits_to_f32(gu_rows[2 * j + 1]);
+            a.act[g.a0 / 2 + j] = f32_to_f16_bits(__fmul_rn(sg, up));
         }
         if (!grid_sync(a, nbar, ct, &ok_sh)) return;
         load_operand(xs, a.act, a.I, ((a.I + 63) / 64) * 64, ct);

@@ -15,7 +15,7 @@ struct StepLayer {
     const uint16_t* qkv;    // q|k|v rows (local heads), K = hidden
     const uint16_t* bias;   // FP16 q|k|v bias or nullptr
     const uint16_t* o;      // [hidden, local heads * head_dim]
-    const uint16_t* gu;     // gate rows [0, I) then up rows [I, 2I) (local I), K = hidden
+    const uint16_t* gu;     // gate and up rows interleaved: row 2j = gate j, 2j + 1 = up j (local I), K = hidden
     const uint16_t* down;   // [hidden, local I]
     const void* ln1;        // RMSNorm gains before attention
     const void* ln2;        // RMSNorm gains before the MLP

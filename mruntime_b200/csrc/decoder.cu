@@ -820,22 +820,6 @@ __global__ void __launch_bounds__(kNT)
     norm_vecs(x, nv, H, w, wdt, eps, normed + row * H, red);
 }
 
-// act = fp16(silu(gate) * up) with silu from the FP16 table
-// (qwen_model.cpp:281-285: silu rounded to FP16, then the product rounded).
-__global__ void silu_mul_kernel(const uint16_t* gu, int64_t ld, int64_t I, int64_t S, const uint16_t* lut,
-                                uint16_t* act) {
-    griddep_launch_dependents();
-    griddep_wait();
-    const int64_t total = S * I;
-    for (int64_t e = blockIdx.x * static_cast<int64_t>(kNT) + threadIdx.x; e < total;
-         e += static_cast<int64_t>(gridDim.x) * kNT) {
-        const int64_t s = e / I, i = e % I;
-        const float a = f16_bits_to_f32(lut[gu[s * ld + i]]);
-        const float u = f16_bits_to_f32(gu[s * ld + I + i]);
-        act[e] = f32_to_f16_bits(__fmul_rn(a, u));
-    }
-}
-
 // After the greedy pick of a forward over `rows` tokens: record the token and
 // move the state to the next position.
 // The cross-GPU all-reduce epoch base (when there is one) advances by the
@@ -896,7 +880,7 @@ struct mrt_decoder_s {
     bool ready = false;
     // activations and state (allocated by finalize)
     uint16_t *x = nullptr, *r = nullptr, *p = nullptr, *normed = nullptr, *qkv = nullptr, *attn = nullptr,
-             *gu = nullptr, *act = nullptr, *logits = nullptr, *kc = nullptr, *vc = nullptr;
+             *act = nullptr, *logits = nullptr, *kc = nullptr, *vc = nullptr;
     float *cos_t = nullptr, *sin_t = nullptr, *part = nullptr, *am_val = nullptr;
     int* counters = nullptr;
     int64_t* am_idx = nullptr;
@@ -1227,7 +1211,21 @@ extern "C" int mrt_decoder_load(mrt_decoder d, const char* name_c, const void* s
             return rc;
         ly.gu_have |= 1u << part;
         if (ly.gu_have == 3u) {
-            rc = upload_f16(ly.st_gu, 2 * il, H, s, &ly.gateup);
+            // Interleave the rows (row 2j = gate j, row 2j + 1 = up j) so
+            // that each pair lands in one GEMM tile and the SwiGLU epilogue
+            // sees both halves of it.
+            uint16_t* inter = nullptr;
+            if ((rc = dec_alloc(d, reinterpret_cast<void**>(&inter), static_cast<size_t>(2 * il * H) * 2,
+                                "interleaving gate|up")) != MRT_OK)
+                return rc;
+            const size_t row = static_cast<size_t>(H) * 2;
+            cudaError_t e = cudaMemcpy2DAsync(inter, 2 * row, ly.st_gu, row, row, static_cast<size_t>(il),
+                                              cudaMemcpyDeviceToDevice, s);
+            if (e == cudaSuccess)
+                e = cudaMemcpy2DAsync(inter + H, 2 * row, ly.st_gu + il * H, row, row, static_cast<size_t>(il),
+                                      cudaMemcpyDeviceToDevice, s);
+            rc = e == cudaSuccess ? upload_f16(inter, 2 * il, H, s, &ly.gateup) : cuda_error(e, "interleaving gate|up");
+            dec_release(d, inter);
             dec_release(d, ly.st_gu);
             ly.st_gu = nullptr;
             return rc;
@@ -1477,7 +1475,7 @@ int dec_finalize(mrt_decoder d) {
     if ((rc = act(&d->x, S * H, "activations")) || (rc = act(&d->r, S * H, "activations")) ||
         (rc = act(&d->p, S * H, "activations")) || (rc = act(&d->normed, S * H, "activations")) ||
         (rc = act(&d->qkv, S * d->n_qkv, "activations")) || (rc = act(&d->attn, S * d->nh * D, "activations")) ||
-        (rc = act(&d->gu, S * 2 * (d->i1 - d->i0), "activations")) || (rc = act(&d->act, S * (d->i1 - d->i0), "activations")) ||
+        (rc = act(&d->act, S * (d->i1 - d->i0), "activations")) ||
         (rc = act(&d->logits, d->v1 - d->v0, "logits")) || (rc = act(&d->kc, d->L * d->nkv * S * D, "the KV cache")) ||
         (rc = act(&d->vc, d->L * d->nkv * S * D, "the KV cache")))
         return rc;
@@ -1538,7 +1536,6 @@ int dec_forward(mrt_decoder d, int64_t S, const int32_t* ids, int64_t pos0, bool
     const size_t row_smem = 0;
     const float eps = d->cfg.rms_norm_eps;
     const float scale = 1.0f / std::sqrt(static_cast<float>(D));  // qwen_model.cpp:220
-    const uint16_t* lut = silu_lut_for_device(d->device);
     const int64_t kv_layer = d->nkv * d->max_seq * D;
     // Row-parallel output: FP32 partials, summed across ranks, rounded once.
     // With the peer path the partial stays in this rank's exchange buffer of
@@ -1596,9 +1593,9 @@ int dec_forward(mrt_decoder d, int64_t S, const int32_t* ids, int64_t pos0, bool
         }
         DEC_TRY(row_parallel(ly.o, d->attn, ad, 0));
         DEC_CU(add_norm(d->x, d->r, ly.ln2, ly.ln2_dt, 0, static_cast<int>(2 * l), 0, S), "add+rmsnorm launch");
-        DEC_TRY(mrt_gemm(ly.gateup, d->normed, H, d->gu, 2 * il, S, 0, s));
-        DEC_CU(launch_pdl(silu_mul_kernel, dim3(grid_for(S * il)), dim3(kNT), 0, s, d->gu, 2 * il, il, S, lut, d->act),
-               "silu*mul launch");
+        // gate|up with SiLU(gate) * up (in the GEMM's epilogue when its plan
+        // keeps whole tiles).
+        DEC_TRY(mrt_gemm_swiglu(ly.gateup, d->normed, H, d->act, il, S, s));
         DEC_TRY(row_parallel(ly.down, d->act, il, 1));
     }
     // Final residual and norm of the last row, lm_head, greedy pick.

@@ -156,6 +156,49 @@ __device__ __forceinline__ void store_swap_chunk(const TcGemmArgs& a, const uint
     }
 }
 
+// SwiGLU epilogue, swap mode: lane = weight row n, r[j] = token m0 + j.  Even
+// rows are gate rows, odd rows the matching up rows (the partner lane n ^ 1);
+// the even lane stores fp16(silu(gate) * up) for its pair n / 2
+// (qwen_model.cpp:278-285: gate and up rounded to FP16, SiLU from the FP16
+// table, the product rounded).  Every lane reaches the shuffles.
+__device__ __forceinline__ void store_swap_chunk_swiglu(const TcGemmArgs& a, const uint32_t (&r)[16], int64_t n,
+                                                        int64_t m0) {
+    uint16_t* y = static_cast<uint16_t*>(a.y);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        const int64_t m = m0 + j;
+        if (m >= a.M) break;  // uniform over the warp
+        const uint32_t h = f32_to_f16_bits(__uint_as_float(r[j]));
+        const uint32_t up = __shfl_xor_sync(0xFFFFFFFFu, h, 1);
+        if ((n & 1) == 0 && n < a.N) {
+            const float sg = f16_bits_to_f32(a.swiglu_lut[h]);
+            y[m * a.ldy + (n >> 1)] = f32_to_f16_bits(__fmul_rn(sg, f16_bits_to_f32(static_cast<uint16_t>(up))));
+        }
+    }
+}
+
+// SwiGLU epilogue, normal mode: lane = token row, r[j] = weight row col0 + j
+// (col0 even), so pairs are (r[2i], r[2i+1]) -> y[row][col0 / 2 + i].
+__device__ __forceinline__ void store_row_chunk_swiglu(const TcGemmArgs& a, const uint32_t (&r)[32], int64_t row,
+                                                       int64_t col0) {
+    uint16_t h[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const uint16_t g = f32_to_f16_bits(__uint_as_float(r[2 * i]));
+        const uint16_t u = f32_to_f16_bits(__uint_as_float(r[2 * i + 1]));
+        h[i] = f32_to_f16_bits(__fmul_rn(f16_bits_to_f32(a.swiglu_lut[g]), f16_bits_to_f32(u)));
+    }
+    uint16_t* dst = static_cast<uint16_t*>(a.y) + row * a.ldy + (col0 >> 1);
+    if (col0 + 32 <= a.N && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+        *reinterpret_cast<uint4*>(dst) = make_uint4(pack_h2(h[0], h[1]), pack_h2(h[2], h[3]), pack_h2(h[4], h[5]),
+                                                    pack_h2(h[6], h[7]));
+        *reinterpret_cast<uint4*>(dst + 8) = make_uint4(pack_h2(h[8], h[9]), pack_h2(h[10], h[11]),
+                                                        pack_h2(h[12], h[13]), pack_h2(h[14], h[15]));
+    } else {
+        for (int i = 0; i < 16 && col0 + 2 * i + 1 < a.N; ++i) dst[i] = h[i];
+    }
+}
+
 // Swap mode: up to 16 FP32 columns (tokens) into a tail slot, laid out as
 // [bn / 4 token groups][128 rows][4 tokens] so that one float4 per lane of a
 // warp (32 consecutive rows) is one contiguous 512-byte run.  Only the
@@ -720,6 +763,8 @@ __global__ void __launch_bounds__(kThreadsTc, SWAP ? 2 : 1)
                     tmem_ld_16cols(t_row + c * 16, r);
                     if (w.slot >= 0) {
                         store_partial_chunk16(a, r, w.slot, quad * 32 + lane, c * 16, BN, min(4, (cols - c * 16 + 3) / 4));
+                    } else if (a.swiglu_lut != nullptr) {
+                        store_swap_chunk_swiglu(a, r, row, static_cast<int64_t>(w.nt) * BN + c * 16);
                     } else {
                         store_swap_chunk(a, r, row, static_cast<int64_t>(w.nt) * BN + c * 16);
                     }
@@ -734,7 +779,10 @@ __global__ void __launch_bounds__(kThreadsTc, SWAP ? 2 : 1)
                     if (w.slot >= 0) {
                         store_partial_chunk(a, r, w.slot, quad * 32 + lane, c * 32, BN);
                     } else if (row < a.M && col0 < a.N) {
-                        store_row_chunk(a, r, row, col0);
+                        if (a.swiglu_lut != nullptr)
+                            store_row_chunk_swiglu(a, r, row, col0);
+                        else
+                            store_row_chunk(a, r, row, col0);
                     }
                 }
             }
@@ -873,6 +921,9 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& a, const CUtensorMap& tmap_x, const
     if (a.full_tiles < tiles && (a.kb_per <= 0 || (a.tail_splits - 1) * a.kb_per >= num_kb ||
                                  a.tail_splits * a.kb_per < num_kb ||
                                  (!clustered && (a.partials == nullptr || (a.swap && a.tile_counters == nullptr)))))
+        return cudaErrorInvalidValue;
+    // SwiGLU pairs: whole-K tiles only, even N, FP16 output, no bias.
+    if (a.swiglu_lut != nullptr && (a.full_tiles != tiles || (a.N & 1) != 0 || a.out_f32 || a.bias != nullptr))
         return cudaErrorInvalidValue;
     // Clusters: swap mode, every tile split, one slice per CTA.
     if (clustered && (!a.swap || a.cluster_k > 8 || a.full_tiles != 0 || a.tail_splits != a.cluster_k ||

@@ -56,6 +56,11 @@ struct TcGemmArgs {
     // summed through distributed shared memory (partials and tile_counters
     // unused).  0: slices are summed through global memory.
     int cluster_k;
+    // Non-null: SwiGLU epilogue for a weight whose rows interleave gate and
+    // up (row 2j = gate j, row 2j + 1 = up j): y[m][j] = fp16(lut[fp16(g)] *
+    // fp16(u)) with y of N / 2 columns.  Plans without a K-split only; no
+    // bias, FP16 output.
+    const uint16_t* swiglu_lut;
 };
 // Whether a swap-mode launch of tile width bn may use clusters of k CTAs on
 // the current device (checked once per device, width and k).

@@ -6,6 +6,7 @@
 // Transcendentals that a GPU library would round differently from glibc are
 // taken from host-built tables instead: SiLU on FP16 (all 65536 inputs) and
 // RoPE's cos/sin (the reference's own float expressions).
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <limits>
@@ -282,6 +283,42 @@ int launch_status(const char* what) {
 
 // The FP16 SiLU table of `device` (built on first use), for fused kernels.
 const uint16_t* silu_lut_for_device(int device) { return silu_lut(device); }
+
+namespace {
+
+// act[m][i] = fp16(silu(gate) * up) from an interleaved gate|up product
+// (gate i at column 2i, up i at 2i + 1 of row m; qwen_model.cpp:278-285).
+__global__ void swiglu_pairs_kernel(const uint16_t* gu, int64_t ld_gu, int64_t I, int64_t M, const uint16_t* lut,
+                                    uint16_t* act, int64_t ld_act) {
+    griddep_launch_dependents();
+    griddep_wait();
+    const int64_t total = M * I;
+    for (int64_t e = blockIdx.x * static_cast<int64_t>(kT) + threadIdx.x; e < total;
+         e += static_cast<int64_t>(gridDim.x) * kT) {
+        const int64_t m = e / I, i = e % I;
+        const uint16_t g = gu[m * ld_gu + 2 * i], u = gu[m * ld_gu + 2 * i + 1];
+        act[m * ld_act + i] = f32_to_f16_bits(__fmul_rn(f16_bits_to_f32(lut[g]), f16_bits_to_f32(u)));
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_swiglu_pairs(const uint16_t* gu, int64_t ld_gu, int64_t I, int64_t M, const uint16_t* lut,
+                                uint16_t* act, int64_t ld_act, cudaStream_t s) {
+    const int64_t blocks = std::min<int64_t>((M * I + kT - 1) / kT, 148 * 16);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(blocks < 1 ? 1 : blocks));
+    cfg.blockDim = dim3(kT);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, swiglu_pairs_kernel, gu, ld_gu, I, M, lut, act, ld_act);
+    if (e == cudaSuccess) note_launches(1);
+    return e;
+}
 
 }  // namespace mrt
 

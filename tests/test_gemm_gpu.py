@@ -316,3 +316,57 @@ def test_argmax_edge_cases_match_reference(cuda_dev):
 
 def test_no_kernel_timed_out(cuda_dev):
     capi.sync(stream())  # raises MrtError(MRT_ERR_TIMEOUT) if any bounded wait gave up
+
+
+# ------------------------------------------------------------------ gate|up with SwiGLU
+
+def _silu_table_f16() -> np.ndarray:
+    """The reference's FP16 SiLU of every FP16 input (qwen_model.cpp:281-283:
+    x / (1 + exp(-x)) in FP32, rounded to FP16); exp correctly rounded."""
+    x = W.f16_bits_to_f32(np.arange(65536, dtype=np.uint32).astype(np.uint16)).astype(np.float32)
+    with np.errstate(over="ignore", invalid="ignore"):
+        e = np.exp(-x.astype(np.float64)).astype(np.float32)
+        y = x / (np.float32(1.0) + e)
+    return W.to_f16_bits(y)
+
+
+# (M, I, K): fused in the swap epilogue (16-, 64-token tiles), fused in the
+# normal-mode epilogue, and K-split plans (global and cluster finish, normal
+# mode with a split tail) that take the product-then-pairs route.
+SWIGLU_SHAPES = [(1, 18944, 3584), (16, 18944, 3584), (40, 18944, 3584), (300, 18944, 3584),
+                 (1, 2304, 3584), (33, 2304, 3584), (65, 10000, 2048)]
+
+
+@pytest.mark.parametrize("MIK", SWIGLU_SHAPES)
+def test_gemm_swiglu(cuda_dev, MIK):
+    """mrt_gemm_swiglu on interleaved gate|up rows equals the plain product's
+    gate and up outputs put through the FP16 SiLU and the rounded multiply."""
+    M, I, K = MIK
+    rng = np.random.default_rng(M + I + K)
+    x = rand_f16(rng, (M, K))
+    w = rand_w(rng, (2 * I, K), BF16)  # row 2j = gate j, row 2j + 1 = up j
+    wt = upload(w, BF16)
+    p = capi.gemm_plan(M, 2 * I, K)
+    tiles = -(-2 * I // 128) if p["kernel"] == "tcgen05-swap" else -(-M // 128) * -(-2 * I // p["bn"])
+    fused = p["full_tiles"] == tiles
+    assert fused == (I in (18944,)), p  # the shapes above cover both routes
+    y = gemm(wt, x)  # same plan: the same FP16 gate and up values
+    xd = dev_u16(x)
+    act = torch.empty((M, I), dtype=torch.int16, device="cuda")
+    capi.gemm_swiglu(wt, xd.data_ptr(), K, act.data_ptr(), I, M, stream())
+    capi.sync(stream())
+    got = host_u16(act)
+    g, u = y[:, 0::2], y[:, 1::2]
+    lut = _silu_table_f16()
+    prod = W.f16_bits_to_f32(lut[g]).astype(np.float32) * W.f16_bits_to_f32(u).astype(np.float32)
+    want = W.to_f16_bits(prod)
+    same = got == want
+    if not same.all():
+        # Only a SiLU input whose exp differs from the host's expf in the last
+        # bit may move one FP16 ulp.
+        diff = np.abs(got.astype(np.int32) - want.astype(np.int32))
+        assert same.mean() > 0.9999 and diff.max() <= 1, (MIK, same.mean(), diff.max())
+    # And the product itself is the oracle's within tolerance (rows sampled).
+    rows = np.unique(np.r_[0, M // 2, M - 1])
+    _, _, s2 = _check_against_oracle(x, w, BF16, y, rows, what=f"swiglu product {MIK}")
+    assert s2 > 0.9
