@@ -734,8 +734,9 @@ __device__ __forceinline__ unsigned long long global_ns() {
 // Row-parallel output finished across GPUs, fused with the residual add and
 // RMSNorm that consume it (qwen_model.cpp:321-332).  Every rank's GEMM left
 // its FP32 partial rows in its own exchange buffer.  Block 0 publishes this
-// rank's epoch to every peer (system-scope release store); each block waits
-// (bounded, 2 s) for every peer's epoch, then reads all W partials of its row
+// rank's epoch to every peer (system-scope release stores, one thread per
+// peer); each block waits (bounded, 2 s, one polling thread per peer) for
+// every peer's epoch, then reads all W partials of its row
 // over NVLink and sums them in rank order -- the same order on every rank, so
 // every rank holds bit-identical rows -- rounds once to FP16 (the projection's
 // output), and continues as add_norm_kernel: out = fp16(a + p), normed =
@@ -751,31 +752,26 @@ __global__ void __launch_bounds__(kNT)
     __shared__ float red[kNT / 32];
     __shared__ unsigned arrived;  // bit q: rank q's partial may be read
     const unsigned long long epoch = *epoch_base + static_cast<unsigned long long>(call) + 1ull;
-    if (threadIdx.x == 0) {
-        if (blockIdx.x == 0) {
-            __threadfence_system();  // this rank's partial (written by the previous kernel) before the flag
-            for (int q = 0; q < pa.world; ++q)
-                if (q != pa.rank) st_release_sys(pa.flags[q] + pa.rank, epoch);
-        }
-        unsigned got = 1u << pa.rank;
+    if (threadIdx.x == 0) arrived = 1u << pa.rank;
+    __syncthreads();
+    // Thread q talks to peer q, so the world's publishes and polls overlap
+    // instead of queueing behind one thread's system-scope fences.
+    const int q = static_cast<int>(threadIdx.x);
+    if (q < pa.world && q != pa.rank) {
+        // This rank's partial (written by the previous kernel) is released
+        // to peer q with the epoch.
+        if (blockIdx.x == 0) st_release_sys(pa.flags[q] + pa.rank, epoch);
         const unsigned long long t0 = global_ns();
-        bool timed_out = false;
-        for (int q = 0; q < pa.world; ++q) {
-            if (q == pa.rank) continue;
-            while (true) {
-                if (ld_acquire_sys(pa.flags[pa.rank] + q) >= epoch) {
-                    got |= 1u << q;
-                    break;
-                }
-                if (global_ns() - t0 > kWaitLimitNs) {
-                    timed_out = true;
-                    break;
-                }
+        while (true) {
+            if (ld_acquire_sys(pa.flags[pa.rank] + q) >= epoch) {
+                atomicOr(&arrived, 1u << q);
+                break;
             }
-            if (timed_out) break;
+            if (global_ns() - t0 > kWaitLimitNs) {
+                raise_error(err, kErrPeerWait);
+                break;
+            }
         }
-        if (timed_out) raise_error(err, kErrPeerWait);
-        arrived = got;
     }
     __syncthreads();
     const unsigned got = arrived;
