@@ -4,8 +4,9 @@ Qwen2.5-7B-shaped decoder (hidden 3584, 28 layers, 28/4 heads, intermediate
 gains 1, RoPE base 1e6, eps 1e-6; a 512-token prompt uniform in
 [0, 152064); seed 3; mruntime_b200.workloads.decoder_tensors / decoder_prompt).
 
-Writes the checkpoint as a safetensors file under _data/ (15.2 GB; git- and
-gpurun-ignored: the GPU side regenerates identical bits from the seed), runs
+Writes the checkpoint as a safetensors file under _data/ (15.2 GB; neither
+committed nor shipped with the tests: the GPU side regenerates identical bits
+from the seed), runs
 oracle/_ref/ref_engine -- the reference's QwenModel + InferenceEngine built
 from its sources (`make -C oracle engine`) -- and stores the 32 generated ids
 in decode_7b_greedy.json beside this script.

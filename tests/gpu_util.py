@@ -11,7 +11,7 @@ from mruntime_b200 import workloads as W
 
 FP16, BF16, FP32 = capi.FP16, capi.BF16, capi.FP32
 
-# Tolerances: relative Frobenius error against FP64 at
+# Tolerances of the linear-layer path: relative Frobenius error against FP64 at
 # most 1e-3, and never worse than the reference's own error against the same
 # ground truth.  "Never worse" allows 1% relative slack for the different FP32
 # summation order, which moves an occasional output across an FP16 rounding
