@@ -425,6 +425,113 @@ def gpu_arm(args, rank, world, local):
 
 
 # ---------------------------------------------------------------------------
+# The smaller reference configurations, timed on one GPU (extras)
+# ---------------------------------------------------------------------------
+
+def configs_arm(peaks) -> dict:
+    """Device time of the reference's smaller configurations through the C ABI
+    (each a graph of repeated calls, CUDA events around the replays; random
+    device-made operands, the values do not change the work):
+
+    * decode GEMV, M=1, W 4864x896 FP16 (8.7 MB): cold = 30 weight copies
+      called in turn (262 MB, more than the 126 MB L2), hot = one copy 30 times;
+    * Qwen2.5-0.5B layer at M=512: the seven projections as the reference
+      calls them (q/k/v with their biases, o, gate, up, down), BF16 weights;
+    * 0.5B lm_head (151936x896 FP16, 272 MB) with the greedy argmax at M=1 and
+      M=128 (mrt_lm_head_argmax).
+
+    GB/s counts 2NK + 2MK + 2MN bytes per call, TFLOP/s 2MNK; HBM fractions
+    against the measured copy bandwidth, tensor fractions against the measured
+    burst bf16 peak (each call runs alone for microseconds)."""
+    import torch
+
+    from mruntime_b200 import capi
+
+    s0 = torch.cuda.current_stream().cuda_stream
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(7)
+
+    def weight(n, k, dt=torch.float16):
+        t = (torch.randn(n, k, generator=gen, device="cuda") * 0.02).to(dt)
+        w = capi.Weight(t.data_ptr(), capi.FP16 if dt == torch.float16 else capi.BF16, True, n, k, None, None, s0)
+        torch.cuda.synchronize()
+        return w
+
+    def act(m, k):
+        return torch.randn(m, k, generator=gen, device="cuda").half()
+
+    def per_call_ms(fn, calls, reps=20):
+        g = capture(fn)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for _ in range(3):
+            g.replay()
+        a.record()
+        for _ in range(reps):
+            g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        del g
+        return a.elapsed_time(b) / reps / calls
+
+    out = {}
+    # decode GEMV
+    N, K = 4864, 896
+    ws = [weight(N, K) for _ in range(30)]
+    x, y = act(1, K), torch.empty(1, N, dtype=torch.float16, device="cuda")
+    nbytes = 2 * N * K + 2 * K + 2 * N
+    cold = per_call_ms(lambda s: [capi.gemm(w, x.data_ptr(), K, y.data_ptr(), N, 1, False, s) for w in ws], 30)
+    hot = per_call_ms(lambda s: [capi.gemm(ws[0], x.data_ptr(), K, y.data_ptr(), N, 1, False, s) for _ in ws], 30)
+    for w in ws:
+        w.free()
+    out["decode_gemv_4864x896_m1"] = {
+        "cold_us": round(cold * 1e3, 2), "cold_GB/s": round(nbytes / (cold * 1e-3) / 1e9, 1),
+        "cold_frac_hbm": round(nbytes / (cold * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
+        "hot_us": round(hot * 1e3, 2), "hot_GB/s": round(nbytes / (hot * 1e-3) / 1e9, 1),
+        "note": "hot: the weight stays in L2, so the HBM fraction does not apply"}
+    # 0.5B layer at M = 512
+    M = 512
+    shapes = WL.LAYER_05B
+    lw = {nm: weight(n, k, torch.bfloat16) for nm, n, k in shapes}
+    keep = []
+    for nm, n in (("q", 896), ("k", 128), ("v", 128)):
+        b = (torch.randn(n, generator=gen, device="cuda") * 0.02).to(torch.bfloat16)
+        keep.append(b)
+        lw[nm].attach_bias(b.data_ptr(), capi.BF16, True, s0)
+    torch.cuda.synchronize()
+    xl, xd = act(M, 896), act(M, 4864)
+    ys = {nm: torch.empty(M, n, dtype=torch.float16, device="cuda") for nm, n, _ in shapes}
+
+    def layer(s):
+        for nm, n, k in shapes:
+            src = xd if nm == "down" else xl
+            capi.gemm(lw[nm], src.data_ptr(), k, ys[nm].data_ptr(), n, M, nm in ("q", "k", "v"), s)
+
+    t = per_call_ms(layer, 1)
+    flops = sum(2.0 * M * n * k for _, n, k in shapes)
+    for w in lw.values():
+        w.free()
+    out["layer_05b_m512"] = {"us": round(t * 1e3, 2), "TFLOP/s": round(flops / (t * 1e-3) / 1e12, 1),
+                             "frac_tensor_burst": round(flops / (t * 1e-3) / 1e12 / peaks["bf16_tflops"], 4),
+                             "calls": 7}
+    # lm_head + argmax
+    V, H = 151936, 896
+    wl = weight(V, H)
+    for m in (1, 128):
+        xm = act(m, H)
+        logits = torch.empty(m, V, dtype=torch.float16, device="cuda")
+        idx = torch.empty(m, dtype=torch.int64, device="cuda")
+        t = per_call_ms(lambda s, m=m, xm=xm, logits=logits, idx=idx: capi.lm_head_argmax(
+            wl, xm.data_ptr(), H, m, logits.data_ptr(), 0, idx.data_ptr(), None, s), 1)
+        nbytes = 2 * V * H + 2 * m * H + 2 * m * V
+        out[f"lm_head_05b_argmax_m{m}"] = {
+            "us": round(t * 1e3, 2), "GB/s": round(nbytes / (t * 1e-3) / 1e9, 1),
+            "frac_hbm": round(nbytes / (t * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
+            "TFLOP/s": round(2.0 * m * V * H / (t * 1e-3) / 1e12, 1)}
+    wl.free()
+    return out
+
+
+# ---------------------------------------------------------------------------
 # Greedy decode of the 7B-shaped decoder (mrt_decoder_*), one GPU
 # ---------------------------------------------------------------------------
 
@@ -609,6 +716,9 @@ def main():
         except FileNotFoundError as e:
             cpu = {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "reference",
                    "sample": f"unavailable: {e}"}
+    configs = None
+    if world == 1 and not args.no_sweep:
+        configs = configs_arm(r["peaks"])
     decode = None
     if not args.no_decode:
         r["projs"] = None  # release the sweep's weights first
@@ -620,7 +730,7 @@ def main():
                 "data": "synthetic (seeded N(0,1) FP16 activations, N(0,0.02) BF16 weights)",
                 "config": workload_config(args.m, world, not args.no_graph), "e2e": r["e2e"], "roofline": r["roofline"],
                 "cpu_baseline": cpu, "clocks": r["clocks"], "gpu_launches": r["launches"], "sweep": r["sweep"],
-                "decode": decode}
+                "configs": configs, "decode": decode}
         print(json.dumps(line))
     if r["tp"] is not None:
         import gc
