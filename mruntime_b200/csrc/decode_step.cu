@@ -80,30 +80,25 @@ __device__ __forceinline__ float gain(const void* w, int dt, int64_t i) {
     return dt == MRT_BF16 ? bf16_bits_to_f32(v) : f16_bits_to_f32(v);
 }
 
-__device__ __forceinline__ void st_release_gpu_u32(unsigned* p, unsigned v) {
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
 
 // Grid barrier of the consumer threads of every CTA (the producer warps keep
-// streaming).  a.bar[0] counts arrivals; the last CTA to arrive at barrier n
-// publishes n in a.bar[32] (another cache line), which the others poll, so
-// pollers never contend with arrivals.  Both start at 0 for each launch.
-// Returns false once the kernel is aborting.
+// streaming).  a.bar[0] counts arrivals (zero at each launch); barrier n is
+// complete when it reaches n * gridDim.x.  Returns false once the kernel is
+// aborting.
 __device__ bool grid_sync(const StepArgs& a, unsigned& nbar, int ct, volatile int* ok_sh) {
     cons_sync();
     ++nbar;
     if (ct == 0) {
         int ok = 1;
-        unsigned old;
-        // Release this CTA's writes with the arrival; the last arrival also
-        // acquires everyone's and releases them with the flag.
-        asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(a.bar) : "memory");
-        if (old == nbar * gridDim.x - 1) {
-            st_release_gpu_u32(a.bar + 32, nbar);
-        } else {
-            const unsigned long long t0 = now_ns();
-            while (ld_acquire_gpu_u32(a.bar + 32) < nbar) {
-                __nanosleep(32);
+        // Arrive without waiting for an answer (the release covers this
+        // CTA's writes, ordered before it by the barrier above), then spin on
+        // the counter itself; the error flag and the clock are checked every
+        // 256 polls only.
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar) : "memory");
+        const unsigned target = nbar * gridDim.x;
+        const unsigned long long t0 = now_ns();
+        for (unsigned it = 1; ld_acquire_gpu_u32(a.bar) < target; ++it) {
+            if ((it & 255u) == 0) {
                 if (error_raised(a.err)) {
                     ok = 0;
                     break;

@@ -55,7 +55,7 @@ struct StepArgs {
     int att_split;
     float* cand_val;            // [grid] per-CTA best logit
     int64_t* cand_idx;
-    unsigned* bar;              // grid barrier: [0] arrivals, [32] released barrier; zeroed before each launch
+    unsigned* bar;              // grid barrier: [0] arrivals; zeroed before each launch
     StepState* st;
     int32_t* tokens;
     int64_t tokens_cap;
