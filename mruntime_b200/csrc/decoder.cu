@@ -355,10 +355,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32)
     const int64_t kw = static_cast<int64_t>(sp) * kSplitKeys + warp * kKeysPerWarp;
     const int nk = kv_len - kw <= 0 ? 0 : (kv_len - kw >= kKeysPerWarp ? kKeysPerWarp : static_cast<int>(kv_len - kw));
     const int icur = pos < max_seq && pos >= kw && pos < kw + nk ? static_cast<int>(pos - kw) : -1;  // warp-uniform
-    float qv[PER];
-    uint16_t qb[PER];
-    load_per<PER>(qkv + static_cast<int64_t>(h) * D + lane * PER, qv);
-    rope_lane_f16<PER>(qv, qb, lane, cos_row, sin_row);
+    // The cached keys and values first: they depend on nothing in this
+    // launch, so their latency overlaps the query's load and rotation.
     const uint16_t* kb = kc + (static_cast<int64_t>(g) * max_seq + kw) * D + lane * PER;
     const uint16_t* vb = vc + (static_cast<int64_t>(g) * max_seq + kw) * D + lane * PER;
     float kx[kKeysPerWarp][PER], vx[kKeysPerWarp][PER];
@@ -368,6 +366,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32)
             load_per<PER>(kb + i * D, kx[i]);
             load_per<PER>(vb + i * D, vx[i]);
         }
+    float qv[PER];
+    uint16_t qb[PER];
+    load_per<PER>(qkv + static_cast<int64_t>(h) * D + lane * PER, qv);
+    rope_lane_f16<PER>(qv, qb, lane, cos_row, sin_row);
     if (icur >= 0) {
         const uint16_t* kr = qkv + static_cast<int64_t>(nh + g) * D + lane * PER;
         const uint16_t* vr = qkv + static_cast<int64_t>(nh + nkv + g) * D + lane * PER;
