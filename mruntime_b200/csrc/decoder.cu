@@ -315,6 +315,7 @@ __device__ __forceinline__ void rope_lane_f16(float (&x)[PER], uint16_t (&bits)[
 }
 
 constexpr int kMergeChunk = 128;  // splits merged per pass (one per thread)
+constexpr int kMergeBatch = 32;   // up to this many splits are merged from one batch of loads
 
 // Decode attention for one query row (cpu_backend.cpp:171-290 with q_len = 1)
 // with the step's RoPE and KV-cache append folded in (qwen_model.cpp:162-205).
@@ -462,6 +463,61 @@ __global__ void __launch_bounds__(kAttnWarps * 32)
     if (!sm_last) return;
     const float* ph = part + static_cast<int64_t>(h) * nsplit * (D + 2);
     const int used = static_cast<int>((kv_len + kSplitKeys - 1) / kSplitKeys);  // splits holding keys
+    constexpr int kJ = (D + kAttnWarps * 32 - 1) / (kAttnWarps * 32);  // output elements per thread
+    if (used <= kMergeBatch) {
+        // Up to 1024 keys: one batch of loads -- every thread's columns of
+        // every split, and split s's maximum and sum of exp by thread s --
+        // before the maximum is reduced; then the same arithmetic in the same
+        // order as the chunked merge below, with no further global loads.
+        float av[kJ][kMergeBatch];
+#pragma unroll
+        for (int s2 = 0; s2 < kMergeBatch; ++s2)
+            if (s2 < used)
+#pragma unroll
+                for (int j = 0; j < kJ; ++j) {
+                    const int d = threadIdx.x + j * kAttnWarps * 32;
+                    if (d < D) av[j][s2] = __ldcg(ph + s2 * (D + 2) + 2 + d);
+                }
+        float my_m = -INFINITY, my_l = 0.0f;
+        if (static_cast<int>(threadIdx.x) < used) {
+            my_m = __ldcg(ph + threadIdx.x * (D + 2));
+            my_l = __ldcg(ph + threadIdx.x * (D + 2) + 1);
+        }
+        float mb = my_m;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mb = fmaxf(mb, __shfl_xor_sync(0xFFFFFFFFu, mb, o));
+        if (lane == 0) sm_red[warp] = mb;
+        __syncthreads();
+        float MMb = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; ++w) MMb = fmaxf(MMb, sm_red[w]);
+        if (static_cast<int>(threadIdx.x) < used) {
+            sm_w[threadIdx.x] = expf(__fsub_rn(my_m, MMb));
+            sm_ls[threadIdx.x] = my_l;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float LLb = 0.0f;
+            for (int s2 = 0; s2 < used; ++s2) LLb = __fadd_rn(LLb, __fmul_rn(sm_ls[s2], sm_w[s2]));
+            sm_red[0] = __fdiv_rn(1.0f, LLb);  // every warp read its maximum above
+        }
+        float Ab[kJ];
+#pragma unroll
+        for (int j = 0; j < kJ; ++j) {
+            Ab[j] = 0.0f;
+#pragma unroll
+            for (int s2 = 0; s2 < kMergeBatch; ++s2)
+                if (s2 < used) Ab[j] = __fadd_rn(Ab[j], __fmul_rn(av[j][s2], sm_w[s2]));
+        }
+        __syncthreads();
+        const float invb = sm_red[0];
+#pragma unroll
+        for (int j = 0; j < kJ; ++j) {
+            const int d = threadIdx.x + j * kAttnWarps * 32;
+            if (d < D) out[static_cast<int64_t>(h) * D + d] = f32_to_f16_bits(__fmul_rn(Ab[j], invb));
+        }
+        return;
+    }
     // M = max over the splits' maxima (order-free).
     float mx = -INFINITY;
     for (int s2 = threadIdx.x; s2 < used; s2 += kAttnWarps * 32) mx = fmaxf(mx, __ldcg(ph + s2 * (D + 2)));
