@@ -84,6 +84,7 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 }
 
 constexpr int kNormVec = 8;  // 16-byte vectors per thread: hidden <= 256 * 8 * 8 = 16384
+constexpr int64_t kPreloadRows = 148;  // row launches up to one wave preload their RMSNorm gains
 
 __device__ __forceinline__ uint4 ld16(const void* p) { return *reinterpret_cast<const uint4*>(p); }
 
@@ -121,8 +122,23 @@ __device__ __forceinline__ void gains8(const void* w, int wdt, int64_t i, float 
 // RMSNorm of one row whose FP16-rounded values this thread holds as
 // x[j][e] = element (threadIdx.x + j * kNT) * 8 + e (cpu_backend.cpp:292-330):
 // rms = sqrt(sum(x^2) / n + eps); out = fp16((x * (1 / rms)) * w).
-__device__ __forceinline__ void norm_vecs(const float (&x)[kNormVec][8], int nv, int64_t H, const void* w, int wdt,
-                                          float eps, uint16_t* __restrict__ out, float* red) {
+// This thread's RMSNorm gains (the vectors norm_vecs writes), loaded before
+// the programmatic wait by kernels of at most one wave of rows (decode): the
+// gains are never written after the decoder is loaded, so their latency
+// overlaps the previous kernel.  Larger launches (prefill) load them after
+// the reduction instead and keep the registers (two blocks per SM).
+__device__ __forceinline__ void load_gains(const void* w, int wdt, int nv, float (&g)[kNormVec][8]) {
+#pragma unroll
+    for (int j = 0; j < kNormVec; ++j) {
+        const int v = static_cast<int>(threadIdx.x) + j * kNT;
+        if (v < nv) gains8(w, wdt, static_cast<int64_t>(v) * 8, g[j]);
+    }
+}
+
+template <bool kPre>
+__device__ __forceinline__ void norm_vecs(const float (&x)[kNormVec][8], int nv, int64_t H,
+                                          const float (&g)[kNormVec][8], const void* w, int wdt, float eps,
+                                          uint16_t* __restrict__ out, float* red) {
     float ss = 0.0f;
 #pragma unroll
     for (int j = 0; j < kNormVec; ++j)
@@ -136,11 +152,16 @@ __device__ __forceinline__ void norm_vecs(const float (&x)[kNormVec][8], int nv,
     for (int j = 0; j < kNormVec; ++j) {
         const int v = static_cast<int>(threadIdx.x) + j * kNT;
         if (v >= nv) continue;
-        float g[8];
-        gains8(w, wdt, static_cast<int64_t>(v) * 8, g);
+        float gl[8];
+        if constexpr (kPre) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) gl[e] = g[j][e];
+        } else {
+            gains8(w, wdt, static_cast<int64_t>(v) * 8, gl);
+        }
         uint16_t h[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) h[e] = f32_to_f16_bits(__fmul_rn(__fmul_rn(x[j][e], inv), g[e]));
+        for (int e = 0; e < 8; ++e) h[e] = f32_to_f16_bits(__fmul_rn(__fmul_rn(x[j][e], inv), gl[e]));
         *reinterpret_cast<uint4*>(out + static_cast<int64_t>(v) * 8) =
             make_uint4(pack2(h[0], h[1]), pack2(h[2], h[3]), pack2(h[4], h[5]), pack2(h[6], h[7]));
     }
@@ -149,11 +170,14 @@ __device__ __forceinline__ void norm_vecs(const float (&x)[kNormVec][8], int nv,
 // Row s: hidden = table[id] (qwen_model.cpp:59-64), normed = RMSNorm(hidden).
 // ids == nullptr: the id is the state's current token.  Rows are 16-byte
 // vectors; every load of a thread is issued before any is used.
+template <bool kPre>
 __global__ void __launch_bounds__(kNT) embed_norm_kernel(const uint16_t* __restrict__ table, int64_t vocab, int64_t H,
                                                          const int32_t* ids, const DecState* st,
                                                          uint16_t* __restrict__ hidden, const void* __restrict__ w,
                                                          int wdt, float eps, uint16_t* __restrict__ normed, int* err) {
     griddep_launch_dependents();
+    float g[kNormVec][8];
+    if constexpr (kPre) load_gains(w, wdt, static_cast<int>(H / 8), g);
     griddep_wait();
     __shared__ float red[kNT / 32];
     const int64_t s = blockIdx.x;
@@ -177,14 +201,17 @@ __global__ void __launch_bounds__(kNT) embed_norm_kernel(const uint16_t* __restr
         *reinterpret_cast<uint4*>(hidden + s * H + static_cast<int64_t>(i) * 8) = v[j];
         unpack8(v[j], x[j]);
     }
-    norm_vecs(x, nv, H, w, wdt, eps, normed + s * H, red);
+    norm_vecs<kPre>(x, nv, H, g, w, wdt, eps, normed + s * H, red);
 }
 
 // Row s: out = fp16(a + b) (cpu_backend.cpp:403-455), normed = RMSNorm(out).
+template <bool kPre>
 __global__ void __launch_bounds__(kNT) add_norm_kernel(const uint16_t* __restrict__ a, const uint16_t* __restrict__ b,
                                                        uint16_t* __restrict__ out, int64_t H, const void* __restrict__ w,
                                                        int wdt, float eps, uint16_t* __restrict__ normed) {
     griddep_launch_dependents();
+    float g[kNormVec][8];
+    if constexpr (kPre) load_gains(w, wdt, static_cast<int>(H / 8), g);
     griddep_wait();
     __shared__ float red[kNT / 32];
     const int64_t s = blockIdx.x;
@@ -215,7 +242,7 @@ __global__ void __launch_bounds__(kNT) add_norm_kernel(const uint16_t* __restric
         *reinterpret_cast<uint4*>(out + s * H + static_cast<int64_t>(i) * 8) =
             make_uint4(pack2(h[0], h[1]), pack2(h[2], h[3]), pack2(h[4], h[5]), pack2(h[6], h[7]));
     }
-    norm_vecs(x, nv, H, w, wdt, eps, normed + s * H, red);
+    norm_vecs<kPre>(x, nv, H, g, w, wdt, eps, normed + s * H, red);
 }
 
 // RoPE on the q and k heads of S rows (cpu_backend.cpp:332-379, cos/sin from
@@ -801,11 +828,14 @@ __device__ __forceinline__ unsigned long long global_ns() {
 // RMSNorm(out).  Rows row0 .. row0 + gridDim.x - 1.  The epoch of call c of a
 // forward is *epoch_base + c + 1; epoch_base advances by the calls per forward.
 // A peer that never arrives leaves its partial out and raises kErrPeerWait.
+template <bool kPre>
 __global__ void __launch_bounds__(kNT)
     ar_add_norm_kernel(const PeerArgs pa, int64_t row0, const uint16_t* __restrict__ a, uint16_t* __restrict__ out,
                        int64_t H, const void* __restrict__ w, int wdt, float eps, uint16_t* __restrict__ normed,
                        const unsigned long long* epoch_base, int call, int* err) {
     griddep_launch_dependents();
+    float g[kNormVec][8];
+    if constexpr (kPre) load_gains(w, wdt, static_cast<int>(H / 8), g);
     griddep_wait();
     __shared__ float red[kNT / 32];
     __shared__ unsigned arrived;  // bit q: rank q's partial may be read
@@ -871,7 +901,7 @@ __global__ void __launch_bounds__(kNT)
         *reinterpret_cast<uint4*>(out + e0) =
             make_uint4(pack2(h[0], h[1]), pack2(h[2], h[3]), pack2(h[4], h[5]), pack2(h[6], h[7]));
     }
-    norm_vecs(x, nv, H, w, wdt, eps, normed + row * H, red);
+    norm_vecs<kPre>(x, nv, H, g, w, wdt, eps, normed + row * H, red);
 }
 
 // After the greedy pick of a forward over `rows` tokens: record the token and
@@ -1604,11 +1634,14 @@ int dec_forward(mrt_decoder d, int64_t S, const int32_t* ids, int64_t pos0, bool
     // out = fp16(a + the row-parallel output of `site`), normed = RMSNorm(out).
     auto add_norm = [&](const uint16_t* a, uint16_t* out, const void* gw, int gdt, int site, int call, int64_t row0,
                         int64_t rows) -> cudaError_t {
+        const bool pre = rows <= kPreloadRows;
         if (d->p2p)
-            return launch_pdl(ar_add_norm_kernel, dim3(static_cast<unsigned>(rows)), dim3(kNT), 0, s, d->pa[site], row0, a,
-                              out, H, gw, gdt, eps, d->normed, d->ar_epoch, call, ctx->d_err);
-        return launch_pdl(add_norm_kernel, dim3(static_cast<unsigned>(rows)), dim3(kNT), row_smem, s, a + row0 * H,
-                          d->p + row0 * H, out + row0 * H, H, gw, gdt, eps, d->normed + row0 * H);
+            return launch_pdl(pre ? ar_add_norm_kernel<true> : ar_add_norm_kernel<false>, dim3(static_cast<unsigned>(rows)),
+                              dim3(kNT), 0, s, d->pa[site], row0, a, out, H, gw, gdt, eps, d->normed, d->ar_epoch, call,
+                              ctx->d_err);
+        return launch_pdl(pre ? add_norm_kernel<true> : add_norm_kernel<false>, dim3(static_cast<unsigned>(rows)),
+                          dim3(kNT), row_smem, s, a + row0 * H, d->p + row0 * H, out + row0 * H, H, gw, gdt, eps,
+                          d->normed + row0 * H);
     };
     const int calls = static_cast<int>(2 * d->L);
     auto grid_for = [](int64_t n) {
@@ -1618,8 +1651,9 @@ int dec_forward(mrt_decoder d, int64_t S, const int32_t* ids, int64_t pos0, bool
     for (int64_t l = 0; l < d->L; ++l) {
         DecLayer& ly = d->layers[static_cast<size_t>(l)];
         if (l == 0) {
-            DEC_CU(launch_pdl(embed_norm_kernel, dim3(static_cast<unsigned>(S)), dim3(kNT), row_smem, s, d->embed, d->V, H,
-                              ids, d->state, d->x, ly.ln1, ly.ln1_dt, eps, d->normed, ctx->d_err),
+            DEC_CU(launch_pdl(S <= kPreloadRows ? embed_norm_kernel<true> : embed_norm_kernel<false>,
+                              dim3(static_cast<unsigned>(S)), dim3(kNT), row_smem, s, d->embed, d->V, H, ids, d->state,
+                              d->x, ly.ln1, ly.ln1_dt, eps, d->normed, ctx->d_err),
                    "embedding launch");
         } else {
             DEC_CU(add_norm(d->r, d->x, ly.ln1, ly.ln1_dt, 1, static_cast<int>(2 * (l - 1) + 1), 0, S), "add+rmsnorm launch");
