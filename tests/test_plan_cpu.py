@@ -1,0 +1,61 @@
+"""Host-side GEMM planner (mrt_gemm_plan, no device needed): every plan it
+returns must be one the tcgen05 launcher accepts.  The same conditions are
+checked by launch_tc_gemm before a launch; here they are swept over the
+reference's shapes, ragged sizes and smaller SM counts on the CPU."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from mruntime_b200 import capi
+from mruntime_b200 import workloads as W
+
+
+def _shapes():
+    ns = set()
+    for _, n, k in W.LAYER_05B:
+        ns.add((n, k))
+    for _, parts, k in W.SWEEP_7B:
+        ns.add((sum(parts), k))
+    ns |= {(4864, 896), (151936, 896), (152064, 3584), (64, 64), (131, 896), (3581, 3576), (20000, 2048)}
+    rng = np.random.default_rng(5)
+    for _ in range(20):
+        ns.add((int(rng.integers(8, 40000)), int(rng.integers(1, 2400)) * 8))
+    return sorted(ns)
+
+
+MS = (1, 2, 4, 7, 16, 17, 32, 33, 63, 64, 65, 100, 128, 129, 300, 512, 1000, 2048, 4096)
+
+
+@pytest.mark.parametrize("sms", [148, 132, 20])
+def test_every_plan_is_launchable(sms):
+    for N, K in _shapes():
+        num_kb = -(-K // 64)
+        for M in MS:
+            p = capi.gemm_plan(M, N, K, sms)
+            swap = M <= 64
+            assert p["kernel"] == ("tcgen05-swap" if swap else "tcgen05"), (M, N, K, p)
+            assert not p["cluster"]  # cluster plans need a device to check residency
+            if swap:
+                assert p["bn"] == (16 if M <= 16 else 32 if M <= 32 else 64), (M, p)
+                tiles = -(-N // 128)
+            else:
+                assert p["bn"] in (64, 128, 256), p
+                tiles = -(-M // 128) * -(-N // p["bn"])
+            full, splits, kb = p["full_tiles"], p["tail_splits"], p["kb_per"]
+            assert 0 <= full <= tiles, (M, N, K, p)
+            assert 1 <= p["grid"] <= sms, (M, N, K, p)
+            if full < tiles:
+                # Every K-slice owns at least one k-block and together they
+                # cover K (otherwise an accumulator would never be written).
+                assert splits >= 2 and kb >= 1, (M, N, K, p)
+                assert (splits - 1) * kb < num_kb <= splits * kb, (M, N, K, p)
+                assert p["grid"] <= full + (tiles - full) * splits, (M, N, K, p)
+            else:
+                assert splits == 1 and p["grid"] <= tiles, (M, N, K, p)
+
+
+def test_plan_rejects_bad_shapes():
+    for M, N, K in ((0, 8, 8), (1, 0, 8), (1, 8, 0), (-1, 8, 8)):
+        with pytest.raises(capi.MrtError):
+            capi.gemm_plan(M, N, K, 148)
