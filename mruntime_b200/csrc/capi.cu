@@ -746,6 +746,45 @@ extern "C" int mrt_gemm_f32(mrt_weight w, const void* x_dev, int64_t ldx, float*
     return gemm_dispatch(w, x_dev, ldx, y_dev, ldy, M, true, false, static_cast<cudaStream_t>(stream));
 }
 
+namespace mrt {
+
+// True when the host pointer is page-locked (cudaHostAlloc / cudaHostRegister),
+// so DMA can read or write it directly and copies can overlap.
+static bool host_pinned(const void* p) {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeHost;
+}
+
+static int io_pipeline_init(DevCtx* c) {
+    if (c->io_in != nullptr) return MRT_OK;
+    cudaError_t e = cudaStreamCreateWithFlags(&c->io_in, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->io_out, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->io_start, cudaEventDisableTiming);
+    for (int i = 0; i < DevCtx::kIoChunks && e == cudaSuccess; ++i) {
+        e = cudaEventCreateWithFlags(&c->io_h2d[i], cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->io_mm[i], cudaEventDisableTiming);
+    }
+    return e == cudaSuccess ? MRT_OK : cuda_error(e, "creating the host-copy streams");
+}
+
+// Rows per chunk of the host-buffer pipeline: whole 128-row tiles, chunks of
+// at least ~2 MB of copies each, at most kIoChunks chunks; 0 = one piece.
+static int64_t io_chunk_rows(int64_t M, int64_t N, int64_t K) {
+    if (M < 256) return 0;
+    const int64_t row_bytes = 2 * (N + K);
+    int64_t rows = std::max<int64_t>(128, ((2 << 20) / row_bytes + 127) / 128 * 128);
+    rows = std::max(rows, (M + DevCtx::kIoChunks - 1) / DevCtx::kIoChunks);
+    rows = std::max<int64_t>(rows, (M / 8 + 127) / 128 * 128);  // about 8 chunks for large M
+    rows = (rows + 127) / 128 * 128;
+    return rows >= M ? 0 : rows;
+}
+
+}  // namespace mrt
+
 extern "C" int mrt_gemm_host(mrt_weight w, const void* x_host, void* y_host, int64_t M, unsigned flags,
                              void* stream) {
     clear_error();
@@ -756,17 +795,63 @@ extern "C" int mrt_gemm_host(mrt_weight w, const void* x_host, void* y_host, int
     DevCtx* c = current_ctx();
     if (!c) return MRT_ERR_CUDA;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const bool bias = (flags & MRT_GEMM_BIAS) != 0;
     const size_t xb = static_cast<size_t>(M * w->k) * 2, yb = static_cast<size_t>(M * w->n) * 2;
     int rc = ensure_buffer(&c->io_x, &c->io_x_bytes, xb, "allocating input staging");
     if (rc == MRT_OK) rc = ensure_buffer(&c->io_y, &c->io_y_bytes, yb, "allocating output staging");
     if (rc != MRT_OK) return rc;
-    cudaError_t e = cudaMemcpyAsync(c->io_x, x_host, xb, cudaMemcpyHostToDevice, s);
-    if (e != cudaSuccess) return cuda_error(e, "copying x to the device");
-    rc = gemm_dispatch(w, c->io_x, w->k, c->io_y, w->n, M, false, (flags & MRT_GEMM_BIAS) != 0, s);
-    if (rc != MRT_OK) return rc;
-    e = cudaMemcpyAsync(y_host, c->io_y, yb, cudaMemcpyDeviceToHost, s);
-    if (e != cudaSuccess) return cuda_error(e, "copying y to the host");
-    e = cudaStreamSynchronize(s);
+    const int64_t chunk = io_chunk_rows(M, w->n, w->k);
+    cudaError_t e;
+    if (chunk == 0 || !host_pinned(x_host) || !host_pinned(y_host)) {
+        // One piece (small M, or pageable memory, which the driver stages
+        // through its own buffers and cannot overlap): copy in, multiply,
+        // copy out, wait.
+        e = cudaMemcpyAsync(c->io_x, x_host, xb, cudaMemcpyHostToDevice, s);
+        if (e != cudaSuccess) return cuda_error(e, "copying x to the device");
+        rc = gemm_dispatch(w, c->io_x, w->k, c->io_y, w->n, M, false, bias, s);
+        if (rc != MRT_OK) return rc;
+        e = cudaMemcpyAsync(y_host, c->io_y, yb, cudaMemcpyDeviceToHost, s);
+        if (e != cudaSuccess) return cuda_error(e, "copying y to the host");
+        e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) return cuda_error(e, "waiting for the host-buffer gemm");
+        return MRT_OK;
+    }
+    // Pinned buffers: rows in chunks through three streams, so chunk i+1's
+    // host-to-device copy, chunk i's product and chunk i-1's device-to-host
+    // copy run at the same time (PCIe carries both directions at once).  The
+    // rows are independent, so the result is the one-piece result bit for bit.
+    if ((rc = io_pipeline_init(c)) != MRT_OK) return rc;
+    const int64_t n_chunks = (M + chunk - 1) / chunk;
+    // The staging buffers may still be read or written by work the caller
+    // queued on s earlier: the side streams start after it.
+    if ((e = cudaEventRecord(c->io_start, s)) != cudaSuccess) return cuda_error(e, "recording the start");
+    if ((e = cudaStreamWaitEvent(c->io_in, c->io_start, 0)) != cudaSuccess ||
+        (e = cudaStreamWaitEvent(c->io_out, c->io_start, 0)) != cudaSuccess)
+        return cuda_error(e, "ordering the copy streams");
+    const char* x8 = static_cast<const char*>(x_host);
+    char* y8 = static_cast<char*>(y_host);
+    uint16_t* dx = static_cast<uint16_t*>(c->io_x);
+    uint16_t* dy = static_cast<uint16_t*>(c->io_y);
+    for (int64_t i = 0; i < n_chunks; ++i) {
+        const int slot = static_cast<int>(i % DevCtx::kIoChunks);
+        const int64_t r0 = i * chunk, rows = std::min(chunk, M - r0);
+        const size_t xo = static_cast<size_t>(r0 * w->k), yo = static_cast<size_t>(r0 * w->n);
+        e = cudaMemcpyAsync(dx + xo, x8 + xo * 2, static_cast<size_t>(rows * w->k) * 2, cudaMemcpyHostToDevice,
+                            c->io_in);
+        if (e == cudaSuccess) e = cudaEventRecord(c->io_h2d[slot], c->io_in);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(s, c->io_h2d[slot], 0);
+        if (e != cudaSuccess) return cuda_error(e, "queueing a chunk's copy to the device");
+        rc = gemm_dispatch(w, dx + xo, w->k, dy + yo, w->n, rows, false, bias, s);
+        if (rc != MRT_OK) return rc;
+        e = cudaEventRecord(c->io_mm[slot], s);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(c->io_out, c->io_mm[slot], 0);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(y8 + yo * 2, dy + yo, static_cast<size_t>(rows * w->n) * 2, cudaMemcpyDeviceToHost,
+                                c->io_out);
+        if (e != cudaSuccess) return cuda_error(e, "queueing a chunk's copy to the host");
+    }
+    e = cudaStreamSynchronize(c->io_out);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) return cuda_error(e, "waiting for the host-buffer gemm");
     return MRT_OK;
 }

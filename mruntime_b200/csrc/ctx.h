@@ -26,6 +26,15 @@ struct DevCtx {
     size_t io_y_bytes = 0;
     void* gu = nullptr;     // interleaved gate|up product of an unfused mrt_gemm_swiglu
     size_t gu_bytes = 0;
+    // Host-buffer pipeline (mrt_gemm_host): a copy-in and a copy-out stream
+    // beside the caller's, and events that hand each row chunk from one to
+    // the next (created on first use).
+    static constexpr int kIoChunks = 16;
+    cudaStream_t io_in = nullptr;
+    cudaStream_t io_out = nullptr;
+    cudaEvent_t io_start = nullptr;
+    cudaEvent_t io_h2d[kIoChunks] = {};
+    cudaEvent_t io_mm[kIoChunks] = {};
 };
 
 // Record an error for mrt_last_error_string() and return its code.

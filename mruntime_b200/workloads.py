@@ -112,6 +112,12 @@ DECODER_7B = {
 }
 
 
+# The 7B width (hidden 3584, 28/4 heads, intermediate 18944, vocabulary 152064)
+# with 4 layers: every projection and the lm_head at full 7B size, small
+# enough that the reference engine regenerates its golden tokens in minutes.
+DECODER_7B_4L = dict(DECODER_7B, num_hidden_layers=4)
+
+
 # A 2-layer, 256-wide model of the same structure (head_dim 64, 2 kv heads):
 # the quick pipeline check of the decoder against the reference engine.
 DECODER_TINY = {

@@ -32,3 +32,17 @@ def cuda_dev():
     torch.cuda.set_device(0)
     capi.init(0)
     return torch.device("cuda", 0)
+
+
+def pytest_sessionfinish(session, exitstatus):
+    """With MRT_ERR_LOG set, write every (case, device error, reference error)
+    the tolerance checks saw, and the largest ratio, to that file."""
+    path = os.environ.get("MRT_ERR_LOG")
+    if not path or "gpu_util" not in sys.modules:
+        return
+    rows = sys.modules["gpu_util"].ERR_RATIOS
+    with open(path, "w") as f:
+        for what, err, ref in rows:
+            f.write(f"{err / ref:.6f} {err:.6e} {ref:.6e} {what}\n")
+        if rows:
+            f.write(f"max ratio {max(e / r for _, e, r in rows):.6f} over {len(rows)} checks\n")

@@ -13,11 +13,16 @@ FP16, BF16, FP32 = capi.FP16, capi.BF16, capi.FP32
 
 # Tolerances of the linear-layer path: relative Frobenius error against FP64 at
 # most 1e-3, and never worse than the reference's own error against the same
-# ground truth.  "Never worse" allows 1% relative slack for the different FP32
-# summation order, which moves an occasional output across an FP16 rounding
-# midpoint in either direction.
+# ground truth.  "Never worse" allows 0.1% relative slack for the different
+# FP32 summation order, which moves an occasional output across an FP16
+# rounding midpoint in either direction (measured spread of err / ref_err over
+# every workload: about +-0.03%).
 REL_FROB_MAX = 1e-3
-REF_ERR_SLACK = 1.01
+REF_ERR_SLACK = 1.001
+
+# (what, err, ref_err) of every check_close with a reference error; written
+# out at the end of the session when MRT_ERR_LOG names a file.
+ERR_RATIOS: list[tuple[str, float, float]] = []
 
 
 def stream() -> int:
@@ -97,6 +102,7 @@ def check_close(got_f16: np.ndarray, truth: np.ndarray, ref_err: float | None = 
     err = rel_frob(got_f16, truth)
     assert err <= REL_FROB_MAX, f"{what}: rel Frobenius {err:.3e} > {REL_FROB_MAX}"
     if ref_err is not None:
+        ERR_RATIOS.append((what, err, ref_err))
         assert err <= ref_err * REF_ERR_SLACK, f"{what}: rel Frobenius {err:.4e} worse than reference {ref_err:.4e}"
     return err
 

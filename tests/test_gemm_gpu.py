@@ -294,6 +294,31 @@ def test_host_buffer_call_matches_device_call(cuda_dev):
         np.testing.assert_array_equal(y_host, y_dev)
 
 
+@pytest.mark.parametrize("M,N,K,bias", [(256, 640, 896, False), (300, 4608, 3584, True), (1000, 1000, 904, False),
+                                        (2048, 3584, 18944, False), (2049, 640, 896, True)])
+def test_pinned_host_call_pipelines_row_chunks(cuda_dev, M, N, K, bias):
+    """Pinned host buffers take the chunked path (copy in, multiply and copy
+    out of different row chunks overlap on three streams); the result is the
+    device call's, bit for bit, including a ragged last chunk and the bias."""
+    rng = np.random.default_rng(M + N)
+    x = rand_f16(rng, (M, K))
+    w = rand_w(rng, (N, K), BF16)
+    wt = upload(w, BF16)
+    if bias:
+        b = dev_u16(W.to_bf16_bits(rng.standard_normal(N, dtype=np.float32) * np.float32(0.02)))
+        wt.attach_bias(b.data_ptr(), BF16, True, stream())
+    xd = dev_u16(x)
+    y_dev = torch.empty((M, N), dtype=torch.int16, device="cuda")
+    capi.gemm(wt, xd.data_ptr(), K, y_dev.data_ptr(), N, M, bias, stream())
+    capi.sync(stream())
+    xh = torch.from_numpy(np.ascontiguousarray(x).view(np.int16)).pin_memory()
+    yh = torch.full((M, N), -1, dtype=torch.int16).pin_memory()
+    for _ in range(2):  # the second call reuses the staging buffers and events
+        capi.gemm_host(wt, xh.data_ptr(), yh.data_ptr(), M, bias, stream())
+        np.testing.assert_array_equal(yh.numpy().view(np.uint16), host_u16(y_dev))
+        yh.fill_(-1)
+
+
 # ------------------------------------------------------------------ argmax
 
 def test_argmax_edge_cases_match_reference(cuda_dev):

@@ -12,6 +12,8 @@ import numpy as np
 import pytest
 import torch
 
+from gpu_util import REF_ERR_SLACK  # noqa: E402
+
 pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
 
 WORLD = 2
@@ -124,11 +126,11 @@ def test_tensor_parallel_two_gpus(tmp_path):
     ref_q = O.gemm(x, O.FP16, wqkv, O.BF16, trans_b=True)
     truth_q = O.gemm_f64(x, wqkv, O.BF16)
     assert np.mean(q_tp == g["yq1"]) > 0.9
-    assert O.rel_frobenius(q_tp, truth_q) <= O.rel_frobenius(ref_q, truth_q) * 1.01
+    assert O.rel_frobenius(q_tp, truth_q) <= O.rel_frobenius(ref_q, truth_q) * REF_ERR_SLACK
     ref_o = O.gemm(x, O.FP16, wo, O.BF16, trans_b=True)
     truth_o = O.gemm_f64(x, wo, O.BF16)
     assert np.mean(g["yo"] == g["yo1"]) > 0.9
-    assert O.rel_frobenius(g["yo"], truth_o) <= O.rel_frobenius(ref_o, truth_o) * 1.01
+    assert O.rel_frobenius(g["yo"], truth_o) <= O.rel_frobenius(ref_o, truth_o) * REF_ERR_SLACK
     logits = O.gemm(x, O.FP16, vocab, O.FP16, trans_b=True)
     f = W.f16_bits_to_f32(logits)
     top2 = np.sort(f, axis=1)[:, -2:]
