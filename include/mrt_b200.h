@@ -246,6 +246,9 @@ int mrt_argmax_f16(const void* logits_dev, int64_t M, int64_t V, int64_t ld, int
  * rows of a 152064-entry vocabulary); larger calls fail with MRT_ERR_SHAPE.
  * The first call on a device resolves the buffer's device address (module
  * set-up inside the CUDA driver), so make it once before any stream capture.
+ * Outside capture every call looks the address up again (no allocation), so
+ * the entry point keeps working after cudaDeviceReset recreates the context;
+ * inside a capture it uses the address of the last call on that device.
  * All calls share the buffer, so calls that overlap on the GPU (different
  * streams, or the same stream from several threads without ordering) race;
  * every slot a call reads was written earlier in the same call, so nothing
@@ -415,6 +418,56 @@ int mrt_decoder_generate(mrt_decoder d, const int32_t* prompt, int64_t n_prompt,
 /* Releases the decoder.  For a tensor-parallel decoder this is collective:
  * every rank calls it (ranks unmap each other's exchange buffers first). */
 void mrt_decoder_free(mrt_decoder d);
+
+/* ---------------------------------------------------------------- checkpoints */
+
+/*
+ * Safetensors checkpoints read straight into device memory.  Replaces the
+ * reference's SafeTensorsFile (include/mruntime/safetensors.h:19-53,
+ * src/loader/safetensors.cpp:71-172): the file is mmap'ed and its JSON header
+ * parsed with the same rules (8-byte little-endian header length,
+ * "__metadata__" skipped, dtypes F16 / BF16 / F32, any other dtype an error),
+ * plus checks the reference leaves out (data offsets inside the file, byte
+ * count equal to dtype x shape).  Tensor bytes travel from the mapping to HBM
+ * through two pinned 16 MiB staging buffers, the host copy of one chunk
+ * overlapping the DMA of the previous one, instead of load_tensor_copy's
+ * host memcpy (safetensors.cpp:166-172).
+ */
+typedef struct mrt_safetensors_s* mrt_safetensors;
+
+/* Open and index a checkpoint (SafeTensorsFile::open, safetensors.cpp:71-131).
+ * Host-only: needs no device. */
+int mrt_safetensors_open(const char* path, mrt_safetensors* out);
+int mrt_safetensors_close(mrt_safetensors f);
+
+/* Tensor count, and the i-th name in sorted order (tensor_names(),
+ * safetensors.cpp:148-155); the name stays valid until close.  Host-only. */
+int mrt_safetensors_count(mrt_safetensors f, int64_t* n);
+int mrt_safetensors_name(mrt_safetensors f, int64_t i, const char** name);
+
+/* dtype (MRT_FP16/BF16/FP32), rank, shape (up to 8 entries written) and byte
+ * size of a tensor (tensor_info, safetensors.cpp:144-146); an unknown name is
+ * MRT_ERR_INVALID_ARG (the reference throws std::out_of_range).  Host-only. */
+int mrt_safetensors_info(mrt_safetensors f, const char* name, int* dtype, int* ndim, int64_t* shape,
+                         uint64_t* nbytes);
+
+/* The tensor's raw bytes into dst (host or device memory, at least its byte
+ * size): the device path stages through pinned memory and waits before
+ * returning (load_tensor_copy, safetensors.cpp:166-172, with the copy landing
+ * in HBM). */
+int mrt_safetensors_read(mrt_safetensors f, const char* name, void* dst, uint64_t dst_bytes, void* stream);
+
+/* mrt_weight_upload of a 2-D checkpoint tensor (with the same shard
+ * arguments), its bytes taken from the file through pinned staging: the
+ * weight is converted and tiled on the device, once. */
+int mrt_safetensors_upload_weight(mrt_safetensors f, const char* name, const int64_t* row_ranges, int64_t n_ranges,
+                                  int64_t k0, int64_t k1, void* stream, mrt_weight* out);
+
+/* Every tensor of the checkpoint the decoder takes (QwenModel::load_weights,
+ * src/models/qwen/qwen_model.cpp:336-353: other tensors are ignored, as
+ * there) through mrt_decoder_load with a device source; *n_loaded (may be
+ * NULL) counts them.  A tensor-parallel decoder keeps its shard of each. */
+int mrt_decoder_load_safetensors(mrt_decoder d, mrt_safetensors f, int64_t* n_loaded);
 
 #ifdef __cplusplus
 }

@@ -35,7 +35,7 @@ NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "-Xc
               "-Xcompiler", "-Wall", "-Xptxas", "-v"]
 
 KERNEL_SOURCES = ["capi.cu", "tp.cu", "gemm_tc.cu", "elementwise.cu", "general_gemm.cu", "ops.cu", "noalloc.cu",
-                  "decoder.cu", "decode_step.cu"]
+                  "decoder.cu", "decode_step.cu", "loader.cu"]
 
 
 def _nvcc() -> str:

@@ -95,6 +95,16 @@ _SIGS = {
     "mrt_decoder_load": (_int, [_vp, C.c_char_p, _vp, _int, _int, _i64, _i64]),
     "mrt_decoder_generate": (_int, [_vp, _vp, _i64, _i64, C.c_int32, _vp, C.POINTER(_i64), _vp, _vp]),
     "mrt_decoder_free": (None, [_vp]),
+    "mrt_safetensors_open": (_int, [C.c_char_p, C.POINTER(_vp)]),
+    "mrt_safetensors_close": (_int, [_vp]),
+    "mrt_safetensors_count": (_int, [_vp, C.POINTER(_i64)]),
+    "mrt_safetensors_name": (_int, [_vp, _i64, C.POINTER(C.c_char_p)]),
+    "mrt_safetensors_info": (_int, [_vp, C.c_char_p, C.POINTER(_int), C.POINTER(_int), C.POINTER(_i64),
+                                    C.POINTER(C.c_uint64)]),
+    "mrt_safetensors_read": (_int, [_vp, C.c_char_p, _vp, C.c_uint64, _vp]),
+    "mrt_safetensors_upload_weight": (_int, [_vp, C.c_char_p, C.POINTER(_i64), _i64, _i64, _i64, _vp,
+                                             C.POINTER(_vp)]),
+    "mrt_decoder_load_safetensors": (_int, [_vp, _vp, C.POINTER(_i64)]),
 }
 
 
@@ -166,6 +176,16 @@ class Weight:
         n, k = C.c_int64(), C.c_int64()
         call("mrt_weight_shape", h, C.byref(n), C.byref(k))
         self.n, self.k = n.value, k.value
+
+    @classmethod
+    def adopt(cls, h: C.c_void_p) -> "Weight":
+        """Wrap a handle another entry point returned (e.g. a checkpoint upload)."""
+        self = cls.__new__(cls)
+        self.h = h
+        n, k = C.c_int64(), C.c_int64()
+        call("mrt_weight_shape", h, C.byref(n), C.byref(k))
+        self.n, self.k = n.value, k.value
+        return self
 
     def attach_bias(self, src_ptr: int, src_dtype: int, src_on_device: bool, stream: int | None = None):
         call("mrt_weight_attach_bias", self.h, src_ptr, src_dtype, int(src_on_device), stream)
@@ -293,6 +313,59 @@ class TensorParallel:
             self.h = None
 
 
+class SafeTensors:
+    """A checkpoint opened by mrt_safetensors_open (mmap + header index; the
+    reference's SafeTensorsFile).  Host-only until a read or upload."""
+
+    def __init__(self, path: str):
+        h = C.c_void_p()
+        call("mrt_safetensors_open", os.fsencode(path), C.byref(h))
+        self.h = h
+
+    def names(self) -> list[str]:
+        n = C.c_int64()
+        call("mrt_safetensors_count", self.h, C.byref(n))
+        out = []
+        for i in range(n.value):
+            p = C.c_char_p()
+            call("mrt_safetensors_name", self.h, i, C.byref(p))
+            out.append(p.value.decode())
+        return out
+
+    def info(self, name: str) -> tuple[int, tuple[int, ...], int]:
+        """(dtype, shape, byte size) of a tensor."""
+        dt, nd, nb = C.c_int(), C.c_int(), C.c_uint64()
+        shape = (C.c_int64 * 8)()
+        call("mrt_safetensors_info", self.h, name.encode(), C.byref(dt), C.byref(nd), shape, C.byref(nb))
+        return dt.value, tuple(shape[i] for i in range(nd.value)), nb.value
+
+    def read(self, name: str, dst_ptr: int, dst_bytes: int, stream: int | None = None) -> None:
+        call("mrt_safetensors_read", self.h, name.encode(), dst_ptr, dst_bytes, stream)
+
+    def upload_weight(self, name: str, row_ranges=None, k_range=None, stream: int | None = None) -> "Weight":
+        _, shape, _ = self.info(name)
+        rr, n_ranges = None, 0
+        if row_ranges:
+            flat = [v for pair in row_ranges for v in pair]
+            rr = (C.c_int64 * len(flat))(*flat)
+            n_ranges = len(row_ranges)
+        k0, k1 = k_range if k_range is not None else (0, shape[1])
+        h = C.c_void_p()
+        call("mrt_safetensors_upload_weight", self.h, name.encode(), rr, n_ranges, k0, k1, stream, C.byref(h))
+        return Weight.adopt(h)
+
+    def close(self):
+        if self.h:
+            lib().mrt_safetensors_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class DecoderConfig(C.Structure):
     """mrt_decoder_config (the reference's QwenConfig fields plus the KV capacity)."""
 
@@ -322,6 +395,12 @@ class Decoder:
         else:
             call("mrt_decoder_create_tp", C.byref(cfg), tp.h, C.byref(h))
         self.h = h
+
+    def load_safetensors(self, f: SafeTensors) -> int:
+        """Every tensor of the checkpoint this decoder takes; returns how many."""
+        n = C.c_int64()
+        call("mrt_decoder_load_safetensors", self.h, f.h, C.byref(n))
+        return n.value
 
     def load(self, name: str, ptr: int, dtype: int, on_device: bool, shape) -> None:
         rows = int(shape[0])

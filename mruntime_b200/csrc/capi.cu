@@ -818,8 +818,11 @@ extern "C" int mrt_gemm_host(mrt_weight w, const void* x_host, void* y_host, int
     }
     // Pinned buffers: rows in chunks through three streams, so chunk i+1's
     // host-to-device copy, chunk i's product and chunk i-1's device-to-host
-    // copy run at the same time (PCIe carries both directions at once).  The
-    // rows are independent, so the result is the one-piece result bit for bit.
+    // copy run at the same time (PCIe carries both directions at once).  Each
+    // chunk is its own GEMM over its rows, so its plan -- and with it the
+    // order of a K-split sum -- may differ from a one-piece call's: results
+    // meet the same error bars, and a given M and buffer kind always takes
+    // the same chunks, so repeated calls give identical bits.
     if ((rc = io_pipeline_init(c)) != MRT_OK) return rc;
     const int64_t n_chunks = (M + chunk - 1) / chunk;
     // The staging buffers may still be read or written by work the caller

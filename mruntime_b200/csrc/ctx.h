@@ -82,6 +82,9 @@ const uint16_t* silu_lut_for_device(int device);
 cudaError_t launch_swiglu_pairs(const uint16_t* gu, int64_t ld_gu, int64_t I, int64_t M, const uint16_t* lut,
                                 uint16_t* act, int64_t ld_act, cudaStream_t s);
 
+// Number of decoder layers of a decoder handle (decoder.cu).
+int64_t decoder_layer_count(mrt_decoder d);
+
 }  // namespace mrt
 
 // Opaque handle types of the public header.

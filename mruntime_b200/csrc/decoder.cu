@@ -1161,6 +1161,10 @@ int dec_create(const mrt_decoder_config* cfg, mrt_tp tp, mrt_decoder* out) {
 
 }  // namespace
 
+namespace mrt {
+int64_t decoder_layer_count(mrt_decoder d) { return d ? d->L : 0; }
+}  // namespace mrt
+
 extern "C" int mrt_decoder_create(const mrt_decoder_config* cfg, mrt_decoder* out) {
     return dec_create(cfg, nullptr, out);
 }

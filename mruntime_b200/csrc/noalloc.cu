@@ -31,11 +31,21 @@ static __device__ __align__(256) unsigned char g_argmax_scratch[kNoAllocBytes];
 std::mutex g_addr_mu;
 void* g_addr[64] = {};
 
-// Device address of g_argmax_scratch on the current device, resolved once per
-// device with that device current.
-int scratch_address(int device, void** out) {
+// Device address of g_argmax_scratch on the current device, looked up with
+// that device current.  Outside stream capture the lookup runs on every call
+// (after the first it only reads the loaded module's symbol table and
+// allocates nothing), so a context torn down by cudaDeviceReset and created
+// again gets the new address; during capture the address of the last lookup
+// on this device is used, which is why the first call must come before any
+// capture.
+int scratch_address(int device, cudaStream_t stream, void** out) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess) {
+        cudaGetLastError();
+        cs = cudaStreamCaptureStatusActive;  // unknown: do not touch the module
+    }
     std::lock_guard<std::mutex> lk(g_addr_mu);
-    if (g_addr[device] == nullptr) {
+    if (cs == cudaStreamCaptureStatusNone || g_addr[device] == nullptr) {
         void* p = nullptr;
         cudaError_t e = cudaGetSymbolAddress(&p, g_argmax_scratch);
         if (e != cudaSuccess) return cuda_error(e, "cudaGetSymbolAddress of the static argmax buffer");
@@ -68,7 +78,7 @@ extern "C" int mrt_argmax_f16_noalloc(const void* logits_dev, int64_t M, int64_t
     if (e != cudaSuccess) return cuda_error(e, "cudaGetDevice");
     if (device < 0 || device >= 64) return set_error(MRT_ERR_INVALID_ARG, "device index out of range");
     void* scratch = nullptr;
-    int rc = scratch_address(device, &scratch);
+    int rc = scratch_address(device, static_cast<cudaStream_t>(stream), &scratch);
     if (rc != MRT_OK) return rc;
     e = launch_argmax(static_cast<const uint16_t*>(logits_dev), M, V, ld, index_base, idx_dev, val_dev, scratch,
                       static_cast<cudaStream_t>(stream));

@@ -298,25 +298,40 @@ def test_host_buffer_call_matches_device_call(cuda_dev):
                                         (2048, 3584, 18944, False), (2049, 640, 896, True)])
 def test_pinned_host_call_pipelines_row_chunks(cuda_dev, M, N, K, bias):
     """Pinned host buffers take the chunked path (copy in, multiply and copy
-    out of different row chunks overlap on three streams); the result is the
-    device call's, bit for bit, including a ragged last chunk and the bias."""
+    out of different row chunks overlap on three streams), including a ragged
+    last chunk and the bias.  Each chunk is its own GEMM, whose plan (and so
+    its K-split summation order) may differ from a one-piece call's: the
+    result meets the same error bars as the device call, agrees with it on
+    the large majority of outputs, and repeats bit for bit."""
     rng = np.random.default_rng(M + N)
     x = rand_f16(rng, (M, K))
     w = rand_w(rng, (N, K), BF16)
     wt = upload(w, BF16)
+    bvec = None
     if bias:
-        b = dev_u16(W.to_bf16_bits(rng.standard_normal(N, dtype=np.float32) * np.float32(0.02)))
+        bvec = W.to_bf16_bits(rng.standard_normal(N, dtype=np.float32) * np.float32(0.02))
+        b = dev_u16(bvec)
         wt.attach_bias(b.data_ptr(), BF16, True, stream())
     xd = dev_u16(x)
     y_dev = torch.empty((M, N), dtype=torch.int16, device="cuda")
     capi.gemm(wt, xd.data_ptr(), K, y_dev.data_ptr(), N, M, bias, stream())
     capi.sync(stream())
+    yd = host_u16(y_dev)
     xh = torch.from_numpy(np.ascontiguousarray(x).view(np.int16)).pin_memory()
     yh = torch.full((M, N), -1, dtype=torch.int16).pin_memory()
-    for _ in range(2):  # the second call reuses the staging buffers and events
-        capi.gemm_host(wt, xh.data_ptr(), yh.data_ptr(), M, bias, stream())
-        np.testing.assert_array_equal(yh.numpy().view(np.uint16), host_u16(y_dev))
-        yh.fill_(-1)
+    capi.gemm_host(wt, xh.data_ptr(), yh.data_ptr(), M, bias, stream())
+    first = yh.numpy().view(np.uint16).copy()
+    yh.fill_(-1)
+    capi.gemm_host(wt, xh.data_ptr(), yh.data_ptr(), M, bias, stream())  # reuses staging buffers and events
+    np.testing.assert_array_equal(yh.numpy().view(np.uint16), first)
+    rows = np.unique(np.linspace(0, M - 1, 24).astype(np.int64))
+    truth = f64_truth(x[rows], w, BF16, bias=bvec)
+    pre = f64_truth(x[rows], w, BF16) if bias else None
+    ad = abs_dot(x[rows], w, BF16)
+    dev_err = check_close(yd[rows], truth, None, "device call", absdot=ad, K=K, pre_round=pre)
+    host_err = check_close(first[rows], truth, None, "pinned host call", absdot=ad, K=K, pre_round=pre)
+    assert host_err <= dev_err * 1.01, f"host call error {host_err:.4e} vs device call {dev_err:.4e}"
+    assert same_fraction(first, yd) > 0.9
 
 
 # ------------------------------------------------------------------ argmax
