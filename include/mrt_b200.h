@@ -203,6 +203,14 @@ int mrt_gemm_swiglu(mrt_weight w, const void* x_dev, int64_t ldx, void* act_dev,
 int mrt_gemm_f32(mrt_weight w, const void* x_dev, int64_t ldx, float* y_dev, int64_t ldy,
                  int64_t M, void* stream);
 
+/* mrt_gemm followed by the residual add the reference applies to the o and
+ * down projections' outputs (src/models/qwen/qwen_model.cpp:316 and 324, the
+ * add op of src/core/cpu_backend.cpp:430-455), in the GEMM's epilogue:
+ * y[m][n] = fp16(res[m][n] + fp16(x.W_n (+ bias))), res_dev FP16 [M, N] with
+ * row stride ldr >= N.  y_dev may be res_dev (in place).  flags as mrt_gemm. */
+int mrt_gemm_residual(mrt_weight w, const void* x_dev, int64_t ldx, const void* res_dev, int64_t ldr,
+                      void* y_dev, int64_t ldy, int64_t M, unsigned flags, void* stream);
+
 /* mrt_gemm on host buffers, the reference's own calling convention (its
  * Tensors live in host memory): copies x_host to the device, runs the
  * product, copies y back and waits.  x is [M, K] and y [M, N], both dense. */
@@ -258,9 +266,13 @@ int mrt_argmax_f16_noalloc(const void* logits_dev, int64_t M, int64_t V, int64_t
                            int64_t* idx_dev, float* val_dev, void* stream);
 
 /* lm_head and greedy pick in one call: logits_dev[M, N] = x * W^T (FP16),
- * then mrt_argmax_f16 on every row (src/models/qwen/qwen_model.cpp:374 followed
- * by src/engine/inference_engine.cpp:84-95).  index_base offsets the indices
- * of a vocabulary shard. */
+ * then the greedy pick of every row (src/models/qwen/qwen_model.cpp:374
+ * followed by src/engine/inference_engine.cpp:84-95).  index_base offsets the
+ * indices of a vocabulary shard.  For M <= 64 the GEMM's epilogue reduces each
+ * 32 vocabulary rows to their best (value, index) per token and one small
+ * kernel picks among those, so logits_dev may be NULL (the logits are then
+ * never written); larger M, or a NULL logits_dev there, computes the logits
+ * (in per-device scratch when NULL) and runs mrt_argmax_f16's two passes. */
 int mrt_lm_head_argmax(mrt_weight w, const void* x_dev, int64_t ldx, int64_t M, void* logits_dev,
                        int64_t index_base, int64_t* idx_dev, float* val_dev, void* stream);
 

@@ -65,6 +65,7 @@ _SIGS = {
     "mrt_gemm": (_int, [_vp, _vp, _i64, _vp, _i64, _i64, _u32, _vp]),
     "mrt_gemm_f32": (_int, [_vp, _vp, _i64, _vp, _i64, _i64, _vp]),
     "mrt_gemm_swiglu": (_int, [_vp, _vp, _i64, _vp, _i64, _i64, _vp]),
+    "mrt_gemm_residual": (_int, [_vp, _vp, _i64, _vp, _i64, _vp, _i64, _i64, _u32, _vp]),
     "mrt_gemm_plan": (_int, [_i64, _i64, _i64, _int] + [C.POINTER(_int)] * 6),
     "mrt_gemm_host": (_int, [_vp, _vp, _vp, _i64, _u32, _vp]),
     "mrt_gemm_general": (_int, [_vp, _int, _i64, _i64, _vp, _int, _i64, _i64, _vp, _int, C.c_float, C.c_float,
@@ -243,6 +244,12 @@ def gemm_swiglu(w: Weight, x_ptr: int, ldx: int, act_ptr: int, ld_act: int, M: i
     call("mrt_gemm_swiglu", w.h, x_ptr, ldx, act_ptr, ld_act, M, stream)
 
 
+def gemm_residual(w: Weight, x_ptr: int, ldx: int, res_ptr: int, ldr: int, y_ptr: int, ldy: int, M: int,
+                  bias: bool = False, stream: int | None = None) -> None:
+    """y = fp16(res + fp16(x W^T (+ bias))); y may be res."""
+    call("mrt_gemm_residual", w.h, x_ptr, ldx, res_ptr, ldr, y_ptr, ldy, M, GEMM_BIAS if bias else 0, stream)
+
+
 def gemm_host(w: Weight, x_host_ptr: int, y_host_ptr: int, M: int, bias: bool = False,
               stream: int | None = None) -> None:
     call("mrt_gemm_host", w.h, x_host_ptr, y_host_ptr, M, GEMM_BIAS if bias else 0, stream)
@@ -259,8 +266,9 @@ def argmax_f16(logits_ptr: int, M: int, V: int, ld: int, index_base: int, idx_pt
     call("mrt_argmax_f16", logits_ptr, M, V, ld, index_base, idx_ptr, val_ptr, stream)
 
 
-def lm_head_argmax(w: Weight, x_ptr: int, ldx: int, M: int, logits_ptr: int, index_base: int, idx_ptr: int,
+def lm_head_argmax(w: Weight, x_ptr: int, ldx: int, M: int, logits_ptr: int | None, index_base: int, idx_ptr: int,
                    val_ptr: int | None, stream: int | None = None) -> None:
+    """Logits (unless logits_ptr is None) and the greedy pick of every row."""
     call("mrt_lm_head_argmax", w.h, x_ptr, ldx, M, logits_ptr, index_base, idx_ptr, val_ptr, stream)
 
 

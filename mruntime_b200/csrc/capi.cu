@@ -489,34 +489,78 @@ static double unit_us(int bn, int64_t kb, int64_t active, int sms, int64_t x_row
 
 // Plan for few tokens (M <= 64), swap mode: the weight is the 128-row MMA
 // operand, so a tile is 128 weight rows x all tokens and the work is streaming
-// W.  Units are costed by their weight bytes at the SM's share of HBM plus a
-// small fixed cost; K is split until about every SM streams.
+// W.  A call's time is modelled as a fixed latency (launch, activation load,
+// epilogue), plus the K-split finish when tiles are split, plus a ramp that
+// grows with the bytes of the whole call and the bytes one CTA streams (each
+// CTA's ring of bulk copies bounds its own rate).  Swap-mode CTAs use ~108 KB
+// of shared memory, so two fit on an SM: plans may launch up to 2 x SMs CTAs.
+// The constants were fitted to graph-replayed chains of decode GEMMs on B200
+// (4864x896, 896x896 and the Qwen2.5-7B projections at 1 token, over every
+// split count and grid size).  Units never exceed kSegMinKb k-blocks, so the
+// tensor cores' accumulation stays as accurate as the reference's loop.
 static TcPlan plan_swap(int64_t M, int64_t N, int64_t K, int sms) {
     const int bn = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
     const int64_t tiles = (N + 127) / 128;
     const int64_t num_kb = (K + 63) / 64;
-    auto unit = [&](int64_t kb, int64_t active) {
-        const double share = std::min(50e9, 6.5e12 / static_cast<double>(std::max<int64_t>(1, std::min<int64_t>(active, sms))));
-        return (128.0 * 128.0 * kb + bn * 128.0 * kb * 0.5) / share * 1e6 + 0.3;
+    const bool long_k = num_kb > kSegMinKb;
+    // Bytes one k-block of a unit streams: the 128 x 64 weight tile, plus half
+    // the token rows' activations (those mostly hit L2).
+    const double kb_bytes = 128.0 * 64.0 * 2.0 + 0.5 * bn * 64.0 * 2.0;
+    const double ramp_all = static_cast<double>(tiles) * num_kb * kb_bytes / 10.0e12 * 1e6;
+    const int64_t max_grid = 2LL * sms;
+    // us for a plan whose busiest CTA streams `cta_kb` k-blocks, with `split`
+    // when some tiles are K-split
+    auto cost = [&](int64_t cta_kb, bool split) {
+        double t = 3.25 + ramp_all + static_cast<double>(cta_kb) * kb_bytes / 80.0e9 * 1e6;
+        if (split) t += 1.0 + 0.1 * static_cast<double>(std::min<int64_t>(M, bn));
+        return t;
     };
-    TcPlan best{bn, static_cast<int>(std::min<int64_t>(tiles, sms)), static_cast<int>(tiles), 1, 0};
-    double best_cost = static_cast<double>((tiles + sms - 1) / sms) * unit(num_kb, tiles);
-    const int64_t full = (tiles / sms) * sms;
-    const int64_t n_tail = tiles - full;
-    if (n_tail == 0) return best;
+    auto waves = [](int64_t units, int64_t grid) { return (units + grid - 1) / grid; };
+    TcPlan best{bn, 1, static_cast<int>(tiles), 1, 0};
+    double best_cost = 1e300;
+    auto consider = [&](double c, const TcPlan& p) {
+        if (c < best_cost - 1e-9) {
+            best_cost = c;
+            best = p;
+        }
+    };
+    if (!long_k) {
+        // every tile over the whole K, one or two CTAs per SM
+        for (int64_t cap : {static_cast<int64_t>(sms), max_grid}) {
+            const int64_t grid = std::min(tiles, cap);
+            consider(cost(waves(tiles, grid) * num_kb, false),
+                     TcPlan{bn, static_cast<int>(grid), static_cast<int>(tiles), 1, 0});
+        }
+        // whole waves of one tile per SM over K, the last partial wave split
+        const int64_t full = (tiles / sms) * sms;
+        const int64_t n_tail = tiles - full;
+        if (full > 0 && n_tail > 0) {
+            for (int64_t s = 2; s <= 32 && s <= num_kb; ++s) {
+                const int64_t kb_per = (num_kb + s - 1) / s;
+                const int64_t splits = (num_kb + kb_per - 1) / kb_per;
+                if (splits < 2) continue;
+                const int64_t tail_units = n_tail * splits;
+                consider(cost(full / sms * num_kb + waves(tail_units, sms) * kb_per, true),
+                         TcPlan{bn, sms, static_cast<int>(full), static_cast<int>(splits), static_cast<int>(kb_per)});
+            }
+        }
+    }
+    // every tile split along K
     for (int64_t s = 2; s <= 32 && s <= num_kb; ++s) {
         const int64_t kb_per = (num_kb + s - 1) / s;
         const int64_t splits = (num_kb + kb_per - 1) / kb_per;
-        if (splits < 2) continue;
-        const int64_t tail_units = n_tail * splits;
-        double cost = static_cast<double>(full / sms) * unit(num_kb, sms);
-        cost += static_cast<double>((tail_units + sms - 1) / sms) * unit(kb_per, tail_units);
-        cost += static_cast<double>(n_tail) * 128.0 * bn * 4.0 * (splits + 1.0) / 6.0e12 * 1e6 + 3.0;
-        if (cost < best_cost - 1e-9) {
-            best_cost = cost;
-            best = TcPlan{bn, static_cast<int>(std::min<int64_t>(full + tail_units, sms)), static_cast<int>(full),
-                          static_cast<int>(splits), static_cast<int>(kb_per)};
-        }
+        if (splits < 2 || kb_per > kSegMinKb) continue;
+        const int64_t units = tiles * splits;
+        const int64_t grid = std::min(units, max_grid);
+        consider(cost(waves(units, grid) * kb_per, true),
+                 TcPlan{bn, static_cast<int>(grid), 0, static_cast<int>(splits), static_cast<int>(kb_per)});
+    }
+    if (best_cost > 1e299) {
+        // K beyond 32 x kSegMinKb k-blocks: the most slices the finish sums
+        const int64_t kb_per = std::max<int64_t>(1, (num_kb + 31) / 32);
+        const int64_t splits = (num_kb + kb_per - 1) / kb_per;
+        best = TcPlan{bn, static_cast<int>(std::min(tiles * splits, max_grid)), 0, static_cast<int>(splits),
+                      static_cast<int>(kb_per)};
     }
     return best;
 }
@@ -593,17 +637,29 @@ static const CUtensorMap* weight_tmap(mrt_weight w, int bn) {
     return &w->tmap[slot];
 }
 
-// Shared body of mrt_gemm / mrt_gemm_f32.
+// Optional epilogue extras of one GEMM call.
+struct GemmEpi {
+    const uint16_t* residual = nullptr;  // y = fp16(residual + fp16(acc)), row stride ldr
+    int64_t ldr = 0;
+    float* am_val = nullptr;             // greedy-pick partials (swap mode; see TcGemmArgs)
+    int64_t* am_idx = nullptr;
+};
+
+// Shared body of mrt_gemm / mrt_gemm_f32 / mrt_gemm_residual and the fused
+// lm_head.  With greedy-pick partials requested, launches nothing and sets
+// *fused = false when the call cannot produce them (the caller falls back).
 static int gemm_dispatch(mrt_weight w, const void* x, int64_t ldx, void* y, int64_t ldy, int64_t M,
                          bool out_f32, bool use_bias, cudaStream_t s, const uint16_t* swiglu_lut = nullptr,
-                         bool* fused = nullptr) {
+                         bool* fused = nullptr, const GemmEpi& epi = GemmEpi{}) {
     if (fused) *fused = false;
     if (w == nullptr) return set_error(MRT_ERR_INVALID_ARG, "NULL weight");
     if (M < 0) return set_error(MRT_ERR_SHAPE, "M must be >= 0");
     if (M == 0) return MRT_OK;
-    if (x == nullptr || y == nullptr) return set_error(MRT_ERR_INVALID_ARG, "NULL x or y");
-    if (ldx < w->k || ldy < (swiglu_lut ? w->n / 2 : w->n))
+    if (x == nullptr || (y == nullptr && epi.am_val == nullptr)) return set_error(MRT_ERR_INVALID_ARG, "NULL x or y");
+    if (ldx < w->k || (y != nullptr && ldy < (swiglu_lut ? w->n / 2 : w->n)))
         return set_error(MRT_ERR_SHAPE, "ldx must be >= K and ldy >= N");
+    if (epi.residual != nullptr && (out_f32 || swiglu_lut != nullptr || epi.ldr < w->n))
+        return set_error(MRT_ERR_SHAPE, "the residual epilogue needs an FP16 output and ldr >= N");
     if (use_bias && w->bias == nullptr) return set_error(MRT_ERR_INVALID_ARG, "MRT_GEMM_BIAS without an attached bias");
     if (M > (1LL << 31) - 1 || w->n > (1LL << 31) - 1 || w->k > (1LL << 31) - 1)
         return set_error(MRT_ERR_SHAPE, "dimensions must fit in 31 bits");
@@ -615,6 +671,7 @@ static int gemm_dispatch(mrt_weight w, const void* x, int64_t ldx, void* y, int6
     const bool fast = (w->k % 8 == 0) && (ldx % 8 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
     cudaError_t e;
     if (swiglu_lut != nullptr && (!fast || (w->n & 1) != 0)) return MRT_OK;  // not fused: the caller falls back
+    if (epi.am_val != nullptr && (!fast || M > 64 || out_f32 || swiglu_lut != nullptr)) return MRT_OK;  // not fused
     if (!fast) {
         GeneralGemmArgs g{};
         g.a = x; g.a_dtype = MRT_FP16; g.a_cols0 = ldx;
@@ -623,6 +680,7 @@ static int gemm_dispatch(mrt_weight w, const void* x, int64_t ldx, void* y, int6
         g.M = M; g.N = w->n; g.K = w->k; g.alpha = 1.0f; g.beta = 0.0f;
         g.trans_a = 0; g.trans_b = 1; g.bias = bias;
         g.b_k_tiles = w->tiled ? w->k_tiles : 0;
+        g.residual = epi.residual; g.ldr = epi.ldr;
         e = launch_general_gemm(g, s);
         return e == cudaSuccess ? MRT_OK : cuda_error(e, "general gemm launch");
     }
@@ -651,9 +709,12 @@ static int gemm_dispatch(mrt_weight w, const void* x, int64_t ldx, void* y, int6
     a.bn = p.bn; a.grid = p.grid; a.full_tiles = p.full; a.tail_splits = p.splits; a.kb_per = p.kb_per;
     a.y = y; a.ldy = ldy; a.out_f32 = out_f32 ? 1 : 0; a.bias = bias; a.err_flag = c->d_err;
     a.swiglu_lut = swiglu_lut;
+    a.residual = epi.residual; a.ldr = epi.ldr;
+    a.am_val = epi.am_val; a.am_idx = epi.am_idx;
+    a.am_chunks = static_cast<int>(4 * ((w->n + 127) / 128));
     const int64_t tiles = tc_gemm_tiles(a);
     const int64_t n_tail = tiles - p.full;
-    if (use_cluster(swap, p, tiles)) a.cluster_k = p.splits;
+    if (use_cluster(swap, p, tiles) && epi.am_val == nullptr) a.cluster_k = p.splits;
     if (n_tail > 0 && a.cluster_k == 0) {
         const size_t need = static_cast<size_t>(n_tail) * p.splits * 128 * p.bn * sizeof(float);
         rc = ensure_buffer(&c->ws, &c->ws_bytes, need, "allocating split-K scratch");
@@ -672,7 +733,7 @@ static int gemm_dispatch(mrt_weight w, const void* x, int64_t ldx, void* y, int6
     }
     e = launch_tc_gemm(a, tx, *tw, s);
     if (e != cudaSuccess) return cuda_error(e, "tcgen05 gemm launch");
-    if (fused) *fused = swiglu_lut != nullptr;
+    if (fused) *fused = swiglu_lut != nullptr || epi.am_val != nullptr;
     if (n_tail > 0 && !swap) {
         e = launch_reduce_tail(a, s);
         if (e != cudaSuccess) return cuda_error(e, "split-K reduction launch");
@@ -905,9 +966,54 @@ extern "C" int mrt_argmax_f16(const void* logits_dev, int64_t M, int64_t V, int6
 
 extern "C" int mrt_lm_head_argmax(mrt_weight w, const void* x_dev, int64_t ldx, int64_t M, void* logits_dev,
                                   int64_t index_base, int64_t* idx_dev, float* val_dev, void* stream) {
-    int rc = mrt_gemm(w, x_dev, ldx, logits_dev, w ? w->n : 0, M, 0, stream);
+    clear_error();
+    if (w == nullptr) return set_error(MRT_ERR_INVALID_ARG, "NULL weight");
+    if (M < 0) return set_error(MRT_ERR_SHAPE, "M must be >= 0");
+    if (M == 0) return MRT_OK;
+    if (M > 65535) return set_error(MRT_ERR_SHAPE, "at most 65535 rows per call");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    DevCtx* c = current_ctx();
+    if (!c) return MRT_ERR_CUDA;
+    // Decode (M <= 64): the GEMM's epilogue leaves the best (value, index) of
+    // every 32 vocabulary rows per token, so the logits need not be written
+    // (logits_dev may be NULL) nor read back; one small kernel picks the row's
+    // best of those partials.
+    if (M <= 64) {
+        const int64_t chunks = 4 * ((w->n + 127) / 128);
+        const size_t bytes = static_cast<size_t>(M * chunks) * (sizeof(float) + sizeof(int64_t));
+        int rc = ensure_buffer(&c->am, &c->am_bytes, bytes, "allocating greedy-pick partials");
+        if (rc != MRT_OK) return rc;
+        GemmEpi epi;
+        epi.am_idx = static_cast<int64_t*>(c->am);
+        epi.am_val = reinterpret_cast<float*>(epi.am_idx + M * chunks);
+        bool fused = false;
+        rc = gemm_dispatch(w, x_dev, ldx, logits_dev, w->n, M, false, false, s, nullptr, &fused, epi);
+        if (rc != MRT_OK) return rc;
+        if (fused) {
+            const cudaError_t e = launch_argmax_final(epi.am_val, epi.am_idx, M, chunks, index_base, idx_dev, val_dev, s);
+            return e == cudaSuccess ? MRT_OK : cuda_error(e, "greedy pick launch");
+        }
+    }
+    if (logits_dev == nullptr) {
+        // the unfused path needs the logits: keep them in per-device scratch
+        int rc = ensure_buffer(&c->gu, &c->gu_bytes, static_cast<size_t>(M * w->n) * 2, "allocating logits scratch");
+        if (rc != MRT_OK) return rc;
+        logits_dev = c->gu;
+    }
+    int rc = mrt_gemm(w, x_dev, ldx, logits_dev, w->n, M, 0, stream);
     if (rc != MRT_OK) return rc;
     return mrt_argmax_f16(logits_dev, M, w->n, w->n, index_base, idx_dev, val_dev, stream);
+}
+
+extern "C" int mrt_gemm_residual(mrt_weight w, const void* x_dev, int64_t ldx, const void* res_dev, int64_t ldr,
+                                 void* y_dev, int64_t ldy, int64_t M, unsigned flags, void* stream) {
+    clear_error();
+    if (res_dev == nullptr) return set_error(MRT_ERR_INVALID_ARG, "NULL residual");
+    GemmEpi epi;
+    epi.residual = static_cast<const uint16_t*>(res_dev);
+    epi.ldr = ldr;
+    return gemm_dispatch(w, x_dev, ldx, y_dev, ldy, M, false, (flags & MRT_GEMM_BIAS) != 0,
+                         static_cast<cudaStream_t>(stream), nullptr, nullptr, epi);
 }
 
 extern "C" int mrt_convert(const void* src_dev, int src_dtype, void* dst_dev, int dst_dtype, int64_t n,

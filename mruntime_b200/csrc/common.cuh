@@ -78,6 +78,48 @@ __device__ __forceinline__ uint16_t round_out(float acc, const uint16_t* bias, i
     return h;
 }
 
+// Residual add after the output rounding, the reference's add op
+// (cpu_backend.cpp:430-455, called at qwen_model.cpp:316 and 324): both FP16
+// operands widened, one FP32 add, rounded to FP16.  `res` null: h unchanged.
+__device__ __forceinline__ uint16_t add_f16(uint16_t r, uint16_t h) {
+    return f32_to_f16_bits(__fadd_rn(f16_bits_to_f32(r), f16_bits_to_f32(h)));
+}
+
+__device__ __forceinline__ uint16_t add_residual(uint16_t h, const uint16_t* res, int64_t i) {
+    return res == nullptr ? h : add_f16(res[i], h);
+}
+
+// ------------------------------------------------------------------ greedy pick
+
+// (value, index) under the reference's greedy rule (inference_engine.cpp:84-95):
+// the larger value wins; on equal values the lower index wins (the reference
+// scans upwards and only a strictly greater value replaces the best); NaN is
+// never chosen, which is the same as reading it as -inf with the lowest-index
+// rule, because an all -inf/NaN row then yields index 0, as the reference does.
+struct ArgBest {
+    float v;
+    int64_t i;
+};
+
+__device__ __forceinline__ ArgBest arg_better(ArgBest a, ArgBest b) {
+    if (b.v > a.v || (b.v == a.v && b.i < a.i)) return b;
+    return a;
+}
+
+__device__ __forceinline__ float nan_to_ninf(float v) { return v != v ? -INFINITY : v; }
+
+// Best (value, index) over the 32 lanes of a warp, valid in lane 0.
+__device__ __forceinline__ ArgBest warp_arg_best(ArgBest b) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        ArgBest o;
+        o.v = __shfl_down_sync(0xFFFFFFFFu, b.v, off);
+        o.i = __shfl_down_sync(0xFFFFFFFFu, b.i, off);
+        b = arg_better(b, o);
+    }
+    return b;
+}
+
 // ------------------------------------------------------------------ error flag
 
 __device__ __forceinline__ void raise_error(int* flag, int code) {
@@ -278,6 +320,18 @@ __device__ __forceinline__ void tmem_ld_16cols(uint32_t taddr, uint32_t (&r)[16]
           "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Store 16 consecutive FP32 columns of this warp's 32 TMEM lanes and wait for
+// the store to complete.
+__device__ __forceinline__ void tmem_st_16cols(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 // Shared-memory matrix descriptor for a K-major tile written by TMA with

@@ -26,6 +26,8 @@ struct DevCtx {
     size_t io_y_bytes = 0;
     void* gu = nullptr;     // interleaved gate|up product of an unfused mrt_gemm_swiglu
     size_t gu_bytes = 0;
+    void* am = nullptr;     // greedy-pick partials of a fused lm_head (mrt_lm_head_argmax)
+    size_t am_bytes = 0;
     // Host-buffer pipeline (mrt_gemm_host): a copy-in and a copy-out stream
     // beside the caller's, and events that hand each row chunk from one to
     // the next (created on first use).

@@ -1694,8 +1694,10 @@ int dec_forward(mrt_decoder d, int64_t S, const int32_t* ids, int64_t pos0, bool
     const int64_t last = (S - 1) * H;
     DEC_CU(add_norm(d->r, d->x, d->norm, d->norm_dt, 1, calls - 1, S - 1, 1), "final norm launch");
     const int64_t vl = d->v1 - d->v0;
-    DEC_TRY(mrt_gemm(d->lm_head, d->normed + last, H, d->logits, vl, 1, 0, s));
-    DEC_CU(launch_argmax(d->logits, 1, vl, vl, d->v0, d->am_idx, d->am_val, d->am_scratch, s), "argmax launch");
+    // The GEMM's epilogue reduces every 32 vocabulary rows to their best
+    // (value, index); one small kernel picks among those.
+    (void)vl;
+    DEC_TRY(mrt_lm_head_argmax(d->lm_head, d->normed + last, H, 1, d->logits, d->v0, d->am_idx, d->am_val, s));
     const int64_t* pick = d->am_idx;
     if (d->world > 1) {
         // Vocabulary shards: the first maximum over every rank's (value, index).

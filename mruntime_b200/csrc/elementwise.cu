@@ -117,7 +117,8 @@ __global__ void reduce_tail_kernel(const TcGemmArgs a, int num_m, int n_tail) {
             if (a.out_f32) {
                 static_cast<float*>(a.y)[row * a.ldy + col + j] = v[j];
             } else {
-                static_cast<uint16_t*>(a.y)[row * a.ldy + col + j] = round_out(v[j], a.bias, col + j);
+                static_cast<uint16_t*>(a.y)[row * a.ldy + col + j] =
+                    add_residual(round_out(v[j], a.bias, col + j), a.residual, row * a.ldr + col + j);
             }
         }
     }
@@ -131,22 +132,9 @@ __global__ void f32_to_f16_kernel(const float* src, uint16_t* dst, int64_t n) {
 
 // ---------------------------------------------------------------- argmax
 
-// (value, index) with the reference's preference: larger value wins; on
-// equal values the lower index wins (the reference scans upwards and only a
-// strictly greater value replaces the best); NaN is never chosen, which is
-// the same as reading it as -inf with the lowest-index rule, because an
-// all -inf/NaN row then yields index 0, as the reference does.
-struct Best {
-    float v;
-    int64_t i;
-};
+using Best = ArgBest;
 
-__device__ __forceinline__ Best better(Best a, Best b) {
-    if (b.v > a.v || (b.v == a.v && b.i < a.i)) return b;
-    return a;
-}
-
-__device__ __forceinline__ float nan_to_ninf(float v) { return v != v ? -INFINITY : v; }
+__device__ __forceinline__ Best better(Best a, Best b) { return arg_better(a, b); }
 
 __device__ __forceinline__ Best block_best(Best b) {
     __shared__ float sv[kThreads / 32];
@@ -327,6 +315,15 @@ cudaError_t launch_argmax(const uint16_t* logits, int64_t M, int64_t V, int64_t 
     note_launches(1);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
+    argmax_final_kernel<<<static_cast<unsigned>(M), kThreads, 0, s>>>(pv, pi, nchunks, index_base, idx, val);
+    note_launches(1);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_argmax_final(const float* pv, const int64_t* pi, int64_t M, int64_t nchunks,
+                                int64_t index_base, int64_t* idx, float* val, cudaStream_t s) {
+    if (M <= 0) return cudaSuccess;
+    if (nchunks <= 0) return cudaErrorInvalidValue;
     argmax_final_kernel<<<static_cast<unsigned>(M), kThreads, 0, s>>>(pv, pi, nchunks, index_base, idx, val);
     note_launches(1);
     return cudaGetLastError();

@@ -33,6 +33,17 @@ constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr int kThreadsTc = 192;
 constexpr int kEpiThreads = 128;
+// Segmented accumulation (normal mode, long K): every kSegKb k-blocks the MMAs
+// move to the other TMEM accumulator and 8 epilogue warps add the finished
+// segment into FP32 registers with IEEE round-to-nearest.  The tensor cores'
+// own accumulation rounds toward zero; over thousands of k-steps that bias
+// makes the result measurably less accurate than the reference's sequential
+// FP32 loop (cpu_backend.cpp:143-166), and segments of 16 k-blocks remove it.
+constexpr int kSegKb = 16;
+constexpr int kThreadsSeg = 64 + 256;
+
+template <bool SEG>
+constexpr int threads_of() { return SEG ? kThreadsSeg : kThreadsTc; }
 
 template <int BN, bool SWAP>
 struct TcCfg {
@@ -122,36 +133,68 @@ __device__ __forceinline__ void store_row_chunk(const TcGemmArgs& a, const uint3
         return;
     }
     uint16_t* dst = static_cast<uint16_t*>(a.y) + row * a.ldy + col0;
-    const bool vec = col0 + 32 <= a.N && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0);
+    const uint16_t* res = a.residual != nullptr ? a.residual + row * a.ldr + col0 : nullptr;
+    const bool vec = col0 + 32 <= a.N && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) &&
+                     ((reinterpret_cast<uintptr_t>(res) & 15) == 0);
     if (vec) {
         uint32_t h[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j)
             h[j] = pack_h2(round_out(__uint_as_float(r[2 * j]), a.bias, col0 + 2 * j),
                            round_out(__uint_as_float(r[2 * j + 1]), a.bias, col0 + 2 * j + 1));
+        if (res != nullptr) {
+            // The residual row chunk is read whole before any output is
+            // written (y may be the residual buffer itself).
+            uint4 q[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) q[j] = *reinterpret_cast<const uint4*>(res + 8 * j);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t w[4] = {q[j].x, q[j].y, q[j].z, q[j].w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const uint32_t o = h[4 * j + i];
+                    h[4 * j + i] = pack_h2(add_f16(static_cast<uint16_t>(w[i] & 0xFFFFu), static_cast<uint16_t>(o & 0xFFFFu)),
+                                           add_f16(static_cast<uint16_t>(w[i] >> 16), static_cast<uint16_t>(o >> 16)));
+                }
+            }
+        }
 #pragma unroll
         for (int j = 0; j < 16; j += 4)
             *reinterpret_cast<uint4*>(dst + 2 * j) = make_uint4(h[j], h[j + 1], h[j + 2], h[j + 3]);
     } else {
         for (int j = 0; j < 32 && col0 + j < a.N; ++j)
-            dst[j] = round_out(__uint_as_float(r[j]), a.bias, col0 + j);
+            dst[j] = add_residual(round_out(__uint_as_float(r[j]), a.bias, col0 + j), res, j);
     }
 }
 
 // Swap mode: 16 accumulator columns (tokens) of one weight row; each column
 // is one token's output at weight row `n`, so a warp's 32 lanes write 32
 // consecutive outputs of that token.
+//
+// With greedy-pick partials (a.am_val) every lane of the warp must call this:
+// the warp's 32 rows (one chunk) are reduced to their best (value, index)
+// per token by shuffles.
 __device__ __forceinline__ void store_swap_chunk(const TcGemmArgs& a, const uint32_t (&r)[16], int64_t n,
                                                  int64_t m0) {
-    if (n >= a.N) return;
+    const bool in = n < a.N;
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
         const int64_t m = m0 + j;
-        if (m >= a.M) break;
+        if (m >= a.M) break;  // uniform over the warp
         if (a.out_f32) {
-            static_cast<float*>(a.y)[m * a.ldy + n] = __uint_as_float(r[j]);
-        } else {
-            static_cast<uint16_t*>(a.y)[m * a.ldy + n] = round_out(__uint_as_float(r[j]), a.bias, n);
+            if (in) static_cast<float*>(a.y)[m * a.ldy + n] = __uint_as_float(r[j]);
+            continue;
+        }
+        const uint16_t h = in ? add_residual(round_out(__uint_as_float(r[j]), a.bias, n), a.residual, m * a.ldr + n) : 0;
+        if (in && a.y != nullptr) static_cast<uint16_t*>(a.y)[m * a.ldy + n] = h;
+        if (a.am_val != nullptr) {
+            const ArgBest b = warp_arg_best(in ? ArgBest{nan_to_ninf(f16_bits_to_f32(h)), n} : ArgBest{-INFINITY, INT64_MAX});
+            if ((threadIdx.x & 31) == 0) {
+                const int64_t at = m * a.am_chunks + (n >> 5);
+                a.am_val[at] = b.v;
+                a.am_idx[at] = b.i;
+            }
         }
     }
 }
@@ -421,11 +464,15 @@ __device__ __forceinline__ void store_swap_rows4(const TcGemmArgs& a, const floa
         return;
     }
     uint16_t* dst = static_cast<uint16_t*>(a.y) + token * a.ldy + n;
+    const int64_t ri = token * a.ldr + n;
     if (whole && (reinterpret_cast<uintptr_t>(dst) & 7) == 0) {
-        *reinterpret_cast<uint2*>(dst) = make_uint2(pack_h2(round_out(v[0], a.bias, n), round_out(v[1], a.bias, n + 1)),
-                                                    pack_h2(round_out(v[2], a.bias, n + 2), round_out(v[3], a.bias, n + 3)));
+        uint16_t h[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) h[i] = add_residual(round_out(v[i], a.bias, n + i), a.residual, ri + i);
+        *reinterpret_cast<uint2*>(dst) = make_uint2(pack_h2(h[0], h[1]), pack_h2(h[2], h[3]));
     } else {
-        for (int i = 0; i < 4 && n + i < a.N; ++i) dst[i] = round_out(v[i], a.bias, n + i);
+        for (int i = 0; i < 4 && n + i < a.N; ++i)
+            dst[i] = add_residual(round_out(v[i], a.bias, n + i), a.residual, ri + i);
     }
 }
 
@@ -509,11 +556,14 @@ __device__ __forceinline__ void swap_cluster_finish(const TcGemmArgs& a, uint8_t
     }
 }
 
-template <int BN, bool SWAP>
-__global__ void __launch_bounds__(kThreadsTc, SWAP ? 2 : 1)
+template <int BN, bool SWAP, bool SEG>
+__global__ void __launch_bounds__(threads_of<SEG>(), SWAP ? 2 : 1)
     tc_gemm_kernel(const TcGemmArgs a, const __grid_constant__ CUtensorMap tma,
                    const __grid_constant__ CUtensorMap tmb) {
+    static_assert(!(SEG && SWAP), "segmented accumulation is a normal-mode variant");
     using Cfg = TcCfg<BN, SWAP>;
+    constexpr int kEpi = SEG ? 256 : kEpiThreads;         // epilogue threads
+    constexpr int kSegLen = SEG ? kSegKb : (1 << 30);     // k-blocks per accumulator segment
     constexpr int S = Cfg::kStages;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -540,7 +590,7 @@ __global__ void __launch_bounds__(kThreadsTc, SWAP ? 2 : 1)
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&tfull[i], 1);
-            mbar_init(&tempty[i], kEpiThreads);
+            mbar_init(&tempty[i], kEpi);
         }
         mbar_init(drain, 1);
         if (clustered) {
@@ -696,39 +746,122 @@ __global__ void __launch_bounds__(kThreadsTc, SWAP ? 2 : 1)
             bool ok = true;
             for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
                 const Unit w = decode_unit(a, u, num_m, n_tail, num_kb);
-                if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, a.err_flag, kErrMmaWait)) break;
-                tc_fence_after();
-                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-                for (int kb = w.kb0; kb < w.kb1; ++kb) {
-                    if (!mbar_wait(&full[stage], phase, a.err_flag, kErrMmaWait)) {
+                // One accumulator per segment of the unit's k-blocks (one
+                // segment unless SEG), alternating between the two.
+                for (int s0 = w.kb0; s0 < w.kb1 && ok; s0 += kSegLen) {
+                    const int s1 = min(s0 + kSegLen, w.kb1);
+                    if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, a.err_flag, kErrMmaWait)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a_addr = smem_u32(sA + stage * Cfg::kABytes);
-                    const uint32_t b_addr = smem_u32(sB + stage * Cfg::kBBytes);
+                    const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+                    for (int kb = s0; kb < s1; ++kb) {
+                        if (!mbar_wait(&full[stage], phase, a.err_flag, kErrMmaWait)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t a_addr = smem_u32(sA + stage * Cfg::kABytes);
+                        const uint32_t b_addr = smem_u32(sB + stage * Cfg::kBBytes);
 #pragma unroll
-                    for (int k = 0; k < kBK / 16; ++k) {
-                        tc_mma_f16(d_tmem, smem_desc_k128(a_addr + k * 32), smem_desc_k128(b_addr + k * 32),
-                                   idesc, (kb > w.kb0 || k > 0) ? 1u : 0u);
+                        for (int k = 0; k < kBK / 16; ++k) {
+                            tc_mma_f16(d_tmem, smem_desc_k128(a_addr + k * 32), smem_desc_k128(b_addr + k * 32),
+                                       idesc, (kb > s0 || k > 0) ? 1u : 0u);
+                        }
+                        tc_commit(&empty[stage]);
+                        any = true;
+                        if (++stage == S) {
+                            stage = 0;
+                            phase ^= 1u;
+                        }
                     }
-                    tc_commit(&empty[stage]);
-                    any = true;
-                    if (++stage == S) {
-                        stage = 0;
-                        phase ^= 1u;
-                    }
+                    if (!ok) break;
+                    tc_commit(&tfull[acc]);
+                    acc ^= 1;
+                    if (acc == 0) acc_phase ^= 1u;
                 }
-                if (!ok) break;
-                tc_commit(&tfull[acc]);
-                acc ^= 1;
-                if (acc == 0) acc_phase ^= 1u;
             }
             if (any) {
                 // Every MMA this thread issued must finish before TMEM is freed.
                 tc_commit(drain);
                 mbar_wait(drain, 0, nullptr, kErrDrainWait);
             }
+        }
+    } else if constexpr (SEG) {
+        // 8 epilogue warps: warp w reads TMEM lanes 32 (w mod 4) .. +31 (its
+        // rows) and columns [half * BN/2, (half + 1) * BN/2) of each segment's
+        // accumulator and keeps their running sums in registers.  The last
+        // segment's sums are written back into its accumulator (which this
+        // thread still owns) and stored from there 32 columns at a time, so
+        // the store code never holds every sum at once.
+        constexpr int HB = BN / 2;
+        const int quad = warp & 3;
+        const int half = (warp - 2) >> 2;
+        griddep_wait();  // before any bounded wait and any global write
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int u = blockIdx.x; u < total; u += gridDim.x) {
+            const Unit w = decode_unit(a, u, num_m, n_tail, num_kb);
+            float sum[HB];
+            bool ok = true;
+            uint32_t t_row = 0;
+            for (int s0 = w.kb0; s0 < w.kb1; s0 += kSegLen) {
+                int got = 1;
+                if (lane == 0) got = mbar_wait(&tfull[acc], acc_phase, a.err_flag, kErrEpiWait) ? 1 : 0;
+                got = __shfl_sync(0xFFFFFFFFu, got, 0);
+                if (!got) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN + half * HB);
+                const bool last = s0 + kSegLen >= w.kb1;
+                // 16 columns per load keeps the running sums and one load's
+                // registers within the 168 a thread has at 10 warps per CTA.
+#pragma unroll
+                for (int c = 0; c < HB / 16; ++c) {
+                    uint32_t r[16];
+                    __syncwarp();
+                    tmem_ld_16cols(t_row + c * 16, r);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        sum[c * 16 + j] = s0 == w.kb0 ? __uint_as_float(r[j]) : __fadd_rn(sum[c * 16 + j], __uint_as_float(r[j]));
+                    if (last) {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) r[j] = __float_as_uint(sum[c * 16 + j]);
+                        tmem_st_16cols(t_row + c * 16, r);
+                    }
+                }
+                if (last) break;  // the accumulator stays owned until the stores below
+                tc_fence_before();
+                mbar_arrive(&tempty[acc]);
+                acc ^= 1;
+                if (acc == 0) acc_phase ^= 1u;
+            }
+            if (!ok) break;
+            const int row_in_tile = quad * 32 + lane;
+            const int64_t row = static_cast<int64_t>(w.mt) * kBM + row_in_tile;
+#pragma unroll 1
+            for (int c = 0; c < HB / 32; ++c) {
+                uint32_t r[32];
+                __syncwarp();
+                tmem_ld_32cols(t_row + c * 32, r);
+                const int col_in_tile = half * HB + c * 32;
+                const int64_t col0 = static_cast<int64_t>(w.nt) * BN + col_in_tile;
+                if (w.slot >= 0) {
+                    store_partial_chunk(a, r, w.slot, row_in_tile, col_in_tile, BN);
+                } else if (row < a.M && col0 < a.N) {
+                    if (a.swiglu_lut != nullptr)
+                        store_row_chunk_swiglu(a, r, row, col0);
+                    else
+                        store_row_chunk(a, r, row, col0);
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&tempty[acc]);
+            acc ^= 1;
+            if (acc == 0) acc_phase ^= 1u;
         }
     } else if (clustered) {
         griddep_wait();  // before any bounded wait and any global write
@@ -810,20 +943,20 @@ __global__ void __launch_bounds__(kThreadsTc, SWAP ? 2 : 1)
 }
 
 // Kernel attributes, once per device.
-template <int BN, bool SWAP>
+template <int BN, bool SWAP, bool SEG>
 cudaError_t prepare_bn() {
     static bool attr_set[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     if (!attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<BN, SWAP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<BN, SWAP, SEG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(TcCfg<BN, SWAP>::kSmem));
         if (e != cudaSuccess) return e;
         // All shared memory, no L1 carve-out: every instance then runs under one
         // SM configuration, so two swap-mode CTAs (of one GEMM and the next)
         // can share an SM.
-        e = cudaFuncSetAttribute(tc_gemm_kernel<BN, SWAP>, cudaFuncAttributePreferredSharedMemoryCarveout,
+        e = cudaFuncSetAttribute(tc_gemm_kernel<BN, SWAP, SEG>, cudaFuncAttributePreferredSharedMemoryCarveout,
                                  cudaSharedmemCarveoutMaxShared);
         if (e != cudaSuccess) return e;
         attr_set[dev] = true;
@@ -831,13 +964,13 @@ cudaError_t prepare_bn() {
     return cudaSuccess;
 }
 
-template <int BN, bool SWAP>
+template <int BN, bool SWAP, bool SEG = false>
 cudaError_t launch_bn(const TcGemmArgs& a, const CUtensorMap& ta, const CUtensorMap& tb, cudaStream_t s) {
-    cudaError_t e = prepare_bn<BN, SWAP>();
+    cudaError_t e = prepare_bn<BN, SWAP, SEG>();
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(static_cast<unsigned>(a.grid));
-    cfg.blockDim = dim3(kThreadsTc);
+    cfg.blockDim = dim3(threads_of<SEG>());
     cfg.dynamicSmemBytes = TcCfg<BN, SWAP>::kSmem;
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
@@ -853,7 +986,7 @@ cudaError_t launch_bn(const TcGemmArgs& a, const CUtensorMap& ta, const CUtensor
     }
     cfg.attrs = attr;
     cfg.numAttrs = n_attr;
-    e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, SWAP>, a, ta, tb);
+    e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, SWAP, SEG>, a, ta, tb);
     if (e != cudaSuccess) return e;
     note_launches(1);
     return cudaGetLastError();
@@ -862,7 +995,7 @@ cudaError_t launch_bn(const TcGemmArgs& a, const CUtensorMap& ta, const CUtensor
 // Whether clusters of k swap-mode CTAs of width BN can be resident at all.
 template <int BN>
 bool cluster_fits(int k) {
-    if (prepare_bn<BN, true>() != cudaSuccess) return false;
+    if (prepare_bn<BN, true, false>() != cudaSuccess) return false;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(static_cast<unsigned>(k));
     cfg.blockDim = dim3(kThreadsTc);
@@ -875,7 +1008,7 @@ bool cluster_fits(int k) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int n = 0;
-    const cudaError_t e = cudaOccupancyMaxActiveClusters(&n, tc_gemm_kernel<BN, true>, &cfg);
+    const cudaError_t e = cudaOccupancyMaxActiveClusters(&n, tc_gemm_kernel<BN, true, false>, &cfg);
     if (e != cudaSuccess) {
         (void)cudaGetLastError();
         return false;
@@ -899,6 +1032,14 @@ bool tc_cluster_ok(int bn, int k) {
         v = ok ? 2 : 1;
     }
     return v == 2;
+}
+
+bool tc_gemm_segmented(const TcGemmArgs& a) {
+    if (a.swap) return false;
+    const int num_kb = (a.K + kBK - 1) / kBK;
+    const bool long_full = a.full_tiles > 0 && num_kb > kSegMinKb;
+    const bool long_tail = a.full_tiles < tc_gemm_tiles(a) && a.kb_per > kSegMinKb;
+    return long_full || long_tail;
 }
 
 int tc_gemm_tiles(const TcGemmArgs& a) {
@@ -934,6 +1075,12 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& a, const CUtensorMap& tmap_x, const
         if (a.bn == 16) return launch_bn<16, true>(a, tmap_w, tmap_x, s);
         if (a.bn == 32) return launch_bn<32, true>(a, tmap_w, tmap_x, s);
         if (a.bn == 64) return launch_bn<64, true>(a, tmap_w, tmap_x, s);
+        return cudaErrorInvalidValue;
+    }
+    if (tc_gemm_segmented(a)) {
+        if (a.bn == 256) return launch_bn<256, false, true>(a, tmap_x, tmap_w, s);
+        if (a.bn == 128) return launch_bn<128, false, true>(a, tmap_x, tmap_w, s);
+        if (a.bn == 64) return launch_bn<64, false, true>(a, tmap_x, tmap_w, s);
         return cudaErrorInvalidValue;
     }
     if (a.bn == 256) return launch_bn<256, false>(a, tmap_x, tmap_w, s);

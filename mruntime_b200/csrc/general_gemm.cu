@@ -73,7 +73,7 @@ __global__ void general_gemm_kernel(const GeneralGemmArgs a) {
     } else if (a.c_dtype == 1) {
         static_cast<uint16_t*>(a.c)[ci] = f32_to_bf16_bits(out);
     } else {
-        static_cast<uint16_t*>(a.c)[ci] = round_out(out, a.bias, n);
+        static_cast<uint16_t*>(a.c)[ci] = add_residual(round_out(out, a.bias, n), a.residual, m * a.ldr + n);
     }
 }
 

@@ -61,6 +61,20 @@ struct TcGemmArgs {
     // fp16(u)) with y of N / 2 columns.  Plans without a K-split only; no
     // bias, FP16 output.
     const uint16_t* swiglu_lut;
+    // Non-null: residual add after the output rounding, y[m][n] =
+    // fp16(res[m][n] + fp16(acc (+ bias))) with res of row stride ldr (the
+    // reference's add op after o_proj and down_proj).  FP16 output only; y may
+    // be res itself (each element is read, then written, by one thread).
+    const uint16_t* residual;
+    int64_t ldr;
+    // Non-null (swap mode, FP16 output, no cluster finish): greedy-pick
+    // partials.  For every token m and every 32 weight rows (chunk c = row / 32)
+    // the epilogue writes the best (value, index) of those rows' FP16 outputs
+    // under the reference's rule to am_val / am_idx[m * am_chunks + c];
+    // am_chunks = 4 * ceil(N / 128).  y may then be null (no logits stored).
+    float* am_val;
+    int64_t* am_idx;
+    int am_chunks;
 };
 // Whether a swap-mode launch of tile width bn may use clusters of k CTAs on
 // the current device (checked once per device, width and k).
@@ -69,6 +83,12 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& a, const CUtensorMap& tmap_x, const
                            cudaStream_t s);
 // Output tiles of a plan (128 A rows x bn B rows each).
 int tc_gemm_tiles(const TcGemmArgs& a);
+// Units longer than this many 64-wide k-blocks accumulate in segments (normal
+// mode: the segmented kernel variant; swap-mode plans keep every unit at or
+// below it).
+constexpr int kSegMinKb = 64;
+// Whether a normal-mode launch uses the segmented-accumulation variant.
+bool tc_gemm_segmented(const TcGemmArgs& a);
 // Normal mode only: sum the K-slices of every tail tile in slice order on
 // the whole GPU, round (+bias) or keep FP32, and store.
 cudaError_t launch_reduce_tail(const TcGemmArgs& a, cudaStream_t s);
@@ -94,6 +114,9 @@ size_t argmax_scratch_bytes(int64_t M, int64_t V);
 cudaError_t launch_argmax(const uint16_t* logits, int64_t M, int64_t V, int64_t ld,
                           int64_t index_base, int64_t* idx, float* val, void* scratch,
                           cudaStream_t s);
+// Second pass alone: best of pv / pi[m * nchunks + c] per row m.
+cudaError_t launch_argmax_final(const float* pv, const int64_t* pi, int64_t M, int64_t nchunks,
+                                int64_t index_base, int64_t* idx, float* val, cudaStream_t s);
 // Combine per-rank (value, index) pairs gathered as [world, M].
 cudaError_t launch_argmax_combine(const float* vals, const int64_t* idxs, int world, int64_t M,
                                   int64_t* idx_out, cudaStream_t s);
@@ -120,6 +143,8 @@ struct GeneralGemmArgs {
     int trans_a, trans_b;
     const uint16_t* bias;  // FP16 [N] added after rounding (FP16 C only) or nullptr
     int64_t b_k_tiles;     // > 0: B is an FP16 weight [N, K] in the tiled layout (trans_b)
+    const uint16_t* residual;  // FP16 C only: c = fp16(residual + fp16(...)) (row stride ldr), or nullptr
+    int64_t ldr;
 };
 cudaError_t launch_general_gemm(const GeneralGemmArgs& a, cudaStream_t s);
 

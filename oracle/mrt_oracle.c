@@ -168,6 +168,12 @@ void orc_add_bias_f16(uint16_t* out, const uint16_t* bias, size_t rows, size_t n
         }
 }
 
+/* CpuBackend::add (src/core/cpu_backend.cpp:430-455) on FP16 operands: each
+ * element widened exactly, one FP32 add, the reference's FP16 rounding. */
+void orc_add_f16(const uint16_t* a, const uint16_t* b, uint16_t* out, size_t n) {
+    for (size_t i = 0; i < n; ++i) out[i] = orc_f32_to_f16(orc_f16_to_f32(a[i]) + orc_f16_to_f32(b[i]));
+}
+
 /* src/engine/inference_engine.cpp:84-95. */
 int64_t orc_argmax_f16(const uint16_t* logits, size_t n) {
     float best = -INFINITY;

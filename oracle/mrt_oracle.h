@@ -65,6 +65,7 @@ void orc_gemm_f64(const uint16_t* X, size_t M, size_t K,
 /* Bias add after the q/k/v projections: out = fp16(fp32(out) + fp32(bias)),
  * applied in place to every row (src/models/qwen/qwen_model.cpp:130-155). */
 void orc_add_bias_f16(uint16_t* out, const uint16_t* bias, size_t rows, size_t n);
+void orc_add_f16(const uint16_t* a, const uint16_t* b, uint16_t* out, size_t n);
 
 /* Greedy argmax over one row of FP16 logits: first index whose value is
  * strictly greater than every earlier one, starting from -inf, so NaN never

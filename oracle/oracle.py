@@ -67,6 +67,8 @@ def oracle_lib() -> C.CDLL:
                                      C.c_size_t, _f64p]
         lib.orc_add_bias_f16.restype = None
         lib.orc_add_bias_f16.argtypes = [_u16p, _u16p, C.c_size_t, C.c_size_t]
+        lib.orc_add_f16.restype = None
+        lib.orc_add_f16.argtypes = [_u16p, _u16p, _u16p, C.c_size_t]
         lib.orc_argmax_f16.restype = C.c_int64
         lib.orc_argmax_f16.argtypes = [_u16p, C.c_size_t]
         lib.orc_rel_frobenius_f16.restype = C.c_double
@@ -103,6 +105,8 @@ def ref_lib() -> C.CDLL:
             fn.argtypes = [a, b, C.c_size_t]
         lib.refb_add_bias.restype = None
         lib.refb_add_bias.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_size_t, C.c_size_t]
+        lib.refb_add.restype = None
+        lib.refb_add.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t]
         lib.refb_argmax.restype = C.c_int64
         lib.refb_argmax.argtypes = [C.c_void_p, C.c_int, C.c_size_t]
         _ref = lib
@@ -234,6 +238,21 @@ def ref_add_bias(out_f16: np.ndarray, bias_f16: np.ndarray) -> np.ndarray:
     return out
 
 
+def ref_add(a_f16: np.ndarray, b_f16: np.ndarray, threads: int = 1) -> np.ndarray:
+    """The reference's CpuBackend::add on two FP16 arrays of one shape."""
+    a = np.ascontiguousarray(a_f16, np.uint16)
+    b = np.ascontiguousarray(b_f16, np.uint16)
+    assert a.shape == b.shape
+    out = np.empty_like(a)
+    lib = ref_lib()
+    be = lib.refb_create(threads)
+    try:
+        lib.refb_add(be, _ptr(a), _ptr(b), _ptr(out), a.size)
+    finally:
+        lib.refb_destroy(be)
+    return out
+
+
 def ref_argmax(logits_f16: np.ndarray) -> int:
     row = np.ascontiguousarray(logits_f16, dtype=np.uint16)
     return int(ref_lib().refb_argmax(_ptr(row), FP16, row.size))
@@ -244,6 +263,16 @@ def add_bias(out_f16: np.ndarray, bias_f16: np.ndarray) -> np.ndarray:
     rows = out.size // bias_f16.size
     oracle_lib().orc_add_bias_f16(out.reshape(-1), np.ascontiguousarray(bias_f16, np.uint16), rows,
                                   bias_f16.size)
+    return out
+
+
+def add(a_f16: np.ndarray, b_f16: np.ndarray) -> np.ndarray:
+    """Element-wise FP16 add with the reference's rounding (orc_add_f16)."""
+    a = np.ascontiguousarray(a_f16, np.uint16)
+    b = np.ascontiguousarray(b_f16, np.uint16)
+    assert a.shape == b.shape
+    out = np.empty_like(a)
+    oracle_lib().orc_add_f16(a.reshape(-1), b.reshape(-1), out.reshape(-1), a.size)
     return out
 
 

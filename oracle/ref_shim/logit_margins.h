@@ -9,8 +9,8 @@
 // reference's calls are synchronous, so the host tensor is complete on
 // return) and keeps, per call, the index the reference's greedy rule would
 // pick (first maximum under strict `>`, inference_engine.cpp:84-95), its value
-// and the runner-up value.  The margin top1 - top2 says how close each greedy
-// decision was.
+// and the runner-up's value and index.  The margin top1 - top2 says how close
+// each greedy decision was.
 #pragma once
 
 #include <cstddef>
@@ -25,6 +25,7 @@ namespace ref_shim {
 
 struct Pick {
     int index = -1;
+    int second_index = -1;  // the runner-up: first index holding top2 (other than `index`)
     float top1 = 0.0f;
     float top2 = 0.0f;
 };
@@ -77,10 +78,12 @@ private:
             const float v = mruntime::load_scalar_as_fp32(C.data(), C.dtype(), base + i);
             if (v > best) {
                 second = best;
+                p.second_index = p.index;
                 best = v;
                 p.index = static_cast<int>(i);
             } else if (v > second) {
                 second = v;
+                p.second_index = static_cast<int>(i);
             }
         }
         if (p.index < 0) p.index = 0;  // all -inf/NaN: the reference's rule keeps index 0

@@ -52,6 +52,15 @@ int refb_gemm(void* backend, const void* A, int a_dtype, size_t a_rows, size_t a
     return 0;
 }
 
+// CpuBackend::add (src/core/cpu_backend.cpp:430-455): out = a + b element-wise
+// over n FP16 values -- the residual adds of src/models/qwen/qwen_model.cpp:316, 324.
+void refb_add(void* backend, const uint16_t* a, const uint16_t* b, uint16_t* out, size_t n) {
+    Tensor ta = Tensor::from_buffer(const_cast<uint16_t*>(a), Shape({n}), DType::FP16);
+    Tensor tb = Tensor::from_buffer(const_cast<uint16_t*>(b), Shape({n}), DType::FP16);
+    Tensor to = Tensor::from_buffer(out, Shape({n}), DType::FP16);
+    static_cast<CpuBackend*>(backend)->add(ta, tb, to);
+}
+
 // Reference converters (include/mruntime/dtype.h:39-167), element-wise.
 void refb_f32_to_f16_n(const float* src, uint16_t* dst, size_t n) {
     for (size_t i = 0; i < n; ++i) dst[i] = mruntime::float_to_fp16_bits(src[i]);

@@ -105,6 +105,15 @@ int main(int argc, char** argv) {
             std::cout << " " << (p.top1 - p.top2);
         }
         std::cout << "\n";
+        // Runner-up index and top logit of the same picks.
+        std::cout << "RUNNERS_UP";
+        for (size_t j = 0; j + prompt.size() - 1 < picks.size() && j < out.size() - prompt.size(); ++j)
+            std::cout << " " << picks[prompt.size() - 1 + j].second_index;
+        std::cout << "\n";
+        std::cout << "TOP1";
+        for (size_t j = 0; j + prompt.size() - 1 < picks.size() && j < out.size() - prompt.size(); ++j)
+            std::cout << " " << picks[prompt.size() - 1 + j].top1;
+        std::cout << "\n";
         if (prof) {
             for (int op = 0; op < static_cast<int>(mruntime::BackendOp::Count); ++op) {
                 const auto s = prof->profiler().snapshot(static_cast<mruntime::BackendOp>(op));

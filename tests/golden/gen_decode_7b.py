@@ -18,10 +18,11 @@ Writes the checkpoint as a safetensors file under _data/ (neither committed nor
 shipped with the tests: the GPU side regenerates identical bits from the
 seed), runs oracle/_ref/ref_engine -- the reference's QwenModel +
 InferenceEngine + CpuBackend built from its sources (`make -C oracle engine`)
--- and stores the generated ids and the top-2 logit margin of every pick
-beside this script.
+-- and stores the generated ids, and the top-2 logit margin, best logit and
+runner-up id of every pick, beside this script.  A seed other than 3 is
+added to the file name (decode_<model>_seed<N>_greedy.json).
 
-    python tests/golden/gen_decode_7b.py [--model tiny|7b4l|7b] [--threads N]
+    python tests/golden/gen_decode_7b.py [--model tiny|7b4l|7b] [--threads N] [--seed N]
 """
 from __future__ import annotations
 
@@ -103,6 +104,10 @@ def run_engine(binary: str, paths: dict, max_new: int, threads: int = 0, profile
             info["tokens"] = [int(t) for t in rest.split()]
         elif key == "MARGINS":
             info["margins"] = [float(t) for t in rest.split()]
+        elif key == "RUNNERS_UP":
+            info["runner_up"] = [int(t) for t in rest.split()]
+        elif key == "TOP1":
+            info["top1"] = [float(t) for t in rest.split()]
         elif key in ("LOAD_SECONDS", "GENERATE_SECONDS", "THREADS"):
             info[key.lower()] = float(rest)
         elif key == "BACKEND":
@@ -120,7 +125,8 @@ def main():
     ap.add_argument("--seed", type=int, default=3)
     args = ap.parse_args()
     cfg, n_prompt, max_new = MODELS[args.model]
-    data = os.path.join(ROOT, "_data", f"decoder_{args.model}")
+    tag = args.model if args.seed == 3 else f"{args.model}_seed{args.seed}"
+    data = os.path.join(ROOT, "_data", f"decoder_{tag}")
     t0 = time.time()
     paths = write_checkpoint(data, cfg, args.seed, n_prompt)
     print(f"checkpoint written in {time.time() - t0:.0f} s", flush=True)
@@ -129,7 +135,7 @@ def main():
     out = {"config": cfg, "seed": args.seed, "prompt_len": n_prompt, "max_new": max_new,
            "prompt_sha256": paths["prompt_sha256"], "weights_sha256": paths["weights_sha256"],
            "host_cpus": os.cpu_count(), **info}
-    dst = os.path.join(HERE, f"decode_{args.model}_greedy.json")
+    dst = os.path.join(HERE, f"decode_{tag}_greedy.json")
     with open(dst, "w") as f:
         json.dump(out, f, indent=1)
     print(json.dumps({k: v for k, v in out.items() if k != "config"}))

@@ -109,3 +109,33 @@ def check_close(got_f16: np.ndarray, truth: np.ndarray, ref_err: float | None = 
 
 def same_fraction(a: np.ndarray, b: np.ndarray) -> float:
     return float(np.mean(a == b))
+
+
+def check_greedy_tokens(got, golden: dict, what: str) -> int:
+    """Greedy tokens against the reference engine's golden.
+
+    Every token must equal the reference's, except that the sequences may
+    part at a step where the reference's two best logits are a tie at FP16
+    resolution (top-2 margin at most one FP16 ulp of the best logit): there
+    the order of the FP32 sums (the reference's sequential loop against the
+    tensor cores' blocked one, in every layer before) decides, and the pick
+    must be the reference's runner-up.  After such a step the two sequences
+    continue different prefixes and are not compared.  Returns the number of
+    leading tokens that are equal."""
+    ref = [int(t) for t in golden["tokens"]]
+    got = [int(t) for t in got]
+    assert len(got) == len(ref), f"{what}: {len(got)} tokens, reference {len(ref)}"
+    t = next((i for i, (a, b) in enumerate(zip(got, ref)) if a != b), None)
+    if t is None:
+        print(f"{what}: all {len(ref)} tokens equal to the reference engine's")
+        return len(ref)
+    margins, top1, runner = golden.get("margins"), golden.get("top1"), golden.get("runner_up")
+    assert margins and top1 and runner, f"{what}: token {t} is {got[t]}, reference {ref[t]} (no margins recorded)"
+    ulp = float(np.spacing(np.float16(abs(top1[t]))))
+    assert margins[t] <= ulp, (f"{what}: token {t} is {got[t]}, reference {ref[t]}, whose top-2 margin "
+                               f"{margins[t]} exceeds one FP16 ulp ({ulp}) of its best logit {top1[t]}")
+    assert got[t] == runner[t], f"{what}: at the tie of step {t} picked {got[t]}, not the runner-up {runner[t]}"
+    print(f"{what}: tokens 0..{t - 1} equal to the reference engine's; step {t} is a tie at FP16 resolution "
+          f"(reference best {top1[t]}, runner-up {runner[t]} {margins[t]} below = one ulp) and the runner-up was "
+          f"picked; the sequences then continue different prefixes")
+    return t

@@ -410,3 +410,130 @@ def test_gemm_swiglu(cuda_dev, MIK):
     rows = np.unique(np.r_[0, M // 2, M - 1])
     _, _, s2 = _check_against_oracle(x, w, BF16, y, rows, what=f"swiglu product {MIK}")
     assert s2 > 0.9
+
+
+# ------------------------------------------------------------------ residual epilogue
+
+# (M, N, K, bias): swap mode with whole tiles, K-split global and cluster
+# finishes, normal mode with whole tiles, a K-split tail and segmented
+# accumulation (K > 4096), and the general kernel (K not a multiple of 8).
+RESIDUAL_SHAPES = [(1, 896, 896, False), (1, 3584, 18944, False), (16, 3584, 3584, True), (40, 896, 4864, False),
+                   (200, 896, 896, True), (300, 3584, 18944, False), (65, 20000, 2048, False), (3, 200, 68, False)]
+
+
+@pytest.mark.parametrize("MNKB", RESIDUAL_SHAPES)
+@pytest.mark.parametrize("inplace", [False, True])
+def test_gemm_residual(cuda_dev, MNKB, inplace):
+    """mrt_gemm_residual equals mrt_gemm followed by the reference's add
+    (CpuBackend::add, cpu_backend.cpp:430-455, as qwen_model.cpp:316/324 use
+    it) applied to that product, bit for bit; in place and with strided
+    residual / output rows."""
+    M, N, K, bias = MNKB
+    rng = np.random.default_rng(M * 3 + N + K)
+    x = rand_f16(rng, (M, K))
+    w = rand_w(rng, (N, K), BF16)
+    res = rand_f16(rng, (M, N))
+    wt = upload(w, BF16)
+    if bias:
+        b = W.to_bf16_bits(rng.standard_normal(N, dtype=np.float32) * np.float32(0.02))
+        bd = dev_u16(b)
+        wt.attach_bias(bd.data_ptr(), BF16, True, stream())
+    y = gemm(wt, x, bias)
+    want = O.add(res, y)
+    xd = dev_u16(x)
+    ld = N + (0 if inplace else 8)  # strided rows when not in place
+    resd = torch.zeros((M, ld), dtype=torch.int16, device="cuda")
+    resd[:, :N] = dev_u16(res)
+    out = resd if inplace else torch.zeros((M, ld), dtype=torch.int16, device="cuda")
+    capi.gemm_residual(wt, xd.data_ptr(), K, resd.data_ptr(), ld, out.data_ptr(), ld, M, bias, stream())
+    capi.sync(stream())
+    got = host_u16(out)[:, :N]
+    np.testing.assert_array_equal(got, want)
+
+
+def test_gemm_residual_rejects_bad_arguments(cuda_dev):
+    rng = np.random.default_rng(2)
+    wt = upload(rand_w(rng, (64, 64), FP16), FP16)
+    x = dev_u16(rand_f16(rng, (2, 64)))
+    y = torch.zeros((2, 64), dtype=torch.int16, device="cuda")
+    with pytest.raises(capi.MrtError):
+        capi.gemm_residual(wt, x.data_ptr(), 64, 0, 64, y.data_ptr(), 64, 2, False, stream())
+    with pytest.raises(capi.MrtError):
+        capi.gemm_residual(wt, x.data_ptr(), 64, y.data_ptr(), 32, y.data_ptr(), 64, 2, False, stream())
+
+
+# ------------------------------------------------------------------ lm_head with the pick in the epilogue
+
+# (M, V, K, index_base): the tied 0.5B head, ragged vocabularies (partial last
+# tile), a vocabulary shard of the 7B head, 17..64-token tiles.
+LM_SHAPES = [(1, 151936, 896, 0), (7, 5000, 896, 0), (16, 152064 // 8, 3584, 3 * (152064 // 8)),
+             (33, 1000, 896, 0), (64, 20000, 896, 7)]
+
+
+@pytest.mark.parametrize("MVKB", LM_SHAPES)
+@pytest.mark.parametrize("with_logits", [True, False])
+def test_lm_head_fused_pick(cuda_dev, MVKB, with_logits):
+    """For M <= 64 mrt_lm_head_argmax picks in the GEMM's epilogue; the
+    picks (and values) must equal the reference's greedy rule
+    (inference_engine.cpp:84-95) over the logits mrt_gemm produces, and the
+    logits, when requested, those same logits."""
+    M, V, K, base = MVKB
+    rng = np.random.default_rng(M + V + K)
+    x = rand_f16(rng, (M, K))
+    w = rand_w(rng, (V, K), FP16)
+    wt = upload(w, FP16)
+    logits = gemm(wt, x)
+    want = np.array([O.argmax(r) for r in logits]) + base
+    xd = dev_u16(x)
+    lg = torch.zeros((M, V), dtype=torch.int16, device="cuda") if with_logits else None
+    idx = torch.full((M,), -1, dtype=torch.int64, device="cuda")
+    val = torch.zeros((M,), dtype=torch.float32, device="cuda")
+    capi.lm_head_argmax(wt, xd.data_ptr(), K, M, lg.data_ptr() if lg is not None else None, base, idx.data_ptr(),
+                        val.data_ptr(), stream())
+    capi.sync(stream())
+    np.testing.assert_array_equal(idx.cpu().numpy(), want)
+    vals = W.f16_bits_to_f32(logits[np.arange(M), want - base])
+    np.testing.assert_array_equal(val.cpu().numpy(), vals)
+    if with_logits:
+        np.testing.assert_array_equal(host_u16(lg), logits)
+
+
+def test_lm_head_fused_pick_edge_cases(cuda_dev):
+    """The reference's rule on crafted logit rows (ties, NaN, +-inf, signed
+    zeros; tests/golden/bias_argmax.npz, picks from the reference build): a
+    one-hot x selects column 0 of a weight holding the row, so the GEMM's
+    logits are the crafted values exactly."""
+    g = golden("bias_argmax.npz")
+    K = 64
+    x = np.zeros((1, K), np.uint16)
+    x[0, 0] = 0x3C00  # 1.0
+    xd = dev_u16(x)
+    for row, want in zip(g["rows"], g["am_rows"]):
+        V = row.size
+        w = np.zeros((V, K), np.uint16)
+        w[:, 0] = row
+        wt = upload(w, FP16)
+        idx = torch.full((1,), -1, dtype=torch.int64, device="cuda")
+        capi.lm_head_argmax(wt, xd.data_ptr(), K, 1, None, 0, idx.data_ptr(), None, stream())
+        capi.sync(stream())
+        assert int(idx.item()) == int(want), (row, want)
+        wt.free()
+
+
+# ------------------------------------------------------------------ segmented accumulation (long K)
+
+@pytest.mark.parametrize("MNK", [(256, 1000, 8192), (130, 3584, 18944), (700, 200, 8200), (2048, 512, 18944)])
+def test_long_k_accumulates_in_segments(cuda_dev, MNK):
+    """Normal-mode GEMMs whose units run over more than 64 k-blocks take the
+    segmented-accumulation kernel; their error against FP64 must stay within
+    the reference's own (the tensor cores' round-toward-zero accumulation over
+    ~300 k-blocks alone is ~0.9 % worse)."""
+    M, N, K = MNK
+    rng = np.random.default_rng(M + N + K)
+    x = rand_f16(rng, (M, K))
+    w = rand_w(rng, (N, K), BF16)
+    wt = upload(w, BF16)
+    y = gemm(wt, x)
+    rows = np.unique(np.r_[0:16, M // 2, M - 16:M])
+    _, _, same = _check_against_oracle(x, w, BF16, y, rows, what=f"segmented M={M} N={N} K={K}")
+    assert same > 0.9

@@ -1,6 +1,7 @@
 """The 7B-width decoder against the reference's own engine, token for token.
 
-Golden: tests/golden/decode_7b4l_greedy.json -- the reference's QwenModel +
+Goldens: tests/golden/decode_7b4l_greedy.json (seed 3) and
+decode_7b4l_seed5_greedy.json (seed 5) -- the reference's QwenModel +
 InferenceEngine + CpuBackend, built from its sources, greedy-decoding 32
 tokens after a 128-token prompt on a seeded random-init checkpoint of the
 Qwen2.5-7B width (hidden 3584, 28/4 heads, head_dim 128, intermediate 18944,
@@ -18,8 +19,11 @@ all 32 tokens:
 * the reference's own QwenModel + InferenceEngine with CudaBackend in
   CpuBackend's place (tests/cpp/_build/ref_engine_cuda), the drop-in.
 
-Every step's top-2 logit margin in the reference's logits is printed, so a
-failure shows how close the decision was.
+Every token must be the reference's; the one exception (gpu_util.
+check_greedy_tokens) is a step whose reference top-2 logits are a tie at FP16
+resolution, where the order of FP32 sums decides and the runner-up is
+accepted -- the sequences then part.  Every step's top-2 margin in the
+reference's logits is printed, so a failure shows how close the decision was.
 """
 from __future__ import annotations
 
@@ -32,6 +36,7 @@ import numpy as np
 import pytest
 
 from conftest import GOLDEN, ROOT
+from gpu_util import check_greedy_tokens
 from mruntime_b200 import capi
 from mruntime_b200 import workloads as W
 
@@ -43,14 +48,14 @@ pytestmark = pytest.mark.gpu
 ENGINE_CUDA = os.path.join(ROOT, "tests", "cpp", "_build", "ref_engine_cuda")
 
 
-def _golden() -> dict:
-    with open(os.path.join(GOLDEN, "decode_7b4l_greedy.json")) as f:
-        return json.load(f)
+GOLDENS = [f for f in ("decode_7b4l_greedy.json", "decode_7b4l_seed5_greedy.json")
+           if os.path.exists(os.path.join(GOLDEN, f))]
 
 
-@pytest.fixture(scope="module")
-def ckpt(tmp_path_factory):
-    g = _golden()
+@pytest.fixture(scope="module", params=GOLDENS)
+def ckpt(request, tmp_path_factory):
+    with open(os.path.join(GOLDEN, request.param)) as f:
+        g = json.load(f)
     d = str(tmp_path_factory.mktemp("decoder_7b4l"))
     paths = G.write_checkpoint(d, g["config"], g["seed"], g["prompt_len"])
     assert paths["weights_sha256"] == g["weights_sha256"], "regenerated weights differ from the golden's"
@@ -103,14 +108,14 @@ def test_decoder_matches_reference_engine_7b_width(cuda_dev, ckpt):
     toks, st = _decoder_tokens(g, paths, persistent=False)
     _report(g, toks, "device decoder (per-op step)")
     print(f"prefill {st.prefill_ms:.2f} ms, {st.decode_steps} graph steps in {st.decode_ms:.2f} ms")
-    assert toks == g["tokens"], f"decoder {toks} != reference {g['tokens']}"
+    check_greedy_tokens(toks, g, f"device decoder, seed {g['seed']}")
 
 
 def test_persistent_step_matches_reference_engine_7b_width(cuda_dev, ckpt):
     g, paths = ckpt
     toks, st = _decoder_tokens(g, paths, persistent=True)
     _report(g, toks, "device decoder (persistent step)")
-    assert toks == g["tokens"], f"persistent step {toks} != reference {g['tokens']}"
+    check_greedy_tokens(toks, g, f"persistent step, seed {g['seed']}")
 
 
 @pytest.mark.parametrize("profile", [False, True], ids=["plain", "ProfilingBackend"])
@@ -125,7 +130,9 @@ def test_reference_engine_on_cuda_backend_7b_width(cuda_dev, ckpt, profile):
     info = G.run_engine(ENGINE_CUDA, paths, g["max_new"], profile=profile, timeout=1200, nice=False)
     _report(g, info["tokens"], info["backend"])
     print(f"generate {info['generate_seconds']:.1f} s")
-    assert info["tokens"] == g["tokens"], f"CudaBackend engine {info['tokens']} != reference {g['tokens']}"
+    same = check_greedy_tokens(info["tokens"], g, f"reference engine on CudaBackend, seed {g['seed']}")
+    if same < len(g["tokens"]):
+        print(f"CudaBackend logits' own top-2 margin at step {same}: {info['margins'][same]}")
     if profile:
         calls = info["profile"]
         n_forward = g["prompt_len"] + g["max_new"]

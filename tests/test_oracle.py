@@ -114,3 +114,15 @@ class TestLiveReference:
         np.testing.assert_array_equal(O.add_bias(acc, bias), O.ref_add_bias(acc, bias))
         for row in acc:
             assert O.argmax(row) == O.ref_argmax(row)
+
+    def test_add_matches_cpu_backend_add(self):
+        """orc_add_f16 against CpuBackend::add (cpu_backend.cpp:430-455): random
+        values of every magnitude, overflow to inf, inf + -inf, NaN, signed
+        zeros and subnormals."""
+        rng = np.random.default_rng(21)
+        a = rng.integers(0, 65536, size=1 << 18, dtype=np.uint32).astype(np.uint16)
+        b = rng.integers(0, 65536, size=1 << 18, dtype=np.uint32).astype(np.uint16)
+        edge = np.array([0x0000, 0x8000, 0x7BFF, 0xFBFF, 0x7C00, 0xFC00, 0x7E00, 0x0001, 0x8001, 0x3C00], np.uint16)
+        a = np.r_[a, np.repeat(edge, edge.size)]
+        b = np.r_[b, np.tile(edge, edge.size)]
+        np.testing.assert_array_equal(O.add(a, b), O.ref_add(a, b))

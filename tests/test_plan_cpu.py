@@ -17,7 +17,8 @@ def _shapes():
         ns.add((n, k))
     for _, parts, k in W.SWEEP_7B:
         ns.add((sum(parts), k))
-    ns |= {(4864, 896), (151936, 896), (152064, 3584), (64, 64), (131, 896), (3581, 3576), (20000, 2048)}
+    ns |= {(4864, 896), (151936, 896), (152064, 3584), (64, 64), (131, 896), (3581, 3576), (20000, 2048),
+           (3584, 18944), (512, 70000), (40000, 4104)}
     rng = np.random.default_rng(5)
     for _ in range(20):
         ns.add((int(rng.integers(8, 40000)), int(rng.integers(1, 2400)) * 8))
@@ -44,7 +45,12 @@ def test_every_plan_is_launchable(sms):
                 tiles = -(-M // 128) * -(-N // p["bn"])
             full, splits, kb = p["full_tiles"], p["tail_splits"], p["kb_per"]
             assert 0 <= full <= tiles, (M, N, K, p)
-            assert 1 <= p["grid"] <= sms, (M, N, K, p)
+            # swap-mode CTAs fit two to an SM
+            assert 1 <= p["grid"] <= (2 * sms if swap else sms), (M, N, K, p)
+            if swap and num_kb <= 32 * 64:
+                # no swap-mode unit accumulates more than 64 k-blocks in TMEM
+                assert full == 0 or num_kb <= 64, (M, N, K, p)
+                assert full == tiles or kb <= 64, (M, N, K, p)
             if full < tiles:
                 # Every K-slice owns at least one k-block and together they
                 # cover K (otherwise an accumulator would never be written).
