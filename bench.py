@@ -519,11 +519,34 @@ def configs_arm(peaks) -> dict:
 
     t = per_call_ms(layer, 1)
     flops = sum(2.0 * M * n * k for _, n, k in shapes)
-    for w in lw.values():
+    # The same outputs from four calls: q|k|v stacked into one 1152-row weight
+    # (with the three biases) and gate|up into one 9728-row weight, as a
+    # decoder holds them; rows are independent, so every output is the same.
+    src = {nm: (torch.randn(n, k, generator=gen, device="cuda") * 0.02).to(torch.bfloat16) for nm, n, k in shapes}
+    fw = {"qkv": capi.Weight(torch.cat([src["q"], src["k"], src["v"]]).data_ptr(), capi.BF16, True, 1152, 896,
+                             None, None, s0),
+          "o": capi.Weight(src["o"].data_ptr(), capi.BF16, True, 896, 896, None, None, s0),
+          "gateup": capi.Weight(torch.cat([src["gate"], src["up"]]).data_ptr(), capi.BF16, True, 9728, 896,
+                                None, None, s0),
+          "down": capi.Weight(src["down"].data_ptr(), capi.BF16, True, 896, 4864, None, None, s0)}
+    qkv_bias = torch.cat(keep)
+    fw["qkv"].attach_bias(qkv_bias.data_ptr(), capi.BF16, True, s0)
+    torch.cuda.synchronize()
+    fy = {nm: torch.empty(M, w.n, dtype=torch.float16, device="cuda") for nm, w in fw.items()}
+
+    def layer_fused(s):
+        for nm, w in fw.items():
+            src_x = xd if nm == "down" else xl
+            capi.gemm(w, src_x.data_ptr(), w.k, fy[nm].data_ptr(), w.n, M, nm == "qkv", s)
+
+    tf = per_call_ms(layer_fused, 1)
+    for w in list(lw.values()) + list(fw.values()):
         w.free()
-    out["layer_05b_m512"] = {"us": round(t * 1e3, 2), "TFLOP/s": round(flops / (t * 1e-3) / 1e12, 1),
-                             "frac_tensor_burst": round(flops / (t * 1e-3) / 1e12 / peaks["bf16_tflops"], 4),
-                             "calls": 7}
+    out["layer_05b_m512"] = {"us": round(tf * 1e3, 2), "TFLOP/s": round(flops / (tf * 1e-3) / 1e12, 1),
+                             "frac_tensor_burst": round(flops / (tf * 1e-3) / 1e12 / peaks["bf16_tflops"], 4),
+                             "calls": 4, "note": "q|k|v and gate|up stacked into one weight each",
+                             "seven_calls_us": round(t * 1e3, 2),
+                             "seven_calls_frac_tensor_burst": round(flops / (t * 1e-3) / 1e12 / peaks["bf16_tflops"], 4)}
     # lm_head + argmax
     V, H = 151936, 896
     wl = weight(V, H)

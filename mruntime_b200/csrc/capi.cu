@@ -489,33 +489,44 @@ static double unit_us(int bn, int64_t kb, int64_t active, int sms, int64_t x_row
 
 // Plan for few tokens (M <= 64), swap mode: the weight is the 128-row MMA
 // operand, so a tile is 128 weight rows x all tokens and the work is streaming
-// W.  A call's time is modelled as a fixed latency (launch, activation load,
-// epilogue), plus the K-split finish when tiles are split, plus a ramp that
-// grows with the bytes of the whole call and the bytes one CTA streams (each
-// CTA's ring of bulk copies bounds its own rate).  Swap-mode CTAs use ~108 KB
-// of shared memory, so two fit on an SM: plans may launch up to 2 x SMs CTAs.
-// The constants were fitted to graph-replayed chains of decode GEMMs on B200
-// (4864x896, 896x896 and the Qwen2.5-7B projections at 1 token, over every
-// split count and grid size).  Units never exceed kSegMinKb k-blocks, so the
-// tensor cores' accumulation stays as accurate as the reference's loop.
+// W.  Swap-mode CTAs use ~108 KB of shared memory, so two fit on an SM and
+// plans may launch up to 2 x SMs CTAs.  Candidates: every tile over the whole
+// K (one or two CTAs per SM) and, when whole tiles cannot fill two CTAs per
+// SM, every tile split along K (K-slices summed through global memory, or
+// inside thread-block clusters for 32/64-token tiles).  (Whole waves with a
+// split last wave, the normal mode's third shape, never won here: with two
+// CTAs per SM the last wave is already short.)  Their times come from a
+// linear model of the busiest CTA's streamed bytes, the call's total bytes,
+// the transposed epilogue stores, the units per CTA and the K-split finish,
+// least-squares fitted to graph-replayed chains of calls on B200 (the
+// Qwen2.5-7B projections, the 4864x896 GEMV and the 151936x896 lm_head at 1..64
+// tokens over every split count and grid; the pick is within ~2.5 % of the
+// fastest measured plan on average).  Units never exceed kSegMinKb k-blocks,
+// so the tensor cores' accumulation stays as accurate as the reference's loop.
 static TcPlan plan_swap(int64_t M, int64_t N, int64_t K, int sms) {
     const int bn = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
     const int64_t tiles = (N + 127) / 128;
     const int64_t num_kb = (K + 63) / 64;
     const bool long_k = num_kb > kSegMinKb;
-    // Bytes one k-block of a unit streams: the 128 x 64 weight tile, plus half
-    // the token rows' activations (those mostly hit L2).
-    const double kb_bytes = 128.0 * 64.0 * 2.0 + 0.5 * bn * 64.0 * 2.0;
-    const double ramp_all = static_cast<double>(tiles) * num_kb * kb_bytes / 10.0e12 * 1e6;
+    const double tokp = static_cast<double>((std::min<int64_t>(M, bn) + 3) / 4 * 4);  // tokens, whole float4 groups
+    const double kb_bytes = 128.0 * 64.0 * 2.0 + 0.5 * bn * 64.0 * 2.0;  // W tile + half the X tile per k-block
+    const double total = static_cast<double>(tiles) * num_kb * kb_bytes;
     const int64_t max_grid = 2LL * sms;
-    // us for a plan whose busiest CTA streams `cta_kb` k-blocks, with `split`
-    // when some tiles are K-split
-    auto cost = [&](int64_t cta_kb, bool split) {
-        double t = 3.25 + ramp_all + static_cast<double>(cta_kb) * kb_bytes / 80.0e9 * 1e6;
-        if (split) t += 1.0 + 0.1 * static_cast<double>(std::min<int64_t>(M, bn));
+    auto ceil_div = [](int64_t a, int64_t b) { return (a + b - 1) / b; };
+    // Predicted us: `cta_kb` k-blocks streamed by the busiest CTA, `upc` units
+    // it runs, `st_tiles` whole-K tiles whose outputs it stores itself, and
+    // the finish of `split_tiles` tiles cut into `splits` slices.
+    auto cost = [&](int64_t grid, int64_t cta_kb, int64_t upc, int64_t st_tiles, int64_t split_tiles, int64_t splits,
+                    bool cluster) {
+        double t = 3.388 + 8.595 * tokp * st_tiles / 64.0 + 12.935 * cta_kb * kb_bytes / 1e6 + 68.437 * total / 1e9 +
+                   0.421 * upc;
+        if (split_tiles > 0 && !cluster)
+            t += 0.287 + 2.013 * tokp * splits / 64.0 + 0.472 * split_tiles * splits * tokp * 512.0 / 1e6;
+        if (split_tiles > 0 && cluster)
+            t += 1.933 + 0.378 * splits * tokp / 64.0 +
+                 1.04 * static_cast<double>(std::max<int64_t>(0, grid - sms)) / sms * splits;
         return t;
     };
-    auto waves = [](int64_t units, int64_t grid) { return (units + grid - 1) / grid; };
     TcPlan best{bn, 1, static_cast<int>(tiles), 1, 0};
     double best_cost = 1e300;
     auto consider = [&](double c, const TcPlan& p) {
@@ -528,37 +539,31 @@ static TcPlan plan_swap(int64_t M, int64_t N, int64_t K, int sms) {
         // every tile over the whole K, one or two CTAs per SM
         for (int64_t cap : {static_cast<int64_t>(sms), max_grid}) {
             const int64_t grid = std::min(tiles, cap);
-            consider(cost(waves(tiles, grid) * num_kb, false),
+            const int64_t upc = ceil_div(tiles, grid);
+            consider(cost(grid, upc * num_kb, upc, upc, 0, 1, false),
                      TcPlan{bn, static_cast<int>(grid), static_cast<int>(tiles), 1, 0});
         }
-        // whole waves of one tile per SM over K, the last partial wave split
-        const int64_t full = (tiles / sms) * sms;
-        const int64_t n_tail = tiles - full;
-        if (full > 0 && n_tail > 0) {
-            for (int64_t s = 2; s <= 32 && s <= num_kb; ++s) {
-                const int64_t kb_per = (num_kb + s - 1) / s;
-                const int64_t splits = (num_kb + kb_per - 1) / kb_per;
-                if (splits < 2) continue;
-                const int64_t tail_units = n_tail * splits;
-                consider(cost(full / sms * num_kb + waves(tail_units, sms) * kb_per, true),
-                         TcPlan{bn, sms, static_cast<int>(full), static_cast<int>(splits), static_cast<int>(kb_per)});
+    }
+    // every tile split along K, when whole tiles cannot fill two CTAs per SM
+    if (long_k || tiles < max_grid) {
+        for (int64_t s = 2; s <= 32 && s <= num_kb; ++s) {
+            const int64_t kb_per = ceil_div(num_kb, s);
+            const int64_t splits = ceil_div(num_kb, kb_per);
+            if (splits < 2 || kb_per > kSegMinKb) continue;
+            const int64_t units = tiles * splits;
+            for (int64_t cap : {static_cast<int64_t>(sms), max_grid}) {
+                const int64_t grid = std::min(units, cap);
+                const int64_t upc = ceil_div(units, grid);
+                const bool cluster = bn >= 32 && splits <= 8 && grid == units;
+                consider(cost(grid, upc * kb_per, upc, 0, tiles, splits, cluster),
+                         TcPlan{bn, static_cast<int>(grid), 0, static_cast<int>(splits), static_cast<int>(kb_per)});
             }
         }
     }
-    // every tile split along K
-    for (int64_t s = 2; s <= 32 && s <= num_kb; ++s) {
-        const int64_t kb_per = (num_kb + s - 1) / s;
-        const int64_t splits = (num_kb + kb_per - 1) / kb_per;
-        if (splits < 2 || kb_per > kSegMinKb) continue;
-        const int64_t units = tiles * splits;
-        const int64_t grid = std::min(units, max_grid);
-        consider(cost(waves(units, grid) * kb_per, true),
-                 TcPlan{bn, static_cast<int>(grid), 0, static_cast<int>(splits), static_cast<int>(kb_per)});
-    }
     if (best_cost > 1e299) {
         // K beyond 32 x kSegMinKb k-blocks: the most slices the finish sums
-        const int64_t kb_per = std::max<int64_t>(1, (num_kb + 31) / 32);
-        const int64_t splits = (num_kb + kb_per - 1) / kb_per;
+        const int64_t kb_per = std::max<int64_t>(1, ceil_div(num_kb, 32));
+        const int64_t splits = ceil_div(num_kb, kb_per);
         best = TcPlan{bn, static_cast<int>(std::min(tiles * splits, max_grid)), 0, static_cast<int>(splits),
                       static_cast<int>(kb_per)};
     }
