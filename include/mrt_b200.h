@@ -358,6 +358,30 @@ int mrt_tp_allreduce_f32_to_f16(mrt_tp tp, float* partial_dev, void* out_dev, in
 int mrt_tp_allgather_cols_f16(mrt_tp tp, const void* local_dev, int64_t M, int64_t n_local,
                               void* out_dev, void* stream);
 
+/* Row-parallel outputs summed over NVLink by this library's kernels (no
+ * NCCL): the exchange the reference's o_proj and down_proj outputs need once
+ * those projections are split along K (src/models/qwen/qwen_model.cpp:256, 288).
+ * mrt_tp_p2p_init (collective, every rank) allocates and exports by CUDA IPC a
+ * region of max_count FP32 partials + max_count FP16 outputs per rank and maps
+ * the peers' regions; it fails with MRT_ERR_CUDA when peer memory cannot be
+ * mapped (then use mrt_tp_allreduce_f32_to_f16).  mrt_tp_p2p_buffers returns
+ * this rank's partial and output areas.
+ * mrt_tp_p2p_allreduce_f32_to_f16 (collective, same order on every rank):
+ * every rank's count partials (written to its partial area by the work
+ * before it on the stream) are summed in rank order, rounded once to FP16 and
+ * left in every rank's output area, identical on all ranks; when out_dev is
+ * given (not the output area) the result is also copied there as rows of
+ * row_len with stride ld_out.  Waits are bounded (2 s; mrt_sync then reports
+ * MRT_ERR_TIMEOUT).  The output area stays valid until the next exchange.
+ * mrt_tp_gemm_rowpar: mrt_gemm_f32 of this rank's K-shard into the partial
+ * area, then the exchange into y_dev [M, N] (row stride ldy). */
+int mrt_tp_p2p_init(mrt_tp tp, int64_t max_count);
+int mrt_tp_p2p_buffers(mrt_tp tp, float** partial_dev, void** out_dev);
+int mrt_tp_p2p_allreduce_f32_to_f16(mrt_tp tp, int64_t count, void* out_dev, int64_t ld_out, int64_t row_len,
+                                    void* stream);
+int mrt_tp_gemm_rowpar(mrt_tp tp, mrt_weight w, const void* x_dev, int64_t ldx, int64_t M, void* y_dev,
+                       int64_t ldy, void* stream);
+
 /* Vocabulary-sharded greedy pick: combine each rank's per-row (value, global
  * index) into the global first maximum; idx_out_dev[M] is the same on every
  * rank. */

@@ -66,6 +66,10 @@ _SIGS = {
     "mrt_gemm_f32": (_int, [_vp, _vp, _i64, _vp, _i64, _i64, _vp]),
     "mrt_gemm_swiglu": (_int, [_vp, _vp, _i64, _vp, _i64, _i64, _vp]),
     "mrt_gemm_residual": (_int, [_vp, _vp, _i64, _vp, _i64, _vp, _i64, _i64, _u32, _vp]),
+    "mrt_tp_p2p_init": (_int, [_vp, _i64]),
+    "mrt_tp_p2p_buffers": (_int, [_vp, C.POINTER(_vp), C.POINTER(_vp)]),
+    "mrt_tp_p2p_allreduce_f32_to_f16": (_int, [_vp, _i64, _vp, _i64, _i64, _vp]),
+    "mrt_tp_gemm_rowpar": (_int, [_vp, _vp, _vp, _i64, _i64, _vp, _i64, _vp]),
     "mrt_gemm_plan": (_int, [_i64, _i64, _i64, _int] + [C.POINTER(_int)] * 6),
     "mrt_gemm_host": (_int, [_vp, _vp, _vp, _i64, _u32, _vp]),
     "mrt_gemm_general": (_int, [_vp, _int, _i64, _i64, _vp, _int, _i64, _i64, _vp, _int, C.c_float, C.c_float,
@@ -314,6 +318,25 @@ class TensorParallel:
 
     def argmax(self, val_ptr: int, idx_ptr: int, M: int, out_ptr: int, stream: int | None = None):
         call("mrt_tp_argmax", self.h, val_ptr, idx_ptr, M, out_ptr, stream)
+
+    def p2p_init(self, max_count: int) -> None:
+        """Map every rank's exchange region (collective); raises MrtError if peers cannot be mapped."""
+        call("mrt_tp_p2p_init", self.h, max_count)
+
+    def p2p_buffers(self) -> tuple[int, int]:
+        """(partial, output) device pointers of this rank's exchange region."""
+        part, out = C.c_void_p(), C.c_void_p()
+        call("mrt_tp_p2p_buffers", self.h, C.byref(part), C.byref(out))
+        return part.value, out.value
+
+    def p2p_allreduce_f32_to_f16(self, count: int, out_ptr: int | None = None, ld_out: int = 0, row_len: int = 0,
+                                 stream: int | None = None) -> None:
+        call("mrt_tp_p2p_allreduce_f32_to_f16", self.h, count, out_ptr, ld_out, row_len, stream)
+
+    def gemm_rowpar(self, w: "Weight", x_ptr: int, ldx: int, M: int, y_ptr: int, ldy: int,
+                    stream: int | None = None) -> None:
+        """This rank's K-shard GEMM, summed over all ranks over NVLink, rounded once to FP16 into y."""
+        call("mrt_tp_gemm_rowpar", self.h, w.h, x_ptr, ldx, M, y_ptr, ldy, stream)
 
     def destroy(self):
         if self.h:

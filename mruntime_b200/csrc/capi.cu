@@ -717,6 +717,7 @@ static int gemm_dispatch(mrt_weight w, const void* x, int64_t ldx, void* y, int6
     a.residual = epi.residual; a.ldr = epi.ldr;
     a.am_val = epi.am_val; a.am_idx = epi.am_idx;
     a.am_chunks = static_cast<int>(4 * ((w->n + 127) / 128));
+    a.seg_kb = kSegKb;
     const int64_t tiles = tc_gemm_tiles(a);
     const int64_t n_tail = tiles - p.full;
     if (use_cluster(swap, p, tiles) && epi.am_val == nullptr) a.cluster_k = p.splits;

@@ -89,6 +89,26 @@ __device__ __forceinline__ uint16_t add_residual(uint16_t h, const uint16_t* res
     return res == nullptr ? h : add_f16(res[i], h);
 }
 
+// ------------------------------------------------------------------ cross-GPU flags
+
+// System-scope release store / acquire load of a 64-bit flag (peer memory
+// mapped by CUDA IPC, read and written over NVLink).
+__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
 // ------------------------------------------------------------------ greedy pick
 
 // (value, index) under the reference's greedy rule (inference_engine.cpp:84-95):

@@ -800,22 +800,6 @@ struct PeerArgs {
     int rank, world;
 };
 
-__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
-    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
-    unsigned long long v;
-    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
-
-__device__ __forceinline__ unsigned long long global_ns() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-    return t;
-}
-
 // Row-parallel output finished across GPUs, fused with the residual add and
 // RMSNorm that consume it (qwen_model.cpp:321-332).  Every rank's GEMM left
 // its FP32 partial rows in its own exchange buffer.  Block 0 publishes this

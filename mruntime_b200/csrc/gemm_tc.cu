@@ -33,13 +33,13 @@ constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr int kThreadsTc = 192;
 constexpr int kEpiThreads = 128;
-// Segmented accumulation (normal mode, long K): every kSegKb k-blocks the MMAs
-// move to the other TMEM accumulator and 8 epilogue warps add the finished
-// segment into FP32 registers with IEEE round-to-nearest.  The tensor cores'
-// own accumulation rounds toward zero; over thousands of k-steps that bias
-// makes the result measurably less accurate than the reference's sequential
-// FP32 loop (cpu_backend.cpp:143-166), and segments of 16 k-blocks remove it.
-constexpr int kSegKb = 16;
+// Segmented accumulation (normal mode, units longer than kSegMinKb k-blocks):
+// every kSegKb k-blocks the MMAs move to the other TMEM accumulator and 8
+// epilogue warps add the finished segment into FP32 registers with IEEE
+// round-to-nearest.  The tensor cores' own accumulation rounds toward zero;
+// over ~1200 MMAs (K = 18944) that bias makes the result ~0.4-0.9 % less
+// accurate than the reference's sequential FP32 loop (cpu_backend.cpp:143-166),
+// and segments of kSegKb k-blocks bring it back to the reference's error.
 constexpr int kThreadsSeg = 64 + 256;
 
 template <bool SEG>
@@ -563,7 +563,7 @@ __global__ void __launch_bounds__(threads_of<SEG>(), SWAP ? 2 : 1)
     static_assert(!(SEG && SWAP), "segmented accumulation is a normal-mode variant");
     using Cfg = TcCfg<BN, SWAP>;
     constexpr int kEpi = SEG ? 256 : kEpiThreads;         // epilogue threads
-    constexpr int kSegLen = SEG ? kSegKb : (1 << 30);     // k-blocks per accumulator segment
+    const int kSegLen = SEG ? max(1, a.seg_kb) : (1 << 30);  // k-blocks per accumulator segment
     constexpr int S = Cfg::kStages;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));

@@ -14,7 +14,9 @@
 
 #include <cstring>
 #include <string>
+#include <vector>
 
+#include "common.cuh"
 #include "ctx.h"
 #include "kernels.h"
 
@@ -64,6 +66,13 @@ int nccl_error(ncclResult_t r, const char* what) {
 }  // namespace
 }  // namespace mrt
 
+namespace mrt {
+namespace {
+constexpr int kP2PMaxRanks = 8;
+constexpr size_t kP2PFlagBytes = 4096;  // two rows of kP2PMaxRanks 64-bit flags, padded
+}  // namespace
+}  // namespace mrt
+
 struct mrt_tp_s {
     ncclComm_t comm = nullptr;
     int rank = 0;
@@ -71,6 +80,15 @@ struct mrt_tp_s {
     int device = -1;
     void* buf = nullptr;  // gather space
     size_t buf_bytes = 0;
+    // Peer exchange (mrt_tp_p2p_init): this rank's region -- flags, an FP32
+    // partial area of p2p_cap elements, an FP16 output area of p2p_cap --
+    // exported by CUDA IPC; every rank's region as this rank maps it; and the
+    // device counter of exchanges made so far.
+    char* p2p_region = nullptr;
+    char* p2p_peer[mrt::kP2PMaxRanks] = {};
+    int64_t p2p_cap = 0;
+    size_t p2p_part_off = 0, p2p_out_off = 0;
+    unsigned long long* p2p_epoch = nullptr;
 };
 
 using namespace mrt;
@@ -173,8 +191,28 @@ extern "C" int mrt_tp_init(int rank, int world, const void* id, size_t len, mrt_
     return MRT_OK;
 }
 
+static void p2p_release(mrt_tp tp) {
+    for (int q = 0; q < mrt::kP2PMaxRanks; ++q) {
+        if (q != tp->rank && tp->p2p_peer[q] != nullptr) cudaIpcCloseMemHandle(tp->p2p_peer[q]);
+        tp->p2p_peer[q] = nullptr;
+    }
+    if (tp->p2p_region) cudaFree(tp->p2p_region);
+    if (tp->p2p_epoch) cudaFree(tp->p2p_epoch);
+    tp->p2p_region = nullptr;
+    tp->p2p_epoch = nullptr;
+    tp->p2p_cap = 0;
+}
+
 extern "C" int mrt_tp_destroy(mrt_tp tp) {
     if (tp == nullptr) return MRT_OK;
+    if (tp->p2p_region != nullptr) {
+        // Every rank stops reading its peers' regions before any region goes.
+        cudaDeviceSynchronize();
+        int one = 1;
+        std::vector<int> all(static_cast<size_t>(tp->world));
+        tp_allgather_host(tp, &one, all.data(), sizeof(int));
+        p2p_release(tp);
+    }
     if (tp->comm) g_nccl.CommDestroy(tp->comm);
     if (tp->buf) cudaFree(tp->buf);
     delete tp;
@@ -240,4 +278,260 @@ extern "C" int mrt_tp_argmax(mrt_tp tp, const float* val_dev, const int64_t* idx
     if (r != ncclSuccess) return nccl_error(r, "ncclAllGather of argmax pairs");
     cudaError_t e = launch_argmax_combine(gv, gi, tp->world, M, idx_out_dev, s);
     return e == cudaSuccess ? MRT_OK : cuda_error(e, "argmax combine launch");
+}
+
+// ====================================================================== peer exchange
+//
+// Row-parallel outputs (o_proj, down_proj split along K) summed over NVLink
+// by this library's own kernels instead of NCCL.  Every rank's GEMM writes its
+// FP32 partial [count] into its exported region; then
+//   kernel 1  publishes "my partial is complete" (epoch e, system-scope
+//             release store into every peer's flag row 0), waits (bounded)
+//             for every peer's, and reduces this rank's 1/world slice: the
+//             world partials read over NVLink and added in rank order (the
+//             same order for every element, so every rank's result is
+//             bit-identical), rounded once to FP16 and stored into every
+//             rank's output area (peer stores) -- reduce-scatter and
+//             all-gather in one pass, 4 B read + 2 B written per element per
+//             peer instead of an FP32 all-reduce's 8 B;
+//   kernel 2  publishes "my stores into your output are complete" (flag row
+//             1), waits (bounded) for every peer's, and advances the epoch.
+// After kernel 2 every peer has finished reading this rank's partial area, so
+// the next GEMM may overwrite it; a rank writes a peer's output area only after
+// that peer published its next partial, which it does after consuming the
+// previous output (stream order).  Waits give up after 2 s with kErrPeerWait
+// (mrt_sync reports MRT_ERR_TIMEOUT); no load uses TMA or cluster broadcast.
+
+namespace mrt {
+namespace {
+
+struct P2PArgs {
+    const float* part[kP2PMaxRanks];
+    uint16_t* out[kP2PMaxRanks];
+    unsigned long long* flags[kP2PMaxRanks];
+    unsigned long long* epoch;
+    int64_t count;
+    int rank, world;
+    int* err;
+};
+
+// Threads 0 .. world-1 of the block: thread q != rank releases `epoch` into
+// peer q's flag row `row` (slot = this rank) when `publish`, then waits for
+// peer q's flag in this rank's row.  Returns the mask of ranks that arrived.
+__device__ __forceinline__ unsigned p2p_meet(const P2PArgs& a, int row, unsigned long long epoch, bool publish) {
+    __shared__ unsigned arrived;
+    if (threadIdx.x == 0) arrived = 1u << a.rank;
+    __syncthreads();
+    const int q = static_cast<int>(threadIdx.x);
+    if (q < a.world && q != a.rank) {
+        if (publish) st_release_sys(a.flags[q] + row * kP2PMaxRanks + a.rank, epoch);
+        const unsigned long long t0 = global_ns();
+        while (true) {
+            if (ld_acquire_sys(a.flags[a.rank] + row * kP2PMaxRanks + q) >= epoch) {
+                atomicOr(&arrived, 1u << q);
+                break;
+            }
+            if (global_ns() - t0 > kWaitLimitNs) {
+                raise_error(a.err, kErrPeerWait);
+                break;
+            }
+        }
+    }
+    __syncthreads();
+    return arrived;
+}
+
+__global__ void __launch_bounds__(256) p2p_reduce_kernel(const P2PArgs a) {
+    const unsigned long long epoch = *a.epoch + 1ull;
+    const unsigned all = (a.world >= 32 ? 0xFFFFFFFFu : ((1u << a.world) - 1u));
+    if (p2p_meet(a, 0, epoch, blockIdx.x == 0) != all) return;  // a peer is missing: error raised
+    const int64_t groups = a.count / 4;
+    const int64_t g0 = groups * a.rank / a.world, g1 = groups * (a.rank + 1) / a.world;
+    for (int64_t g = g0 + blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; g < g1;
+         g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        float4 v[kP2PMaxRanks];
+#pragma unroll
+        for (int q = 0; q < kP2PMaxRanks; ++q)
+            if (q < a.world) v[q] = __ldcg(reinterpret_cast<const float4*>(a.part[q]) + g);
+        float4 s = v[0];
+#pragma unroll
+        for (int q = 1; q < kP2PMaxRanks; ++q)
+            if (q < a.world) {
+                s.x = __fadd_rn(s.x, v[q].x);
+                s.y = __fadd_rn(s.y, v[q].y);
+                s.z = __fadd_rn(s.z, v[q].z);
+                s.w = __fadd_rn(s.w, v[q].w);
+            }
+        const uint2 h = make_uint2(static_cast<uint32_t>(f32_to_f16_bits(s.x)) | (static_cast<uint32_t>(f32_to_f16_bits(s.y)) << 16),
+                                   static_cast<uint32_t>(f32_to_f16_bits(s.z)) | (static_cast<uint32_t>(f32_to_f16_bits(s.w)) << 16));
+#pragma unroll
+        for (int q = 0; q < kP2PMaxRanks; ++q)
+            if (q < a.world) reinterpret_cast<uint2*>(a.out[q])[g] = h;
+    }
+    // the last count % 4 elements: the last rank's first thread
+    if (a.rank == a.world - 1 && blockIdx.x == 0 && threadIdx.x == 0) {
+        for (int64_t i = groups * 4; i < a.count; ++i) {
+            float s = a.part[0][i];
+            for (int q = 1; q < a.world; ++q) s = __fadd_rn(s, a.part[q][i]);
+            const uint16_t h = f32_to_f16_bits(s);
+            for (int q = 0; q < a.world; ++q) a.out[q][i] = h;
+        }
+    }
+}
+
+__global__ void p2p_done_kernel(const P2PArgs a) {
+    const unsigned long long epoch = *a.epoch + 1ull;
+    __threadfence_system();  // this rank's output stores (previous kernel) before the release
+    p2p_meet(a, 1, epoch, true);
+    if (threadIdx.x == 0) *a.epoch = epoch;
+}
+
+}  // namespace
+}  // namespace mrt
+
+extern "C" int mrt_tp_p2p_init(mrt_tp tp, int64_t max_count) {
+    clear_error();
+    if (tp == nullptr) return set_error(MRT_ERR_INVALID_ARG, "NULL tensor-parallel handle");
+    if (max_count <= 0) return set_error(MRT_ERR_SHAPE, "max_count must be > 0");
+    if (tp->world > kP2PMaxRanks) return set_error(MRT_ERR_INVALID_ARG, "the peer exchange serves at most 8 ranks");
+    if (tp->p2p_region != nullptr && tp->p2p_cap >= max_count) return MRT_OK;
+    DevCtx* c = current_ctx();
+    if (!c) return MRT_ERR_CUDA;
+    if (tp->p2p_region != nullptr) {
+        cudaDeviceSynchronize();
+        int one = 1;
+        std::vector<int> all(static_cast<size_t>(tp->world));
+        int rc = tp_allgather_host(tp, &one, all.data(), sizeof(int));
+        if (rc != MRT_OK) return rc;
+        p2p_release(tp);
+    }
+    auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
+    const size_t part_off = kP2PFlagBytes;
+    const size_t out_off = part_off + up(static_cast<size_t>(max_count) * 4);
+    const size_t bytes = out_off + up(static_cast<size_t>(max_count) * 2);
+    cudaError_t e = cudaMalloc(&tp->p2p_region, bytes);
+    if (e != cudaSuccess) {
+        tp->p2p_region = nullptr;
+        return cuda_error(e, "allocating the peer exchange region");
+    }
+    e = cudaMalloc(&tp->p2p_epoch, sizeof(unsigned long long));
+    if (e == cudaSuccess) e = cudaMemset(tp->p2p_region, 0, kP2PFlagBytes);
+    if (e == cudaSuccess) e = cudaMemset(tp->p2p_epoch, 0, sizeof(unsigned long long));
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        p2p_release(tp);
+        return cuda_error(e, "preparing the peer exchange region");
+    }
+    struct Rec {
+        cudaIpcMemHandle_t h;
+        int ok;
+        int pad[15];
+    } rec{};
+    rec.ok = cudaIpcGetMemHandle(&rec.h, tp->p2p_region) == cudaSuccess ? 1 : 0;
+    cudaGetLastError();
+    std::vector<Rec> recs(static_cast<size_t>(tp->world));
+    int rc = tp_allgather_host(tp, &rec, recs.data(), sizeof(Rec));
+    if (rc != MRT_OK) {
+        p2p_release(tp);
+        return rc;
+    }
+    bool ok = true;
+    for (const Rec& r : recs) ok = ok && r.ok;
+    for (int q = 0; q < tp->world && ok; ++q) {
+        if (q == tp->rank) {
+            tp->p2p_peer[q] = tp->p2p_region;
+            continue;
+        }
+        void* p = nullptr;
+        if (cudaIpcOpenMemHandle(&p, recs[static_cast<size_t>(q)].h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            cudaGetLastError();
+            ok = false;
+        } else {
+            tp->p2p_peer[q] = static_cast<char*>(p);
+        }
+    }
+    // Every rank must have mapped every peer before any of them uses the path.
+    int mine = ok ? 1 : 0;
+    std::vector<int> oks(static_cast<size_t>(tp->world));
+    rc = tp_allgather_host(tp, &mine, oks.data(), sizeof(int));
+    if (rc != MRT_OK) {
+        p2p_release(tp);
+        return rc;
+    }
+    for (int v : oks) ok = ok && v;
+    if (!ok) {
+        p2p_release(tp);
+        return set_error(MRT_ERR_CUDA, "peer memory cannot be mapped between these ranks (CUDA IPC)");
+    }
+    tp->p2p_cap = max_count;
+    tp->p2p_part_off = part_off;
+    tp->p2p_out_off = out_off;
+    return MRT_OK;
+}
+
+extern "C" int mrt_tp_p2p_buffers(mrt_tp tp, float** partial_dev, void** out_dev) {
+    clear_error();
+    if (tp == nullptr || tp->p2p_region == nullptr) return set_error(MRT_ERR_INVALID_ARG, "peer exchange not initialised");
+    if (partial_dev) *partial_dev = reinterpret_cast<float*>(tp->p2p_region + tp->p2p_part_off);
+    if (out_dev) *out_dev = tp->p2p_region + tp->p2p_out_off;
+    return MRT_OK;
+}
+
+extern "C" int mrt_tp_p2p_allreduce_f32_to_f16(mrt_tp tp, int64_t count, void* out_dev, int64_t ld_out,
+                                               int64_t row_len, void* stream) {
+    clear_error();
+    if (tp == nullptr || tp->p2p_region == nullptr) return set_error(MRT_ERR_INVALID_ARG, "peer exchange not initialised");
+    if (count < 0 || count > tp->p2p_cap) return set_error(MRT_ERR_SHAPE, "count exceeds the exchange region");
+    if (count == 0) return MRT_OK;
+    DevCtx* c = current_ctx();
+    if (!c) return MRT_ERR_CUDA;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    P2PArgs a{};
+    for (int q = 0; q < tp->world; ++q) {
+        a.part[q] = reinterpret_cast<const float*>(tp->p2p_peer[q] + tp->p2p_part_off);
+        a.out[q] = reinterpret_cast<uint16_t*>(tp->p2p_peer[q] + tp->p2p_out_off);
+        a.flags[q] = reinterpret_cast<unsigned long long*>(tp->p2p_peer[q]);
+    }
+    a.epoch = tp->p2p_epoch;
+    a.count = count;
+    a.rank = tp->rank;
+    a.world = tp->world;
+    a.err = c->d_err;
+    const int64_t per_rank = (count / 4 + tp->world - 1) / tp->world;
+    int64_t blocks = (per_rank + 255) / 256;
+    blocks = std::max<int64_t>(1, std::min<int64_t>(blocks, static_cast<int64_t>(c->sms) * 4));
+    p2p_reduce_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(a);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_error(e, "peer reduce launch");
+    p2p_done_kernel<<<1, 32, 0, s>>>(a);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_error(e, "peer exchange completion launch");
+    note_launches(2);
+    void* region_out = tp->p2p_region + tp->p2p_out_off;
+    if (out_dev != nullptr && out_dev != region_out) {
+        // The summed rows into the caller's buffer (rows of row_len, stride ld_out).
+        if (row_len <= 0 || count % row_len != 0 || ld_out < row_len)
+            return set_error(MRT_ERR_SHAPE, "count must be a whole number of rows of row_len <= ld_out");
+        e = cudaMemcpy2DAsync(out_dev, static_cast<size_t>(ld_out) * 2, region_out, static_cast<size_t>(row_len) * 2,
+                              static_cast<size_t>(row_len) * 2, static_cast<size_t>(count / row_len),
+                              cudaMemcpyDeviceToDevice, s);
+        if (e != cudaSuccess) return cuda_error(e, "copying the summed rows out");
+    }
+    return MRT_OK;
+}
+
+extern "C" int mrt_tp_gemm_rowpar(mrt_tp tp, mrt_weight w, const void* x_dev, int64_t ldx, int64_t M, void* y_dev,
+                                  int64_t ldy, void* stream) {
+    clear_error();
+    if (tp == nullptr || tp->p2p_region == nullptr) return set_error(MRT_ERR_INVALID_ARG, "peer exchange not initialised");
+    int64_t n = 0, k = 0;
+    int rc = mrt_weight_shape(w, &n, &k);
+    if (rc != MRT_OK) return rc;
+    if (M < 0) return set_error(MRT_ERR_SHAPE, "M must be >= 0");
+    if (M == 0) return MRT_OK;
+    if (M * n > tp->p2p_cap) return set_error(MRT_ERR_SHAPE, "M x N exceeds the exchange region");
+    float* part = reinterpret_cast<float*>(tp->p2p_region + tp->p2p_part_off);
+    rc = mrt_gemm_f32(w, x_dev, ldx, part, n, M, stream);
+    if (rc != MRT_OK) return rc;
+    return mrt_tp_p2p_allreduce_f32_to_f16(tp, M * n, y_dev, ldy, n, stream);
 }

@@ -1,9 +1,11 @@
-"""Tensor parallelism on two or more GPUs through the C ABI (NCCL over NVLink).
+"""Tensor parallelism on two or more GPUs through the C ABI (NCCL and the
+library's own NVLink peer exchange).
 
 Each rank uploads its shard (column-parallel fused q,k,v and vocabulary;
 row-parallel o), runs its GEMM, and the collectives assemble the result:
-all-gather of q,k,v columns, FP32 all-reduce + one rounding for o, and the
-sharded greedy pick.  Rank 0 compares with the same GEMMs on one GPU and with
+all-gather of q,k,v columns, FP32 all-reduce + one rounding for o (NCCL, and
+again through mrt_tp_gemm_rowpar's peer exchange), and the sharded greedy
+pick.  Rank 0 compares with the same GEMMs on one GPU and with
 the oracle.  Needs >= 2 GPUs; skipped otherwise."""
 import os
 import socket
@@ -73,6 +75,18 @@ def _worker(rank: int, port: int, out_dir: str):
         yo = torch.empty((M, wot.n), dtype=torch.int16, device="cuda")
         capi.gemm_f32(wot, xs.data_ptr(), k1 - k0, part.data_ptr(), wot.n, M, s)
         tp.allreduce_f32_to_f16(part.data_ptr(), yo.data_ptr(), M * wot.n, s)
+        # the same row-parallel o through the NVLink peer exchange (no NCCL),
+        # three calls in a row (the exchange's epochs advance), the second on
+        # fewer rows and into a strided output
+        tp.p2p_init(M * wot.n)
+        yo_p2p = torch.empty((M, wot.n), dtype=torch.int16, device="cuda")
+        yo_p2p_strided = torch.zeros((M - 5, wot.n + 8), dtype=torch.int16, device="cuda")
+        tp.gemm_rowpar(wot, xs.data_ptr(), k1 - k0, M, yo_p2p.data_ptr(), wot.n, s)
+        tp.gemm_rowpar(wot, xs.data_ptr(), k1 - k0, M - 5, yo_p2p_strided.data_ptr(), wot.n + 8, s)
+        tp.gemm_rowpar(wot, xs.data_ptr(), k1 - k0, M, yo_p2p.data_ptr(), wot.n, s)
+        capi.sync(s)
+        np.save(os.path.join(out_dir, f"yo_p2p_{rank}.npy"), yo_p2p.cpu().numpy().view(np.uint16))
+        np.save(os.path.join(out_dir, f"yo_p2p_strided_{rank}.npy"), yo_p2p_strided.cpu().numpy().view(np.uint16))
         # vocabulary-sharded lm_head + greedy pick
         (vb, ve), = capi.shard_rows([vocab.shape[0]], WORLD, rank)
         wv = capi.Weight(vocab.ctypes.data, capi.FP16, False, vocab.shape[0], K, [(vb, ve)], None, s)
@@ -131,6 +145,16 @@ def test_tensor_parallel_two_gpus(tmp_path):
     truth_o = O.gemm_f64(x, wo, O.BF16)
     assert np.mean(g["yo"] == g["yo1"]) > 0.9
     assert O.rel_frobenius(g["yo"], truth_o) <= O.rel_frobenius(ref_o, truth_o) * REF_ERR_SLACK
+    # NVLink peer exchange: identical on every rank, the NCCL path's sum (two
+    # partials: one FP32 add, order-free), strided and shorter calls agree
+    p2p = [np.load(tmp_path / f"yo_p2p_{r}.npy") for r in range(WORLD)]
+    strided = [np.load(tmp_path / f"yo_p2p_strided_{r}.npy") for r in range(WORLD)]
+    for r in range(1, WORLD):
+        np.testing.assert_array_equal(p2p[r], p2p[0])
+        np.testing.assert_array_equal(strided[r], strided[0])
+    np.testing.assert_array_equal(p2p[0], g["yo"])
+    np.testing.assert_array_equal(strided[0][:, : g["yo"].shape[1]], g["yo"][: strided[0].shape[0]])
+    assert not strided[0][:, g["yo"].shape[1]:].any()
     logits = O.gemm(x, O.FP16, vocab, O.FP16, trans_b=True)
     f = W.f16_bits_to_f32(logits)
     top2 = np.sort(f, axis=1)[:, -2:]
