@@ -189,6 +189,15 @@ def setup_gpu(rank: int, world: int, local: int, max_m: int):
         partial = torch.empty((max_m, wt.n), dtype=torch.float32, device="cuda") if (world > 1 and kind == "row") else None
         projs.append(Proj(name, kind, wt, x, y, partial, n, k))
     del d
+    if tp is not None:
+        # Row-parallel outputs through the library's NVLink peer exchange when
+        # every rank can map its peers' memory; NCCL otherwise.
+        tp.p2p = False
+        try:
+            tp.p2p_init(max_m * max(p.w.n for p in projs if p.partial is not None))
+            tp.p2p = True
+        except capi.MrtError:
+            pass
     torch.cuda.synchronize()
     return projs, tp, stream
 
@@ -203,6 +212,10 @@ def run_step(projs, tp, stream, M, ev=None):
             ev[0].record()
         if p.partial is None:
             capi.gemm(p.w, p.x.data_ptr(), p.x.shape[1], p.y.data_ptr(), p.w.n, M, False, stream)
+        elif tp.p2p:
+            # FP32 partial into the exchange region, summed across ranks over
+            # NVLink and rounded once; the FP16 rows land in p.y on every rank
+            tp.gemm_rowpar(p.w, p.x.data_ptr(), p.x.shape[1], M, p.y.data_ptr(), p.w.n, stream)
         else:
             capi.gemm_f32(p.w, p.x.data_ptr(), p.x.shape[1], p.partial.data_ptr(), p.w.n, M, stream)
             tp.allreduce_f32_to_f16(p.partial.data_ptr(), p.y.data_ptr(), M * p.w.n, stream)
@@ -393,7 +406,8 @@ def gpu_arm(args, rank, world, local):
            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
            "path": "mrt_gemm_host (pinned host buffers; row chunks pipelined over copy-in, compute and copy-out "
                    "streams inside each call; copies inside the timed region)" if world == 1 else
-           "pinned-host copies + mrt_gemm / mrt_gemm_f32 + mrt_tp_allreduce_f32_to_f16"}
+           "pinned-host copies + mrt_gemm / " + ("mrt_tp_gemm_rowpar (NVLink peer exchange)" if tp.p2p else
+                                                  "mrt_gemm_f32 + mrt_tp_allreduce_f32_to_f16 (NCCL)")}
 
     sweep = []
     if not args.no_sweep:
@@ -767,6 +781,10 @@ def main():
                 "config": workload_config(args.m, world, not args.no_graph), "e2e": r["e2e"], "roofline": r["roofline"],
                 "cpu_baseline": cpu, "clocks": r["clocks"], "gpu_launches": r["launches"], "sweep": r["sweep"],
                 "configs": configs, "decode": decode}
+        if r["tp"] is not None:
+            line["config"]["row_parallel_exchange"] = (
+                "NVLink peer exchange in the library's kernels (mrt_tp_gemm_rowpar)" if r["tp"].p2p else
+                "NCCL all-reduce of FP32 partials + one FP16 rounding")
         print(json.dumps(line))
     if r["tp"] is not None:
         import gc
