@@ -300,8 +300,10 @@ def time_projections(projs, tp, stream, M, iters):
     import torch
 
     out = {}
+    world = tp.world if tp is not None else 1
     for p in projs:
         g = capture(lambda s, p=p: run_step([p], tp, s, M))
+        barrier_sync(world)  # ranks start together (a row-parallel call waits for its peers)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         for _ in range(iters):

@@ -135,6 +135,22 @@ int make_tmap_f16(CUtensorMap* map, const void* base, int64_t rows, int64_t cols
     return MRT_OK;
 }
 
+int make_tmap_f16_rows64(CUtensorMap* map, const void* base, int64_t rows, int box_rows) {
+    EncodeTiledFn enc = encode_tiled_fn();
+    if (enc == nullptr) return set_error(MRT_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return set_error(MRT_ERR_INVALID_ARG, "TMA operand must be 16-byte aligned");
+    const cuuint64_t dims[2] = {64u, static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {128u};
+    const cuuint32_t box[2] = {64u, static_cast<cuuint32_t>(box_rows)};
+    const cuuint32_t estr[2] = {1u, 1u};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return set_error(MRT_ERR_CUDA, "cuTensorMapEncodeTiled failed with CUresult " + std::to_string(static_cast<int>(r)));
+    return MRT_OK;
+}
+
 }  // namespace mrt
 
 using namespace mrt;
@@ -474,7 +490,14 @@ namespace mrt {
 // no whole wave).  Split slices pay for writing and re-reading FP32 partials.
 struct TcPlan {
     int bn = 256, grid = 1, full = 0, splits = 1, kb_per = 0;
+    bool pair = false;  // SM-pair kernel (cta_group::2), 256-row tiles, whole K
 };
+
+// SM pairs for normal-mode plans (MRT_GEMM_PAIR=1 enables them).
+static bool pair_enabled() {
+    const char* v = std::getenv("MRT_GEMM_PAIR");
+    return v != nullptr && std::strcmp(v, "1") == 0;
+}
 
 static double unit_us(int bn, int64_t kb, int64_t active, int sms, int64_t x_rows) {
     const double compute = (bn / 128.0) * (static_cast<double>(kb) + 2.0) * 0.22;
@@ -570,12 +593,19 @@ static TcPlan plan_swap(int64_t M, int64_t N, int64_t K, int sms) {
     return best;
 }
 
-static TcPlan plan_tc(int64_t M, int64_t N, int64_t K, int sms) {
+static TcPlan plan_tc(int64_t M, int64_t N, int64_t K, int sms, bool tiled = true) {
     const int64_t num_m = (M + 127) / 128;
     const int64_t num_kb = (K + 63) / 64;
     const int64_t x_rows = std::min<int64_t>(M, 128);
     TcPlan best;
     double best_cost = 1e300;
+    if (tiled && pair_enabled() && M >= 256 && num_kb <= kSegMinKb && sms >= 2) {
+        // SM pairs: 256 x 256 tiles over the whole K, sms / 2 pairs.
+        const int64_t tiles = ((M + 255) / 256) * ((N + 255) / 256);
+        const int64_t pairs = std::min<int64_t>(tiles, sms / 2);
+        best = TcPlan{256, static_cast<int>(2 * pairs), static_cast<int>(tiles), 1, 0, true};
+        return best;
+    }
     for (int bn : {256, 128, 64}) {
         const int64_t tiles = num_m * ((N + bn - 1) / bn);
         // every tile over the whole K
@@ -690,7 +720,27 @@ static int gemm_dispatch(mrt_weight w, const void* x, int64_t ldx, void* y, int6
         return e == cudaSuccess ? MRT_OK : cuda_error(e, "general gemm launch");
     }
     const bool swap = M <= 64;
-    const TcPlan p = swap ? plan_swap(M, w->n, w->k, c->sms) : plan_tc(M, w->n, w->k, c->sms);
+    const TcPlan p = swap ? plan_swap(M, w->n, w->k, c->sms) : plan_tc(M, w->n, w->k, c->sms, w->tiled);
+    if (p.pair && epi.am_val == nullptr) {
+        CUtensorMap tx;
+        int rc = make_tmap_f16(&tx, x, M, w->k, ldx, 128);
+        if (rc != MRT_OK) return rc;
+        if (!w->tmap_rows_ok) {
+            rc = make_tmap_f16_rows64(&w->tmap_rows, w->data, w->n_pad * w->k_tiles, 128);
+            if (rc != MRT_OK) return rc;
+            w->tmap_rows_ok = true;
+        }
+        TcGemmArgs a{};
+        a.M = static_cast<int>(M); a.N = static_cast<int>(w->n); a.K = static_cast<int>(w->k);
+        a.w_tiled = w->data; a.w_k_tiles = w->k_tiles; a.w_prefetch = 1;
+        a.bn = p.bn; a.grid = p.grid; a.full_tiles = p.full; a.tail_splits = 1; a.kb_per = 0;
+        a.y = y; a.ldy = ldy; a.out_f32 = out_f32 ? 1 : 0; a.bias = bias; a.err_flag = c->d_err;
+        a.swiglu_lut = swiglu_lut; a.residual = epi.residual; a.ldr = epi.ldr;
+        e = launch_tc_pair(a, tx, w->tmap_rows, s);
+        if (e != cudaSuccess) return cuda_error(e, "tcgen05 pair gemm launch");
+        if (fused) *fused = swiglu_lut != nullptr;
+        return MRT_OK;
+    }
     if (swiglu_lut != nullptr) {
         const int64_t tiles = swap ? (w->n + 127) / 128 : ((M + 127) / 128) * ((w->n + p.bn - 1) / p.bn);
         if (p.full != tiles) return MRT_OK;  // K-split plan: not fused
@@ -767,7 +817,7 @@ extern "C" int mrt_gemm_plan(int64_t M, int64_t N, int64_t K, int sms, int* kern
     const bool swap = M <= 64;
     const TcPlan p = swap ? plan_swap(M, N, K, sms) : plan_tc(M, N, K, sms);
     const int64_t tiles = swap ? ((N + 127) / 128) : 0;
-    if (kernel) *kernel = swap ? (use_cluster(true, p, tiles) ? 3 : 2) : 1;
+    if (kernel) *kernel = swap ? (use_cluster(true, p, tiles) ? 3 : 2) : (p.pair ? 4 : 1);
     if (bn) *bn = p.bn;
     if (full_tiles) *full_tiles = p.full;
     if (tail_splits) *tail_splits = p.splits;

@@ -64,6 +64,8 @@ EncodeTiledFn encode_tiled_fn();
 // `ld` elements, box = 64 columns x box_rows rows, 128-byte swizzle, zero fill.
 int make_tmap_f16(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld,
                   int box_rows);
+// The same over rows of exactly 64 FP16 with no swizzle (box 64 x box_rows).
+int make_tmap_f16_rows64(CUtensorMap* map, const void* base, int64_t rows, int box_rows);
 
 // Rank and world size of a tensor-parallel handle (tp.cu).
 int tp_rank_world(mrt_tp tp, int* rank, int* world);
@@ -113,4 +115,8 @@ struct mrt_weight_s {
     // map's box must equal the kernel's W tile or the copy overruns the ring.
     CUtensorMap tmap[3];
     bool tmap_ok[3] = {false, false, false};
+    // Tiled weights: the tiles as rows of 64 FP16 ([n_pad / 128 * k_tiles * 128]
+    // rows, 64 x 128 box, no swizzle), for the SM-pair kernel's copies.
+    CUtensorMap tmap_rows;
+    bool tmap_rows_ok = false;
 };

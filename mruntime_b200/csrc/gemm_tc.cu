@@ -1016,6 +1016,358 @@ bool cluster_fits(int k) {
     return n > 0;
 }
 
+
+// ------------------------------------------------ 2-SM pairs (cta_group::2)
+//
+// Normal mode, whole-K tiles of 256 X rows x BN W rows computed by a cluster
+// of two CTAs on two SMs with tcgen05.mma.cta_group::2 (M = 256).  CTA r of
+// the pair holds X rows [256 mt + 128 r, +128) and W rows [BN nt + BN/2 r,
+// +BN/2) in its shared memory; the MMA, issued by CTA 0 alone, reads both
+// CTAs' halves and leaves rows 128 r .. of the 256 x BN product in CTA r's
+// tensor memory.  Per k-block each CTA loads 16 KB of X and BN/2 x 128 B of W
+// (32 KB at BN = 256) instead of 48 KB, so six ring stages fit where the
+// one-SM kernel has four, and every W byte crosses L2 -> SM once per pair.
+//
+// Both CTAs' copies are counted on CTA 0's `full` barrier (the copy's
+// mbarrier operand is CTA 0's, addressed through mapa); CTA 0's commits
+// arrive on both CTAs' `empty`, `tfull` and `drain` barriers (multicast to
+// the pair).  CTA 1's epilogue tells CTA 0's `tempty` by one remote arrival
+// after its 128 threads are done with the accumulator.  Copies use the
+// cta_group::2 form of the tensor copy; none broadcasts to several CTAs.
+// Every wait is bounded; the two hardware cluster barriers (after set-up,
+// before TMEM is freed) are reached by every thread unconditionally.
+
+template <int BN>
+struct PairCfg {
+    static constexpr int kABytes = kBM * kBK * 2;         // 128 X rows
+    static constexpr int kBBytes = (BN / 2) * kBK * 2;    // BN / 2 W rows
+    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr int kStages = (200 * 1024) / kStageBytes > 12 ? 12 : (200 * 1024) / kStageBytes;
+    static constexpr uint32_t kTmemCols = 2 * BN <= 256 ? 256 : 512;
+    // full[S], empty[S], tfull[2], tempty[2], drain; TMEM slot.
+    static constexpr int kBarBytes = (2 * kStages + 5) * 8 + 16;
+    static constexpr size_t kSmem = static_cast<size_t>(kStages) * kStageBytes + kBarBytes + 1024;
+};
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+                 "r"(ncols)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void tc_mma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                                uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrive once on `bar` in both CTAs of the pair when every tcgen05 operation
+// this thread issued so far has completed.
+__device__ __forceinline__ void tc_commit_pair(uint64_t* bar) {
+    const uint16_t both = 3;
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_u32(bar)),
+        "h"(both)
+        : "memory");
+}
+
+// 2-D tensor copy into this CTA's shared memory whose completion is counted
+// on the mbarrier at shared::cluster address `bar_cluster` (CTA 0's barrier).
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const void* tmap, uint32_t bar_cluster, int32_t c0,
+                                                 int32_t c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(bar_cluster)
+        : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx_local(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+// tma: X map (box 64 x 128 rows, 128-byte swizzle); tmw: the tiled weight as
+// rows of 64 (box 64 x 128, no swizzle: each box is one pre-swizzled tile).
+template <int BN>
+__global__ void __launch_bounds__(kThreadsTc, 1)
+    tc_pair_kernel(const TcGemmArgs a, const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmw) {
+    using Cfg = PairCfg<BN>;
+    constexpr int S = Cfg::kStages;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + S * Cfg::kABytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sB + S * Cfg::kBBytes);
+    uint64_t* full = bars;
+    uint64_t* empty = bars + S;
+    uint64_t* tfull = bars + 2 * S;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* drain = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);   // CTA 0: its producer's arrive.expect_tx (+ both CTAs' bytes)
+            mbar_init(&empty[s], 1);  // one multicast commit
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&tfull[i], 1);
+            mbar_init(&tempty[i], kEpiThreads + 1);  // CTA 0: its 128 epilogue threads + CTA 1's one arrival
+        }
+        mbar_init(drain, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(tmem_slot, Cfg::kTmemCols);
+        tmem_relinquish_pair();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&tma);
+        prefetch_tmap(&tmw);
+    }
+    griddep_launch_dependents();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    // Both CTAs' barriers are initialised before anything addresses the other's.
+    cluster_arrive();
+    cluster_wait();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int num_m2 = (a.M + 2 * kBM - 1) / (2 * kBM);
+    const int num_n = (a.N + BN - 1) / BN;
+    const int total = num_m2 * num_n;
+    const int pair = blockIdx.x >> 1;
+    const int npairs = gridDim.x >> 1;
+    const int num_kb = (a.K + kBK - 1) / kBK;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            const uint32_t full0 = cluster_map(smem_u32(full), 0);  // CTA 0's full[0]
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t issued = 0, issued_parity = 0;
+            bool ok = true;
+            auto load_w = [&](int u, int kb, int st) {
+                const int nt = u / num_m2;
+                // this CTA's BN / 2 W rows = BN / 256 whole 128-row tiles (BN = 256: one)
+                const int64_t wtile = (static_cast<int64_t>(nt) * BN + rank * (BN / 2)) / kBM;
+#pragma unroll
+                for (int h = 0; h < BN / 256; ++h)
+                    tma_load_2d_pair(sB + st * Cfg::kBBytes + h * (kBM * kBK * 2), &tmw, full0 + st * 8, 0,
+                                     static_cast<int32_t>(((wtile + h) * a.w_k_tiles + kb) * kBM));
+            };
+            auto load_x = [&](int u, int kb, int st) {
+                const int mt = u % num_m2;
+                tma_load_2d_pair(sA + st * Cfg::kABytes, &tma, full0 + st * 8, kb * kBK, mt * 2 * kBM + static_cast<int>(rank) * kBM);
+            };
+            auto claim = [&](int st) {
+                if (leader) mbar_arrive_expect_tx_local(&full[st], 2 * Cfg::kStageBytes);
+                issued |= 1u << st;
+                issued_parity = (issued_parity & ~(1u << st)) | (phase << st);
+            };
+            int u = pair, kb = 0;
+            // First ring pass of weight tiles before waiting for the kernel
+            // this one overlaps (weights are never written by it).
+            int pre = 0;
+            if (a.w_prefetch) {
+                int uu = u, kk = kb;
+                for (; pre < S && uu < total; ++pre) {
+                    claim(stage);
+                    load_w(uu, kk, stage);
+                    if (++kk == num_kb) {
+                        kk = 0;
+                        uu += npairs;
+                    }
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            griddep_wait();
+            {
+                int uu = u, kk = kb;
+                for (int i = 0; i < pre; ++i) {
+                    load_x(uu, kk, i);
+                    if (++kk == num_kb) {
+                        kk = 0;
+                        uu += npairs;
+                    }
+                }
+                u = uu;
+                kb = kk;
+            }
+            for (; u < total;) {
+                if (!mbar_wait(&empty[stage], phase ^ 1u, a.err_flag, kErrTmaWait)) {
+                    ok = false;
+                    break;
+                }
+                claim(stage);
+                load_w(u, kb, stage);
+                load_x(u, kb, stage);
+                if (++stage == S) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+                if (++kb == num_kb) {
+                    kb = 0;
+                    u += npairs;
+                }
+            }
+            if (!ok) {
+                // Copies still in flight land in this CTA's shared memory: wait
+                // (bounded) for the stages this thread filled last.
+                for (int s2 = 0; s2 < S; ++s2)
+                    if ((issued & (1u << s2)) && leader) mbar_wait(&full[s2], (issued_parity >> s2) & 1u, nullptr, kErrDrainWait);
+            }
+        }
+    } else if (warp == 1) {
+        griddep_wait();
+        if (lane == 0) {
+            if (leader) {
+                const uint32_t idesc = idesc_f16_f32(2 * kBM, BN);
+                int stage = 0;
+                uint32_t phase = 0;
+                int acc = 0;
+                uint32_t acc_phase = 0;
+                bool ok = true;
+                for (int u = pair; u < total && ok; u += npairs) {
+                    if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, a.err_flag, kErrMmaWait)) break;
+                    tc_fence_after();
+                    const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+                    for (int kb = 0; kb < num_kb; ++kb) {
+                        if (!mbar_wait(&full[stage], phase, a.err_flag, kErrMmaWait)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t a_addr = smem_u32(sA + stage * Cfg::kABytes);
+                        const uint32_t b_addr = smem_u32(sB + stage * Cfg::kBBytes);
+#pragma unroll
+                        for (int k = 0; k < kBK / 16; ++k)
+                            tc_mma_f16_pair(d_tmem, smem_desc_k128(a_addr + k * 32), smem_desc_k128(b_addr + k * 32),
+                                            idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                        tc_commit_pair(&empty[stage]);
+                        if (++stage == S) {
+                            stage = 0;
+                            phase ^= 1u;
+                        }
+                    }
+                    if (!ok) break;
+                    tc_commit_pair(&tfull[acc]);
+                    acc ^= 1;
+                    if (acc == 0) acc_phase ^= 1u;
+                }
+                // Both CTAs learn when every MMA (reading both CTAs' shared
+                // memory, writing both CTAs' TMEM) has completed.
+                tc_commit_pair(drain);
+            }
+            mbar_wait(drain, 0, nullptr, kErrDrainWait);
+        }
+    } else {
+        const int quad = warp & 3;
+        const int et = threadIdx.x - 64;
+        griddep_wait();
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int u = pair; u < total; u += npairs) {
+            const int mt = u % num_m2, nt = u / num_m2;
+            int ok = 1;
+            if (lane == 0) ok = mbar_wait(&tfull[acc], acc_phase, a.err_flag, kErrEpiWait) ? 1 : 0;
+            ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+            // The four warps leave together (the named barrier below needs all 128).
+            if (!epi_bar_and(ok != 0)) break;
+            tc_fence_after();
+            const int64_t row = static_cast<int64_t>(mt) * 2 * kBM + rank * kBM + quad * 32 + lane;
+            const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                __syncwarp();
+                tmem_ld_32cols(t_row + c * 32, r);
+                const int64_t col0 = static_cast<int64_t>(nt) * BN + c * 32;
+                if (row < a.M && col0 < a.N) {
+                    if (a.swiglu_lut != nullptr)
+                        store_row_chunk_swiglu(a, r, row, col0);
+                    else
+                        store_row_chunk(a, r, row, col0);
+                }
+            }
+            tc_fence_before();
+            if (leader) {
+                mbar_arrive(&tempty[acc]);
+            } else {
+                epi_bar_sync();  // this CTA's 128 threads are done with the accumulator
+                if (et == 0) mbar_arrive_cluster(&tempty[acc], 0);
+            }
+            acc ^= 1;
+            if (acc == 0) acc_phase ^= 1u;
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    // The other CTA is done too (its remote arrivals and its MMA operands).
+    cluster_arrive();
+    cluster_wait();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
+    }
+}
+
+template <int BN>
+cudaError_t launch_pair_bn(const TcGemmArgs& a, const CUtensorMap& tx, const CUtensorMap& tw, cudaStream_t s) {
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(tc_pair_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(PairCfg<BN>::kSmem));
+        if (e != cudaSuccess) return e;
+        attr_set[dev] = true;
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(a.grid));
+    cfg.blockDim = dim3(kThreadsTc);
+    cfg.dynamicSmemBytes = PairCfg<BN>::kSmem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 2;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, tc_pair_kernel<BN>, a, tx, tw);
+    if (e != cudaSuccess) return e;
+    note_launches(1);
+    return cudaGetLastError();
+}
+
 }  // namespace
 
 bool tc_cluster_ok(int bn, int k) {
@@ -1040,6 +1392,19 @@ bool tc_gemm_segmented(const TcGemmArgs& a) {
     const bool long_full = a.full_tiles > 0 && num_kb > kSegMinKb;
     const bool long_tail = a.full_tiles < tc_gemm_tiles(a) && a.kb_per > kSegMinKb;
     return long_full || long_tail;
+}
+
+cudaError_t launch_tc_pair(const TcGemmArgs& a, const CUtensorMap& tmap_x, const CUtensorMap& tmap_w_rows,
+                           cudaStream_t s) {
+    if (a.M <= 0 || a.N <= 0) return cudaSuccess;
+    // Whole-K tiles of 256 x BN, an even persistent grid of at most one pair
+    // per tile, FP16 or FP32 output (no greedy-pick partials).
+    const int tiles = ((a.M + 255) / 256) * ((a.N + a.bn - 1) / a.bn);
+    if (a.swap || a.K <= 0 || a.w_tiled == nullptr || a.grid < 2 || (a.grid & 1) != 0 || a.grid > 2 * tiles ||
+        a.full_tiles != tiles || a.tail_splits != 1 || a.am_val != nullptr || a.cluster_k != 0)
+        return cudaErrorInvalidValue;
+    if (a.bn == 256) return launch_pair_bn<256>(a, tmap_x, tmap_w_rows, s);
+    return cudaErrorInvalidValue;
 }
 
 int tc_gemm_tiles(const TcGemmArgs& a) {

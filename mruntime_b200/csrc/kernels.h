@@ -95,6 +95,12 @@ constexpr int kSegMinKb = 64;
 constexpr int kSegKb = 64;
 // Whether a normal-mode launch uses the segmented-accumulation variant.
 bool tc_gemm_segmented(const TcGemmArgs& a);
+// Normal mode on SM pairs (tcgen05 cta_group::2): tiles of 256 X rows x bn
+// (256) W rows over the whole K, a.grid = 2 x pairs (even), full_tiles =
+// every tile.  tmap_w_rows views the tiled weight as [n_pad * k_tiles * 128]
+// rows of 64 FP16 with a 64 x 128 box and no swizzle (one tile per box).
+cudaError_t launch_tc_pair(const TcGemmArgs& a, const CUtensorMap& tmap_x, const CUtensorMap& tmap_w_rows,
+                           cudaStream_t s);
 // Normal mode only: sum the K-slices of every tail tile in slice order on
 // the whole GPU, round (+bias) or keep FP32, and store.
 cudaError_t launch_reduce_tail(const TcGemmArgs& a, cudaStream_t s);

@@ -1,0 +1,102 @@
+"""The SM-pair GEMM (tcgen05.mma.cta_group::2, 256-row tiles over two SMs)
+against the one-SM kernel and the oracle.
+
+MRT_GEMM_PAIR=1 (read at every plan) makes the planner hand normal-mode
+GEMMs (M >= 256, K <= 4096, tiled weights) to the pair kernel; the same call
+without it runs the one-SM kernel.  Both accumulate every output over K in
+the same 16-wide steps, so their outputs are compared bit for bit, and the
+pair's against the reference's arithmetic within the suite's tolerance."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import BF16, FP16, abs_dot, check_close, dev_u16, f64_truth, host_u16, stream, upload
+from mruntime_b200 import capi
+from mruntime_b200 import workloads as W
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _rand(rng, shape, std):
+    return W.to_f16_bits(rng.standard_normal(shape, dtype=np.float32) * np.float32(std))
+
+
+def _run(wt, x, flags=0, out_f32=False, residual=None):
+    M, K = x.shape
+    xd = dev_u16(x)
+    if out_f32:
+        y = torch.empty((M, wt.n), dtype=torch.float32, device="cuda")
+        capi.gemm_f32(wt, xd.data_ptr(), K, y.data_ptr(), wt.n, M, stream())
+        capi.sync(stream())
+        return y.cpu().numpy()
+    y = torch.empty((M, wt.n), dtype=torch.int16, device="cuda")
+    if residual is not None:
+        rd = dev_u16(residual)
+        capi.gemm_residual(wt, xd.data_ptr(), K, rd.data_ptr(), wt.n, y.data_ptr(), wt.n, M, bool(flags), stream())
+    else:
+        capi.gemm(wt, xd.data_ptr(), K, y.data_ptr(), wt.n, M, bool(flags), stream())
+    capi.sync(stream())
+    return host_u16(y)
+
+
+def _both(fn):
+    os.environ.pop("MRT_GEMM_PAIR", None)
+    one = fn()
+    os.environ["MRT_GEMM_PAIR"] = "1"
+    try:
+        two = fn()
+    finally:
+        os.environ.pop("MRT_GEMM_PAIR", None)
+    return one, two
+
+
+# (M, N, K): ragged M and N, K of one k-block, K not a multiple of 64, the
+# 7B q|k|v and gate+up widths.
+SHAPES = [(256, 256, 64), (300, 1000, 904), (512, 4608, 3584), (2048, 2304, 3584), (257, 37888, 896)]
+
+
+@pytest.mark.parametrize("MNK", SHAPES)
+def test_pair_matches_one_sm_and_oracle(cuda_dev, MNK):
+    M, N, K = MNK
+    rng = np.random.default_rng(M + N + K)
+    x = _rand(rng, (M, K), 1.0)
+    w = W.to_bf16_bits(rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02))
+    wt = upload(w, BF16)
+    os.environ["MRT_GEMM_PAIR"] = "1"
+    p = capi.gemm_plan(M, N, K)
+    os.environ.pop("MRT_GEMM_PAIR", None)
+    assert p["pair"], p
+    one, two = _both(lambda: _run(wt, x))
+    np.testing.assert_array_equal(two, one)
+    rows = np.unique(np.r_[0:4, M // 2, M - 4:M])
+    xs = x[rows]
+    truth = f64_truth(xs, w, BF16)
+    ref = O.gemm(xs, FP16, w, BF16, trans_b=True)
+    check_close(two[rows], truth, O.rel_frobenius(ref, truth), f"pair {MNK}", absdot=abs_dot(xs, w, BF16), K=K)
+
+
+def test_pair_epilogues(cuda_dev):
+    """Bias (double rounding), FP32 output and the residual add through the
+    pair kernel equal the one-SM kernel's."""
+    rng = np.random.default_rng(77)
+    M, N, K = 384, 1152, 896
+    x = _rand(rng, (M, K), 1.0)
+    w = W.to_bf16_bits(rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02))
+    b = W.to_bf16_bits(rng.standard_normal(N, dtype=np.float32) * np.float32(0.02))
+    res = _rand(rng, (M, N), 1.0)
+    wt = upload(w, BF16)
+    bd = dev_u16(b)
+    wt.attach_bias(bd.data_ptr(), BF16, True, stream())
+    for kw in ({"flags": 1}, {"out_f32": True}, {"residual": res}):
+        one, two = _both(lambda: _run(wt, x, **kw))
+        if kw.get("out_f32"):
+            np.testing.assert_array_equal(two.view(np.uint32), one.view(np.uint32))
+        else:
+            np.testing.assert_array_equal(two, one)
+
+
+def test_pair_no_timeout(cuda_dev):
+    capi.sync(stream())
