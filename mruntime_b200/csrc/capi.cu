@@ -493,10 +493,12 @@ struct TcPlan {
     bool pair = false;  // SM-pair kernel (cta_group::2), 256-row tiles, whole K
 };
 
-// SM pairs for normal-mode plans (MRT_GEMM_PAIR=1 enables them).
-static bool pair_enabled() {
+// SM pairs for normal-mode plans: chosen by cost; MRT_GEMM_PAIR=0 never
+// uses them, MRT_GEMM_PAIR=1 always when the shape allows (read per plan).
+static int pair_mode() {
     const char* v = std::getenv("MRT_GEMM_PAIR");
-    return v != nullptr && std::strcmp(v, "1") == 0;
+    if (v == nullptr) return -1;
+    return std::strcmp(v, "0") == 0 ? 0 : (std::strcmp(v, "1") == 0 ? 1 : -1);
 }
 
 static double unit_us(int bn, int64_t kb, int64_t active, int sms, int64_t x_rows) {
@@ -599,12 +601,19 @@ static TcPlan plan_tc(int64_t M, int64_t N, int64_t K, int sms, bool tiled = tru
     const int64_t x_rows = std::min<int64_t>(M, 128);
     TcPlan best;
     double best_cost = 1e300;
-    if (tiled && pair_enabled() && M >= 256 && num_kb <= kSegMinKb && sms >= 2) {
-        // SM pairs: 256 x 256 tiles over the whole K, sms / 2 pairs.
+    const int pm = pair_mode();
+    if (tiled && pm != 0 && M >= 256 && num_kb <= kSegMinKb && sms >= 2) {
+        // SM pairs (tcgen05 cta_group::2): 256 x 256 tiles over the whole K on
+        // sms / 2 pairs.  Each CTA computes a 128 x 256 tile per k-block as in
+        // the one-SM kernel but loads a third less; measured 6-9 % faster per
+        // tile at M >= 512 (7B gate+up, q|k|v), so its waves cost 0.92 of the
+        // one-SM kernel's.
         const int64_t tiles = ((M + 255) / 256) * ((N + 255) / 256);
         const int64_t pairs = std::min<int64_t>(tiles, sms / 2);
         best = TcPlan{256, static_cast<int>(2 * pairs), static_cast<int>(tiles), 1, 0, true};
-        return best;
+        if (pm == 1) return best;
+        const int64_t waves = (tiles + pairs - 1) / pairs;
+        best_cost = 0.92 * static_cast<double>(waves) * unit_us(256, num_kb, 2 * pairs, sms, x_rows);
     }
     for (int bn : {256, 128, 64}) {
         const int64_t tiles = num_m * ((N + bn - 1) / bn);

@@ -1,9 +1,10 @@
 """The SM-pair GEMM (tcgen05.mma.cta_group::2, 256-row tiles over two SMs)
 against the one-SM kernel and the oracle.
 
-MRT_GEMM_PAIR=1 (read at every plan) makes the planner hand normal-mode
-GEMMs (M >= 256, K <= 4096, tiled weights) to the pair kernel; the same call
-without it runs the one-SM kernel.  Both accumulate every output over K in
+MRT_GEMM_PAIR=1 (read at every plan) makes the planner hand every eligible
+normal-mode GEMM (M >= 256, K <= 4096, tiled weights) to the pair kernel and
+MRT_GEMM_PAIR=0 none of them (without the variable the planner compares
+costs).  Both accumulate every output over K in
 the same 16-wide steps, so their outputs are compared bit for bit, and the
 pair's against the reference's arithmetic within the suite's tolerance."""
 import os
@@ -43,7 +44,7 @@ def _run(wt, x, flags=0, out_f32=False, residual=None):
 
 
 def _both(fn):
-    os.environ.pop("MRT_GEMM_PAIR", None)
+    os.environ["MRT_GEMM_PAIR"] = "0"
     one = fn()
     os.environ["MRT_GEMM_PAIR"] = "1"
     try:
