@@ -40,6 +40,11 @@ def test_every_plan_is_launchable(sms):
             if swap:
                 assert p["bn"] == (16 if M <= 16 else 32 if M <= 32 else 64), (M, p)
                 tiles = -(-N // 128)
+            elif p["pair"]:
+                # SM pairs: 256 x 256 tiles over the whole K, an even grid
+                assert p["bn"] == 256 and M >= 256 and num_kb <= 64, (M, N, K, p)
+                tiles = -(-M // 256) * -(-N // 256)
+                assert p["grid"] % 2 == 0 and p["full_tiles"] == tiles, (M, N, K, p)
             else:
                 assert p["bn"] in (64, 128, 256), p
                 tiles = -(-M // 128) * -(-N // p["bn"])
