@@ -63,7 +63,7 @@ def test_every_plan_is_launchable(sms):
                 assert (splits - 1) * kb < num_kb <= splits * kb, (M, N, K, p)
                 assert p["grid"] <= full + (tiles - full) * splits, (M, N, K, p)
             else:
-                assert splits == 1 and p["grid"] <= tiles, (M, N, K, p)
+                assert splits == 1 and p["grid"] <= (2 * tiles if p["pair"] else tiles), (M, N, K, p)
 
 
 def test_plan_rejects_bad_shapes():
