@@ -602,7 +602,7 @@ static TcPlan plan_tc(int64_t M, int64_t N, int64_t K, int sms, bool tiled = tru
     TcPlan best;
     double best_cost = 1e300;
     const int pm = pair_mode();
-    if (tiled && pm != 0 && M >= 256 && num_kb <= kSegMinKb && sms >= 2) {
+    if (tiled && pm != 0 && M >= 256 && sms >= 2) {
         // SM pairs (tcgen05 cta_group::2): 256 x 256 tiles over the whole K on
         // sms / 2 pairs.  Each CTA computes a 128 x 256 tile per k-block as in
         // the one-SM kernel but loads a third less; measured 6-9 % faster per
@@ -745,6 +745,7 @@ static int gemm_dispatch(mrt_weight w, const void* x, int64_t ldx, void* y, int6
         a.bn = p.bn; a.grid = p.grid; a.full_tiles = p.full; a.tail_splits = 1; a.kb_per = 0;
         a.y = y; a.ldy = ldy; a.out_f32 = out_f32 ? 1 : 0; a.bias = bias; a.err_flag = c->d_err;
         a.swiglu_lut = swiglu_lut; a.residual = epi.residual; a.ldr = epi.ldr;
+        a.seg_kb = kSegKb;
         e = launch_tc_pair(a, tx, w->tmap_rows, s);
         if (e != cudaSuccess) return cuda_error(e, "tcgen05 pair gemm launch");
         if (fused) *fused = swiglu_lut != nullptr;

@@ -448,6 +448,26 @@ __device__ __forceinline__ bool epi_bar_and(bool pred) {
 
 __device__ __forceinline__ void epi_bar_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
+// The same over the N epilogue threads of a kernel (named barrier 1).
+template <int N>
+__device__ __forceinline__ bool epi_bar_and_n(bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.and.pred q, 1, %2, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"(pred ? 1u : 0u), "n"(N)
+        : "memory");
+    return r != 0;
+}
+
+template <int N>
+__device__ __forceinline__ void epi_bar_sync_n() {
+    asm volatile("bar.sync 1, %0;" ::"n"(N) : "memory");
+}
+
 // Four consecutive outputs n..n+3 of one token (swap mode: consecutive weight
 // rows), rounded like every other store of this kernel.
 __device__ __forceinline__ void store_swap_rows4(const TcGemmArgs& a, const float4& s, int64_t n, int64_t token) {
@@ -1101,11 +1121,13 @@ __device__ __forceinline__ void mbar_arrive_expect_tx_local(uint64_t* bar, uint3
 
 // tma: X map (box 64 x 128 rows, 128-byte swizzle); tmw: the tiled weight as
 // rows of 64 (box 64 x 128, no swizzle: each box is one pre-swizzled tile).
-template <int BN>
-__global__ void __launch_bounds__(kThreadsTc, 1)
+template <int BN, bool SEG>
+__global__ void __launch_bounds__(threads_of<SEG>(), 1)
     tc_pair_kernel(const TcGemmArgs a, const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmw) {
     using Cfg = PairCfg<BN>;
     constexpr int S = Cfg::kStages;
+    constexpr int kEpi = SEG ? 256 : kEpiThreads;               // epilogue threads per CTA
+    const int kSegLen = SEG ? max(1, a.seg_kb) : (1 << 30);     // k-blocks per accumulator segment
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
@@ -1130,7 +1152,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&tfull[i], 1);
-            mbar_init(&tempty[i], kEpiThreads + 1);  // CTA 0: its 128 epilogue threads + CTA 1's one arrival
+            mbar_init(&tempty[i], kEpi + 1);  // CTA 0: its epilogue threads + CTA 1's one arrival
         }
         mbar_init(drain, 1);
         fence_barrier_init();
@@ -1251,37 +1273,121 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
                 uint32_t acc_phase = 0;
                 bool ok = true;
                 for (int u = pair; u < total && ok; u += npairs) {
-                    if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, a.err_flag, kErrMmaWait)) break;
-                    tc_fence_after();
-                    const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-                    for (int kb = 0; kb < num_kb; ++kb) {
-                        if (!mbar_wait(&full[stage], phase, a.err_flag, kErrMmaWait)) {
+                    for (int s0 = 0; s0 < num_kb && ok; s0 += kSegLen) {
+                        const int s1 = min(s0 + kSegLen, num_kb);
+                        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, a.err_flag, kErrMmaWait)) {
                             ok = false;
                             break;
                         }
                         tc_fence_after();
-                        const uint32_t a_addr = smem_u32(sA + stage * Cfg::kABytes);
-                        const uint32_t b_addr = smem_u32(sB + stage * Cfg::kBBytes);
+                        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+                        for (int kb = s0; kb < s1; ++kb) {
+                            if (!mbar_wait(&full[stage], phase, a.err_flag, kErrMmaWait)) {
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
+                            const uint32_t a_addr = smem_u32(sA + stage * Cfg::kABytes);
+                            const uint32_t b_addr = smem_u32(sB + stage * Cfg::kBBytes);
 #pragma unroll
-                        for (int k = 0; k < kBK / 16; ++k)
-                            tc_mma_f16_pair(d_tmem, smem_desc_k128(a_addr + k * 32), smem_desc_k128(b_addr + k * 32),
-                                            idesc, (kb > 0 || k > 0) ? 1u : 0u);
-                        tc_commit_pair(&empty[stage]);
-                        if (++stage == S) {
-                            stage = 0;
-                            phase ^= 1u;
+                            for (int k = 0; k < kBK / 16; ++k)
+                                tc_mma_f16_pair(d_tmem, smem_desc_k128(a_addr + k * 32), smem_desc_k128(b_addr + k * 32),
+                                                idesc, (kb > s0 || k > 0) ? 1u : 0u);
+                            tc_commit_pair(&empty[stage]);
+                            if (++stage == S) {
+                                stage = 0;
+                                phase ^= 1u;
+                            }
                         }
+                        if (!ok) break;
+                        tc_commit_pair(&tfull[acc]);
+                        acc ^= 1;
+                        if (acc == 0) acc_phase ^= 1u;
                     }
-                    if (!ok) break;
-                    tc_commit_pair(&tfull[acc]);
-                    acc ^= 1;
-                    if (acc == 0) acc_phase ^= 1u;
                 }
                 // Both CTAs learn when every MMA (reading both CTAs' shared
                 // memory, writing both CTAs' TMEM) has completed.
                 tc_commit_pair(drain);
             }
             mbar_wait(drain, 0, nullptr, kErrDrainWait);
+        }
+    } else if constexpr (SEG) {
+        // As the one-SM kernel's segmented epilogue: 8 warps, warp w reads
+        // TMEM lanes 32 (w mod 4) .. +31 and half the columns, keeps running
+        // sums of the segments in FP32 registers (round to nearest), writes
+        // the last segment's sums back and stores from there.
+        constexpr int HB = BN / 2;
+        const int quad = warp & 3;
+        const int half = (warp - 2) >> 2;
+        const int et = threadIdx.x - 64;
+        griddep_wait();
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        bool go = true;
+        for (int u = pair; u < total && go; u += npairs) {
+            const int mt = u % num_m2, nt = u / num_m2;
+            float sum[HB];
+            uint32_t t_row = 0;
+            for (int s0 = 0; s0 < num_kb; s0 += kSegLen) {
+                int ok = 1;
+                if (lane == 0) ok = mbar_wait(&tfull[acc], acc_phase, a.err_flag, kErrEpiWait) ? 1 : 0;
+                ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+                if (!epi_bar_and_n<kEpi>(ok != 0)) {
+                    go = false;
+                    break;
+                }
+                tc_fence_after();
+                t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN + half * HB);
+                const bool last = s0 + kSegLen >= num_kb;
+#pragma unroll
+                for (int c = 0; c < HB / 16; ++c) {
+                    uint32_t r[16];
+                    __syncwarp();
+                    tmem_ld_16cols(t_row + c * 16, r);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        sum[c * 16 + j] = s0 == 0 ? __uint_as_float(r[j]) : __fadd_rn(sum[c * 16 + j], __uint_as_float(r[j]));
+                    if (last) {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) r[j] = __float_as_uint(sum[c * 16 + j]);
+                        tmem_st_16cols(t_row + c * 16, r);
+                    }
+                }
+                if (last) break;  // the accumulator stays owned until the stores below
+                tc_fence_before();
+                if (leader) {
+                    mbar_arrive(&tempty[acc]);
+                } else {
+                    epi_bar_sync_n<kEpi>();
+                    if (et == 0) mbar_arrive_cluster(&tempty[acc], 0);
+                }
+                acc ^= 1;
+                if (acc == 0) acc_phase ^= 1u;
+            }
+            if (!go) break;
+            const int64_t row = static_cast<int64_t>(mt) * 2 * kBM + rank * kBM + quad * 32 + lane;
+#pragma unroll 1
+            for (int c = 0; c < HB / 32; ++c) {
+                uint32_t r[32];
+                __syncwarp();
+                tmem_ld_32cols(t_row + c * 32, r);
+                const int64_t col0 = static_cast<int64_t>(nt) * BN + half * HB + c * 32;
+                if (row < a.M && col0 < a.N) {
+                    if (a.swiglu_lut != nullptr)
+                        store_row_chunk_swiglu(a, r, row, col0);
+                    else
+                        store_row_chunk(a, r, row, col0);
+                }
+            }
+            tc_fence_before();
+            if (leader) {
+                mbar_arrive(&tempty[acc]);
+            } else {
+                epi_bar_sync_n<kEpi>();
+                if (et == 0) mbar_arrive_cluster(&tempty[acc], 0);
+            }
+            acc ^= 1;
+            if (acc == 0) acc_phase ^= 1u;
         }
     } else {
         const int quad = warp & 3;
@@ -1336,21 +1442,21 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     }
 }
 
-template <int BN>
+template <int BN, bool SEG>
 cudaError_t launch_pair_bn(const TcGemmArgs& a, const CUtensorMap& tx, const CUtensorMap& tw, cudaStream_t s) {
     static bool attr_set[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     if (!attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(tc_pair_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(tc_pair_kernel<BN, SEG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(PairCfg<BN>::kSmem));
         if (e != cudaSuccess) return e;
         attr_set[dev] = true;
     }
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(static_cast<unsigned>(a.grid));
-    cfg.blockDim = dim3(kThreadsTc);
+    cfg.blockDim = dim3(threads_of<SEG>());
     cfg.dynamicSmemBytes = PairCfg<BN>::kSmem;
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
@@ -1362,7 +1468,7 @@ cudaError_t launch_pair_bn(const TcGemmArgs& a, const CUtensorMap& tx, const CUt
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, tc_pair_kernel<BN>, a, tx, tw);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, tc_pair_kernel<BN, SEG>, a, tx, tw);
     if (e != cudaSuccess) return e;
     note_launches(1);
     return cudaGetLastError();
@@ -1403,7 +1509,9 @@ cudaError_t launch_tc_pair(const TcGemmArgs& a, const CUtensorMap& tmap_x, const
     if (a.swap || a.K <= 0 || a.w_tiled == nullptr || a.grid < 2 || (a.grid & 1) != 0 || a.grid > 2 * tiles ||
         a.full_tiles != tiles || a.tail_splits != 1 || a.am_val != nullptr || a.cluster_k != 0)
         return cudaErrorInvalidValue;
-    if (a.bn == 256) return launch_pair_bn<256>(a, tmap_x, tmap_w_rows, s);
+    const int num_kb = (a.K + kBK - 1) / kBK;
+    if (a.bn == 256) return num_kb > kSegMinKb ? launch_pair_bn<256, true>(a, tmap_x, tmap_w_rows, s)
+                                               : launch_pair_bn<256, false>(a, tmap_x, tmap_w_rows, s);
     return cudaErrorInvalidValue;
 }
 

@@ -55,8 +55,10 @@ def _both(fn):
 
 
 # (M, N, K): ragged M and N, K of one k-block, K not a multiple of 64, the
-# 7B q|k|v and gate+up widths.
-SHAPES = [(256, 256, 64), (300, 1000, 904), (512, 4608, 3584), (2048, 2304, 3584), (257, 37888, 896)]
+# 7B q|k|v and gate+up widths; then K longer than 64 k-blocks (segmented
+# accumulation in the pair kernel), the 7B down projection among them.
+SHAPES = [(256, 256, 64), (300, 1000, 904), (512, 4608, 3584), (2048, 2304, 3584), (257, 37888, 896),
+          (512, 1000, 8192), (300, 3584, 18944), (2048, 512, 18944)]
 
 
 @pytest.mark.parametrize("MNK", SHAPES)
@@ -71,7 +73,13 @@ def test_pair_matches_one_sm_and_oracle(cuda_dev, MNK):
     os.environ.pop("MRT_GEMM_PAIR", None)
     assert p["pair"], p
     one, two = _both(lambda: _run(wt, x))
-    np.testing.assert_array_equal(two, one)
+    if K <= 64 * 64:
+        # same 16-wide steps in the same order: bit for bit
+        np.testing.assert_array_equal(two, one)
+    else:
+        # 64-k-block segments summed in registers (the one-SM plan may cut K
+        # into slices instead): both within the tolerance below
+        assert np.mean(two == one) > 0.9
     rows = np.unique(np.r_[0:4, M // 2, M - 4:M])
     xs = x[rows]
     truth = f64_truth(xs, w, BF16)
