@@ -48,7 +48,7 @@ HEADLINE_M = 2048
 # M=2048, 2048x37888x3584): dram__bytes_read.sum + dram__bytes_write.sum of
 # one launch in an ncu capture of this kernel build (the capture's command
 # and date are kept with the kernel's profile summary).
-GATEUP_TRAFFIC_BYTES = 418244608
+GATEUP_TRAFFIC_BYTES = 423869952
 
 
 def parse_args():
@@ -355,6 +355,12 @@ def e2e_host_buffers(projs, tp, stream, M, steps, world):
     return max_over_ranks(start.elapsed_time(end), world) / steps, h2d, d2h
 
 
+def WL_plan_pair(M: int, N: int, K: int) -> bool:
+    from mruntime_b200 import capi
+
+    return bool(capi.gemm_plan(M, N, K).get("pair"))
+
+
 def step_flops(M: int) -> float:
     return WL.sweep_flops(M)
 
@@ -395,7 +401,8 @@ def gpu_arm(args, rank, world, local):
     peak = peaks["bf16_tflops"]
     roofline = {"bound": "tensor", "achieved": round(dom_tflops, 1), "peak": peak, "unit": "TFLOP/s",
                 "frac": round(dom_tflops / peak, 4), "traffic": GATEUP_TRAFFIC_BYTES,
-                "kernel": f"tc_gemm_kernel gate+up {M}x{gate.w.n}x{gate.w.k} (rank-local shard)",
+                "kernel": f"{'tc_pair_kernel' if WL_plan_pair(M, gate.w.n, gate.w.k) else 'tc_gemm_kernel'} gate+up "
+                          f"{M}x{gate.w.n}x{gate.w.k} (rank-local shard)",
                 "peak_source": f"{peaks['source']} bf16 cuBLAS 8192^3, burst (timed alone like this kernel)",
                 "frac_of_sustained": round(dom_tflops / peaks["bf16_tflops_sustained"], 4),
                 "sustained_peak": peaks["bf16_tflops_sustained"],
