@@ -611,7 +611,11 @@ static TcPlan plan_tc(int64_t M, int64_t N, int64_t K, int sms, bool tiled = tru
         const int64_t tiles = ((M + 255) / 256) * ((N + 255) / 256);
         const int64_t pairs = std::min<int64_t>(tiles, sms / 2);
         best = TcPlan{256, static_cast<int>(2 * pairs), static_cast<int>(tiles), 1, 0, true};
-        if (pm == 1) return best;
+        // With at least a full wave of pair tiles the pairs win outright
+        // (measured: also at 1.5 waves, against the one-SM kernel's K-split
+        // tails, e.g. 7B o and down at M = 2048); below it they leave SMs idle
+        // and compete on cost.
+        if (pm == 1 || tiles >= sms / 2) return best;
         const int64_t waves = (tiles + pairs - 1) / pairs;
         best_cost = 0.92 * static_cast<double>(waves) * unit_us(256, num_kb, 2 * pairs, sms, x_rows);
     }
