@@ -70,9 +70,11 @@ int mrt_init(int device);
 /* Text of the last error raised on this thread ("" if none). */
 const char* mrt_last_error_string(void);
 
-/* Wait for all work on `stream`, then read and clear the device-side error
- * flag that bounded waits inside the kernels set when they give up.
- * Returns MRT_ERR_TIMEOUT if a kernel reported a timed-out wait. */
+/* Wait for all work on `stream` (and for the host copies that
+ * mrt_gemm_host_async queued on the library's copy streams), then read and
+ * clear the device-side error flag that bounded waits inside the kernels set
+ * when they give up.  Returns MRT_ERR_TIMEOUT if a kernel reported a
+ * timed-out wait. */
 int mrt_sync(void* stream);
 
 /* Grow the context's scratch buffer to at least `bytes` now (call before
@@ -216,6 +218,16 @@ int mrt_gemm_residual(mrt_weight w, const void* x_dev, int64_t ldx, const void* 
  * product, copies y back and waits.  x is [M, K] and y [M, N], both dense. */
 int mrt_gemm_host(mrt_weight w, const void* x_host, void* y_host, int64_t M, unsigned flags,
                   void* stream);
+
+/* mrt_gemm_host without waiting, for hosts that queue several products on
+ * host buffers: both buffers must be page-locked (cudaHostAlloc /
+ * cudaHostRegister) and stay valid, x unmodified and y unread, until
+ * mrt_sync(stream) returns.  Rows travel in chunks on the library's copy
+ * streams as in mrt_gemm_host; consecutive calls use two device staging sets
+ * in turn, so one call's copies to the host overlap the next call's copies to
+ * the device and its products.  Every call of a thread must use one stream. */
+int mrt_gemm_host_async(mrt_weight w, const void* x_host, void* y_host, int64_t M, unsigned flags,
+                        void* stream);
 
 /*
  * The full Backend::gemm contract (include/mruntime/backend.h:13-21) for call

@@ -72,6 +72,7 @@ _SIGS = {
     "mrt_tp_gemm_rowpar": (_int, [_vp, _vp, _vp, _i64, _i64, _vp, _i64, _vp]),
     "mrt_gemm_plan": (_int, [_i64, _i64, _i64, _int] + [C.POINTER(_int)] * 6),
     "mrt_gemm_host": (_int, [_vp, _vp, _vp, _i64, _u32, _vp]),
+    "mrt_gemm_host_async": (_int, [_vp, _vp, _vp, _i64, _u32, _vp]),
     "mrt_gemm_general": (_int, [_vp, _int, _i64, _i64, _vp, _int, _i64, _i64, _vp, _int, C.c_float, C.c_float,
                                 _int, _int, _vp]),
     "mrt_argmax_f16": (_int, [_vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp]),
@@ -258,6 +259,12 @@ def gemm_residual(w: Weight, x_ptr: int, ldx: int, res_ptr: int, ldr: int, y_ptr
 def gemm_host(w: Weight, x_host_ptr: int, y_host_ptr: int, M: int, bias: bool = False,
               stream: int | None = None) -> None:
     call("mrt_gemm_host", w.h, x_host_ptr, y_host_ptr, M, GEMM_BIAS if bias else 0, stream)
+
+
+def gemm_host_async(w: Weight, x_host_ptr: int, y_host_ptr: int, M: int, bias: bool = False,
+                    stream: int | None = None) -> None:
+    """mrt_gemm_host without the wait (pinned buffers; valid until sync())."""
+    call("mrt_gemm_host_async", w.h, x_host_ptr, y_host_ptr, M, GEMM_BIAS if bias else 0, stream)
 
 
 def gemm_general(a_ptr, a_dtype, a_shape, b_ptr, b_dtype, b_shape, c_ptr, c_dtype, alpha=1.0, beta=0.0,

@@ -185,6 +185,9 @@ extern "C" int mrt_sync(void* stream) {
     DevCtx* c = current_ctx();
     if (!c) return MRT_ERR_CUDA;
     cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+    // the host-buffer copies queued by mrt_gemm_host_async
+    if (e == cudaSuccess && c->io_out != nullptr) e = cudaStreamSynchronize(c->io_out);
+    if (e == cudaSuccess && c->io_in != nullptr) e = cudaStreamSynchronize(c->io_in);
     if (e != cudaSuccess) return cuda_error(e, "cudaStreamSynchronize");
     int flag = 0;
     e = cudaMemcpy(&flag, c->d_err, sizeof(int), cudaMemcpyDeviceToHost);
@@ -988,6 +991,68 @@ extern "C" int mrt_gemm_host(mrt_weight w, const void* x_host, void* y_host, int
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) return cuda_error(e, "waiting for the host-buffer gemm");
     return MRT_OK;
+}
+
+extern "C" int mrt_gemm_host_async(mrt_weight w, const void* x_host, void* y_host, int64_t M, unsigned flags,
+                                   void* stream) {
+    clear_error();
+    if (w == nullptr) return set_error(MRT_ERR_INVALID_ARG, "NULL weight");
+    if (M < 0) return set_error(MRT_ERR_SHAPE, "M must be >= 0");
+    if (M == 0) return MRT_OK;
+    if (x_host == nullptr || y_host == nullptr) return set_error(MRT_ERR_INVALID_ARG, "NULL x or y");
+    if (!host_pinned(x_host) || !host_pinned(y_host))
+        return set_error(MRT_ERR_INVALID_ARG, "mrt_gemm_host_async needs page-locked (pinned) host buffers");
+    DevCtx* c = current_ctx();
+    if (!c) return MRT_ERR_CUDA;
+    int rc = io_pipeline_init(c);
+    if (rc != MRT_OK) return rc;
+    cudaError_t e = cudaSuccess;
+    for (int k = 0; k < 2 && e == cudaSuccess; ++k)
+        if (c->a_free[k] == nullptr) e = cudaEventCreateWithFlags(&c->a_free[k], cudaEventDisableTiming);
+    if (e != cudaSuccess) return cuda_error(e, "creating the staging events");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const bool bias = (flags & MRT_GEMM_BIAS) != 0;
+    const int set = c->a_next;
+    c->a_next ^= 1;
+    const size_t xb = static_cast<size_t>(M * w->k) * 2, yb = static_cast<size_t>(M * w->n) * 2;
+    if (c->ax_bytes[set] < xb || c->ay_bytes[set] < yb) {
+        // Growing a set waits for its last user (ensure_buffer synchronises).
+        rc = ensure_buffer(&c->ax[set], &c->ax_bytes[set], xb, "allocating input staging");
+        if (rc == MRT_OK) rc = ensure_buffer(&c->ay[set], &c->ay_bytes[set], yb, "allocating output staging");
+        if (rc != MRT_OK) return rc;
+    }
+    // This set's previous call is done with it (its last copy to the host);
+    // the other set's call may still be copying in either direction.
+    if ((e = cudaStreamWaitEvent(c->io_in, c->a_free[set], 0)) != cudaSuccess ||
+        (e = cudaStreamWaitEvent(s, c->a_free[set], 0)) != cudaSuccess)
+        return cuda_error(e, "ordering the staging set");
+    int64_t chunk = io_chunk_rows(M, w->n, w->k);
+    if (chunk == 0) chunk = M;
+    const int64_t n_chunks = (M + chunk - 1) / chunk;
+    const char* x8 = static_cast<const char*>(x_host);
+    char* y8 = static_cast<char*>(y_host);
+    uint16_t* dx = static_cast<uint16_t*>(c->ax[set]);
+    uint16_t* dy = static_cast<uint16_t*>(c->ay[set]);
+    for (int64_t i = 0; i < n_chunks; ++i) {
+        const int slot = static_cast<int>(i % DevCtx::kIoChunks);
+        const int64_t r0 = i * chunk, rows = std::min(chunk, M - r0);
+        const size_t xo = static_cast<size_t>(r0 * w->k), yo = static_cast<size_t>(r0 * w->n);
+        e = cudaMemcpyAsync(dx + xo, x8 + xo * 2, static_cast<size_t>(rows * w->k) * 2, cudaMemcpyHostToDevice,
+                            c->io_in);
+        if (e == cudaSuccess) e = cudaEventRecord(c->io_h2d[slot], c->io_in);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(s, c->io_h2d[slot], 0);
+        if (e != cudaSuccess) return cuda_error(e, "queueing a chunk's copy to the device");
+        rc = gemm_dispatch(w, dx + xo, w->k, dy + yo, w->n, rows, false, bias, s);
+        if (rc != MRT_OK) return rc;
+        e = cudaEventRecord(c->io_mm[slot], s);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(c->io_out, c->io_mm[slot], 0);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(y8 + yo * 2, dy + yo, static_cast<size_t>(rows * w->n) * 2, cudaMemcpyDeviceToHost,
+                                c->io_out);
+        if (e != cudaSuccess) return cuda_error(e, "queueing a chunk's copy to the host");
+    }
+    e = cudaEventRecord(c->a_free[set], c->io_out);
+    return e == cudaSuccess ? MRT_OK : cuda_error(e, "recording the staging set's release");
 }
 
 extern "C" int mrt_gemm_general(const void* a_dev, int a_dtype, int64_t a_rows, int64_t a_cols,

@@ -37,6 +37,14 @@ struct DevCtx {
     cudaEvent_t io_start = nullptr;
     cudaEvent_t io_h2d[kIoChunks] = {};
     cudaEvent_t io_mm[kIoChunks] = {};
+    // mrt_gemm_host_async: two staging sets used in turn, each free again once
+    // the event recorded after its last copy to the host has completed.
+    void* ax[2] = {};
+    size_t ax_bytes[2] = {};
+    void* ay[2] = {};
+    size_t ay_bytes[2] = {};
+    cudaEvent_t a_free[2] = {};
+    int a_next = 0;
 };
 
 // Record an error for mrt_last_error_string() and return its code.

@@ -536,3 +536,33 @@ def test_long_k_accumulates_in_segments(cuda_dev, MNK):
     rows = np.unique(np.r_[0:16, M // 2, M - 16:M])
     _, _, same = _check_against_oracle(x, w, BF16, y, rows, what=f"segmented M={M} N={N} K={K}")
     assert same > 0.9
+
+
+def test_host_async_matches_host_call(cuda_dev):
+    """mrt_gemm_host_async: several products queued on pinned buffers (the two
+    staging sets in turn, different weights and sizes), one wait; each equals
+    the synchronous mrt_gemm_host call bit for bit (same row chunks).
+    Pageable buffers are refused."""
+    rng = np.random.default_rng(31)
+    cases = [(2048, 3584, 896), (300, 4608, 3584), (64, 896, 896), (1024, 3584, 3584)]
+    ws, xs, ys, want = [], [], [], []
+    for M, N, K in cases:
+        w = rand_w(rng, (N, K), BF16)
+        wt = upload(w, BF16)
+        x = torch.from_numpy(rand_f16(rng, (M, K)).view(np.int16)).pin_memory()
+        y_sync = torch.empty((M, N), dtype=torch.int16).pin_memory()
+        capi.gemm_host(wt, x.data_ptr(), y_sync.data_ptr(), M, False, stream())
+        ws.append(wt)
+        xs.append(x)
+        ys.append(torch.zeros((M, N), dtype=torch.int16).pin_memory())
+        want.append(y_sync.numpy().copy())
+    for _ in range(2):
+        for wt, x, y, (M, N, K) in zip(ws, xs, ys, cases):
+            capi.gemm_host_async(wt, x.data_ptr(), y.data_ptr(), M, False, stream())
+        capi.sync(stream())
+        for y, w_ in zip(ys, want):
+            np.testing.assert_array_equal(y.numpy(), w_)
+    pageable = np.zeros((64, 896), np.uint16)
+    out = np.zeros((64, 896), np.uint16)
+    with pytest.raises(capi.MrtError):
+        capi.gemm_host_async(ws[2], pageable.ctypes.data, out.ctypes.data, 64, False, stream())
