@@ -386,7 +386,10 @@ def test_gemm_swiglu(cuda_dev, MIK):
     w = rand_w(rng, (2 * I, K), BF16)  # row 2j = gate j, row 2j + 1 = up j
     wt = upload(w, BF16)
     p = capi.gemm_plan(M, 2 * I, K)
-    tiles = -(-2 * I // 128) if p["kernel"] == "tcgen05-swap" else -(-M // 128) * -(-2 * I // p["bn"])
+    if p["pair"]:
+        tiles = -(-M // 256) * -(-2 * I // 256)  # SM pairs: 256-row tiles, always the whole K
+    else:
+        tiles = -(-2 * I // 128) if p["kernel"] == "tcgen05-swap" else -(-M // 128) * -(-2 * I // p["bn"])
     fused = p["full_tiles"] == tiles
     assert fused == (I in (18944,)), p  # the shapes above cover both routes
     y = gemm(wt, x)  # same plan: the same FP16 gate and up values
