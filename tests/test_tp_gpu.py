@@ -161,3 +161,69 @@ def test_tensor_parallel_two_gpus(tmp_path):
     decisive = (top2[:, 1] - top2[:, 0]) > 2 * 2.0 ** (np.floor(np.log2(np.abs(top2[:, 1]))) - 10)
     ref_picks = np.array([O.argmax(r) for r in logits])
     assert np.all(g["picks"][decisive] == ref_picks[decisive])
+
+
+def _exchange_worker(rank: int, world: int, port: int, out_dir: str):
+    """Row-parallel o through the NVLink peer exchange at `world` ranks, five
+    calls in a row on two sizes."""
+    import datetime
+
+    import torch.distributed as dist
+
+    from mruntime_b200 import capi
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    tp = None
+    try:
+        capi.init(rank)
+        s = torch.cuda.current_stream().cuda_stream
+        uid = [capi.TensorParallel.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        tp = capi.TensorParallel(rank, world, uid[0])
+        x, _, _, wo, _ = _inputs()
+        M, K = x.shape
+        k0, k1 = capi.shard_cols(K, world, rank)
+        wot = capi.Weight(wo.ctypes.data, capi.BF16, False, wo.shape[0], K, None, (k0, k1), s)
+        xs = torch.from_numpy(np.ascontiguousarray(x[:, k0:k1]).view(np.int16)).cuda()
+        tp.p2p_init(M * wot.n)
+        y = torch.empty((M, wot.n), dtype=torch.int16, device="cuda")
+        y_short = torch.empty((M - 11, wot.n), dtype=torch.int16, device="cuda")
+        for i in range(5):
+            if i % 2:
+                tp.gemm_rowpar(wot, xs.data_ptr(), k1 - k0, M - 11, y_short.data_ptr(), wot.n, s)
+            else:
+                tp.gemm_rowpar(wot, xs.data_ptr(), k1 - k0, M, y.data_ptr(), wot.n, s)
+        capi.sync(s)
+        np.save(os.path.join(out_dir, f"y_{rank}.npy"), y.cpu().numpy().view(np.uint16))
+        np.save(os.path.join(out_dir, f"ys_{rank}.npy"), y_short.cpu().numpy().view(np.uint16))
+        dist.barrier()
+    finally:
+        if tp is not None:
+            tp.destroy()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 3,
+                    reason="needs three or more GPUs")
+def test_peer_exchange_every_gpu(tmp_path):
+    """The peer exchange on every GPU of the box (up to 8 ranks): every rank
+    holds the same rows, within the tolerance of the reference's arithmetic."""
+    import torch.multiprocessing as mp
+
+    from oracle import oracle as O
+
+    world = min(torch.cuda.device_count(), 8)
+    mp.start_processes(_exchange_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+                       start_method="spawn", join=True)
+    x, _, _, wo, _ = _inputs()
+    ys = [np.load(tmp_path / f"y_{r}.npy") for r in range(world)]
+    shorts = [np.load(tmp_path / f"ys_{r}.npy") for r in range(world)]
+    for r in range(1, world):
+        np.testing.assert_array_equal(ys[r], ys[0])
+        np.testing.assert_array_equal(shorts[r], shorts[0])
+    np.testing.assert_array_equal(shorts[0], ys[0][: shorts[0].shape[0]])
+    truth = O.gemm_f64(x, wo, O.BF16)
+    ref = O.gemm(x, O.FP16, wo, O.BF16, trans_b=True)
+    assert O.rel_frobenius(ys[0], truth) <= O.rel_frobenius(ref, truth) * REF_ERR_SLACK
