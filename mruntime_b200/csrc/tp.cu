@@ -12,6 +12,7 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -596,11 +597,17 @@ extern "C" int mrt_tp_gemm_rowpar(mrt_tp tp, mrt_weight w, const void* x_dev, in
     DevCtx* c = current_ctx();
     if (!c) return MRT_ERR_CUDA;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    // Fused: the GEMM stores each FP32 row straight into its owner's region
-    // ([source rank][rows per rank][N]); the owner sums from its own memory.
+    // Fused (MRT_TP_SCATTER=1, read per call): the GEMM stores each FP32 row
+    // straight into its owner's region ([source rank][rows per rank][N]) and
+    // the owner sums from its own memory.  Measured slower than the two-pass
+    // exchange on 2 and 4 B200s (7B o at M = 2048: 171 / 219 us against 129 /
+    // 161 for the GEMM + the exchange): the epilogue's row-per-thread stores
+    // reach a peer as 16-byte pieces, and the tensor cores wait for them.
+    const char* scatter_env = std::getenv("MRT_TP_SCATTER");
+    const bool scatter = scatter_env != nullptr && std::strcmp(scatter_env, "1") == 0;
     const int64_t rpr = (M + tp->world - 1) / tp->world;
     const bool fits = static_cast<int64_t>(tp->world) * rpr * n <= tp->p2p_cap && (rpr * n) % 8 == 0;
-    if (fits) {
+    if (scatter && fits) {
         float* peers[kP2PMaxRanks] = {};
         for (int q = 0; q < tp->world; ++q) peers[q] = reinterpret_cast<float*>(tp->p2p_peer[q] + tp->p2p_part_off);
         rc = gemm_rowpar_scatter(w, x_dev, ldx, M, peers, tp->rank, tp->world, rpr, s);
@@ -637,7 +644,7 @@ extern "C" int mrt_tp_gemm_rowpar(mrt_tp tp, mrt_weight w, const void* x_dev, in
         if (rc != MRT_ERR_UNSUPPORTED) return rc;
         clear_error();
     }
-    // Unfused: the whole partial in this rank's area, then the exchange.
+    // Two passes: the whole partial in this rank's area, then the exchange.
     float* part = reinterpret_cast<float*>(tp->p2p_region + tp->p2p_part_off);
     rc = mrt_gemm_f32(w, x_dev, ldx, part, n, M, stream);
     if (rc != MRT_OK) return rc;
