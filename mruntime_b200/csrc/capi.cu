@@ -694,9 +694,6 @@ struct GemmEpi {
     int64_t ldr = 0;
     float* am_val = nullptr;             // greedy-pick partials (swap mode; see TcGemmArgs)
     int64_t* am_idx = nullptr;
-    float* const* xpeer = nullptr;       // row-parallel scatter of FP32 rows (see TcGemmArgs)
-    int xrank = 0, xworld = 0;
-    int64_t xrpr = 0;
 };
 
 // Shared body of mrt_gemm / mrt_gemm_f32 / mrt_gemm_residual and the fused
@@ -726,14 +723,6 @@ static int gemm_dispatch(mrt_weight w, const void* x, int64_t ldx, void* y, int6
     cudaError_t e;
     if (swiglu_lut != nullptr && (!fast || (w->n & 1) != 0)) return MRT_OK;  // not fused: the caller falls back
     if (epi.am_val != nullptr && (!fast || M > 64 || out_f32 || swiglu_lut != nullptr)) return MRT_OK;  // not fused
-    if (epi.xworld > 0 && (!fast || !out_f32 || swiglu_lut != nullptr || epi.am_val != nullptr || epi.xworld > 8))
-        return set_error(MRT_ERR_UNSUPPORTED, "row-parallel scatter needs the tensor-core path and an FP32 output");
-    auto set_scatter = [&](TcGemmArgs& t) {
-        for (int q = 0; q < epi.xworld; ++q) t.xpeer[q] = epi.xpeer[q];
-        t.xrank = epi.xrank;
-        t.xworld = epi.xworld;
-        t.xrpr = epi.xrpr;
-    };
     if (!fast) {
         GeneralGemmArgs g{};
         g.a = x; g.a_dtype = MRT_FP16; g.a_cols0 = ldx;
@@ -764,7 +753,6 @@ static int gemm_dispatch(mrt_weight w, const void* x, int64_t ldx, void* y, int6
         a.y = y; a.ldy = ldy; a.out_f32 = out_f32 ? 1 : 0; a.bias = bias; a.err_flag = c->d_err;
         a.swiglu_lut = swiglu_lut; a.residual = epi.residual; a.ldr = epi.ldr;
         a.seg_kb = kSegKb;
-        set_scatter(a);
         e = launch_tc_pair(a, tx, w->tmap_rows, s);
         if (e != cudaSuccess) return cuda_error(e, "tcgen05 pair gemm launch");
         if (fused) *fused = swiglu_lut != nullptr;
@@ -797,7 +785,6 @@ static int gemm_dispatch(mrt_weight w, const void* x, int64_t ldx, void* y, int6
     a.am_val = epi.am_val; a.am_idx = epi.am_idx;
     a.am_chunks = static_cast<int>(4 * ((w->n + 127) / 128));
     a.seg_kb = kSegKb;
-    set_scatter(a);
     const int64_t tiles = tc_gemm_tiles(a);
     const int64_t n_tail = tiles - p.full;
     if (use_cluster(swap, p, tiles) && epi.am_val == nullptr) a.cluster_k = p.splits;
@@ -825,17 +812,6 @@ static int gemm_dispatch(mrt_weight w, const void* x, int64_t ldx, void* y, int6
         if (e != cudaSuccess) return cuda_error(e, "split-K reduction launch");
     }
     return MRT_OK;
-}
-
-int gemm_rowpar_scatter(mrt_weight w, const void* x, int64_t ldx, int64_t M, float* const* peers, int rank,
-                        int world, int64_t rows_per_rank, cudaStream_t s) {
-    GemmEpi epi;
-    epi.xpeer = peers;
-    epi.xrank = rank;
-    epi.xworld = world;
-    epi.xrpr = rows_per_rank;
-    // y is not written under the scatter; ldy = N is the rows' stride in the regions
-    return gemm_dispatch(w, x, ldx, peers[rank], w->n, M, true, false, s, nullptr, nullptr, epi);
 }
 
 int gemm_swiglu(mrt_weight w, const void* x, int64_t ldx, void* act, int64_t ld_act, int64_t M,

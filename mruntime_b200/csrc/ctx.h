@@ -88,13 +88,6 @@ int tp_allgather_host(mrt_tp tp, const void* in, void* out, size_t bytes);
 // launches nothing and sets *fused = false.
 int gemm_swiglu(mrt_weight w, const void* x, int64_t ldx, void* act, int64_t ld_act, int64_t M,
                 const uint16_t* lut, cudaStream_t s, bool* fused);
-// mrt_gemm_f32 of a row-parallel K-shard whose FP32 output rows go straight
-// to their owner rank's exchange region over NVLink (rank o owns rows
-// [o * rows_per_rank, (o + 1) * rows_per_rank); region q is peers[q], laid out
-// [source rank][rows_per_rank][N]).  MRT_ERR_UNSUPPORTED when the shape needs
-// the general kernel.
-int gemm_rowpar_scatter(mrt_weight w, const void* x, int64_t ldx, int64_t M, float* const* peers, int rank,
-                        int world, int64_t rows_per_rank, cudaStream_t s);
 // The FP16 SiLU table of a device (ops.cu; nullptr if it cannot be built).
 const uint16_t* silu_lut_for_device(int device);
 // act[m][i] = fp16(lut[gu[m][2i]] * gu[m][2i+1]) for i < I (ops.cu).

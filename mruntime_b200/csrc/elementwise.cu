@@ -115,7 +115,7 @@ __global__ void reduce_tail_kernel(const TcGemmArgs a, int num_m, int n_tail) {
         const float v[4] = {s.x, s.y, s.z, s.w};
         for (int j = 0; j < 4 && col + j < a.N; ++j) {
             if (a.out_f32) {
-                f32_out_row(a, row)[col + j] = v[j];
+                static_cast<float*>(a.y)[row * a.ldy + col + j] = v[j];
             } else {
                 static_cast<uint16_t*>(a.y)[row * a.ldy + col + j] =
                     add_residual(round_out(v[j], a.bias, col + j), a.residual, row * a.ldr + col + j);

@@ -121,7 +121,7 @@ __device__ __forceinline__ void store_partial_chunk(const TcGemmArgs& a, const u
 __device__ __forceinline__ void store_row_chunk(const TcGemmArgs& a, const uint32_t (&r)[32],
                                                 int64_t row, int64_t col0) {
     if (a.out_f32) {
-        float* dst = f32_out_row(a, row) + col0;
+        float* dst = static_cast<float*>(a.y) + row * a.ldy + col0;
         const bool vec = col0 + 32 <= a.N && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0);
         if (vec) {
 #pragma unroll
@@ -183,7 +183,7 @@ __device__ __forceinline__ void store_swap_chunk(const TcGemmArgs& a, const uint
         const int64_t m = m0 + j;
         if (m >= a.M) break;  // uniform over the warp
         if (a.out_f32) {
-            if (in) f32_out_row(a, m)[n] = __uint_as_float(r[j]);
+            if (in) static_cast<float*>(a.y)[m * a.ldy + n] = __uint_as_float(r[j]);
             continue;
         }
         const uint16_t h = in ? add_residual(round_out(__uint_as_float(r[j]), a.bias, n), a.residual, m * a.ldr + n) : 0;
@@ -475,7 +475,7 @@ __device__ __forceinline__ void store_swap_rows4(const TcGemmArgs& a, const floa
     const float v[4] = {s.x, s.y, s.z, s.w};
     const bool whole = n + 4 <= a.N;
     if (a.out_f32) {
-        float* dst = f32_out_row(a, token) + n;
+        float* dst = static_cast<float*>(a.y) + token * a.ldy + n;
         if (whole && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
             *reinterpret_cast<float4*>(dst) = s;
         } else {

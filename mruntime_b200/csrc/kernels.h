@@ -77,26 +77,8 @@ struct TcGemmArgs {
     int am_chunks;
     // Segmented variant only: k-blocks per accumulator segment (kSegKb).
     int seg_kb;
-    // Row-parallel scatter (FP32 output only; xworld > 0): output row r
-    // belongs to rank o = r / xrpr and goes to o's exchange region,
-    // xpeer[o] + (xrank * xrpr + r - o * xrpr) * ldy, over NVLink for o != xrank
-    // (the region is [source rank][xrpr rows][ldy]); y is unused.
-    float* xpeer[8];
-    int xrank, xworld;
-    int64_t xrpr;
 };
 
-#ifdef __CUDACC__
-// Row `row` of an FP32 output: y's, or the owner rank's slot in its exchange
-// region under a row-parallel scatter.
-__device__ __forceinline__ float* f32_out_row(const TcGemmArgs& a, int64_t row) {
-    if (a.xworld > 0) {
-        const int64_t o = row / a.xrpr;
-        return a.xpeer[o] + (static_cast<int64_t>(a.xrank) * a.xrpr + (row - o * a.xrpr)) * a.ldy;
-    }
-    return static_cast<float*>(a.y) + row * a.ldy;
-}
-#endif
 // Whether a swap-mode launch of tile width bn may use clusters of k CTAs on
 // the current device (checked once per device, width and k).
 bool tc_cluster_ok(int bn, int k);

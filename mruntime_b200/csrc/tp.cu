@@ -388,60 +388,6 @@ __global__ void __launch_bounds__(256) p2p_reduce_kernel(const P2PArgs a) {
     }
 }
 
-// The fused row-parallel exchange, owner side (mrt_tp_gemm_rowpar): every
-// rank's GEMM stored the FP32 rows this rank owns straight into this rank's
-// region, [source rank][rpr rows][N] -- over NVLink, while its tensor cores
-// went on with later tiles.  Once every rank has published its epoch (its
-// GEMM, and with it its stores here, is complete), the slabs are summed in
-// rank order from local HBM, rounded once, and the FP16 rows stored at their
-// global position into every rank's output area.
-__global__ void __launch_bounds__(256) p2p_owner_reduce_kernel(const P2PArgs a, int64_t rows_mine, int64_t n,
-                                                               int64_t rpr) {
-    const unsigned long long epoch = *a.epoch + 1ull;
-    const unsigned all = (a.world >= 32 ? 0xFFFFFFFFu : ((1u << a.world) - 1u));
-    if (p2p_meet(a, 0, epoch, blockIdx.x == 0) != all) return;
-    const float* mine = a.part[a.rank];
-    const int64_t slab = rpr * n;
-    const int64_t elems = rows_mine * n;
-    const int64_t out0 = static_cast<int64_t>(a.rank) * slab;  // a multiple of 8 (host check)
-    const int64_t octets = elems / 8;
-    for (int64_t g = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; g < octets;
-         g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        float4 v0[kP2PMaxRanks], v1[kP2PMaxRanks];
-#pragma unroll
-        for (int q = 0; q < kP2PMaxRanks; ++q)
-            if (q < a.world) {
-                const float4* src = reinterpret_cast<const float4*>(mine + q * slab) + 2 * g;
-                v0[q] = __ldcs(src);
-                v1[q] = __ldcs(src + 1);
-            }
-        float t[8] = {v0[0].x, v0[0].y, v0[0].z, v0[0].w, v1[0].x, v1[0].y, v1[0].z, v1[0].w};
-#pragma unroll
-        for (int q = 1; q < kP2PMaxRanks; ++q)
-            if (q < a.world) {
-                const float u[8] = {v0[q].x, v0[q].y, v0[q].z, v0[q].w, v1[q].x, v1[q].y, v1[q].z, v1[q].w};
-#pragma unroll
-                for (int e = 0; e < 8; ++e) t[e] = __fadd_rn(t[e], u[e]);
-            }
-        uint32_t h[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-            h[e] = static_cast<uint32_t>(f32_to_f16_bits(t[2 * e])) | (static_cast<uint32_t>(f32_to_f16_bits(t[2 * e + 1])) << 16);
-        const uint4 hv = make_uint4(h[0], h[1], h[2], h[3]);
-#pragma unroll
-        for (int q = 0; q < kP2PMaxRanks; ++q)
-            if (q < a.world) reinterpret_cast<uint4*>(a.out[q] + out0)[g] = hv;
-    }
-    if (blockIdx.x == 0 && threadIdx.x == 0) {
-        for (int64_t i = octets * 8; i < elems; ++i) {
-            float t = mine[i];
-            for (int q = 1; q < a.world; ++q) t = __fadd_rn(t, mine[q * slab + i]);
-            const uint16_t h = f32_to_f16_bits(t);
-            for (int q = 0; q < a.world; ++q) a.out[q][out0 + i] = h;
-        }
-    }
-}
-
 __global__ void p2p_done_kernel(const P2PArgs a) {
     const unsigned long long epoch = *a.epoch + 1ull;
     __threadfence_system();  // this rank's output stores (previous kernel) before the release
@@ -594,57 +540,7 @@ extern "C" int mrt_tp_gemm_rowpar(mrt_tp tp, mrt_weight w, const void* x_dev, in
     if (M == 0) return MRT_OK;
     if (M * n > tp->p2p_cap) return set_error(MRT_ERR_SHAPE, "M x N exceeds the exchange region");
     if (y_dev != nullptr && ldy < n) return set_error(MRT_ERR_SHAPE, "ldy must be >= N");
-    DevCtx* c = current_ctx();
-    if (!c) return MRT_ERR_CUDA;
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    // Fused (MRT_TP_SCATTER=1, read per call): the GEMM stores each FP32 row
-    // straight into its owner's region ([source rank][rows per rank][N]) and
-    // the owner sums from its own memory.  Measured slower than the two-pass
-    // exchange on 2 and 4 B200s (7B o at M = 2048: 171 / 219 us against 129 /
-    // 161 for the GEMM + the exchange): the epilogue's row-per-thread stores
-    // reach a peer as 16-byte pieces, and the tensor cores wait for them.
-    const char* scatter_env = std::getenv("MRT_TP_SCATTER");
-    const bool scatter = scatter_env != nullptr && std::strcmp(scatter_env, "1") == 0;
-    const int64_t rpr = (M + tp->world - 1) / tp->world;
-    const bool fits = static_cast<int64_t>(tp->world) * rpr * n <= tp->p2p_cap && (rpr * n) % 8 == 0;
-    if (scatter && fits) {
-        float* peers[kP2PMaxRanks] = {};
-        for (int q = 0; q < tp->world; ++q) peers[q] = reinterpret_cast<float*>(tp->p2p_peer[q] + tp->p2p_part_off);
-        rc = gemm_rowpar_scatter(w, x_dev, ldx, M, peers, tp->rank, tp->world, rpr, s);
-        if (rc == MRT_OK) {
-            P2PArgs a{};
-            for (int q = 0; q < tp->world; ++q) {
-                a.part[q] = peers[q];
-                a.out[q] = reinterpret_cast<uint16_t*>(tp->p2p_peer[q] + tp->p2p_out_off);
-                a.flags[q] = reinterpret_cast<unsigned long long*>(tp->p2p_peer[q]);
-            }
-            a.epoch = tp->p2p_epoch;
-            a.count = M * n;
-            a.rank = tp->rank;
-            a.world = tp->world;
-            a.err = c->d_err;
-            const int64_t rows_mine = std::max<int64_t>(0, std::min<int64_t>(rpr, M - tp->rank * rpr));
-            int64_t blocks = (rows_mine * n / 8 + 255) / 256;
-            blocks = std::max<int64_t>(1, std::min<int64_t>(blocks, static_cast<int64_t>(c->sms) * 8));
-            p2p_owner_reduce_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(a, rows_mine, n, rpr);
-            cudaError_t e = cudaGetLastError();
-            if (e != cudaSuccess) return cuda_error(e, "owner reduce launch");
-            p2p_done_kernel<<<1, 32, 0, s>>>(a);
-            e = cudaGetLastError();
-            if (e != cudaSuccess) return cuda_error(e, "peer exchange completion launch");
-            note_launches(2);
-            void* region_out = tp->p2p_region + tp->p2p_out_off;
-            if (y_dev != nullptr && y_dev != region_out) {
-                e = cudaMemcpy2DAsync(y_dev, static_cast<size_t>(ldy) * 2, region_out, static_cast<size_t>(n) * 2,
-                                      static_cast<size_t>(n) * 2, static_cast<size_t>(M), cudaMemcpyDeviceToDevice, s);
-                if (e != cudaSuccess) return cuda_error(e, "copying the summed rows out");
-            }
-            return MRT_OK;
-        }
-        if (rc != MRT_ERR_UNSUPPORTED) return rc;
-        clear_error();
-    }
-    // Two passes: the whole partial in this rank's area, then the exchange.
+    // The whole FP32 partial into this rank's area, then the exchange.
     float* part = reinterpret_cast<float*>(tp->p2p_region + tp->p2p_part_off);
     rc = mrt_gemm_f32(w, x_dev, ldx, part, n, M, stream);
     if (rc != MRT_OK) return rc;
