@@ -515,6 +515,12 @@ static double unit_us(int bn, int64_t kb, int64_t active, int sms, int64_t x_row
     return std::max(compute, mem);
 }
 
+// K-slices of swap-mode tiles are summed inside thread-block clusters for more
+// than 8 tokens (measured on the 7B decode step: at 9-16 tokens the cluster
+// finish is 1-6 % faster per step, at 8 and fewer 5 % slower than the
+// global-memory finish, which reads so little there that one pass suffices).
+static bool cluster_tokens(int64_t M) { return M > 8; }
+
 // Plan for few tokens (M <= 64), swap mode: the weight is the 128-row MMA
 // operand, so a tile is 128 weight rows x all tokens and the work is streaming
 // W.  Swap-mode CTAs use ~108 KB of shared memory, so two fit on an SM and
@@ -582,7 +588,7 @@ static TcPlan plan_swap(int64_t M, int64_t N, int64_t K, int sms) {
             for (int64_t cap : {static_cast<int64_t>(sms), max_grid}) {
                 const int64_t grid = std::min(units, cap);
                 const int64_t upc = ceil_div(units, grid);
-                const bool cluster = bn >= 32 && splits <= 8 && grid == units;
+                const bool cluster = cluster_tokens(M) && splits <= 8 && grid == units;
                 consider(cost(grid, upc * kb_per, upc, 0, tiles, splits, cluster),
                          TcPlan{bn, static_cast<int>(grid), 0, static_cast<int>(splits), static_cast<int>(kb_per)});
             }
@@ -657,20 +663,19 @@ static TcPlan plan_tc(int64_t M, int64_t N, int64_t K, int sms, bool tiled = tru
     return best;
 }
 
-// Swap-mode plans of 32 or 64 tokens per tile whose every tile is split into
-// 2..8 K-slices, one slice per CTA, sum the slices inside thread-block
-// clusters (distributed shared memory) instead of through global memory:
-// there the global finish re-reads 32..64 FP32 columns per slice in several
-// dependent passes.  With 16 tokens per tile the global finish is one pass
-// and cheaper than the cost of cluster placement (clusters of 4..5 CTAs do
-// not tile the GPCs' SM counts, so some SMs take two CTAs of the launch).
+// Swap-mode plans of more than 8 tokens whose every tile is split into 2..8
+// K-slices, one slice per CTA (the grid is the slices, up to two CTAs per
+// SM), sum the slices inside thread-block clusters (distributed shared
+// memory) instead of through global memory, where the finish re-reads the
+// tokens' FP32 columns of every slice; with 8 tokens or fewer that read is one
+// short pass and the global finish is the faster one (cluster_tokens).
 // MRT_GEMM_CLUSTER=0 (read once) keeps the global-memory finish everywhere.
-static bool use_cluster(bool swap, const TcPlan& p, int64_t tiles) {
+static bool use_cluster(bool swap, const TcPlan& p, int64_t tiles, int64_t M) {
     static const bool enabled = [] {
         const char* v = std::getenv("MRT_GEMM_CLUSTER");
         return v == nullptr || std::strcmp(v, "0") != 0;
     }();
-    return enabled && swap && p.bn >= 32 && p.full == 0 && p.splits >= 2 && p.splits <= 8 &&
+    return enabled && swap && cluster_tokens(M) && p.full == 0 && p.splits >= 2 && p.splits <= 8 &&
            static_cast<int64_t>(p.grid) == tiles * p.splits && tc_cluster_ok(p.bn, p.splits);
 }
 
@@ -787,7 +792,7 @@ static int gemm_dispatch(mrt_weight w, const void* x, int64_t ldx, void* y, int6
     a.seg_kb = kSegKb;
     const int64_t tiles = tc_gemm_tiles(a);
     const int64_t n_tail = tiles - p.full;
-    if (use_cluster(swap, p, tiles) && epi.am_val == nullptr) a.cluster_k = p.splits;
+    if (use_cluster(swap, p, tiles, M) && epi.am_val == nullptr) a.cluster_k = p.splits;
     if (n_tail > 0 && a.cluster_k == 0) {
         const size_t need = static_cast<size_t>(n_tail) * p.splits * 128 * p.bn * sizeof(float);
         rc = ensure_buffer(&c->ws, &c->ws_bytes, need, "allocating split-K scratch");
@@ -834,7 +839,7 @@ extern "C" int mrt_gemm_plan(int64_t M, int64_t N, int64_t K, int sms, int* kern
     const bool swap = M <= 64;
     const TcPlan p = swap ? plan_swap(M, N, K, sms) : plan_tc(M, N, K, sms);
     const int64_t tiles = swap ? ((N + 127) / 128) : 0;
-    if (kernel) *kernel = swap ? (use_cluster(true, p, tiles) ? 3 : 2) : (p.pair ? 4 : 1);
+    if (kernel) *kernel = swap ? (use_cluster(true, p, tiles, M) ? 3 : 2) : (p.pair ? 4 : 1);
     if (bn) *bn = p.bn;
     if (full_tiles) *full_tiles = p.full;
     if (tail_splits) *tail_splits = p.splits;

@@ -27,11 +27,14 @@ pytestmark = pytest.mark.gpu
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 
-# (M, N, K, bias, fp32 output): the 7B projections q|k|v, o and down at 17..64
-# tokens (tile widths 32 and 64), token counts that leave a partial 16-column
+# (M, N, K, bias, fp32 output): the 7B projections q|k|v, o and down at 9..64
+# tokens (tile widths 16, 32 and 64), token counts that leave a partial 16-column
 # chunk, N not a multiple of 4 with K not a multiple of 64 (and unaligned
 # output rows), the q/k/v bias and the FP32 output.
 CASES = [
+    (12, 4608, 3584, False, False),
+    (16, 3584, 3584, False, False),
+    (9, 3584, 3584, True, False),
     (17, 4608, 3584, False, False),
     (20, 3584, 3584, False, False),
     (32, 3584, 18944, False, False),
