@@ -493,15 +493,25 @@ namespace mrt {
 // no whole wave).  Split slices pay for writing and re-reading FP32 partials.
 struct TcPlan {
     int bn = 256, grid = 1, full = 0, splits = 1, kb_per = 0;
-    bool pair = false;  // SM-pair kernel (cta_group::2), 256-row tiles, whole K
+    bool pair = false;  // SM-pair kernel (cta_group::2), 256-row tiles
 };
 
 // SM pairs for normal-mode plans: chosen by cost; MRT_GEMM_PAIR=0 never
-// uses them, MRT_GEMM_PAIR=1 always when the shape allows (read per plan).
+// uses them, MRT_GEMM_PAIR=1 always when the shape allows, over the whole K
+// (read per plan).
 static int pair_mode() {
     const char* v = std::getenv("MRT_GEMM_PAIR");
     if (v == nullptr) return -1;
     return std::strcmp(v, "0") == 0 ? 0 : (std::strcmp(v, "1") == 0 ? 1 : -1);
+}
+
+// MRT_GEMM_PAIR_SPLITS=s (2..16, read per plan): SM-pair plans cut the last
+// partial wave's tiles into s K-slices whatever the cost (for tests).
+static int pair_splits_forced() {
+    const char* v = std::getenv("MRT_GEMM_PAIR_SPLITS");
+    if (v == nullptr) return 0;
+    const int n = std::atoi(v);
+    return n >= 2 && n <= 16 ? n : 0;
 }
 
 static double unit_us(int bn, int64_t kb, int64_t active, int sms, int64_t x_rows) {
@@ -612,19 +622,64 @@ static TcPlan plan_tc(int64_t M, int64_t N, int64_t K, int sms, bool tiled = tru
     double best_cost = 1e300;
     const int pm = pair_mode();
     if (tiled && pm != 0 && M >= 256 && sms >= 2) {
-        // SM pairs (tcgen05 cta_group::2): 256 x 256 tiles over the whole K on
-        // sms / 2 pairs.  Each CTA computes a 128 x 256 tile per k-block as in
-        // the one-SM kernel but loads a third less; measured 6-9 % faster per
-        // tile at M >= 512 (7B gate+up, q|k|v), so its waves cost 0.92 of the
-        // one-SM kernel's.
+        // SM pairs (tcgen05 cta_group::2): 256 x 256 tiles on sms / 2 pairs.
+        // Each CTA computes a 128 x 256 tile per k-block as in the one-SM
+        // kernel but loads a third less; measured 6-9 % faster per tile at
+        // M >= 512 (7B gate+up, q|k|v), so its units cost 0.92 of the one-SM
+        // kernel's.
         const int64_t tiles = ((M + 255) / 256) * ((N + 255) / 256);
-        const int64_t pairs = std::min<int64_t>(tiles, sms / 2);
+        const int64_t all_pairs = sms / 2;
+        const int64_t pairs = std::min<int64_t>(tiles, all_pairs);
         best = TcPlan{256, static_cast<int>(2 * pairs), static_cast<int>(tiles), 1, 0, true};
-        // With at least a full wave of pair tiles the pairs win outright
-        // (measured: also at 1.5 waves, against the one-SM kernel's K-split
-        // tails, e.g. 7B o and down at M = 2048); below it they leave SMs idle
-        // and compete on cost.
-        if (pm == 1 || tiles >= sms / 2) return best;
+        if (pm == 1) return best;
+        // Tiles [0, full) over the whole K, the other tiles cut into s
+        // K-slices; returns the busiest pair's k-blocks in slices, each slice
+        // counted with `unit_kb` extra k-blocks (its partial tile's store,
+        // pipeline refill and share of the reduction).
+        auto split_plan = [&](int64_t full, int64_t s, double unit_kb, TcPlan* out) -> double {
+            const int64_t kb_per = (num_kb + s - 1) / s;
+            const int64_t splits = (num_kb + kb_per - 1) / kb_per;
+            if (splits < 2) return 1e300;
+            const int64_t units = (tiles - full) * splits;
+            *out = TcPlan{256, static_cast<int>(2 * std::min(full + units, all_pairs)), static_cast<int>(full),
+                          static_cast<int>(splits), static_cast<int>(kb_per), true};
+            return static_cast<double>((units + all_pairs - 1) / all_pairs) * (static_cast<double>(kb_per) + unit_kb);
+        };
+        const int64_t full = (tiles / all_pairs) * all_pairs;
+        if (const int forced = pair_splits_forced()) {
+            TcPlan p;
+            if (tiles > full && forced <= num_kb && split_plan(full, forced, 0.0, &p) < 1e299) best = p;
+            return best;
+        }
+        // K-split slices pay off only for long K (measured on the 7B down
+        // projection, K = 18944, against whole-K pairs: M = 2048 (1.5 waves)
+        // 3 % faster with the last half wave in 5 slices, M = 4096 9 % with
+        // its two leftover tiles in 16, M = 256 / 512 (14 / 28 tiles) 2.4x /
+        // 1.8x with every tile in 5, 7-8 % faster than the one-SM kernel
+        // there; at K = 3584 (7B o, M = 2048) slices were 25 % slower).
+        // Below a full wave the slices keep every pair busy, at more
+        // than half a wave whole tiles do (M = 1024: 56 tiles).  The per-slice
+        // overhead (12 k-blocks) is fitted to those measurements.
+        if (num_kb >= 256 && (tiles >= all_pairs || 2 * tiles <= all_pairs)) {
+            const int64_t f = tiles >= all_pairs ? full : 0;
+            const double unit_kb = 12.0;
+            // the whole-K alternative: its last partial wave runs num_kb
+            double best_kb = tiles > f ? static_cast<double>(num_kb) : 1e300;
+            for (int64_t s = 2; tiles > f && s <= 16 && s <= num_kb; ++s) {
+                TcPlan p;
+                const double kb = split_plan(f, s, unit_kb, &p);
+                if (kb < best_kb - 1e-9) {
+                    best_kb = kb;
+                    best = p;
+                }
+            }
+            return best;
+        }
+        // With at least half a wave of pair tiles the pairs win outright
+        // (measured at 1.5 waves against the one-SM kernel's K-split tails,
+        // e.g. 7B o and down at M = 2048; at 0.57 waves, M = 768 o, 7 %
+        // faster); below it they leave SMs idle and compete on cost.
+        if (2 * tiles >= all_pairs || num_kb >= 256) return best;
         const int64_t waves = (tiles + pairs - 1) / pairs;
         best_cost = 0.92 * static_cast<double>(waves) * unit_us(256, num_kb, 2 * pairs, sms, x_rows);
     }
@@ -753,13 +808,27 @@ static int gemm_dispatch(mrt_weight w, const void* x, int64_t ldx, void* y, int6
         }
         TcGemmArgs a{};
         a.M = static_cast<int>(M); a.N = static_cast<int>(w->n); a.K = static_cast<int>(w->k);
+        a.pair = 1;
         a.w_tiled = w->data; a.w_k_tiles = w->k_tiles; a.w_prefetch = 1;
-        a.bn = p.bn; a.grid = p.grid; a.full_tiles = p.full; a.tail_splits = 1; a.kb_per = 0;
+        a.bn = p.bn; a.grid = p.grid; a.full_tiles = p.full; a.tail_splits = p.splits; a.kb_per = p.kb_per;
         a.y = y; a.ldy = ldy; a.out_f32 = out_f32 ? 1 : 0; a.bias = bias; a.err_flag = c->d_err;
-        a.swiglu_lut = swiglu_lut; a.residual = epi.residual; a.ldr = epi.ldr;
+        a.residual = epi.residual; a.ldr = epi.ldr;
         a.seg_kb = kSegKb;
+        const int64_t n_tail = tc_gemm_tiles(a) - p.full;
+        if (swiglu_lut != nullptr && n_tail > 0) return MRT_OK;  // K-split plan: not fused
+        a.swiglu_lut = swiglu_lut;
+        if (n_tail > 0) {
+            const size_t need = static_cast<size_t>(n_tail) * p.splits * 256 * p.bn * sizeof(float);
+            rc = ensure_buffer(&c->ws, &c->ws_bytes, need, "allocating split-K scratch");
+            if (rc != MRT_OK) return rc;
+            a.partials = static_cast<float*>(c->ws);
+        }
         e = launch_tc_pair(a, tx, w->tmap_rows, s);
         if (e != cudaSuccess) return cuda_error(e, "tcgen05 pair gemm launch");
+        if (n_tail > 0) {
+            e = launch_reduce_tail(a, s);
+            if (e != cudaSuccess) return cuda_error(e, "split-K reduction launch");
+        }
         if (fused) *fused = swiglu_lut != nullptr;
         return MRT_OK;
     }

@@ -86,12 +86,16 @@ __global__ void untile_kernel(const uint16_t* src, int64_t n, int64_t k, int64_t
 
 // Finish the K-split tail tiles of a normal-mode tensor-core GEMM plan (the
 // swap mode finishes its small tiles inside the GEMM kernel): partials are
-// [tail_splits][n_tail][128][bn] FP32; slices are added in index order, so
-// results are deterministic.  The whole GPU shares the work, which matters
-// for wide tiles (a 128 x 256 tile is 128 KB per slice).
-__global__ void reduce_tail_kernel(const TcGemmArgs a, int num_m, int n_tail) {
+// [tail_splits][n_tail][tile_m][bn] FP32 (tile_m = 128, or 256 for SM-pair
+// plans); slices are added in index order, so results are deterministic.  The
+// whole GPU shares the work, which matters for wide tiles (a 128 x 256 tile
+// is 128 KB per slice).
+__global__ void reduce_tail_kernel(const TcGemmArgs a, int num_m, int n_tail, int tile_m) {
+    // Launched while the GEMM still runs; its partials are read after it.
+    griddep_launch_dependents();
+    griddep_wait();
     const int bn = a.bn;
-    const int64_t per_tile = 128LL * bn;
+    const int64_t per_tile = static_cast<int64_t>(tile_m) * bn;
     const int64_t total4 = static_cast<int64_t>(n_tail) * per_tile / 4;
     for (int64_t e4 = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e4 < total4;
          e4 += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -100,7 +104,7 @@ __global__ void reduce_tail_kernel(const TcGemmArgs a, int num_m, int n_tail) {
         const int64_t rem = e - ti * per_tile;
         const int64_t r = rem / bn, c = rem - r * bn;
         const int64_t t = a.full_tiles + ti;
-        const int64_t row = (t % num_m) * 128 + r;
+        const int64_t row = (t % num_m) * tile_m + r;
         const int64_t col = (t / num_m) * bn + c;
         if (row >= a.M || col >= a.N) continue;
         float4 s = *reinterpret_cast<const float4*>(a.partials + e);
@@ -275,10 +279,21 @@ cudaError_t launch_untile(const uint16_t* src, int64_t n, int64_t k, int64_t k_t
 
 cudaError_t launch_reduce_tail(const TcGemmArgs& a, cudaStream_t s) {
     if (a.swap) return cudaErrorInvalidValue;  // swap mode finishes its tail tiles in the GEMM kernel
-    const int num_m = (a.M + 127) / 128;
+    const int tile_m = a.pair ? 256 : 128;
+    const int num_m = (a.M + tile_m - 1) / tile_m;
     const int n_tail = tc_gemm_tiles(a) - a.full_tiles;
     if (n_tail <= 0) return cudaSuccess;
-    reduce_tail_kernel<<<grid_for(static_cast<int64_t>(n_tail) * 128 * a.bn / 4), kThreads, 0, s>>>(a, num_m, n_tail);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid_for(static_cast<int64_t>(n_tail) * tile_m * a.bn / 4));
+    cfg.blockDim = dim3(kThreads);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, reduce_tail_kernel, a, num_m, n_tail, tile_m);
+    if (e != cudaSuccess) return e;
     note_launches(1);
     return cudaGetLastError();
 }

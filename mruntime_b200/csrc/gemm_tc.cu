@@ -108,10 +108,10 @@ __device__ __forceinline__ uint32_t pack_h2(uint16_t lo, uint16_t hi) {
 }
 
 // Store 32 FP32 accumulator columns of one tile row into a tail slot
-// (tile-local layout [128][bn]; always in bounds and 16-byte aligned).
+// (tile-local layout [tile_rows][bn]; always in bounds and 16-byte aligned).
 __device__ __forceinline__ void store_partial_chunk(const TcGemmArgs& a, const uint32_t (&r)[32], int slot,
-                                                   int row_in_tile, int col_in_tile, int bn) {
-    float* dst = a.partials + (static_cast<int64_t>(slot) * kBM + row_in_tile) * bn + col_in_tile;
+                                                   int row_in_tile, int col_in_tile, int bn, int tile_rows = kBM) {
+    float* dst = a.partials + (static_cast<int64_t>(slot) * tile_rows + row_in_tile) * bn + col_in_tile;
 #pragma unroll
     for (int j = 0; j < 32; j += 4)
         *reinterpret_cast<uint4*>(dst + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
@@ -1174,9 +1174,12 @@ __global__ void __launch_bounds__(threads_of<SEG>(), 1)
     cluster_wait();
     const uint32_t tmem_base = *tmem_slot;
 
+    // Units as in the one-SM kernel (decode_unit with 256-row m-tiles):
+    // whole-K tiles, then the K-slices of the tail tiles.
     const int num_m2 = (a.M + 2 * kBM - 1) / (2 * kBM);
     const int num_n = (a.N + BN - 1) / BN;
-    const int total = num_m2 * num_n;
+    const int n_tail = num_m2 * num_n - a.full_tiles;
+    const int total = a.full_tiles + n_tail * a.tail_splits;
     const int pair = blockIdx.x >> 1;
     const int npairs = gridDim.x >> 1;
     const int num_kb = (a.K + kBK - 1) / kBK;
@@ -1188,37 +1191,44 @@ __global__ void __launch_bounds__(threads_of<SEG>(), 1)
             uint32_t phase = 0;
             uint32_t issued = 0, issued_parity = 0;
             bool ok = true;
-            auto load_w = [&](int u, int kb, int st) {
-                const int nt = u / num_m2;
+            auto load_w = [&](const Unit& w, int kb, int st) {
                 // this CTA's BN / 2 W rows = BN / 256 whole 128-row tiles (BN = 256: one)
-                const int64_t wtile = (static_cast<int64_t>(nt) * BN + rank * (BN / 2)) / kBM;
+                const int64_t wtile = (static_cast<int64_t>(w.nt) * BN + rank * (BN / 2)) / kBM;
 #pragma unroll
                 for (int h = 0; h < BN / 256; ++h)
                     tma_load_2d_pair(sB + st * Cfg::kBBytes + h * (kBM * kBK * 2), &tmw, full0 + st * 8, 0,
                                      static_cast<int32_t>(((wtile + h) * a.w_k_tiles + kb) * kBM));
             };
-            auto load_x = [&](int u, int kb, int st) {
-                const int mt = u % num_m2;
-                tma_load_2d_pair(sA + st * Cfg::kABytes, &tma, full0 + st * 8, kb * kBK, mt * 2 * kBM + static_cast<int>(rank) * kBM);
+            auto load_x = [&](const Unit& w, int kb, int st) {
+                tma_load_2d_pair(sA + st * Cfg::kABytes, &tma, full0 + st * 8, kb * kBK,
+                                 w.mt * 2 * kBM + static_cast<int>(rank) * kBM);
             };
             auto claim = [&](int st) {
                 if (leader) mbar_arrive_expect_tx_local(&full[st], 2 * Cfg::kStageBytes);
                 issued |= 1u << st;
                 issued_parity = (issued_parity & ~(1u << st)) | (phase << st);
             };
-            int u = pair, kb = 0;
+            // Next k-block of this pair's unit sequence.
+            auto advance = [&](int& uu, Unit& ww, int& kk) {
+                if (++kk == ww.kb1) {
+                    uu += npairs;
+                    if (uu < total) ww = decode_unit(a, uu, num_m2, n_tail, num_kb);
+                    kk = ww.kb0;
+                }
+            };
+            int u = pair;
+            Unit w = decode_unit(a, u, num_m2, n_tail, num_kb);
+            int kb = w.kb0;
             // First ring pass of weight tiles before waiting for the kernel
             // this one overlaps (weights are never written by it).
             int pre = 0;
             if (a.w_prefetch) {
                 int uu = u, kk = kb;
+                Unit ww = w;
                 for (; pre < S && uu < total; ++pre) {
                     claim(stage);
-                    load_w(uu, kk, stage);
-                    if (++kk == num_kb) {
-                        kk = 0;
-                        uu += npairs;
-                    }
+                    load_w(ww, kk, stage);
+                    advance(uu, ww, kk);
                     if (++stage == S) {
                         stage = 0;
                         phase ^= 1u;
@@ -1226,17 +1236,9 @@ __global__ void __launch_bounds__(threads_of<SEG>(), 1)
                 }
             }
             griddep_wait();
-            {
-                int uu = u, kk = kb;
-                for (int i = 0; i < pre; ++i) {
-                    load_x(uu, kk, i);
-                    if (++kk == num_kb) {
-                        kk = 0;
-                        uu += npairs;
-                    }
-                }
-                u = uu;
-                kb = kk;
+            for (int i = 0; i < pre; ++i) {
+                load_x(w, kb, i);
+                advance(u, w, kb);
             }
             for (; u < total;) {
                 if (!mbar_wait(&empty[stage], phase ^ 1u, a.err_flag, kErrTmaWait)) {
@@ -1244,16 +1246,13 @@ __global__ void __launch_bounds__(threads_of<SEG>(), 1)
                     break;
                 }
                 claim(stage);
-                load_w(u, kb, stage);
-                load_x(u, kb, stage);
+                load_w(w, kb, stage);
+                load_x(w, kb, stage);
                 if (++stage == S) {
                     stage = 0;
                     phase ^= 1u;
                 }
-                if (++kb == num_kb) {
-                    kb = 0;
-                    u += npairs;
-                }
+                advance(u, w, kb);
             }
             if (!ok) {
                 // Copies still in flight land in this CTA's shared memory: wait
@@ -1273,8 +1272,9 @@ __global__ void __launch_bounds__(threads_of<SEG>(), 1)
                 uint32_t acc_phase = 0;
                 bool ok = true;
                 for (int u = pair; u < total && ok; u += npairs) {
-                    for (int s0 = 0; s0 < num_kb && ok; s0 += kSegLen) {
-                        const int s1 = min(s0 + kSegLen, num_kb);
+                    const Unit w = decode_unit(a, u, num_m2, n_tail, num_kb);
+                    for (int s0 = w.kb0; s0 < w.kb1 && ok; s0 += kSegLen) {
+                        const int s1 = min(s0 + kSegLen, w.kb1);
                         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, a.err_flag, kErrMmaWait)) {
                             ok = false;
                             break;
@@ -1325,10 +1325,10 @@ __global__ void __launch_bounds__(threads_of<SEG>(), 1)
         uint32_t acc_phase = 0;
         bool go = true;
         for (int u = pair; u < total && go; u += npairs) {
-            const int mt = u % num_m2, nt = u / num_m2;
+            const Unit w = decode_unit(a, u, num_m2, n_tail, num_kb);
             float sum[HB];
             uint32_t t_row = 0;
-            for (int s0 = 0; s0 < num_kb; s0 += kSegLen) {
+            for (int s0 = w.kb0; s0 < w.kb1; s0 += kSegLen) {
                 int ok = 1;
                 if (lane == 0) ok = mbar_wait(&tfull[acc], acc_phase, a.err_flag, kErrEpiWait) ? 1 : 0;
                 ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
@@ -1338,7 +1338,8 @@ __global__ void __launch_bounds__(threads_of<SEG>(), 1)
                 }
                 tc_fence_after();
                 t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN + half * HB);
-                const bool last = s0 + kSegLen >= num_kb;
+                const bool last = s0 + kSegLen >= w.kb1;
+                const bool first = s0 == w.kb0;
 #pragma unroll
                 for (int c = 0; c < HB / 16; ++c) {
                     uint32_t r[16];
@@ -1346,7 +1347,7 @@ __global__ void __launch_bounds__(threads_of<SEG>(), 1)
                     tmem_ld_16cols(t_row + c * 16, r);
 #pragma unroll
                     for (int j = 0; j < 16; ++j)
-                        sum[c * 16 + j] = s0 == 0 ? __uint_as_float(r[j]) : __fadd_rn(sum[c * 16 + j], __uint_as_float(r[j]));
+                        sum[c * 16 + j] = first ? __uint_as_float(r[j]) : __fadd_rn(sum[c * 16 + j], __uint_as_float(r[j]));
                     if (last) {
 #pragma unroll
                         for (int j = 0; j < 16; ++j) r[j] = __float_as_uint(sum[c * 16 + j]);
@@ -1365,14 +1366,17 @@ __global__ void __launch_bounds__(threads_of<SEG>(), 1)
                 if (acc == 0) acc_phase ^= 1u;
             }
             if (!go) break;
-            const int64_t row = static_cast<int64_t>(mt) * 2 * kBM + rank * kBM + quad * 32 + lane;
+            const int row_in_tile = static_cast<int>(rank) * kBM + quad * 32 + lane;
+            const int64_t row = static_cast<int64_t>(w.mt) * 2 * kBM + row_in_tile;
 #pragma unroll 1
             for (int c = 0; c < HB / 32; ++c) {
                 uint32_t r[32];
                 __syncwarp();
                 tmem_ld_32cols(t_row + c * 32, r);
-                const int64_t col0 = static_cast<int64_t>(nt) * BN + half * HB + c * 32;
-                if (row < a.M && col0 < a.N) {
+                const int64_t col0 = static_cast<int64_t>(w.nt) * BN + half * HB + c * 32;
+                if (w.slot >= 0) {
+                    store_partial_chunk(a, r, w.slot, row_in_tile, half * HB + c * 32, BN, 2 * kBM);
+                } else if (row < a.M && col0 < a.N) {
                     if (a.swiglu_lut != nullptr)
                         store_row_chunk_swiglu(a, r, row, col0);
                     else
@@ -1396,22 +1400,25 @@ __global__ void __launch_bounds__(threads_of<SEG>(), 1)
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int u = pair; u < total; u += npairs) {
-            const int mt = u % num_m2, nt = u / num_m2;
+            const Unit w = decode_unit(a, u, num_m2, n_tail, num_kb);
             int ok = 1;
             if (lane == 0) ok = mbar_wait(&tfull[acc], acc_phase, a.err_flag, kErrEpiWait) ? 1 : 0;
             ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
             // The four warps leave together (the named barrier below needs all 128).
             if (!epi_bar_and(ok != 0)) break;
             tc_fence_after();
-            const int64_t row = static_cast<int64_t>(mt) * 2 * kBM + rank * kBM + quad * 32 + lane;
+            const int row_in_tile = static_cast<int>(rank) * kBM + quad * 32 + lane;
+            const int64_t row = static_cast<int64_t>(w.mt) * 2 * kBM + row_in_tile;
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
 #pragma unroll 1
             for (int c = 0; c < BN / 32; ++c) {
                 uint32_t r[32];
                 __syncwarp();
                 tmem_ld_32cols(t_row + c * 32, r);
-                const int64_t col0 = static_cast<int64_t>(nt) * BN + c * 32;
-                if (row < a.M && col0 < a.N) {
+                const int64_t col0 = static_cast<int64_t>(w.nt) * BN + c * 32;
+                if (w.slot >= 0) {
+                    store_partial_chunk(a, r, w.slot, row_in_tile, c * 32, BN, 2 * kBM);
+                } else if (row < a.M && col0 < a.N) {
                     if (a.swiglu_lut != nullptr)
                         store_row_chunk_swiglu(a, r, row, col0);
                     else
@@ -1503,19 +1510,29 @@ bool tc_gemm_segmented(const TcGemmArgs& a) {
 cudaError_t launch_tc_pair(const TcGemmArgs& a, const CUtensorMap& tmap_x, const CUtensorMap& tmap_w_rows,
                            cudaStream_t s) {
     if (a.M <= 0 || a.N <= 0) return cudaSuccess;
-    // Whole-K tiles of 256 x BN, an even persistent grid of at most one pair
-    // per tile, FP16 or FP32 output (no greedy-pick partials).
-    const int tiles = ((a.M + 255) / 256) * ((a.N + a.bn - 1) / a.bn);
-    if (a.swap || a.K <= 0 || a.w_tiled == nullptr || a.grid < 2 || (a.grid & 1) != 0 || a.grid > 2 * tiles ||
-        a.full_tiles != tiles || a.tail_splits != 1 || a.am_val != nullptr || a.cluster_k != 0)
+    // Tiles of 256 x BN, an even persistent grid of at most one pair per
+    // unit, FP16 or FP32 output (no greedy-pick partials); every tail slice
+    // owns at least one k-block and stores into `partials`.
+    if (!a.pair || a.swap || a.K <= 0 || a.w_tiled == nullptr || a.grid < 2 || (a.grid & 1) != 0 ||
+        a.tail_splits <= 0 || a.am_val != nullptr || a.cluster_k != 0)
         return cudaErrorInvalidValue;
+    const int tiles = tc_gemm_tiles(a);
     const int num_kb = (a.K + kBK - 1) / kBK;
-    if (a.bn == 256) return num_kb > kSegMinKb ? launch_pair_bn<256, true>(a, tmap_x, tmap_w_rows, s)
-                                               : launch_pair_bn<256, false>(a, tmap_x, tmap_w_rows, s);
+    if (a.full_tiles < 0 || a.full_tiles > tiles) return cudaErrorInvalidValue;
+    const bool tail = a.full_tiles < tiles;
+    if (tail && (a.kb_per <= 0 || (a.tail_splits - 1) * a.kb_per >= num_kb || a.tail_splits * a.kb_per < num_kb ||
+                 a.partials == nullptr || a.swiglu_lut != nullptr))
+        return cudaErrorInvalidValue;
+    const int64_t units = a.full_tiles + static_cast<int64_t>(tiles - a.full_tiles) * (tail ? a.tail_splits : 0);
+    if (a.grid > 2 * units) return cudaErrorInvalidValue;
+    const bool seg = (a.full_tiles > 0 && num_kb > kSegMinKb) || (tail && a.kb_per > kSegMinKb);
+    if (a.bn == 256) return seg ? launch_pair_bn<256, true>(a, tmap_x, tmap_w_rows, s)
+                                : launch_pair_bn<256, false>(a, tmap_x, tmap_w_rows, s);
     return cudaErrorInvalidValue;
 }
 
 int tc_gemm_tiles(const TcGemmArgs& a) {
+    if (a.pair) return ((a.M + 2 * kBM - 1) / (2 * kBM)) * ((a.N + a.bn - 1) / a.bn);
     return a.swap ? ((a.N + kBM - 1) / kBM) * ((a.M + a.bn - 1) / a.bn)
                   : ((a.M + kBM - 1) / kBM) * ((a.N + a.bn - 1) / a.bn);
 }

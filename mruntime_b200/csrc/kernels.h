@@ -77,6 +77,9 @@ struct TcGemmArgs {
     int am_chunks;
     // Segmented variant only: k-blocks per accumulator segment (kSegKb).
     int seg_kb;
+    // 1: SM-pair plan (launch_tc_pair): tiles of 256 X rows, partials
+    // [tail_splits][n_tail][256][bn].
+    int pair;
 };
 
 // Whether a swap-mode launch of tile width bn may use clusters of k CTAs on
@@ -84,7 +87,7 @@ struct TcGemmArgs {
 bool tc_cluster_ok(int bn, int k);
 cudaError_t launch_tc_gemm(const TcGemmArgs& a, const CUtensorMap& tmap_x, const CUtensorMap& tmap_w,
                            cudaStream_t s);
-// Output tiles of a plan (128 A rows x bn B rows each).
+// Output tiles of a plan (128 A rows x bn B rows each; 256 A rows for pairs).
 int tc_gemm_tiles(const TcGemmArgs& a);
 // Units longer than this many 64-wide k-blocks accumulate in segments (normal
 // mode: the segmented kernel variant; swap-mode plans keep every unit at or
@@ -96,10 +99,13 @@ constexpr int kSegMinKb = 64;
 constexpr int kSegKb = 64;
 // Whether a normal-mode launch uses the segmented-accumulation variant.
 bool tc_gemm_segmented(const TcGemmArgs& a);
-// Normal mode on SM pairs (tcgen05 cta_group::2): tiles of 256 X rows x bn
-// (256) W rows over the whole K, a.grid = 2 x pairs (even), full_tiles =
-// every tile.  tmap_w_rows views the tiled weight as [n_pad * k_tiles * 128]
-// rows of 64 FP16 with a 64 x 128 box and no swizzle (one tile per box).
+// Normal mode on SM pairs (tcgen05 cta_group::2, a.pair = 1): tiles of 256
+// X rows x bn (256) W rows, numbered m-fastest, a.grid = 2 x pairs (even).
+// Tiles [0, full_tiles) run over the whole K; each remaining tile runs as
+// tail_splits K-slices whose FP32 partials launch_reduce_tail sums, as in the
+// one-SM kernel.  tmap_w_rows views the tiled weight as
+// [n_pad * k_tiles * 128] rows of 64 FP16 with a 64 x 128 box and no swizzle
+// (one tile per box).
 cudaError_t launch_tc_pair(const TcGemmArgs& a, const CUtensorMap& tmap_x, const CUtensorMap& tmap_w_rows,
                            cudaStream_t s);
 // Normal mode only: sum the K-slices of every tail tile in slice order on

@@ -107,5 +107,80 @@ def test_pair_epilogues(cuda_dev):
             np.testing.assert_array_equal(two, one)
 
 
+def _forced_splits(n, fn):
+    os.environ["MRT_GEMM_PAIR_SPLITS"] = str(n)
+    try:
+        return fn()
+    finally:
+        os.environ.pop("MRT_GEMM_PAIR_SPLITS", None)
+
+
+# (M, N, K, slices): K-split tails on SM pairs -- whole waves of 74 pairs over
+# the whole K and the last partial wave's tiles cut into K-slices, or (fewer
+# tiles than pairs) every tile cut; slices of one k-block, ragged last slices,
+# and slices longer than 64 k-blocks (segmented accumulation), the 7B o and
+# down projections at M = 2048 among them.
+TAIL_SHAPES = [(2048, 3584, 3584, 3), (2048, 3584, 18944, 2), (2048, 3584, 18944, 7), (300, 1000, 904, 3),
+               (257, 640, 128, 2), (512, 1000, 8192, 5), (2304, 2304, 1000, 16)]
+
+
+@pytest.mark.parametrize("MNKS", TAIL_SHAPES)
+def test_pair_k_split_tails(cuda_dev, MNKS):
+    """Pair plans with K-split tails: within the reference's error bars on
+    sampled rows (tail tiles included), close to the whole-K pair plan, and
+    repeatable bit for bit (slices are summed in slice order)."""
+    M, N, K, n = MNKS
+    rng = np.random.default_rng(M * 7 + N + K + n)
+    x = _rand(rng, (M, K), 1.0)
+    w = W.to_bf16_bits(rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02))
+    wt = upload(w, BF16)
+    p = _forced_splits(n, lambda: capi.gemm_plan(M, N, K, 148))
+    tiles = -(-M // 256) * -(-N // 256)
+    assert p["pair"] and p["full_tiles"] == (tiles // 74) * 74 and p["tail_splits"] >= 2, p
+    if torch.cuda.get_device_properties(0).multi_processor_count != 148:
+        pytest.skip("the forced plan is laid out for 148 SMs")
+    got = _forced_splits(n, lambda: _run(wt, x))
+    again = _forced_splits(n, lambda: _run(wt, x))
+    np.testing.assert_array_equal(got, again)
+    os.environ["MRT_GEMM_PAIR"] = "1"
+    try:
+        whole = _run(wt, x)
+    finally:
+        os.environ.pop("MRT_GEMM_PAIR", None)
+    assert np.mean(got == whole) > 0.8
+    # rows of the first m-tiles and the last (tail tiles are the last in
+    # m-fastest order: every m-tile of the last n-tiles)
+    rows = np.unique(np.r_[0:4, 130:132, M // 2, M - 4:M])
+    xs = x[rows]
+    truth = f64_truth(xs, w, BF16)
+    ref = O.gemm(xs, FP16, w, BF16, trans_b=True)
+    check_close(got[rows], truth, O.rel_frobenius(ref, truth), f"pair tails {MNKS}", absdot=abs_dot(xs, w, BF16),
+                K=K)
+
+
+def test_pair_k_split_tail_epilogues(cuda_dev):
+    """Bias (double rounding), FP32 output and the residual add of tail
+    tiles come from the tail reduction: each equals the reference's
+    operation applied to the same plan's plain output."""
+    if torch.cuda.get_device_properties(0).multi_processor_count != 148:
+        pytest.skip("the forced plan is laid out for 148 SMs")
+    rng = np.random.default_rng(78)
+    M, N, K = 384, 1152, 896
+    x = _rand(rng, (M, K), 1.0)
+    w = W.to_bf16_bits(rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02))
+    b = W.to_bf16_bits(rng.standard_normal(N, dtype=np.float32) * np.float32(0.02))
+    res = _rand(rng, (M, N), 1.0)
+    wt = upload(w, BF16)
+    bd = dev_u16(b)
+    wt.attach_bias(bd.data_ptr(), BF16, True, stream())
+    plain = _forced_splits(3, lambda: _run(wt, x))
+    with_bias = _forced_splits(3, lambda: _run(wt, x, flags=1))
+    np.testing.assert_array_equal(with_bias, O.add_bias(plain, W.bf16_to_f16_bits(b)))
+    y32 = _forced_splits(3, lambda: _run(wt, x, out_f32=True))
+    np.testing.assert_array_equal(O.f32_to_f16(y32), plain)
+    with_res = _forced_splits(3, lambda: _run(wt, x, residual=res))
+    np.testing.assert_array_equal(with_res, O.add(res, plain))
+
+
 def test_pair_no_timeout(cuda_dev):
     capi.sync(stream())
