@@ -128,7 +128,9 @@ __device__ __forceinline__ void store_row_chunk(const TcGemmArgs& a, const uint3
             for (int j = 0; j < 32; j += 4)
                 *reinterpret_cast<uint4*>(dst + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
         } else {
-            for (int j = 0; j < 32 && col0 + j < a.N; ++j) dst[j] = __uint_as_float(r[j]);
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (col0 + j < a.N) dst[j] = __uint_as_float(r[j]);
         }
         return;
     }
@@ -163,8 +165,9 @@ __device__ __forceinline__ void store_row_chunk(const TcGemmArgs& a, const uint3
         for (int j = 0; j < 16; j += 4)
             *reinterpret_cast<uint4*>(dst + 2 * j) = make_uint4(h[j], h[j + 1], h[j + 2], h[j + 3]);
     } else {
-        for (int j = 0; j < 32 && col0 + j < a.N; ++j)
-            dst[j] = add_residual(round_out(__uint_as_float(r[j]), a.bias, col0 + j), res, j);
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            if (col0 + j < a.N) dst[j] = add_residual(round_out(__uint_as_float(r[j]), a.bias, col0 + j), res, j);
     }
 }
 
@@ -238,7 +241,9 @@ __device__ __forceinline__ void store_row_chunk_swiglu(const TcGemmArgs& a, cons
         *reinterpret_cast<uint4*>(dst + 8) = make_uint4(pack_h2(h[8], h[9]), pack_h2(h[10], h[11]),
                                                         pack_h2(h[12], h[13]), pack_h2(h[14], h[15]));
     } else {
-        for (int i = 0; i < 16 && col0 + 2 * i + 1 < a.N; ++i) dst[i] = h[i];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+            if (col0 + 2 * i + 1 < a.N) dst[i] = h[i];
     }
 }
 
