@@ -223,9 +223,11 @@ int mrt_gemm_host(mrt_weight w, const void* x_host, void* y_host, int64_t M, uns
  * host buffers: both buffers must be page-locked (cudaHostAlloc /
  * cudaHostRegister) and stay valid, x unmodified and y unread, until
  * mrt_sync(stream) returns.  Rows travel in chunks on the library's copy
- * streams as in mrt_gemm_host; consecutive calls use two device staging sets
- * in turn, so one call's copies to the host overlap the next call's copies to
- * the device and its products.  Every call of a thread must use one stream. */
+ * streams as in mrt_gemm_host; consecutive calls use four device staging
+ * sets in turn, so earlier calls' copies to the host overlap later calls'
+ * copies to the device and their products (PCIe carries both directions at
+ * once: queue calls with large outputs before calls with large inputs).
+ * Every call of a thread must use one stream. */
 int mrt_gemm_host_async(mrt_weight w, const void* x_host, void* y_host, int64_t M, unsigned flags,
                         void* stream);
 

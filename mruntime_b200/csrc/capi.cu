@@ -1081,13 +1081,13 @@ extern "C" int mrt_gemm_host_async(mrt_weight w, const void* x_host, void* y_hos
     int rc = io_pipeline_init(c);
     if (rc != MRT_OK) return rc;
     cudaError_t e = cudaSuccess;
-    for (int k = 0; k < 2 && e == cudaSuccess; ++k)
+    for (int k = 0; k < DevCtx::kAsyncSets && e == cudaSuccess; ++k)
         if (c->a_free[k] == nullptr) e = cudaEventCreateWithFlags(&c->a_free[k], cudaEventDisableTiming);
     if (e != cudaSuccess) return cuda_error(e, "creating the staging events");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const bool bias = (flags & MRT_GEMM_BIAS) != 0;
     const int set = c->a_next;
-    c->a_next ^= 1;
+    c->a_next = (set + 1) % DevCtx::kAsyncSets;
     const size_t xb = static_cast<size_t>(M * w->k) * 2, yb = static_cast<size_t>(M * w->n) * 2;
     if (c->ax_bytes[set] < xb || c->ay_bytes[set] < yb) {
         // Growing a set waits for its last user (ensure_buffer synchronises).
@@ -1096,7 +1096,7 @@ extern "C" int mrt_gemm_host_async(mrt_weight w, const void* x_host, void* y_hos
         if (rc != MRT_OK) return rc;
     }
     // This set's previous call is done with it (its last copy to the host);
-    // the other set's call may still be copying in either direction.
+    // the other sets' calls may still be copying in either direction.
     if ((e = cudaStreamWaitEvent(c->io_in, c->a_free[set], 0)) != cudaSuccess ||
         (e = cudaStreamWaitEvent(s, c->a_free[set], 0)) != cudaSuccess)
         return cuda_error(e, "ordering the staging set");

@@ -37,13 +37,16 @@ struct DevCtx {
     cudaEvent_t io_start = nullptr;
     cudaEvent_t io_h2d[kIoChunks] = {};
     cudaEvent_t io_mm[kIoChunks] = {};
-    // mrt_gemm_host_async: two staging sets used in turn, each free again once
-    // the event recorded after its last copy to the host has completed.
-    void* ax[2] = {};
-    size_t ax_bytes[2] = {};
-    void* ay[2] = {};
-    size_t ay_bytes[2] = {};
-    cudaEvent_t a_free[2] = {};
+    // mrt_gemm_host_async: kAsyncSets staging sets used in turn, each free
+    // again once the event recorded after its last copy to the host has
+    // completed (four: a step of four projections never waits for its own
+    // earlier calls' copies to the host before copying its inputs in).
+    static constexpr int kAsyncSets = 4;
+    void* ax[kAsyncSets] = {};
+    size_t ax_bytes[kAsyncSets] = {};
+    void* ay[kAsyncSets] = {};
+    size_t ay_bytes[kAsyncSets] = {};
+    cudaEvent_t a_free[kAsyncSets] = {};
     int a_next = 0;
 };
 
