@@ -257,6 +257,14 @@ __host__ __device__ __forceinline__ int64_t tiled_offset(int64_t r, int64_t k, i
     return (((r >> 7) * k_tiles + (k >> 6)) << 13) + (rr << 6) + (chunk << 3) + (kk & 7);
 }
 
+// 32-byte store (one whole L2 sector per thread); p must be 32-byte aligned.
+__device__ __forceinline__ void st_global_v8(void* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d, uint32_t e,
+                                             uint32_t f, uint32_t g, uint32_t h) {
+    asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(a), "r"(b), "r"(c), "r"(d),
+                 "r"(e), "r"(f), "r"(g), "r"(h)
+                 : "memory");
+}
+
 // ------------------------------------------------------------------ dependent launch
 
 // Let the next kernel in the stream (launched with programmatic stream

@@ -112,9 +112,17 @@ __device__ __forceinline__ uint32_t pack_h2(uint16_t lo, uint16_t hi) {
 __device__ __forceinline__ void store_partial_chunk(const TcGemmArgs& a, const uint32_t (&r)[32], int slot,
                                                    int row_in_tile, int col_in_tile, int bn, int tile_rows = kBM) {
     float* dst = a.partials + (static_cast<int64_t>(slot) * tile_rows + row_in_tile) * bn + col_in_tile;
+    if ((reinterpret_cast<uintptr_t>(dst) & 31) == 0) {
+        // whole 32-byte sectors: a partial-sector write costs the memory
+        // system a read-modify-write of the sector
 #pragma unroll
-    for (int j = 0; j < 32; j += 4)
-        *reinterpret_cast<uint4*>(dst + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+        for (int j = 0; j < 32; j += 8)
+            st_global_v8(dst + j, r[j], r[j + 1], r[j + 2], r[j + 3], r[j + 4], r[j + 5], r[j + 6], r[j + 7]);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<uint4*>(dst + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+    }
 }
 
 // Store 32 accumulator columns of one output row.
@@ -123,7 +131,11 @@ __device__ __forceinline__ void store_row_chunk(const TcGemmArgs& a, const uint3
     if (a.out_f32) {
         float* dst = static_cast<float*>(a.y) + row * a.ldy + col0;
         const bool vec = col0 + 32 <= a.N && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0);
-        if (vec) {
+        if (vec && (reinterpret_cast<uintptr_t>(dst) & 31) == 0) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8)
+                st_global_v8(dst + j, r[j], r[j + 1], r[j + 2], r[j + 3], r[j + 4], r[j + 5], r[j + 6], r[j + 7]);
+        } else if (vec) {
 #pragma unroll
             for (int j = 0; j < 32; j += 4)
                 *reinterpret_cast<uint4*>(dst + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
@@ -161,9 +173,15 @@ __device__ __forceinline__ void store_row_chunk(const TcGemmArgs& a, const uint3
                 }
             }
         }
+        if ((reinterpret_cast<uintptr_t>(dst) & 31) == 0) {
+            // whole 32-byte sectors (see store_partial_chunk)
+            st_global_v8(dst, h[0], h[1], h[2], h[3], h[4], h[5], h[6], h[7]);
+            st_global_v8(dst + 16, h[8], h[9], h[10], h[11], h[12], h[13], h[14], h[15]);
+        } else {
 #pragma unroll
-        for (int j = 0; j < 16; j += 4)
-            *reinterpret_cast<uint4*>(dst + 2 * j) = make_uint4(h[j], h[j + 1], h[j + 2], h[j + 3]);
+            for (int j = 0; j < 16; j += 4)
+                *reinterpret_cast<uint4*>(dst + 2 * j) = make_uint4(h[j], h[j + 1], h[j + 2], h[j + 3]);
+        }
     } else {
 #pragma unroll
         for (int j = 0; j < 32; ++j)
