@@ -675,11 +675,16 @@ static TcPlan plan_tc(int64_t M, int64_t N, int64_t K, int sms, bool tiled = tru
             }
             return best;
         }
-        // With at least half a wave of pair tiles the pairs win outright
+        // With at least half a wave of pair tiles, and a last wave at least
+        // half full (or four waves and more), the pairs win outright
         // (measured at 1.5 waves against the one-SM kernel's K-split tails,
         // e.g. 7B o and down at M = 2048; at 0.57 waves, M = 768 o, 7 %
-        // faster); below it they leave SMs idle and compete on cost.
-        if (2 * tiles >= all_pairs || num_kb >= 256) return best;
+        // faster); otherwise they compete on cost (a 1.03-wave gate|up of
+        // the 0.5B layer at M = 512 ran 25.6 us on pairs, 20.9 us on one-SM
+        // 128-column tiles).
+        const int64_t rem = tiles % all_pairs;
+        const bool fills = rem == 0 || 2 * rem >= all_pairs || tiles >= 4 * all_pairs;
+        if ((2 * tiles >= all_pairs && fills) || num_kb >= 256) return best;
         const int64_t waves = (tiles + pairs - 1) / pairs;
         best_cost = 0.92 * static_cast<double>(waves) * unit_us(256, num_kb, 2 * pairs, sms, x_rows);
     }
