@@ -410,8 +410,16 @@ __device__ __forceinline__ bool gemv_split(const Gemv& g, const uint16_t* xs, co
 // the tile before), every later CTA's in segment 0.  Units are < 2^31 / G, so
 // 32-bit arithmetic is exact.
 struct TileSrc {
-    int c0, c1, seg0;
+    int c0, c1, seg0, units;
 };
+
+// Whether CTA c of the grid was given any unit of a split GEMV of `units`
+// units (with fewer units than CTAs some get none and never write their
+// partial slots, which are then not part of any tile's sum).
+__device__ __forceinline__ bool cta_has_units(int c, int units) {
+    const int G = static_cast<int>(gridDim.x);
+    return units * (c + 1) / G > units * c / G;
+}
 
 __device__ __forceinline__ int unit_owner(int u, int units) {
     const int G = static_cast<int>(gridDim.x);
@@ -427,6 +435,7 @@ __device__ __forceinline__ TileSrc tile_src(int64_t t, int64_t kt, int64_t units
     s.c0 = unit_owner(u, U);
     s.c1 = unit_owner(u + static_cast<int>(kt) - 1, U);
     s.seg0 = (U * s.c0 / G) / static_cast<int>(kt) == static_cast<int>(t) ? 0 : 1;
+    s.units = U;
     return s;
 }
 
@@ -441,10 +450,11 @@ __device__ __forceinline__ float tile_sum(const float* part, const TileSrc& s, i
     for (int cb = s.c0; cb <= s.c1; cb += 8) {
         float p[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) p[j] = cb + j <= s.c1 ? __ldcg(tile_part(part, s, cb + j) + r) : 0.0f;
+        for (int j = 0; j < 8; ++j)
+            p[j] = cb + j <= s.c1 && cta_has_units(cb + j, s.units) ? __ldcg(tile_part(part, s, cb + j) + r) : 0.0f;
 #pragma unroll
         for (int j = 0; j < 8; ++j)
-            if (cb + j <= s.c1) v = cb + j == s.c0 ? p[j] : __fadd_rn(v, p[j]);
+            if (cb + j <= s.c1 && cta_has_units(cb + j, s.units)) v = cb + j == s.c0 ? p[j] : __fadd_rn(v, p[j]);
     }
     return v;
 }
@@ -455,14 +465,14 @@ __device__ __forceinline__ void tile_sum8(const float* part, const TileSrc& s, i
         float4 p0[8], p1[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j)
-            if (cb + j <= s.c1) {
+            if (cb + j <= s.c1 && cta_has_units(cb + j, s.units)) {
                 const float4* q = reinterpret_cast<const float4*>(tile_part(part, s, cb + j) + r0);
                 p0[j] = __ldcg(q);
                 p1[j] = __ldcg(q + 1);
             }
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            if (cb + j > s.c1) continue;
+            if (cb + j > s.c1 || !cta_has_units(cb + j, s.units)) continue;
             const float w[8] = {p0[j].x, p0[j].y, p0[j].z, p0[j].w, p1[j].x, p1[j].y, p1[j].z, p1[j].w};
 #pragma unroll
             for (int e = 0; e < 8; ++e) v[e] = cb + j == s.c0 ? w[e] : __fadd_rn(v[e], w[e]);
