@@ -166,10 +166,32 @@ class _PersistentStep:
             os.environ["MRT_DECODE_STEP"] = self.old
 
 
-def test_tiny_persistent_step_matches_reference_engine(cuda_dev):
+def _dirty_device_memory(mib: int = 64) -> None:
+    """Allocate device memory through the library, fill it with non-zero
+    values and free it, so buffers a decoder allocates next may start with
+    stale contents instead of the driver's zeroed pages."""
+    import ctypes as C
+
+    n = (mib << 20) // 2
+    ptr = C.c_void_p()
+    capi.call("mrt_device_alloc", C.c_size_t(n * 2), C.byref(ptr))
+    src = torch.full((n,), 3.0, dtype=torch.float32, device="cuda")
+    capi.convert(src.data_ptr(), capi.FP32, ptr.value, capi.FP16, n, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    del src
+    capi.call("mrt_device_free", ptr)
+
+
+@pytest.mark.parametrize("dirty", [False, True])
+def test_tiny_persistent_step_matches_reference_engine(cuda_dev, dirty):
+    """The persistent step on the tiny model (fewer split-GEMV units than
+    CTAs: the tile sums must skip the CTAs that got none), also after stale
+    non-zero memory was handed back to the driver."""
     g = _golden("tiny")
     cfg = W.DECODER_TINY
     prompt = W.decoder_prompt(g["seed"], g["prompt_len"], cfg["vocab_size"])
+    if dirty:
+        _dirty_device_memory()
     with _PersistentStep():  # read when the decoder finalises, at its first generate
         dec = _build(cfg, g["prompt_len"] + g["max_new"], g["seed"])
         toks, st = dec.generate(prompt, g["max_new"])
