@@ -689,6 +689,11 @@ static TcPlan plan_tc(int64_t M, int64_t N, int64_t K, int sms, bool tiled = tru
         best_cost = 0.92 * static_cast<double>(waves) * unit_us(256, num_kb, 2 * pairs, sms, x_rows);
     }
     for (int bn : {256, 128, 64}) {
+        // One 128-row m-tile (decode batches of 65..128 tokens): 256-column
+        // tiles measured slower than 128-column ones on every 7B projection
+        // and the 0.5B lm_head at M = 128 (gate+up 53.2 vs 50.5 us, lm_head
+        // 63.6 vs 57.4, down 35.6 vs 34.8), so they are not considered.
+        if (num_m == 1 && bn == 256) continue;
         const int64_t tiles = num_m * ((N + bn - 1) / bn);
         // every tile over the whole K
         {
