@@ -346,36 +346,54 @@ __global__ void __launch_bounds__(256) p2p_reduce_kernel(const P2PArgs a) {
     const unsigned long long epoch = *a.epoch + 1ull;
     const unsigned all = (a.world >= 32 ? 0xFFFFFFFFu : ((1u << a.world) - 1u));
     if (p2p_meet(a, 0, epoch, blockIdx.x == 0) != all) return;  // a peer is missing: error raised
-    // Octets of 8 elements: 32 bytes read from every rank and 16 bytes
-    // written to every rank per thread and step (a warp: 1 KB / 512 B runs).
+    // This rank's slice (whole octets of elements), walked 256 elements per
+    // warp and step: lane i reads float4 i and 32 + i of the step from every
+    // rank -- each instruction one contiguous 512-byte run, four whole lines
+    // per request over NVLink -- and writes the rounded halves back as two
+    // 8-byte pieces per rank (256-byte runs).
     const int64_t groups = a.count / 8;
     const int64_t g0 = groups * a.rank / a.world, g1 = groups * (a.rank + 1) / a.world;
-    for (int64_t g = g0 + blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; g < g1;
-         g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        float4 v0[kP2PMaxRanks], v1[kP2PMaxRanks];
+    const int64_t f_begin = g0 * 2, f_end = g1 * 2;  // float4 indices
+    const int lane = static_cast<int>(threadIdx.x) & 31;
+    const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+    for (int64_t base = f_begin + warp0 * 64; base < f_end; base += nwarps * 64) {
+        const int64_t fa = base + lane, fb = base + 32 + lane;
+        const bool ha = fa < f_end, hb = fb < f_end;
+        float4 va[kP2PMaxRanks], vb[kP2PMaxRanks];
 #pragma unroll
         for (int q = 0; q < kP2PMaxRanks; ++q)
             if (q < a.world) {
-                const float4* src = reinterpret_cast<const float4*>(a.part[q]) + 2 * g;
-                v0[q] = __ldcg(src);
-                v1[q] = __ldcg(src + 1);
+                const float4* src = reinterpret_cast<const float4*>(a.part[q]);
+                if (ha) va[q] = __ldcg(src + fa);
+                if (hb) vb[q] = __ldcg(src + fb);
             }
-        float t[8] = {v0[0].x, v0[0].y, v0[0].z, v0[0].w, v1[0].x, v1[0].y, v1[0].z, v1[0].w};
+        float ta[4] = {va[0].x, va[0].y, va[0].z, va[0].w};
+        float tb[4] = {vb[0].x, vb[0].y, vb[0].z, vb[0].w};
 #pragma unroll
         for (int q = 1; q < kP2PMaxRanks; ++q)
             if (q < a.world) {
-                const float u[8] = {v0[q].x, v0[q].y, v0[q].z, v0[q].w, v1[q].x, v1[q].y, v1[q].z, v1[q].w};
+                const float ua[4] = {va[q].x, va[q].y, va[q].z, va[q].w};
+                const float ub[4] = {vb[q].x, vb[q].y, vb[q].z, vb[q].w};
 #pragma unroll
-                for (int e = 0; e < 8; ++e) t[e] = __fadd_rn(t[e], u[e]);
+                for (int e = 0; e < 4; ++e) {
+                    ta[e] = __fadd_rn(ta[e], ua[e]);
+                    tb[e] = __fadd_rn(tb[e], ub[e]);
+                }
             }
-        uint32_t h[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-            h[e] = static_cast<uint32_t>(f32_to_f16_bits(t[2 * e])) | (static_cast<uint32_t>(f32_to_f16_bits(t[2 * e + 1])) << 16);
-        const uint4 hv = make_uint4(h[0], h[1], h[2], h[3]);
+        const uint2 ha2 = make_uint2(
+            static_cast<uint32_t>(f32_to_f16_bits(ta[0])) | (static_cast<uint32_t>(f32_to_f16_bits(ta[1])) << 16),
+            static_cast<uint32_t>(f32_to_f16_bits(ta[2])) | (static_cast<uint32_t>(f32_to_f16_bits(ta[3])) << 16));
+        const uint2 hb2 = make_uint2(
+            static_cast<uint32_t>(f32_to_f16_bits(tb[0])) | (static_cast<uint32_t>(f32_to_f16_bits(tb[1])) << 16),
+            static_cast<uint32_t>(f32_to_f16_bits(tb[2])) | (static_cast<uint32_t>(f32_to_f16_bits(tb[3])) << 16));
 #pragma unroll
         for (int q = 0; q < kP2PMaxRanks; ++q)
-            if (q < a.world) reinterpret_cast<uint4*>(a.out[q])[g] = hv;
+            if (q < a.world) {
+                uint2* dst = reinterpret_cast<uint2*>(a.out[q]);
+                if (ha) dst[fa] = ha2;
+                if (hb) dst[fb] = hb2;
+            }
     }
     // the last count % 8 elements: the last rank's first thread
     if (a.rank == a.world - 1 && blockIdx.x == 0 && threadIdx.x == 0) {
