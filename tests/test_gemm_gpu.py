@@ -198,12 +198,14 @@ def test_tensor_core_kernel(cuda_dev, M, NK):
 # One shape per tcgen05 plan kind the planner can pick: mode (X or W as the
 # 128-row operand) x bn x (every tile over the whole K | whole waves + K-split
 # tail (normal mode) | every tile split).  Swap mode's whole-tile plans run
-# one or two CTAs per SM (20000 rows: 157 tiles on 157 CTAs).
+# one or two CTAs per SM (20000 rows: 157 tiles on 157 CTAs).  256-column
+# normal-mode tiles need two 128-row m-tiles (single m-tile plans use 128 or
+# 64 columns).
 PLAN_SHAPES = {
     ("tcgen05", 64, "full"): (65, 64, 64), ("tcgen05", 64, "uniform"): (65, 64, 896),
     ("tcgen05", 128, "full"): (200, 4864, 64), ("tcgen05", 128, "hybrid"): (65, 20000, 2048),
-    ("tcgen05", 128, "uniform"): (700, 200, 2048), ("tcgen05", 256, "full"): (65, 20000, 136),
-    ("tcgen05", 256, "hybrid"): (65, 40000, 896), ("tcgen05", 256, "uniform"): (65, 4864, 4864),
+    ("tcgen05", 128, "uniform"): (700, 200, 2048), ("tcgen05", 256, "full"): (129, 40000, 136),
+    ("tcgen05", 256, "hybrid"): (129, 20000, 512), ("tcgen05", 256, "uniform"): (129, 4864, 2048),
     ("tcgen05-swap", 16, "full"): (1, 20000, 896), ("tcgen05-swap", 16, "uniform"): (1, 64, 896),
     ("tcgen05-swap", 32, "full"): (17, 20000, 896), ("tcgen05-swap", 32, "uniform"): (17, 64, 896),
     ("tcgen05-swap", 64, "full"): (40, 20000, 896), ("tcgen05-swap", 64, "uniform"): (40, 640, 896),
