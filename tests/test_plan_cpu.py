@@ -4,6 +4,8 @@ checked by launch_tc_gemm before a launch; here they are swept over the
 reference's shapes, ragged sizes and smaller SM counts on the CPU."""
 from __future__ import annotations
 
+import os
+
 import numpy as np
 import pytest
 
@@ -71,3 +73,31 @@ def test_plan_rejects_bad_shapes():
     for M, N, K in ((0, 8, 8), (1, 0, 8), (1, 8, 0), (-1, 8, 8)):
         with pytest.raises(capi.MrtError):
             capi.gemm_plan(M, N, K, 148)
+
+
+def test_plan_rules_from_measurements():
+    """Planner rules fitted to B200 measurements: single m-tile plans (65..128
+    tokens) use 128- or 64-column tiles; SM pairs take over whole-K at a full
+    last wave, K-split tails only for long K (down, K = 18944), and give way to
+    the cost comparison when their last wave is nearly empty."""
+    # single m-tile: never 256-column tiles
+    for N, K in ((4608, 3584), (3584, 3584), (37888, 3584), (3584, 18944), (151936, 896)):
+        for M in (65, 100, 128):
+            assert capi.gemm_plan(M, N, K, 148)["bn"] in (64, 128), (M, N, K)
+    # 7B prefill at M = 2048: pairs; whole K for q|k|v, o, gate+up; the down
+    # projection's last half wave cut into K-slices
+    for N, K in ((4608, 3584), (3584, 3584), (37888, 3584)):
+        p = capi.gemm_plan(2048, N, K, 148)
+        tiles = 8 * -(-N // 256)
+        assert p["pair"] and p["full_tiles"] == tiles and p["tail_splits"] == 1, (N, K, p)
+    p = capi.gemm_plan(2048, 3584, 18944, 148)
+    assert p["pair"] and p["full_tiles"] == 74 and p["tail_splits"] >= 2, p
+    # 76 pair tiles (a last wave of 2 on 74 pairs) at short K: not pairs
+    assert not capi.gemm_plan(512, 9728, 896, 148)["pair"]
+    # MRT_GEMM_PAIR_SPLITS forces the pair tail's slice count
+    os.environ["MRT_GEMM_PAIR_SPLITS"] = "3"
+    try:
+        p = capi.gemm_plan(2048, 3584, 3584, 148)
+    finally:
+        os.environ.pop("MRT_GEMM_PAIR_SPLITS", None)
+    assert p["pair"] and p["full_tiles"] == 74 and p["tail_splits"] == 3, p
