@@ -184,9 +184,11 @@ int mrt_gemm(mrt_weight w, const void* x_dev, int64_t ldx, void* y_dev, int64_t 
  * as the 128-row MMA operand (M > 64), 2 = tcgen05 in swap mode with the
  * weight as the 128-row operand and the tokens as N (M <= 64), 3 = swap mode
  * whose K-slices (every tile split, 2..8 slices, one per CTA) are summed
- * inside thread-block clusters on the current device; then the tile's bn,
- * the number of tiles run over the whole K, the K-slices of each remaining
- * tile, k-blocks per slice and the persistent grid.  Host-only. */
+ * inside thread-block clusters on the current device, 4 = kernel 1 on SM
+ * pairs, 5 = the SIMT GEMV (one token, a tiled weight of at most 20 MB;
+ * bn 0, no tiles, kb_per = the k-blocks of K, grid = its CTAs); then the
+ * tile's bn, the number of tiles run over the whole K, the K-slices of each
+ * remaining tile, k-blocks per slice and the persistent grid.  Host-only. */
 int mrt_gemm_plan(int64_t M, int64_t N, int64_t K, int sms, int* kernel, int* bn, int* full_tiles,
                   int* tail_splits, int* kb_per, int* grid);
 

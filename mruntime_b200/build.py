@@ -34,7 +34,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "-Xcompiler", "-fPIC",
               "-Xcompiler", "-Wall", "-Xptxas", "-v"]
 
-KERNEL_SOURCES = ["capi.cu", "tp.cu", "gemm_tc.cu", "elementwise.cu", "general_gemm.cu", "ops.cu", "noalloc.cu",
+KERNEL_SOURCES = ["capi.cu", "tp.cu", "gemm_tc.cu", "gemv.cu", "elementwise.cu", "general_gemm.cu", "ops.cu", "noalloc.cu",
                   "decoder.cu", "decode_step.cu", "loader.cu"]
 
 

@@ -236,7 +236,7 @@ def gemm_plan(M: int, N: int, K: int, sms: int = 0) -> dict:
     d = dict(zip(keys, (v.value for v in vals)))
     d["cluster"] = d["kernel"] == 3  # swap mode, K-slices summed inside clusters
     d["pair"] = d["kernel"] == 4  # normal mode on SM pairs (cta_group::2)
-    d["kernel"] = {1: "tcgen05", 2: "tcgen05-swap", 3: "tcgen05-swap", 4: "tcgen05"}[d["kernel"]]
+    d["kernel"] = {1: "tcgen05", 2: "tcgen05-swap", 3: "tcgen05-swap", 4: "tcgen05", 5: "gemv"}[d["kernel"]]
     return d
 
 

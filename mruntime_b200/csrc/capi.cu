@@ -735,6 +735,40 @@ static TcPlan plan_tc(int64_t M, int64_t N, int64_t K, int sms, bool tiled = tru
 // tokens' FP32 columns of every slice; with 8 tokens or fewer that read is one
 // short pass and the global finish is the faster one (cluster_tokens).
 // MRT_GEMM_CLUSTER=0 (read once) keeps the global-memory finish everywhere.
+// The SIMT GEMV (gemv.cu) on a tiled weight: by default for one token and
+// weights of at most kGemvMaxBytes.  Measured on B200 in graph-chained calls
+// with the weights cold in L2: 4864x896 (8.7 MB) 4.17 us against 5.44 for the
+// swap-mode tcgen05 kernel, the Qwen2.5-0.5B projections 17.0 against 22.9 us
+// per layer, the 7B projections sharded eight ways 25.0 against 26.9 us; but
+// the weights of 30 MB and more stream faster through the tcgen05 ring (7B
+// gate+up 41.6 against 51.8 us), and from two tokens on the activation loads
+// per weight load cost more than the tensor cores' set-up.  MRT_GEMV=1 takes
+// it for every call of 1..4 tokens it can run, MRT_GEMV=0 never (read per
+// call).
+constexpr double kGemvMaxBytes = 20e6;
+
+static bool use_gemv(int64_t M, int64_t N, int64_t K) {
+    if (M < 1 || M > 4) return false;
+    const char* v = std::getenv("MRT_GEMV");
+    if (v != nullptr && std::strcmp(v, "1") == 0) return true;
+    if (v != nullptr && std::strcmp(v, "0") == 0) return false;
+    return M == 1 && 2.0 * static_cast<double>(N) * static_cast<double>(K) <= kGemvMaxBytes;
+}
+
+// Row quads per GEMV CTA: the most (whole K per warp) that still gives at
+// least two CTAs per SM, else one quad whose eight warps split K.
+// MRT_GEMV_RQ=1|2|4|8 forces it (read per call).
+static int gemv_row_quads(int64_t N, int sms) {
+    if (const char* v = std::getenv("MRT_GEMV_RQ")) {
+        const int f = std::atoi(v);
+        if (f == 1 || f == 2 || f == 4 || f == 8) return f;
+    }
+    const int64_t quads = (N + 3) / 4;
+    int rq = 8;
+    while (rq > 1 && (quads + rq - 1) / rq < 2LL * sms) rq /= 2;
+    return rq;
+}
+
 static bool use_cluster(bool swap, const TcPlan& p, int64_t tiles, int64_t M) {
     static const bool enabled = [] {
         const char* v = std::getenv("MRT_GEMM_CLUSTER");
@@ -804,6 +838,21 @@ static int gemm_dispatch(mrt_weight w, const void* x, int64_t ldx, void* y, int6
         g.residual = epi.residual; g.ldr = epi.ldr;
         e = launch_general_gemm(g, s);
         return e == cudaSuccess ? MRT_OK : cuda_error(e, "general gemm launch");
+    }
+    if (w->tiled && epi.am_val == nullptr && use_gemv(M, w->n, w->k) &&
+        (swiglu_lut == nullptr || ((w->n & 1) == 0 && !out_f32 && bias == nullptr))) {
+        GemvArgs g{};
+        g.w = w->data; g.k_tiles = w->k_tiles;
+        g.x = static_cast<const uint16_t*>(x); g.ldx = ldx;
+        g.y = y; g.ldy = ldy; g.out_f32 = out_f32 ? 1 : 0; g.bias = bias;
+        g.residual = epi.residual; g.ldr = epi.ldr;
+        g.M = static_cast<int>(M); g.N = static_cast<int>(w->n); g.K = static_cast<int>(w->k);
+        g.swiglu_lut = swiglu_lut;
+        g.rq = gemv_row_quads(w->n, c->sms);
+        e = launch_gemv_tiled(g, s);
+        if (e != cudaSuccess) return cuda_error(e, "gemv launch");
+        if (fused) *fused = swiglu_lut != nullptr;
+        return MRT_OK;
     }
     const bool swap = M <= 64;
     const TcPlan p = swap ? plan_swap(M, w->n, w->k, c->sms) : plan_tc(M, w->n, w->k, c->sms, w->tiled);
@@ -914,6 +963,16 @@ extern "C" int mrt_gemm_plan(int64_t M, int64_t N, int64_t K, int sms, int* kern
         DevCtx* c = current_ctx();
         if (!c) return MRT_ERR_CUDA;
         sms = c->sms;
+    }
+    if (use_gemv(M, N, K)) {
+        const int rq = gemv_row_quads(N, sms);
+        if (kernel) *kernel = 5;
+        if (bn) *bn = 0;
+        if (full_tiles) *full_tiles = 0;
+        if (tail_splits) *tail_splits = 1;
+        if (kb_per) *kb_per = static_cast<int>((K + 63) / 64);
+        if (grid) *grid = static_cast<int>(((N + 3) / 4 + rq - 1) / rq);
+        return MRT_OK;
     }
     const bool swap = M <= 64;
     const TcPlan p = swap ? plan_swap(M, N, K, sms) : plan_tc(M, N, K, sms);

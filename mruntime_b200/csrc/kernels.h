@@ -112,6 +112,27 @@ cudaError_t launch_tc_pair(const TcGemmArgs& a, const CUtensorMap& tmap_x, const
 // the whole GPU, round (+bias) or keep FP32, and store.
 cudaError_t launch_reduce_tail(const TcGemmArgs& a, cudaStream_t s);
 
+// y = x * W^T for 1..4 tokens on the tiled weight layout (gemv.cu): SIMT
+// 16-byte weight loads, FP32 sums, no scratch memory.  x: M rows of K FP16
+// (16-byte aligned, ldx a multiple of 8); y: FP16 (bias, residual or SwiGLU
+// as in the tcgen05 kernel's epilogue) or FP32.  rq: row quads per CTA (1, 2, 4, 8).
+struct GemvArgs {
+    const uint16_t* w;  // tiled weight [n_pad / 128][k_tiles][128][64]
+    int64_t k_tiles;
+    const uint16_t* x;
+    int64_t ldx;
+    void* y;
+    int64_t ldy;
+    int out_f32;
+    const uint16_t* bias;      // FP16, N entries, or null
+    const uint16_t* residual;  // y = fp16(residual + fp16(acc)), or null
+    int64_t ldr;
+    const uint16_t* swiglu_lut;  // SwiGLU on interleaved gate|up rows (N even, FP16 out, no bias), or null
+    int M, N, K;
+    int rq;
+};
+cudaError_t launch_gemv_tiled(const GemvArgs& a, cudaStream_t s);
+
 
 // Element-wise conversions with the reference's rounding.
 cudaError_t launch_convert(const void* src, int src_dtype, void* dst, int dst_dtype, int64_t n,

@@ -170,7 +170,8 @@ def _check_against_oracle(x, w, wdt, y, rows=None, what=""):
 
 @pytest.mark.parametrize("M", [1, 2, 3, 4, 7, 8, 9, 15, 16, 17, 31, 32, 33, 48, 63, 64])
 @pytest.mark.parametrize("NK", [(200, 64), (257, 136), (1000, 896)])
-def test_skinny_kernel(cuda_dev, M, NK):
+def test_skinny_kernel(cuda_dev, monkeypatch, M, NK):
+    monkeypatch.setenv("MRT_GEMV", "0")  # the swap-mode tcgen05 kernel (the GEMV has tests of its own)
     N, K = NK
     rng = np.random.default_rng(M * 7 + N)
     x = rand_f16(rng, (M, K))
@@ -213,7 +214,8 @@ PLAN_SHAPES = {
 
 
 @pytest.mark.parametrize("key", sorted(PLAN_SHAPES))
-def test_tensor_core_plan_kinds(cuda_dev, key):
+def test_tensor_core_plan_kinds(cuda_dev, monkeypatch, key):
+    monkeypatch.setenv("MRT_GEMV", "0")
     M, N, K = PLAN_SHAPES[key]
     p = capi.gemm_plan(M, N, K)
     tiles = -(-N // 128) if p["kernel"] == "tcgen05-swap" else -(-M // 128) * -(-N // p["bn"])
@@ -388,12 +390,15 @@ def test_gemm_swiglu(cuda_dev, MIK):
     w = rand_w(rng, (2 * I, K), BF16)  # row 2j = gate j, row 2j + 1 = up j
     wt = upload(w, BF16)
     p = capi.gemm_plan(M, 2 * I, K)
-    if p["pair"]:
+    if p["kernel"] == "gemv":
+        tiles = 0  # the GEMV runs SwiGLU in its own epilogue
+    elif p["pair"]:
         tiles = -(-M // 256) * -(-2 * I // 256)  # SM pairs: 256-row tiles, always the whole K
     else:
         tiles = -(-2 * I // 128) if p["kernel"] == "tcgen05-swap" else -(-M // 128) * -(-2 * I // p["bn"])
     fused = p["full_tiles"] == tiles
-    assert fused == (I in (18944,)), p  # the shapes above cover both routes
+    if p["kernel"] != "gemv":
+        assert fused == (I in (18944,)), p  # the shapes above cover both routes
     y = gemm(wt, x)  # same plan: the same FP16 gate and up values
     xd = dev_u16(x)
     act = torch.empty((M, I), dtype=torch.int16, device="cuda")

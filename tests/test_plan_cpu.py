@@ -36,6 +36,12 @@ def test_every_plan_is_launchable(sms):
         num_kb = -(-K // 64)
         for M in MS:
             p = capi.gemm_plan(M, N, K, sms)
+            if M == 1 and 2 * N * K <= 20e6:
+                # one token, a small weight: the SIMT GEMV, row quads 1/2/4/8 per CTA
+                assert p["kernel"] == "gemv" and p["bn"] == 0 and p["kb_per"] == num_kb, (N, K, p)
+                quads = -(-N // 4)
+                assert p["grid"] in [-(-quads // rq) for rq in (1, 2, 4, 8)], (N, K, p)
+                continue
             swap = M <= 64
             assert p["kernel"] == ("tcgen05-swap" if swap else "tcgen05"), (M, N, K, p)
             assert not p["cluster"]  # cluster plans need a device to check residency
@@ -67,6 +73,24 @@ def test_every_plan_is_launchable(sms):
                 assert p["grid"] <= (2 * units if p["pair"] else units), (M, N, K, p)
             else:
                 assert splits == 1 and p["grid"] <= (2 * tiles if p["pair"] else tiles), (M, N, K, p)
+
+
+def test_gemv_plan_rule(monkeypatch):
+    """One token on a weight of at most 20 MB runs the SIMT GEMV (measured
+    faster there than the swap-mode tcgen05 kernel); larger weights, and two
+    or more tokens, keep the tensor cores; MRT_GEMV forces either way."""
+    assert capi.gemm_plan(1, 4864, 896, 148)["kernel"] == "gemv"
+    assert capi.gemm_plan(1, 896, 4864, 148)["kernel"] == "gemv"
+    for N, K in ((4608, 3584), (3584, 3584), (37888, 3584), (3584, 18944), (151936, 896)):
+        assert capi.gemm_plan(1, N, K, 148)["kernel"] == "tcgen05-swap", (N, K)
+    assert capi.gemm_plan(2, 4864, 896, 148)["kernel"] == "tcgen05-swap"
+    # enough CTAs for two per SM where the rows allow it
+    assert capi.gemm_plan(1, 4864, 896, 148)["grid"] == 304
+    monkeypatch.setenv("MRT_GEMV", "0")
+    assert capi.gemm_plan(1, 4864, 896, 148)["kernel"] == "tcgen05-swap"
+    monkeypatch.setenv("MRT_GEMV", "1")
+    assert capi.gemm_plan(4, 37888, 3584, 148)["kernel"] == "gemv"
+    assert capi.gemm_plan(5, 64, 64, 148)["kernel"] == "tcgen05-swap"
 
 
 def test_plan_rejects_bad_shapes():
