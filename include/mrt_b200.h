@@ -173,7 +173,9 @@ int mrt_weight_read(mrt_weight w, void* dst_dev, int64_t ld, void* stream);
  * bias step does it: fp16(fp32(fp16(acc)) + fp32(bias))
  * (src/models/qwen/qwen_model.cpp:130-155).
  * Both regimes run the tcgen05 tensor-core kernel: M <= 64 (decode) with the
- * weight as the 128-row MMA operand streamed from HBM, larger M with X.  Replaces Backend::gemm (include/mruntime/backend.h:13-21)
+ * weight as the 128-row MMA operand streamed from HBM, larger M with X.  One
+ * token on a tiled weight of at most 20 MB runs a SIMT GEMV instead (no
+ * scratch memory; MRT_GEMV=0/1 never/always for 1..4 tokens).  Replaces Backend::gemm (include/mruntime/backend.h:13-21)
  * as implemented by CpuBackend::gemm (src/core/cpu_backend.cpp:72-169).
  */
 int mrt_gemm(mrt_weight w, const void* x_dev, int64_t ldx, void* y_dev, int64_t ldy, int64_t M,
